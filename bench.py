@@ -1,0 +1,422 @@
+#!/usr/bin/env python
+"""LIF-FDE layer throughput on B200: neuron-timesteps/s, forward + backward.
+
+Workload (one "step"): for T in (8, 16) and each scheme of the hot path -- distributed-order
+GL "glmulti" (full-history gradient, learnable Softplus masses), single-order GL,
+L1-2 trapezoid and the fractional predictor -- one LIFNeuronFDE layer forward and backward
+on an input current [T, 16, 128, 64, 64] (8,388,608 neurons) drawn i.i.d. N(0.3, 0.5^2),
+with upstream gradients N(0, 1) on the spikes (and on the membrane for the single-order
+schemes, which expose it).  Inputs are larger than L2 (537 MB per [16, N] tensor), so no
+L2 flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+N > 1 runs one process per GPU under torchrun: every rank processes its own 8.4M neurons
+(weak scaling) and the gradients of the shared Softplus masses are summed with one NCCL
+all-reduce per step.  Rank 0 prints one JSON line.
+"""
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "df-snn-official_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "LIF-FDE neuron-timesteps/s fwd+bwd"
+UNIT = "neuron-timesteps/s"
+SHAPE = (16, 128, 64, 64)
+TS = (8, 16)
+SCHEMES = ("glmulti", "gl", "trap", "predictor")
+TAU, TH, SG, H = 2.0, 1.0, 5.0, 0.1
+MULTI_BETA = [0.3, 0.4, 0.5]
+MASSES = [0.5, 0.5, 0.7]
+BETA = 0.5
+FALLBACK_HBM_GBS = 6650.0
+WORKLOAD = ("LIFNeuronFDE layer fwd+bwd, schemes glmulti(full history, softplus masses)/gl/trap/"
+            "predictor at T=8 and T=16, input [T,16,128,64,64] = 8,388,608 neurons per GPU, "
+            "x~N(0.3,0.5^2), upstream grads N(0,1)")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("native", "reference"), default="native")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--cpu-sample", type=int, default=1 << 22,
+                    help="neurons of the bounded CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def units_per_step(neurons):
+    return sum(T * neurons for T in TS for _ in SCHEMES)
+
+
+# -----------------------------------------------------------------------------------------
+# CPU side: the reference's own kernel sources compiled for the host (oracle/_ref) when
+# built, else the oracle port; bounded sample of the same workload, all host threads.
+# -----------------------------------------------------------------------------------------
+def cpu_workload_time(n_sample, seed=0):
+    import numpy as np
+
+    from oracle import oracle as O
+    import torch
+    from dfsnn_b200 import schedule
+
+    kind = "reference" if O.ref_available() else "port"
+    impl = "ref" if kind == "reference" else "oracle"
+    g = np.random.default_rng(seed)
+    x16 = g.normal(0.3, 0.5, size=(16, n_sample)).astype(np.float32)
+    gS16 = g.standard_normal((16, n_sample)).astype(np.float32)
+    gV16 = g.standard_normal((16, n_sample)).astype(np.float32)
+    v0 = np.zeros(n_sample, np.float32)
+    tables = {}
+    for T in TS:
+        basis = schedule.glmulti_basis(MULTI_BETA, T)
+        terms = schedule.build_glmulti_schedule(torch.tensor(MASSES), torch.tensor(MULTI_BETA),
+                                                basis, H, T)
+        tables[("glmulti", T)] = (terms["scale"].contiguous().numpy(), terms["weights"].numpy())
+        tables[("gl", T)] = schedule.gl_weights(BETA, T).numpy()
+        tables[("trap", T)] = schedule.trap_weights(BETA, T).numpy()
+        tables[("predictor", T)] = schedule.predictor_weights(BETA, T).numpy()
+    hb, g1 = schedule.predictor_constants(BETA, H)
+    t0 = time.perf_counter()
+    for T in TS:
+        x, gS, gV = x16[:T], gS16[:T], gV16[:T]
+        for sch in SCHEMES:
+            if sch == "glmulti":
+                scale, W = tables[(sch, T)]
+                fw = O.glmulti_forward(x, v0, scale, W, TAU, TH, impl=impl)
+                _, _, gpre = O.glmulti_backward(True, gS, scale, W, fw["vpre"], TAU, TH, SG, impl=impl)
+                O.glmulti_param_grads(gpre, fw["drift"], fw["vhist"])
+            else:
+                w = tables[(sch, T)]
+                s, v = O.single_forward(sch, x, v0, w, TAU, BETA, TH, hb, g1, impl=impl)
+                O.single_backward(sch, gS, gV, x, v0, w, TAU, BETA, TH, SG, hb, g1, impl=impl,
+                                  spike=s, vseq=v)
+    dt = time.perf_counter() - t0
+    return dt, kind, O.num_threads()
+
+
+def cpu_sample_desc(n, kind):
+    src = ("the reference's CUDA kernel sources compiled for the host with OpenMP "
+           "(oracle/_ref); shared-parameter reductions by the oracle in double"
+           if kind == "reference" else "the oracle port (oracle/lif_fde_oracle.c, OpenMP)")
+    return (f"{n} neurons (of 8,388,608) of the same workload: 4 schemes x T in (8,16), "
+            f"forward+backward, via {src}")
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    K, W = args.steps, max(args.warmup, 3)
+    # size each step so that the whole run stays within ~2 minutes
+    probe_n = 1 << 14
+    dt, kind, cores = cpu_workload_time(probe_n)
+    per_neuron = dt / probe_n
+    n = int(min(1 << 20, max(1 << 12, 90.0 / max(K + W, 1) / per_neuron)))
+    n = max(256, (n // 256) * 256)
+    for _ in range(W):
+        cpu_workload_time(n, seed=1)
+    t = 0.0
+    for i in range(K):
+        dt, kind, cores = cpu_workload_time(n, seed=2 + i % 3)
+        t += dt
+    units = units_per_step(n) * K
+    value = units / t
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": K, "warmup": W, "ms_per_step": 1e3 * t / K, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "neurons_per_step_sample": n},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": cpu_sample_desc(n, kind)},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# -----------------------------------------------------------------------------------------
+# GPU side
+# -----------------------------------------------------------------------------------------
+def measured_hbm_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(kernel, T):
+    """DRAM bytes per launch from the committed ncu summary, if one covers this kernel."""
+    path = os.path.join(REPO, "profiles", "ncu_traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d.get(f"{kernel}_T{T}")
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        import torch
+        self.proc = None
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", uuid], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            return None
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sms:
+            return None
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def make_layers(device):
+    from dfsnn_b200.neuron import LIFNeuronFDE
+    layers = {}
+    for T in TS:
+        for sch in SCHEMES:
+            kw = dict(tau=TAU, threshold=TH, surrogate_grad_scale=SG, surrogate_function="arctan",
+                      T=T, method=sch, step_size=H, batchsize=SHAPE[0], step_mode="m",
+                      backend="cupy")
+            if sch == "glmulti":
+                kw.update(beta=MULTI_BETA[0], multi_beta=MULTI_BETA, multi_coefficient=MASSES,
+                          learn_coefficient=True, coefficient_constraint="softplus",
+                          glmulti_history_grad="full")
+            else:
+                kw.update(beta=BETA, store_v_seq=True)
+            layers[(T, sch)] = LIFNeuronFDE(**kw).to(device)
+    return layers
+
+
+def layer_step(layer, x, gS, gV, single):
+    """One layer forward + backward; returns the gradients of the learnable masses."""
+    import torch
+    layer.reset()
+    x = x.detach().requires_grad_(True)
+    s = layer(x)
+    outs, grads = [s], [gS]
+    if single:
+        outs.append(layer.v_seq)
+        grads.append(gV)
+    params = [p for p in layer.parameters()]
+    res = torch.autograd.grad(outs, [x] + params, grads)
+    return res[0], s, list(res[1:])
+
+
+def run_native(args):
+    import torch
+    import torch.distributed as dist
+    from dfsnn_b200 import profiling
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    K, W = args.steps, max(args.warmup, 3)
+    neurons = math.prod(SHAPE)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    x16 = torch.randn((16,) + SHAPE, device=dev, generator=g).mul_(0.5).add_(0.3)
+    gS16 = torch.randn((16,) + SHAPE, device=dev, generator=g)
+    gV16 = torch.randn((16,) + SHAPE, device=dev, generator=g)
+    layers = make_layers(dev)
+
+    def step():
+        mass_grads = []
+        for T in TS:
+            for sch in SCHEMES:
+                _, _, pg = layer_step(layers[(T, sch)], x16[:T], gS16[:T], gV16[:T], sch != "glmulti")
+                mass_grads += pg
+        if world > 1 and mass_grads:
+            flat = torch.cat([p.reshape(-1) for p in mass_grads])
+            dist.all_reduce(flat)
+        return mass_grads
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with profiling.NativeCallTimer() as timer:
+        start.record()
+        for _ in range(K):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * K * units_per_step(neurons) / (ms_max / 1e3)
+    summary = timer.summary()
+    launches = timer.total_launches()
+
+    # dominant kernel (largest device time in the timed region) and its roofline
+    dom = max(summary.items(), key=lambda kv: kv[1]["ms_total"]) if summary else None
+    peak, peak_src = measured_hbm_peak()
+    roofline = None
+    if dom is not None:
+        name, d = dom
+        achieved = d["gbs"]
+        roofline = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": peak,
+                    "unit": "GB/s", "frac": achieved / peak if achieved else None,
+                    "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
+                    "algorithmic_bytes_per_launch": d["bytes_per_call"],
+                    "traffic": ncu_traffic(name, 16)}
+    kernels = {k: {"calls_per_step": v["calls"] / K, "ms_per_call": round(v["ms_per_call"], 4),
+                   "gbs": round(v["gbs"], 1) if v["gbs"] else None,
+                   "frac_of_hbm": round(v["gbs"] / peak, 4) if v["gbs"] else None}
+               for k, v in summary.items()}
+
+    # end to end through the public API with host buffers (pinned), copies timed
+    e2e = run_e2e(args, layers, x16, gS16, gV16, dev, world)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "neurons_per_gpu": neurons, "T": list(TS),
+                   "schemes": list(SCHEMES), "l2": "inputs larger than L2 (no flush)",
+                   "parallelism": f"dp{world}" + (" (one NCCL all-reduce of the mass grads per step)"
+                                                  if world > 1 else "")},
+        "gpu_launches": launches,
+        "roofline": roofline,
+        "kernels": kernels,
+        "clocks": clk,
+        "e2e": e2e,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        n = args.cpu_sample
+        dt, kind, cores = cpu_workload_time(n)
+        line["cpu_baseline"] = {"value": units_per_step(n) / dt, "unit": UNIT, "cores": cores,
+                                "kind": kind, "sample": cpu_sample_desc(n, kind)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(args, layers, x16, gS16, gV16, dev, world):
+    """Same step through LIFNeuronFDE with host inputs: every step copies each layer's input
+    current and upstream gradients from pinned host memory and reads its spikes and input
+    gradient back."""
+    import torch
+    import torch.distributed as dist
+    steps = max(1, args.e2e_steps)
+    hx = x16.cpu().pin_memory()
+    hgS = gS16.cpu().pin_memory()
+    hgV = gV16.cpu().pin_memory()
+    out_s = torch.empty(hx.shape, dtype=torch.float32).pin_memory()
+    out_g = torch.empty(hx.shape, dtype=torch.float32).pin_memory()
+    dx = torch.empty_like(x16)
+    dgS = torch.empty_like(gS16)
+    dgV = torch.empty_like(gV16)
+    h2d = d2h = 0
+
+    def one():
+        nonlocal h2d, d2h
+        h2d = d2h = 0
+        for T in TS:
+            for sch in SCHEMES:
+                single = sch != "glmulti"
+                dx[:T].copy_(hx[:T], non_blocking=True)
+                dgS[:T].copy_(hgS[:T], non_blocking=True)
+                h2d += 2 * hx[:T].numel() * 4
+                if single:
+                    dgV[:T].copy_(hgV[:T], non_blocking=True)
+                    h2d += hx[:T].numel() * 4
+                gx, s, _ = layer_step(layers[(T, sch)], dx[:T], dgS[:T], dgV[:T], single)
+                out_s[:T].copy_(s, non_blocking=True)
+                out_g[:T].copy_(gx, non_blocking=True)
+                d2h += 2 * hx[:T].numel() * 4
+
+    one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        one()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    value = world * steps * units_per_step(math.prod(SHAPE)) / (float(t.item()) / 1e3)
+    return {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": steps}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_native(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,249 @@
+// capi.cu -- extern "C" entry points declared in include/dfsnn_b200.h.
+// Validates arguments (nothing is launched on a bad call), picks the kernel variant
+// (T bucket, tau a power of two or not) and launches on the caller's stream.
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+
+#include "../../include/dfsnn_b200.h"
+#include "kernels.h"
+
+namespace {
+
+thread_local int g_last_cuda_error = 0;
+
+int cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return DFSNN_OK;
+    g_last_cuda_error = (int)e;
+    return DFSNN_ERR_CUDA;
+}
+
+bool finite(float v) { return std::isfinite(v); }
+
+bool valid_tau(float tau) { return finite(tau) && tau != 0.0f; }
+
+// 1/tau is exact and x/tau == x*(1/tau) for every x iff |tau| is a power of two
+// whose reciprocal is a normal float.
+bool tau_is_pow2(float tau) {
+    if (!finite(tau) || tau == 0.0f) return false;
+    int ex = 0;
+    const float m = std::frexp(std::fabs(tau), &ex);
+    return m == 0.5f && ex > -125 && ex < 126;
+}
+
+int check_seq(int T, long long N, int tmax) {
+    if (T < 1 || N < 0) return DFSNN_ERR_SHAPE;
+    if (T > tmax) return DFSNN_ERR_T_LIMIT;
+    return DFSNN_OK;
+}
+
+bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* dfsnn_status_string(int status) {
+    switch (status) {
+        case DFSNN_OK: return "ok";
+        case DFSNN_ERR_NULL: return "a required pointer is NULL";
+        case DFSNN_ERR_SHAPE: return "invalid shape (T < 1 or N < 0)";
+        case DFSNN_ERR_T_LIMIT: return "T exceeds the limit of this entry point";
+        case DFSNN_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+        case DFSNN_ERR_CUDA: return "CUDA error (see dfsnn_last_cuda_error)";
+        case DFSNN_ERR_SCHEME: return "unknown scheme id";
+        case DFSNN_ERR_PARAM: return "invalid scalar parameter (tau == 0 or non-finite)";
+        default: return "unknown status";
+    }
+}
+
+int dfsnn_last_cuda_error(void) { return g_last_cuda_error; }
+
+const char* dfsnn_version(void) { return "dfsnn_b200 0.1 sm_100a"; }
+
+// ---------------------------------------------------------------------------------------
+// library glmulti
+// ---------------------------------------------------------------------------------------
+int dfsnn_glmulti_forward(const float* x, const float* v0, const float* scale,
+                          const float* weights, float* spike, int T, long long N, float tau,
+                          float threshold, void* stream) {
+    if (int s = check_seq(T, N, DFSNN_MAX_T)) return s;
+    if (N > 0 && (!x || !v0 || !scale || !weights || !spike)) return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(threshold)) return DFSNN_ERR_PARAM;
+    return cuda_status(dfsnn::glmulti_forward_launch(x, v0, scale, weights, spike, T, N, tau,
+                                                     threshold, tau_is_pow2(tau),
+                                                     (cudaStream_t)stream));
+}
+
+size_t dfsnn_glmulti_backward_workspace_size(int T, long long N, int full_history) {
+    if (T < 1 || T > DFSNN_MAX_T_FULL || N < 0) return 0;
+    const int b1 = dfsnn::glmulti_bwd_blocks(T, N, full_history != 0, true);
+    const int b2 = dfsnn::glmulti_bwd_blocks(T, N, full_history != 0, false);
+    const int b = b1 > b2 ? b1 : b2;
+    return (size_t)b * (size_t)dfsnn::glmulti_part_stride(T) * sizeof(double);
+}
+
+int dfsnn_glmulti_backward(const float* grad_spike, const float* x, const float* v0,
+                           const float* scale, const float* weights, float* grad_x,
+                           float* grad_v0, float* grad_scale, float* grad_weights, int T,
+                           long long N, float tau, float threshold, float surrogate_scale,
+                           int full_history, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+    if (int s = check_seq(T, N, DFSNN_MAX_T_FULL)) return s;
+    if (!scale || !weights) return DFSNN_ERR_NULL;
+    if (N > 0 && (!grad_spike || !x || !v0 || !grad_x || !grad_v0)) return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(threshold) || !finite(surrogate_scale)) return DFSNN_ERR_PARAM;
+    if (!workspace || !aligned8(workspace)) return DFSNN_ERR_WORKSPACE;
+    const bool p2 = tau_is_pow2(tau);
+    const size_t stride = (size_t)dfsnn::glmulti_part_stride(T) * sizeof(double);
+    long long nb = dfsnn::glmulti_bwd_blocks(T, N, full_history != 0, p2);
+    const long long cap = (long long)(workspace_bytes / stride);
+    if (cap < 1) return DFSNN_ERR_WORKSPACE;
+    if (nb > cap) nb = cap;
+    return cuda_status(dfsnn::glmulti_backward_launch(
+        grad_spike, x, v0, scale, weights, grad_x, grad_v0, grad_scale, grad_weights, T, N, tau,
+        threshold, surrogate_scale, full_history != 0, p2, static_cast<double*>(workspace),
+        (int)nb, (cudaStream_t)stream));
+}
+
+// ---------------------------------------------------------------------------------------
+// aligned glmulti
+// ---------------------------------------------------------------------------------------
+int dfsnn_aligned_forward(const float* x, const float* v0, const float* a,
+                          const float* weights, float* spike, int T, long long N, float tau,
+                          float threshold, void* stream) {
+    if (int s = check_seq(T, N, DFSNN_MAX_T_FULL)) return s;
+    if (N > 0 && (!x || !v0 || !a || !weights || !spike)) return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(threshold)) return DFSNN_ERR_PARAM;
+    return cuda_status(dfsnn::aligned_forward_launch(x, v0, a, weights, spike, T, N, tau,
+                                                     threshold, tau_is_pow2(tau),
+                                                     (cudaStream_t)stream));
+}
+
+size_t dfsnn_aligned_backward_workspace_size(int T, long long N) {
+    if (T < 1 || T > DFSNN_MAX_T_FULL || N < 0) return 0;
+    const int b1 = dfsnn::aligned_bwd_blocks(T, N, true);
+    const int b2 = dfsnn::aligned_bwd_blocks(T, N, false);
+    const int b = b1 > b2 ? b1 : b2;
+    return (size_t)b * (size_t)dfsnn::aligned_part_stride(T) * sizeof(double);
+}
+
+int dfsnn_aligned_backward(const float* grad_spike, const float* x, const float* v0,
+                           const float* a, const float* weights, float* grad_x,
+                           float* grad_v0, float* grad_a, float* grad_weights, int T,
+                           long long N, float tau, float threshold, float surrogate_scale,
+                           float rho, void* workspace, size_t workspace_bytes, void* stream) {
+    if (int s = check_seq(T, N, DFSNN_MAX_T_FULL)) return s;
+    if (!a || !weights) return DFSNN_ERR_NULL;
+    if (N > 0 && (!grad_spike || !x || !v0 || !grad_x || !grad_v0)) return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(threshold) || !finite(surrogate_scale) || !finite(rho))
+        return DFSNN_ERR_PARAM;
+    if (!workspace || !aligned8(workspace)) return DFSNN_ERR_WORKSPACE;
+    const bool p2 = tau_is_pow2(tau);
+    const size_t stride = (size_t)dfsnn::aligned_part_stride(T) * sizeof(double);
+    long long nb = dfsnn::aligned_bwd_blocks(T, N, p2);
+    const long long cap = (long long)(workspace_bytes / stride);
+    if (cap < 1) return DFSNN_ERR_WORKSPACE;
+    if (nb > cap) nb = cap;
+    return cuda_status(dfsnn::aligned_backward_launch(
+        grad_spike, x, v0, a, weights, grad_x, grad_v0, grad_a, grad_weights, T, N, tau,
+        threshold, surrogate_scale, rho, p2, static_cast<double*>(workspace), (int)nb,
+        (cudaStream_t)stream));
+}
+
+// ---------------------------------------------------------------------------------------
+// single-order schemes
+// ---------------------------------------------------------------------------------------
+size_t dfsnn_spike_bits_words(int T, long long N) {
+    if (T < 1 || N < 0) return 0;
+    return (size_t)((T + 31) / 32) * (size_t)N;
+}
+
+int dfsnn_single_forward(int scheme, const float* x, const float* v0, const float* weights,
+                         float* spike, float* v_seq, unsigned int* spike_bits, int T,
+                         long long N, float tau, float beta, float threshold, float h_beta,
+                         float gamma_beta_plus_1, void* stream) {
+    if (scheme < DFSNN_GL || scheme > DFSNN_GL1) return DFSNN_ERR_SCHEME;
+    if (int s = check_seq(T, N, DFSNN_MAX_T)) return s;
+    if (!weights) return DFSNN_ERR_NULL;
+    if (N > 0 && (!x || !v0 || !spike || !v_seq || !spike_bits)) return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(beta) || !finite(threshold) || !finite(h_beta) ||
+        !finite(gamma_beta_plus_1))
+        return DFSNN_ERR_PARAM;
+    return cuda_status(dfsnn::single_forward_launch(scheme, x, v0, weights, spike, v_seq,
+                                                    reinterpret_cast<uint32_t*>(spike_bits), T, N,
+                                                    tau, beta, threshold, h_beta,
+                                                    gamma_beta_plus_1, tau_is_pow2(tau),
+                                                    (cudaStream_t)stream));
+}
+
+int dfsnn_single_backward(int scheme, const float* grad_spike, const float* grad_v,
+                          const float* v_seq, const unsigned int* spike_bits,
+                          const float* weights, float* grad_x, float* grad_v0, int T,
+                          long long N, float tau, float beta, float threshold,
+                          float surrogate_scale, float h_beta, float gamma_beta_plus_1,
+                          void* stream) {
+    if (scheme < DFSNN_GL || scheme > DFSNN_GL1) return DFSNN_ERR_SCHEME;
+    if (int s = check_seq(T, N, DFSNN_MAX_T)) return s;
+    if (!weights) return DFSNN_ERR_NULL;
+    if (N > 0 && (!grad_spike || !grad_v || !v_seq || !spike_bits || !grad_x || !grad_v0))
+        return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(beta) || !finite(threshold) || !finite(surrogate_scale) ||
+        !finite(h_beta) || !finite(gamma_beta_plus_1))
+        return DFSNN_ERR_PARAM;
+    return cuda_status(dfsnn::single_backward_launch(
+        scheme, grad_spike, grad_v, v_seq, reinterpret_cast<const uint32_t*>(spike_bits), weights,
+        grad_x, grad_v0, T, N, tau, beta, threshold, surrogate_scale, h_beta, gamma_beta_plus_1,
+        tau_is_pow2(tau), (cudaStream_t)stream));
+}
+
+// ---------------------------------------------------------------------------------------
+// direct LIF-like Euler
+// ---------------------------------------------------------------------------------------
+int dfsnn_direct_euler_forward(const float* x, const float* z0, const float* input_scale,
+                               const float* spike_gain, const float* spike_bias, float* spike,
+                               float* z_final, int T, long long N, float tau, float threshold,
+                               float step_size, float reset_strength, float spike_update_dt,
+                               void* stream) {
+    if (int s = check_seq(T, N, 1024)) return s;
+    if (!input_scale || !spike_gain || !spike_bias) return DFSNN_ERR_NULL;
+    if (N > 0 && (!x || !z0 || !spike || !z_final)) return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(threshold) || !finite(step_size) || !finite(reset_strength) ||
+        !finite(spike_update_dt))
+        return DFSNN_ERR_PARAM;
+    return cuda_status(dfsnn::euler_forward_launch(x, z0, input_scale, spike_gain, spike_bias,
+                                                   spike, z_final, T, N, tau, threshold,
+                                                   step_size, reset_strength, spike_update_dt,
+                                                   (cudaStream_t)stream));
+}
+
+size_t dfsnn_direct_euler_backward_workspace_size(long long N) {
+    if (N < 0) return 0;
+    const long long nb = dfsnn::euler_bwd_blocks(N);
+    return (size_t)(nb > 0 ? nb : 1) * 3 * sizeof(double);
+}
+
+int dfsnn_direct_euler_backward(const float* grad_spike, const float* grad_z_final,
+                                const float* x, const float* z0, const float* input_scale,
+                                const float* spike_gain, const float* spike_bias,
+                                float* grad_x, float* grad_z0, float* grad3, int T, long long N,
+                                float tau, float threshold, float step_size,
+                                float reset_strength, float surrogate_scale,
+                                float spike_update_dt, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+    if (int s = check_seq(T, N, 1024)) return s;
+    if (!input_scale || !spike_gain || !spike_bias || !grad3) return DFSNN_ERR_NULL;
+    if (N > 0 && (!grad_spike || !x || !z0 || !grad_x || !grad_z0)) return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(threshold) || !finite(step_size) || !finite(reset_strength) ||
+        !finite(surrogate_scale) || !finite(spike_update_dt))
+        return DFSNN_ERR_PARAM;
+    if (!workspace || !aligned8(workspace) ||
+        workspace_bytes < dfsnn_direct_euler_backward_workspace_size(N))
+        return DFSNN_ERR_WORKSPACE;
+    return cuda_status(dfsnn::euler_backward_launch(
+        grad_spike, grad_z_final, x, z0, input_scale, spike_gain, spike_bias, grad_x, grad_z0,
+        grad3, T, N, tau, threshold, step_size, reset_strength, surrogate_scale, spike_update_dt,
+        static_cast<double*>(workspace), (cudaStream_t)stream));
+}
+
+}  // extern "C"

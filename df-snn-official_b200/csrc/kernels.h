@@ -1,0 +1,61 @@
+// kernels.h -- internal host launchers of the LIF-FDE kernels (not part of the C-ABI;
+// include/dfsnn_b200.h is the public interface, implemented in capi.cu).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace dfsnn {
+
+enum Scheme { kGL = 0, kTRAP = 1, kPRED = 2, kGL1 = 3 };
+
+// library glmulti
+cudaError_t glmulti_forward_launch(const float* x, const float* v0, const float* scale,
+                                   const float* W, float* spike, int T, long long N, float tau,
+                                   float th, bool tau_pow2, cudaStream_t st);
+int glmulti_bwd_blocks(int T, long long N, bool full, bool tau_pow2);
+int glmulti_part_stride(int T);
+cudaError_t glmulti_backward_launch(const float* gS, const float* x, const float* v0,
+                                    const float* scale, const float* W, float* gx, float* gv0,
+                                    float* gscale, float* gW, int T, long long N, float tau,
+                                    float th, float sg, bool full, bool tau_pow2, double* part,
+                                    int nblocks, cudaStream_t st);
+__global__ void param_finalize(const double* part, int nblocks, int TB, int T, float* gscale,
+                               float* gW, int lower_only);
+
+// aligned glmulti
+cudaError_t aligned_forward_launch(const float* x, const float* v0, const float* a,
+                                   const float* W, float* spike, int T, long long N, float tau,
+                                   float th, bool tau_pow2, cudaStream_t st);
+int aligned_bwd_blocks(int T, long long N, bool tau_pow2);
+int aligned_part_stride(int T);
+cudaError_t aligned_backward_launch(const float* g, const float* x, const float* v0,
+                                    const float* a, const float* W, float* gx, float* gv0,
+                                    float* ga, float* gW, int T, long long N, float tau, float th,
+                                    float sg, float rho, bool tau_pow2, double* part, int nblocks,
+                                    cudaStream_t st);
+
+// single-order schemes
+cudaError_t single_forward_launch(int scheme, const float* x, const float* v0, const float* w,
+                                  float* spike, float* v, uint32_t* bits, int T, long long N,
+                                  float tau, float beta, float th, float h_beta, float gamma1,
+                                  bool tau_pow2, cudaStream_t st);
+cudaError_t single_backward_launch(int scheme, const float* gS, const float* gV, const float* v,
+                                   const uint32_t* bits, const float* w, float* gx, float* gv0,
+                                   int T, long long N, float tau, float beta, float th, float sg,
+                                   float h_beta, float gamma1, bool tau_pow2, cudaStream_t st);
+
+// direct LIF-like Euler
+int euler_bwd_blocks(long long N);
+cudaError_t euler_forward_launch(const float* x, const float* z0, const float* in_scale,
+                                 const float* gain, const float* bias, float* spike, float* zfinal,
+                                 int T, long long N, float tau, float th, float step,
+                                 float reset_strength, float sdt, cudaStream_t st);
+cudaError_t euler_backward_launch(const float* gS, const float* gzf, const float* x,
+                                  const float* z0, const float* in_scale, const float* gain,
+                                  const float* bias, float* gx, float* gz0, float* g3, int T,
+                                  long long N, float tau, float th, float step,
+                                  float reset_strength, float sg, float sdt, double* part,
+                                  cudaStream_t st);
+
+}  // namespace dfsnn

@@ -1,0 +1,333 @@
+// single_order.cu -- single-order fractional LIF kernels for sm_100a:
+//   GL        lif_fde_gl_forward/backward_kernel         (fde_cupy_kernels_all.py:24-163)
+//   GL1       lif_fde_gl1_forward/backward_kernel        (:170-320)
+//   TRAP      lif_fde_trap_forward/backward_kernel       (:327-472)
+//   PREDICTOR lif_fde_predictor_forward/backward_kernel  (:479-637)
+// The forward reproduces the reference's Kahan-compensated history sum term by term.
+// The reference backward recomputes the whole forward (O(T^2) per neuron, 2 KB of local
+// arrays per thread) only to recover v_t and spike_t; here the forward also emits a spike
+// bitmask (one bit per step) and the backward streams the saved membrane v[T,N] and the
+// bits: O(T) per neuron, no recompute, bit-identical surrogate inputs (v_t + s_t*theta).
+#include "kernels.h"
+#include "lif_common.cuh"
+
+namespace dfsnn {
+
+struct SingleArgs {
+    const float* x;      // [T, N]
+    const float* v0;     // [N]
+    const float* w;      // [T+1] reversed weights (c_rev / trap_w / pred_w)
+    float* spike;        // [T, N]
+    float* v;            // [T, N]
+    uint32_t* bits;      // [ceil(T/32), N] spike bitmask
+    const float* gS;     // [T, N]
+    const float* gV;     // [T, N]
+    const float* vs;     // [T, N] saved membrane (backward input)
+    const uint32_t* bits_in;
+    float* gx;           // [T, N]
+    float* gv0;          // [N]
+    int T;
+    long long N;
+    float tau, inv_tau, beta, th, sg, h_beta, gamma1;
+};
+
+// Per-step update of the pre-reset potential given drift dv and history sum hist.
+template <int SCHEME>
+__device__ __forceinline__ float single_update(float v, float dv, float hist, float trap_factor,
+                                               float pred_scale, float w_cur, float h_beta) {
+    if constexpr (SCHEME == kGL) return __fsub_rn(dv, hist);                         // :66
+    else if constexpr (SCHEME == kGL1) return __fmaf_rn(h_beta, dv, -hist);          // :213
+    else if constexpr (SCHEME == kTRAP) return __fadd_rn(v, __fmaf_rn(trap_factor, dv, -hist));  // :372
+    else return __fmaf_rn(pred_scale, __fmaf_rn(w_cur, dv, hist), v);                // :528
+}
+
+// ------------------------------------------------------------------------------------
+// forward, T <= TB <= 32: history in registers
+// ------------------------------------------------------------------------------------
+template <int SCHEME, int TB, bool TP2>
+__global__ void __launch_bounds__(256) single_fwd_reg(SingleArgs a) {
+    __shared__ float sw[TB + 1];
+    const int T = a.T;
+    for (int e = threadIdx.x; e <= T; e += blockDim.x) sw[e] = a.w[e];
+    __syncthreads();
+    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= a.N) return;
+    const long long N = a.N;
+    const float trap_factor = __fmaf_rn(1.5f, a.beta, 0.5f);     // :346
+    const float pred_scale = __fdiv_rn(a.h_beta, a.gamma1);       // :528
+    const float w_cur = sw[T];
+    float xr[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t)
+        if (t < T) xr[t] = ld_stream(a.x + t * N + n);
+    float v = a.v0[n];
+    float hv[TB];
+    uint32_t bits = 0;
+#pragma unroll
+    for (int k = 0; k < TB; ++k) {
+        if (k < T) {
+            const float dv = div_tau<TP2>(__fsub_rn(xr[k], v), a.tau, a.inv_tau);
+            float sum = 0.0f, c = 0.0f;                            // Kahan, :52-63
+#pragma unroll
+            for (int i = 0; i < k; ++i) {
+                const float y = __fmaf_rn(sw[T - k + i], hv[i], -c);
+                const float t = __fadd_rn(sum, y);
+                c = __fsub_rn(__fsub_rn(t, sum), y);
+                sum = t;
+            }
+            const float p = single_update<SCHEME>(v, dv, sum, trap_factor, pred_scale, w_cur, a.h_beta);
+            const bool fire = p >= a.th;
+            const float s = fire ? 1.0f : 0.0f;
+            v = __fsub_rn(p, s * a.th);
+            hv[k] = (SCHEME == kPRED) ? div_tau<TP2>(-v, a.tau, a.inv_tau) : v;
+            bits |= (fire ? 1u : 0u) << k;
+            st_stream(a.spike + k * N + n, s);
+            st_stream(a.v + k * N + n, v);
+        }
+    }
+    a.bits[n] = bits;
+}
+
+// ------------------------------------------------------------------------------------
+// forward, any T: history in shared memory [T][64]
+// ------------------------------------------------------------------------------------
+constexpr int kLongBlock = 64;
+
+template <int SCHEME, bool TP2>
+__global__ void __launch_bounds__(kLongBlock) single_fwd_smem(SingleArgs a) {
+    extern __shared__ float sh[];
+    const int T = a.T;
+    float* sw = sh;                                  // [T+1]
+    float* hv = sh + ((T + 1 + 3) & ~3) + threadIdx.x;   // [T][kLongBlock]
+    for (int e = threadIdx.x; e <= T; e += blockDim.x) sw[e] = a.w[e];
+    __syncthreads();
+    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= a.N) return;
+    const long long N = a.N;
+    const float trap_factor = __fmaf_rn(1.5f, a.beta, 0.5f);
+    const float pred_scale = __fdiv_rn(a.h_beta, a.gamma1);
+    const float w_cur = sw[T];
+    float v = a.v0[n];
+    uint32_t bits = 0;
+    float xn = ld_stream(a.x + n);
+    for (int k = 0; k < T; ++k) {
+        const float xk = xn;
+        if (k + 1 < T) xn = ld_stream(a.x + (k + 1) * N + n);
+        const float dv = div_tau<TP2>(__fsub_rn(xk, v), a.tau, a.inv_tau);
+        float sum = 0.0f, c = 0.0f;
+        const float* wk = sw + (T - k);
+        for (int i = 0; i < k; ++i) {
+            const float y = __fmaf_rn(wk[i], hv[i * kLongBlock], -c);
+            const float t = __fadd_rn(sum, y);
+            c = __fsub_rn(__fsub_rn(t, sum), y);
+            sum = t;
+        }
+        const float p = single_update<SCHEME>(v, dv, sum, trap_factor, pred_scale, w_cur, a.h_beta);
+        const bool fire = p >= a.th;
+        const float s = fire ? 1.0f : 0.0f;
+        v = __fsub_rn(p, s * a.th);
+        hv[k * kLongBlock] = (SCHEME == kPRED) ? div_tau<TP2>(-v, a.tau, a.inv_tau) : v;
+        bits |= (fire ? 1u : 0u) << (k & 31);
+        st_stream(a.spike + k * N + n, s);
+        st_stream(a.v + k * N + n, v);
+        if ((k & 31) == 31 || k == T - 1) {
+            a.bits[(long long)(k >> 5) * N + n] = bits;
+            bits = 0;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// backward: truncated reverse sweep from the saved membrane and spike bits (any T)
+// ------------------------------------------------------------------------------------
+template <int SCHEME, bool TP2>
+__device__ __forceinline__ void single_bwd_step(const SingleArgs& a, int t, float vt, bool fire,
+                                                float gst, float gvt, float& gv, float trap_factor,
+                                                float pred_scale, float w_cur, float* gx_out,
+                                                const float* sw) {
+    gv = __fadd_rn(gv, gvt);
+    const float p = __fmaf_rn(fire ? 1.0f : 0.0f, a.th, vt);          // v + spike*theta
+    const float surr = surrogate_fma(__fsub_rn(p, a.th), a.sg);
+    gv = __fmaf_rn(gst, surr, gv);
+    float gvm;
+    if constexpr (SCHEME == kGL) {                                      // :150-154
+        *gx_out = div_tau<TP2>(gv, a.tau, a.inv_tau);
+        gvm = div_tau<TP2>(-gv, a.tau, a.inv_tau);
+    } else if constexpr (SCHEME == kTRAP) {                             // :459-463
+        const float gsd = __fmul_rn(gv, trap_factor);
+        const float q = div_tau<TP2>(gsd, a.tau, a.inv_tau);
+        *gx_out = q;
+        gvm = __fsub_rn(gv, q);
+    } else if constexpr (SCHEME == kPRED) {                             // :621-629
+        const float gdc = __fmul_rn(__fmul_rn(gv, pred_scale), w_cur);
+        const float q = div_tau<TP2>(gdc, a.tau, a.inv_tau);
+        *gx_out = q;
+        gvm = __fsub_rn(gv, q);
+    } else {                                                            // GL1 :296-312
+        const float gd = __fmul_rn(a.h_beta, gv);
+        *gx_out = div_tau<TP2>(gd, a.tau, a.inv_tau);
+        gvm = div_tau<TP2>(-gd, a.tau, a.inv_tau);
+        const int T = a.T;
+        for (int i = 0; i < t; ++i) gvm = __fmaf_rn(-sw[T - t + i], gv, gvm);
+    }
+    gv = gvm;
+}
+
+template <int SCHEME, int TB, bool TP2>
+__global__ void __launch_bounds__(256) single_bwd_reg(SingleArgs a) {
+    __shared__ float sw[(SCHEME == kGL1) ? TB + 1 : 1];
+    const int T = a.T;
+    if constexpr (SCHEME == kGL1) {
+        for (int e = threadIdx.x; e <= T; e += blockDim.x) sw[e] = a.w[e];
+        __syncthreads();
+    }
+    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= a.N) return;
+    const long long N = a.N;
+    const float trap_factor = __fmaf_rn(1.5f, a.beta, 0.5f);
+    const float pred_scale = __fdiv_rn(a.h_beta, a.gamma1);
+    const float w_cur = (SCHEME == kPRED) ? __ldg(a.w + T) : 0.0f;
+    float vr[TB], gsr[TB], gvr[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) {
+        if (t < T) {
+            vr[t] = ld_stream(a.vs + t * N + n);
+            gsr[t] = ld_stream(a.gS + t * N + n);
+            gvr[t] = ld_stream(a.gV + t * N + n);
+        }
+    }
+    const uint32_t bits = a.bits_in[n];
+    float gv = 0.0f;
+#pragma unroll
+    for (int t = TB - 1; t >= 0; --t) {
+        if (t < T) {
+            float gxt;
+            single_bwd_step<SCHEME, TP2>(a, t, vr[t], (bits >> t) & 1u, gsr[t], gvr[t], gv,
+                                         trap_factor, pred_scale, w_cur, &gxt, sw);
+            st_stream(a.gx + t * N + n, gxt);
+        }
+    }
+    a.gv0[n] = gv;
+}
+
+template <int SCHEME, bool TP2>
+__global__ void __launch_bounds__(256) single_bwd_loop(SingleArgs a) {
+    extern __shared__ float sw[];
+    const int T = a.T;
+    if constexpr (SCHEME == kGL1) {
+        for (int e = threadIdx.x; e <= T; e += blockDim.x) sw[e] = a.w[e];
+        __syncthreads();
+    }
+    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= a.N) return;
+    const long long N = a.N;
+    const float trap_factor = __fmaf_rn(1.5f, a.beta, 0.5f);
+    const float pred_scale = __fdiv_rn(a.h_beta, a.gamma1);
+    const float w_cur = (SCHEME == kPRED) ? __ldg(a.w + T) : 0.0f;
+    float gv = 0.0f;
+    uint32_t bits = 0;
+    for (int t = T - 1; t >= 0; --t) {
+        if (t == T - 1 || (t & 31) == 31) bits = a.bits_in[(long long)(t >> 5) * N + n];
+        const float vt = ld_stream(a.vs + t * N + n);
+        const float gst = ld_stream(a.gS + t * N + n);
+        const float gvt = ld_stream(a.gV + t * N + n);
+        float gxt;
+        single_bwd_step<SCHEME, TP2>(a, t, vt, (bits >> (t & 31)) & 1u, gst, gvt, gv, trap_factor,
+                                     pred_scale, w_cur, &gxt, sw);
+        st_stream(a.gx + t * N + n, gxt);
+    }
+    a.gv0[n] = gv;
+}
+
+// ------------------------------------------------------------------------------------
+// host launchers
+// ------------------------------------------------------------------------------------
+namespace {
+
+SingleArgs make_args(int T, long long N, float tau, float beta, float th, float sg, float h_beta,
+                     float gamma1) {
+    SingleArgs a{};
+    a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau; a.beta = beta; a.th = th; a.sg = sg;
+    a.h_beta = h_beta; a.gamma1 = gamma1;
+    return a;
+}
+
+template <int SCHEME, bool TP2>
+cudaError_t fwd_dispatch(const SingleArgs& a, cudaStream_t st) {
+    const int T = a.T;
+    if (T <= 32) {
+        const unsigned grid = (unsigned)((a.N + 255) / 256);
+        if (T <= 8) single_fwd_reg<SCHEME, 8, TP2><<<grid, 256, 0, st>>>(a);
+        else if (T <= 16) single_fwd_reg<SCHEME, 16, TP2><<<grid, 256, 0, st>>>(a);
+        else single_fwd_reg<SCHEME, 32, TP2><<<grid, 256, 0, st>>>(a);
+        return cudaGetLastError();
+    }
+    const unsigned grid = (unsigned)((a.N + kLongBlock - 1) / kLongBlock);
+    const size_t smem = sizeof(float) * (((T + 1 + 3) & ~3) + (size_t)T * kLongBlock);
+    auto k = single_fwd_smem<SCHEME, TP2>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k<<<grid, kLongBlock, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+template <int SCHEME, bool TP2>
+cudaError_t bwd_dispatch(const SingleArgs& a, cudaStream_t st) {
+    const int T = a.T;
+    const unsigned grid = (unsigned)((a.N + 255) / 256);
+    if (T <= 32) {
+        if (T <= 8) single_bwd_reg<SCHEME, 8, TP2><<<grid, 256, 0, st>>>(a);
+        else if (T <= 16) single_bwd_reg<SCHEME, 16, TP2><<<grid, 256, 0, st>>>(a);
+        else single_bwd_reg<SCHEME, 32, TP2><<<grid, 256, 0, st>>>(a);
+        return cudaGetLastError();
+    }
+    const size_t smem = (SCHEME == kGL1) ? sizeof(float) * (size_t)(T + 1) : 0;
+    single_bwd_loop<SCHEME, TP2><<<grid, 256, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+template <bool TP2>
+cudaError_t fwd_scheme(int scheme, const SingleArgs& a, cudaStream_t st) {
+    switch (scheme) {
+        case kGL: return fwd_dispatch<kGL, TP2>(a, st);
+        case kTRAP: return fwd_dispatch<kTRAP, TP2>(a, st);
+        case kPRED: return fwd_dispatch<kPRED, TP2>(a, st);
+        case kGL1: return fwd_dispatch<kGL1, TP2>(a, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <bool TP2>
+cudaError_t bwd_scheme(int scheme, const SingleArgs& a, cudaStream_t st) {
+    switch (scheme) {
+        case kGL: return bwd_dispatch<kGL, TP2>(a, st);
+        case kTRAP: return bwd_dispatch<kTRAP, TP2>(a, st);
+        case kPRED: return bwd_dispatch<kPRED, TP2>(a, st);
+        case kGL1: return bwd_dispatch<kGL1, TP2>(a, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+cudaError_t single_forward_launch(int scheme, const float* x, const float* v0, const float* w,
+                                  float* spike, float* v, uint32_t* bits, int T, long long N,
+                                  float tau, float beta, float th, float h_beta, float gamma1,
+                                  bool tau_pow2, cudaStream_t st) {
+    if (N == 0) return cudaSuccess;
+    SingleArgs a = make_args(T, N, tau, beta, th, 0.0f, h_beta, gamma1);
+    a.x = x; a.v0 = v0; a.w = w; a.spike = spike; a.v = v; a.bits = bits;
+    return tau_pow2 ? fwd_scheme<true>(scheme, a, st) : fwd_scheme<false>(scheme, a, st);
+}
+
+cudaError_t single_backward_launch(int scheme, const float* gS, const float* gV, const float* v,
+                                   const uint32_t* bits, const float* w, float* gx, float* gv0,
+                                   int T, long long N, float tau, float beta, float th, float sg,
+                                   float h_beta, float gamma1, bool tau_pow2, cudaStream_t st) {
+    if (N == 0) return cudaSuccess;
+    SingleArgs a = make_args(T, N, tau, beta, th, sg, h_beta, gamma1);
+    a.gS = gS; a.gV = gV; a.vs = v; a.bits_in = bits; a.w = w; a.gx = gx; a.gv0 = gv0;
+    return tau_pow2 ? bwd_scheme<true>(scheme, a, st) : bwd_scheme<false>(scheme, a, st);
+}
+
+}  // namespace dfsnn

@@ -1,0 +1,105 @@
+"""Optional timing of the native calls (CUDA events on the launching stream).
+
+Disabled by default (one global check per call).  When a NativeCallTimer is active, every
+C-ABI call made by the autograd Functions is bracketed by a pair of CUDA events recorded
+on the stream the kernels are launched on, together with the number of kernels the call
+launches and its algorithmic HBM bytes (compulsory reads + writes), so a harness can
+report per-kernel durations and achieved bandwidth measured inside its own timed region.
+
+    with profiling.NativeCallTimer() as timer:
+        ... run steps ...
+    torch.cuda.synchronize()
+    print(timer.summary())
+"""
+import contextlib
+from collections import defaultdict
+
+import torch
+
+_ACTIVE = None
+
+
+class NativeCallTimer:
+    def __init__(self):
+        self._events = defaultdict(list)     # name -> [(start, end)]
+        self.launches = defaultdict(int)     # name -> kernels launched
+        self.bytes = defaultdict(int)        # name -> algorithmic bytes moved
+        self.calls = defaultdict(int)
+
+    def __enter__(self):
+        global _ACTIVE
+        self._prev = _ACTIVE
+        _ACTIVE = self
+        return self
+
+    def __exit__(self, *exc):
+        global _ACTIVE
+        _ACTIVE = self._prev
+        return False
+
+    def add(self, name, start, end, launches, nbytes):
+        self._events[name].append((start, end))
+        self.launches[name] += launches
+        self.bytes[name] += nbytes
+        self.calls[name] += 1
+
+    def summary(self):
+        """{name: {calls, launches, ms_total, ms_per_call, bytes_per_call, gbs}} (call after
+        synchronising the device)."""
+        out = {}
+        for name, evs in self._events.items():
+            ms = sum(s.elapsed_time(e) for s, e in evs)
+            calls = self.calls[name]
+            out[name] = {
+                "calls": calls,
+                "launches": self.launches[name],
+                "ms_total": ms,
+                "ms_per_call": ms / calls,
+                "bytes_per_call": self.bytes[name] / calls,
+                "gbs": (self.bytes[name] / 1e9) / (ms / 1e3) if ms > 0 else None,
+            }
+        return out
+
+    def total_launches(self):
+        return sum(self.launches.values())
+
+
+@contextlib.contextmanager
+def native_call(name, launches, nbytes, device):
+    """Bracket one native call with CUDA events when a timer is active."""
+    timer = _ACTIVE
+    if timer is None:
+        yield
+        return
+    stream = torch.cuda.current_stream(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    yield
+    end.record(stream)
+    timer.add(name, start, end, launches, int(nbytes))
+
+
+# Algorithmic bytes per call (fp32 I/O): compulsory HBM reads + writes of one call.
+def glmulti_forward_bytes(T, N):
+    return N * (8 * T + 4)                       # x in, spikes out; v0 in
+
+
+def glmulti_backward_bytes(T, N):
+    return N * (12 * T + 8)                      # x, grad_spike in; grad_x out; v0 in, grad_v0 out
+
+
+def single_forward_bytes(T, N):
+    return N * (12 * T + 4 + 4 * ((T + 31) // 32))   # x in; spike, v, bits out; v0 in
+
+
+def single_backward_bytes(T, N):
+    return N * (16 * T + 4 + 4 * ((T + 31) // 32))   # grad_s, grad_v, v, bits in; grad_x, grad_v0 out
+
+
+def euler_forward_bytes(T, N):
+    return N * (8 * T + 8)                       # x in, spikes out; z0 in, z_final out
+
+
+def euler_backward_bytes(T, N):
+    return N * (12 * T + 12)                     # x, grad_s in, grad_x out; z0, grad_zf in, grad_z0 out

@@ -1,0 +1,102 @@
+"""Weight tables of the LIF-FDE schemes (host side, torch ops).
+
+Restates the reference builders in spikeDE_dis/neuron.py with the same fp32 operations, so
+the tables are bit-identical to the ones LIFNeuronFDE hands to its kernels:
+  * glmulti basis c_m^(beta_j) (:1314-1317), masses softplus(raw) (:1488-1489),
+    c~ = sum_j m_j h^-beta_j c^(beta_j) (:1461-1479) and the [T,T] schedule (:1494-1514).
+    The reference fills W row by row in a Python loop (2T small launches per call); here
+    W[t,i] = c~[t-i] / c~[0] is one gather, bit-identical, differentiable in the masses.
+  * GL c_rev (:1446-1459), L1-2 trapezoid (:1516-1546), fractional predictor (:1548-1570).
+"""
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+def glmulti_basis(multi_beta, T):
+    """[J, T+1] basis c_lag^(beta_j): c_0 = 1, c_m = (1 - (1+beta)/m) c_{m-1}."""
+    beta = torch.as_tensor(multi_beta, dtype=torch.float32)
+    basis = torch.zeros(beta.numel(), T + 1, dtype=torch.float32)
+    basis[:, 0] = 1.0
+    for lag in range(1, T + 1):
+        basis[:, lag] = (1.0 - (1.0 + beta) / lag) * basis[:, lag - 1]
+    return basis
+
+
+def softplus_masses(raw):
+    return F.softplus(raw)
+
+
+def glmulti_c_tilde(coefficient, multi_beta, basis, h):
+    """c~ (length T+1) and 1/c~_0 exactly as _get_glmulti_weights computes them."""
+    device = basis.device
+    beta = multi_beta.to(device=device, dtype=torch.float32)
+    coefficient = coefficient.to(device=device, dtype=torch.float32)
+    hh = torch.tensor(h, device=device, dtype=torch.float32)
+    weighted_h = coefficient * torch.pow(hh, -beta)
+    c_tilde = torch.sum(weighted_h.unsqueeze(1) * basis, dim=0)
+    return c_tilde, 1.0 / c_tilde[0]
+
+
+_LAG_CACHE = {}
+
+
+def _lag_index(T, device):
+    key = (T, device.type, device.index)
+    got = _LAG_CACHE.get(key)
+    if got is None:
+        t = torch.arange(T, device=device)
+        lag = t[:, None] - t[None, :]
+        mask = lag > 0
+        got = (lag.clamp_min(0), mask)
+        _LAG_CACHE[key] = got
+    return got
+
+
+def build_glmulti_schedule(coefficient, multi_beta, basis, h, T):
+    """{'scale': [T], 'weights': [T,T]} of LIFNeuronFDE._build_glmulti_schedule."""
+    c_tilde, c0_inv = glmulti_c_tilde(coefficient, multi_beta, basis, h)
+    lag, mask = _lag_index(T, c_tilde.device)
+    weights = torch.where(mask, c_tilde[lag] * c0_inv, torch.zeros((), device=c_tilde.device))
+    return {"scale": c0_inv.expand(T), "weights": weights}
+
+
+def gl_weights(beta_val, T, device=None, dtype=torch.float32):
+    c = torch.zeros(T + 1, device=device, dtype=dtype)
+    c[0] = 1
+    for j in range(1, T + 1):
+        c[j] = (1 - (1 + beta_val) / j) * c[j - 1]
+    return torch.flip(c, dims=[0])
+
+
+def trap_weights(beta_val, T, device=None, dtype=torch.float32):
+    w = torch.zeros(T + 1, device=device, dtype=dtype)
+    w[0] = 1.0
+    alpha = 1.0 - beta_val
+    for j in range(1, T + 1):
+        if j == 1:
+            w[j] = torch.pow(torch.tensor(2.0, device=device, dtype=dtype), alpha) - 2.0
+        else:
+            term1 = torch.pow(torch.tensor(j + 1.0, device=device, dtype=dtype), alpha)
+            term2 = 2.0 * torch.pow(torch.tensor(j, device=device, dtype=dtype), alpha)
+            term3 = torch.pow(torch.tensor(j - 1.0, device=device, dtype=dtype), alpha)
+            w[j] = term1 - term2 + term3
+    return torch.flip(w, dims=[0])
+
+
+def predictor_weights(beta_val, T, device=None, dtype=torch.float32):
+    w = torch.zeros(T + 1, device=device, dtype=dtype)
+    w[0] = 1.0
+    for j in range(1, T + 1):
+        if j == 1:
+            w[j] = 1.0
+        else:
+            w[j] = (torch.pow(torch.tensor(j, dtype=dtype, device=device), beta_val - 1)
+                    - torch.pow(torch.tensor(j - 1, dtype=dtype, device=device), beta_val - 1))
+    return torch.flip(w, dims=[0])
+
+
+def predictor_constants(beta, h):
+    """(h^beta, Gamma(beta+1)) as _multi_step_forward_cupy passes them (:2211-2215)."""
+    return h ** beta, math.exp(math.lgamma(beta + 1.0))

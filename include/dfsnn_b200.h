@@ -1,0 +1,163 @@
+/*
+ * dfsnn_b200.h -- C ABI of the B200 (sm_100a) LIF-FDE kernels.
+ *
+ * Drop-in boundary for the hot path of DF-SNN's LIFNeuronFDE
+ * (cjge-ustc/DF-SNN-official, spikeDE_dis/neuron.py:1058).  In the reference, every
+ * entry below is a CuPy RawKernel launch made from a torch.autograd.Function in
+ * spikeDE_dis/fde_cupy_kernels_all.py, examples/cnn128/aligned_glmulti.py or
+ * spikeDE_dis/direct_euler_cupy.py; each declaration names the launch(es) it replaces.
+ *
+ * Conventions
+ *   - Every pointer is a device pointer (cudaMalloc / torch CUDA memory) unless stated;
+ *     the library never allocates, frees or retains them.
+ *   - Sequences are time-major float32 [T, N], row-major (element (t, n) at t*N + n),
+ *     exactly the [T, N] layout the reference Functions pass to their kernels.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); every call is
+ *     asynchronous on that stream and launches on the calling thread's current device.
+ *   - Return value: DFSNN_OK or one of the DFSNN_ERR_* codes; nothing is launched when
+ *     argument validation fails.  dfsnn_status_string() names a code,
+ *     dfsnn_last_cuda_error() gives the cudaError_t behind DFSNN_ERR_CUDA.
+ *   - Arithmetic reproduces the reference kernels' fp32 operation order (including the
+ *     fused multiply-adds NVRTC forms under --fmad=true, and none for the aligned kernels
+ *     compiled with --fmad=false), so spikes, membranes and per-neuron gradients match the
+ *     reference bit for bit; reductions over neurons are accumulated in a fixed order
+ *     (deterministic) with compensated fp32 and double partials.
+ */
+#ifndef DFSNN_B200_H
+#define DFSNN_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DFSNN_OK 0
+#define DFSNN_ERR_NULL 1        /* a required pointer is NULL */
+#define DFSNN_ERR_SHAPE 2       /* T < 1 or N < 0 */
+#define DFSNN_ERR_T_LIMIT 3     /* T above this entry point's limit */
+#define DFSNN_ERR_WORKSPACE 4   /* workspace NULL, misaligned or too small */
+#define DFSNN_ERR_CUDA 5        /* a CUDA call or kernel launch failed */
+#define DFSNN_ERR_SCHEME 6      /* unknown scheme id */
+#define DFSNN_ERR_PARAM 7       /* tau == 0 or a non-finite scalar parameter */
+
+#define DFSNN_MAX_T 256         /* forward / truncated limit (reference: 256-entry locals) */
+#define DFSNN_MAX_T_FULL 32     /* full-history glmulti and aligned backward (reference: 64) */
+
+/* scheme ids of the single-order family */
+#define DFSNN_GL 0
+#define DFSNN_TRAP 1
+#define DFSNN_PREDICTOR 2
+#define DFSNN_GL1 3
+
+const char* dfsnn_status_string(int status);
+int dfsnn_last_cuda_error(void);
+const char* dfsnn_version(void);
+
+/* ---------------------------------------------------------------------------------
+ * Library distributed-order GL (LIFFDEGLMultiFunction, fde_cupy_kernels_all.py:1916-2011)
+ * ------------------------------------------------------------------------------- */
+
+/* Replaces the lif_fde_vo_gl1_forward_kernel launch with per_batch=0
+ * (fde_cupy_kernels_all.py:1938-1971 launching :1594-1630).
+ * p_t = scale[t]*d_t - sum_{i<t} W[t,i] v_i, d_t = (x_t - v_{t-1})/tau, spike = p_t >= th,
+ * v_t = p_t - spike*th.  Writes spike[T,N] only (the backward recomputes the rest). */
+int dfsnn_glmulti_forward(const float* x, const float* v0, const float* scale,
+                          const float* weights, float* spike, int T, long long N, float tau,
+                          float threshold, void* stream);
+
+/* Bytes of device workspace dfsnn_glmulti_backward needs (8-byte aligned). */
+size_t dfsnn_glmulti_backward_workspace_size(int T, long long N, int full_history);
+
+/* Replaces LIFFDEGLMultiFunction.backward (fde_cupy_kernels_all.py:1973-2011): the
+ * lif_fde_glmulti_backward_kernel (:1845-1875, full_history=0) or
+ * lif_fde_glmulti_full_backward_kernel (:1877-1913, full_history=1) launch, then
+ * grad_scale[t] = sum_n grad_pre*drift and grad_weights = -grad_pre @ v_hist^T (full T x T).
+ * grad_scale / grad_weights may be NULL (not needed).  T <= DFSNN_MAX_T_FULL. */
+int dfsnn_glmulti_backward(const float* grad_spike, const float* x, const float* v0,
+                           const float* scale, const float* weights, float* grad_x,
+                           float* grad_v0, float* grad_scale, float* grad_weights, int T,
+                           long long N, float tau, float threshold, float surrogate_scale,
+                           int full_history, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Aligned distributed-order GL (AlignedGLMulti, examples/cnn128/aligned_glmulti.py)
+ * ------------------------------------------------------------------------------- */
+
+/* Replaces the aligned_forward launch (aligned_glmulti.py:106-121 launching :7-17). */
+int dfsnn_aligned_forward(const float* x, const float* v0, const float* a,
+                          const float* weights, float* spike, int T, long long N, float tau,
+                          float threshold, void* stream);
+
+size_t dfsnn_aligned_backward_workspace_size(int T, long long N);
+
+/* Replaces AlignedGLMulti.backward (aligned_glmulti.py:123-145): aligned_backward (:20-32)
+ * with HISTORY_RHO = rho, aligned_scale (:33-41) + sum, and -(ga@h^T)*tril(-1).
+ * grad_a / grad_weights may be NULL.  T <= DFSNN_MAX_T_FULL. */
+int dfsnn_aligned_backward(const float* grad_spike, const float* x, const float* v0,
+                           const float* a, const float* weights, float* grad_x,
+                           float* grad_v0, float* grad_a, float* grad_weights, int T,
+                           long long N, float tau, float threshold, float surrogate_scale,
+                           float rho, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Single-order schemes: GL, TRAP, PREDICTOR, GL1 (LIFFDEGLFunction, LIFFDETRAPFunction,
+ * LIFFDEPREDICTORFunction, LIFFDEGL1Function)
+ * ------------------------------------------------------------------------------- */
+
+/* Number of uint32 words of the spike bitmask for (T, N): ceil(T/32) * N. */
+size_t dfsnn_spike_bits_words(int T, long long N);
+
+/* Replaces the lif_fde_{gl,trap,predictor,gl1}_forward_kernel launches
+ * (fde_cupy_kernels_all.py:24-75, :327-381, :479-539, :170-260; launched from the Functions'
+ * forward at :658-698, :843-882, :933-975, :749-793).  weights = the reversed table of T+1 entries.
+ * Writes spike[T,N], v_seq[T,N] and the spike bitmask the backward consumes.
+ * h_beta / gamma_beta_plus_1 are used by PREDICTOR (both) and GL1 (h_beta). */
+int dfsnn_single_forward(int scheme, const float* x, const float* v0, const float* weights,
+                         float* spike, float* v_seq, unsigned int* spike_bits, int T,
+                         long long N, float tau, float beta, float threshold, float h_beta,
+                         float gamma_beta_plus_1, void* stream);
+
+/* Replaces the lif_fde_{gl,trap,predictor,gl1}_backward_kernel launches (:77-163,
+ * :383-472, :541-637, :262-320; launched from :700-732, :884-916, :977-1010, :795-827):
+ * truncated reverse sweep, from the saved v_seq and
+ * spike bitmask instead of a recompute. */
+int dfsnn_single_backward(int scheme, const float* grad_spike, const float* grad_v,
+                          const float* v_seq, const unsigned int* spike_bits,
+                          const float* weights, float* grad_x, float* grad_v0, int T,
+                          long long N, float tau, float beta, float threshold,
+                          float surrogate_scale, float h_beta, float gamma_beta_plus_1,
+                          void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Direct LIF-like Euler (DirectLIFLikeEulerCuPyFunction, spikeDE_dis/direct_euler_cupy.py)
+ * ------------------------------------------------------------------------------- */
+
+/* Replaces direct_lif_euler_forward (direct_euler_cupy.py:22-58, launched :157-182).
+ * input_scale / spike_gain / spike_bias are device scalars. */
+int dfsnn_direct_euler_forward(const float* x, const float* z0, const float* input_scale,
+                               const float* spike_gain, const float* spike_bias, float* spike,
+                               float* z_final, int T, long long N, float tau, float threshold,
+                               float step_size, float reset_strength, float spike_update_dt,
+                               void* stream);
+
+size_t dfsnn_direct_euler_backward_workspace_size(long long N);
+
+/* Replaces direct_lif_euler_backward (direct_euler_cupy.py:66-131, launched :200-236).
+ * grad_z_final may be NULL (zeros).  grad3 receives {grad_input_scale, grad_spike_gain,
+ * grad_spike_bias} (3 device floats), reduced without atomics.  T <= 1024. */
+int dfsnn_direct_euler_backward(const float* grad_spike, const float* grad_z_final,
+                                const float* x, const float* z0, const float* input_scale,
+                                const float* spike_gain, const float* spike_bias,
+                                float* grad_x, float* grad_z0, float* grad3, int T, long long N,
+                                float tau, float threshold, float step_size,
+                                float reset_strength, float surrogate_scale,
+                                float spike_update_dt, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DFSNN_B200_H */

@@ -1,0 +1,216 @@
+"""Compile the reference's own LIF-FDE kernel sources for the host CPU (oracle/_ref/).
+
+TEST INFRASTRUCTURE ONLY.  The reference (cjge-ustc/DF-SNN-official) ships its kernels as
+CUDA C strings inside Python modules (spikeDE_dis/fde_cupy_kernels_all.py,
+examples/cnn128/aligned_glmulti.py, spikeDE_dis/direct_euler_cupy.py).  This recipe reads
+those strings from the reference checkout, where they lie, wraps them with
+oracle/ref_shim.h (a host-side stand-in for the CUDA thread indices) and compiles them with
+g++ into oracle/_ref/libdfsnn_ref.so.  Nothing of the reference is committed: the generated
+sources and the library live only under oracle/_ref/ (git-ignored).
+
+Floating-point contraction follows the reference's compile flags: the library kernels are
+built by NVRTC with its default --fmad=true (here: -ffp-contract=fast with FMA hardware),
+the aligned kernels with --fmad=false (here: -ffp-contract=off).
+
+Usage: python oracle/build_ref.py [--reference /root/reference]
+Exits 0 without building when the reference checkout is absent.
+"""
+import argparse
+import ast
+import os
+import subprocess
+import sys
+import types
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+OUT = os.path.join(HERE, "_ref")
+
+# The reference's kernels that run one thread per neuron with no inter-thread traffic.
+LIB_KERNELS = [
+    "gl_forward_kernel_code", "gl_backward_kernel_code",
+    "gl1_forward_kernel_code", "gl1_backward_kernel_code",
+    "trap_forward_kernel_code", "trap_backward_kernel_code",
+    "predictor_forward_kernel_code", "predictor_backward_kernel_code",
+    "vo_gl1_forward_kernel_code",
+    "glmulti_backward_kernel_code", "glmulti_full_backward_kernel_code",
+]
+
+# Host launchers (this repository's code): one OpenMP loop over global thread indices.
+WRAPPERS_FMA = r'''
+#define DFSNN_REF_LOOP(NTHREADS, CALL)                                   \
+    do {                                                                  \
+        const long long _total = ((long long)(NTHREADS) + 255) / 256 * 256; \
+        _Pragma("omp parallel for schedule(static)")                      \
+        for (long long _g = 0; _g < _total; ++_g) {                       \
+            dfsnn_ref_set_thread(_g);                                     \
+            CALL;                                                         \
+        }                                                                 \
+    } while (0)
+
+extern "C" {
+void ref_gl_forward(const float* x, const float* v0, const float* w, float* s, float* v,
+                    int T, int N, float tau, float beta, float th, float v_reset) {
+    DFSNN_REF_LOOP(N, lif_fde_gl_forward_kernel(x, v0, w, s, v, T, N, tau, beta, th, v_reset));
+}
+void ref_gl_backward(const float* gs, const float* gv, const float* x, const float* v0,
+                     const float* w, float* gx, float* gv0, int T, int N, float tau, float beta,
+                     float th, float sg) {
+    DFSNN_REF_LOOP(N, lif_fde_gl_backward_kernel(gs, gv, x, v0, w, gx, gv0, T, N, tau, beta, th, sg));
+}
+void ref_gl1_forward(const float* x, const float* v0, const float* w, float* s, float* v,
+                     int T, int N, float tau, float beta, float th, float v_reset, float h_beta) {
+    DFSNN_REF_LOOP(N, lif_fde_gl1_forward_kernel(x, v0, w, s, v, T, N, tau, beta, th, v_reset, h_beta));
+}
+void ref_gl1_backward(const float* gs, const float* gv, const float* x, const float* v0,
+                      const float* w, float* gx, float* gv0, int T, int N, float tau, float beta,
+                      float th, float sg, float h_beta) {
+    DFSNN_REF_LOOP(N, lif_fde_gl1_backward_kernel(gs, gv, x, v0, w, gx, gv0, T, N, tau, beta, th, sg, h_beta));
+}
+void ref_trap_forward(const float* x, const float* v0, const float* w, float* s, float* v,
+                      int T, int N, float tau, float beta, float th, float v_reset) {
+    DFSNN_REF_LOOP(N, lif_fde_trap_forward_kernel(x, v0, w, s, v, T, N, tau, beta, th, v_reset));
+}
+void ref_trap_backward(const float* gs, const float* gv, const float* x, const float* v0,
+                       const float* w, float* gx, float* gv0, int T, int N, float tau, float beta,
+                       float th, float sg) {
+    DFSNN_REF_LOOP(N, lif_fde_trap_backward_kernel(gs, gv, x, v0, w, gx, gv0, T, N, tau, beta, th, sg));
+}
+void ref_predictor_forward(const float* x, const float* v0, const float* w, float* s, float* v,
+                           int T, int N, float tau, float beta, float th, float v_reset,
+                           float h_beta, float gamma1) {
+    DFSNN_REF_LOOP(N, lif_fde_predictor_forward_kernel(x, v0, w, s, v, T, N, tau, beta, th, v_reset, h_beta, gamma1));
+}
+void ref_predictor_backward(const float* gs, const float* gv, const float* x, const float* v0,
+                            const float* w, float* gx, float* gv0, int T, int N, float tau,
+                            float beta, float th, float sg, float h_beta, float gamma1) {
+    DFSNN_REF_LOOP(N, lif_fde_predictor_backward_kernel(gs, gv, x, v0, w, gx, gv0, T, N, tau, beta, th, sg, h_beta, gamma1));
+}
+void ref_glmulti_forward(const float* x, const float* v0, const float* scale, const float* W,
+                         float* s, float* vpre, float* vhist, float* drift, int T, int N,
+                         float tau, float th) {
+    DFSNN_REF_LOOP(N, lif_fde_vo_gl1_forward_kernel(x, v0, scale, W, s, vpre, vhist, drift, T, N, 1, 0, tau, th));
+}
+void ref_glmulti_backward(int full, const float* gs, const float* scale, const float* W,
+                          const float* vpre, float* gx, float* gv0, float* gpre, int T, int N,
+                          float tau, float th, float sg) {
+    if (full)
+        DFSNN_REF_LOOP(N, lif_fde_glmulti_full_backward_kernel(gs, scale, W, vpre, gx, gv0, gpre, T, N, tau, th, sg));
+    else
+        DFSNN_REF_LOOP(N, lif_fde_glmulti_backward_kernel(gs, scale, vpre, gx, gv0, gpre, T, N, tau, th, sg));
+}
+void ref_euler_forward(const float* x, const float* z0, float* s, float* zpre, float* sin_,
+                       float* zf, int T, int N, float in_scale, float gain, float bias, float tau,
+                       float th, float step, float reset_strength, float sdt) {
+    DFSNN_REF_LOOP(N, direct_lif_euler_forward(x, z0, s, zpre, sin_, zf, T, N, in_scale, gain, bias, tau, th, step, reset_strength, sdt));
+}
+void ref_euler_backward(const float* gs, const float* gzf, const float* x, const float* zpre,
+                        const float* sin_, float* gx, float* gz0, float* g_scale, float* g_gain,
+                        float* g_bias, int T, int N, float in_scale, float gain, float tau,
+                        float step, float sg, float sdt) {
+    DFSNN_REF_LOOP(N, direct_lif_euler_backward(gs, gzf, x, zpre, sin_, gx, gz0, g_scale, g_gain, g_bias, T, N, in_scale, gain, tau, step, sg, sdt));
+}
+}
+'''
+
+WRAPPERS_NOFMA = r'''
+extern "C" {
+void ref_aligned_forward(const float* x, const float* v0, const float* a, const float* w,
+                         float* s, float* p, float* hist, int T, int N, float tau, float th) {
+    const long long total = ((long long)N + 255) / 256 * 256;
+#pragma omp parallel for schedule(static)
+    for (long long g = 0; g < total; ++g) {
+        dfsnn_ref_set_thread(g);
+        aligned_forward(x, v0, a, w, s, p, hist, T, N, tau, th);
+    }
+}
+void ref_aligned_backward(const float* g, const float* a, const float* w, const float* p,
+                          float* gx, float* gv, float* ga, int T, int N, float tau, float th,
+                          float sg, float rho) {
+    dfsnn_ref_rho = rho;
+    const long long total = ((long long)N + 255) / 256 * 256;
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < total; ++i) {
+        dfsnn_ref_set_thread(i);
+        aligned_backward(g, a, w, p, gx, gv, ga, T, N, tau, th, sg);
+    }
+}
+}
+'''
+
+
+def _stub_h5py():
+    # spikeDE_dis/__init__ imports solver.py, which imports h5py.h5z.FLAG_SKIP_EDC.
+    if "h5py" not in sys.modules:
+        h5 = types.ModuleType("h5py")
+        h5z = types.ModuleType("h5py.h5z")
+        h5z.FLAG_SKIP_EDC = 0
+        h5.h5z = h5z
+        sys.modules["h5py"] = h5
+        sys.modules["h5py.h5z"] = h5z
+
+
+def _function_local_string(path, func_name, var_name="code"):
+    """Return the string literal assigned to `var_name` inside `func_name` of a file."""
+    with open(path) as f:
+        tree = ast.parse(f.read())
+    for node in ast.walk(tree):
+        if isinstance(node, ast.FunctionDef) and node.name == func_name:
+            for sub in ast.walk(node):
+                if (isinstance(sub, ast.Assign) and len(sub.targets) == 1
+                        and isinstance(sub.targets[0], ast.Name) and sub.targets[0].id == var_name
+                        and isinstance(sub.value, ast.Constant) and isinstance(sub.value.value, str)):
+                    return sub.value.value
+    raise RuntimeError(f"{func_name}.{var_name} not found in {path}")
+
+
+def collect_sources(reference):
+    _stub_h5py()
+    sys.path.insert(0, reference)
+    sys.path.insert(0, os.path.join(reference, "examples", "cnn128"))
+    import spikeDE_dis.fde_cupy_kernels_all as lib  # noqa: E402
+    import aligned_glmulti as alg  # noqa: E402
+    fma_parts = [getattr(lib, name) for name in LIB_KERNELS]
+    euler_path = os.path.join(reference, "spikeDE_dis", "direct_euler_cupy.py")
+    fma_parts.append(_function_local_string(euler_path, "_get_forward_kernel"))
+    fma_parts.append(_function_local_string(euler_path, "_get_backward_kernel"))
+    # The reference substitutes HISTORY_RHO into this statement as text before compiling
+    # (aligned_glmulti.py:90); do the same with a run-time variable.
+    target = "adj[j]-=w[t*T+j]*r;"
+    if target not in alg.BACKWARD:
+        raise RuntimeError("aligned_backward history statement not found")
+    backward = alg.BACKWARD.replace(target, "adj[j]-=dfsnn_ref_rho*w[t*T+j]*r;")
+    nofma = "static float dfsnn_ref_rho = 1.0f;\n" + alg.FORWARD + backward
+    return "\n".join(fma_parts), nofma
+
+
+def build(reference, cxx="g++"):
+    if not os.path.isdir(os.path.join(reference, "spikeDE_dis")):
+        print(f"build_ref: no reference checkout at {reference}; skipped")
+        return None
+    os.makedirs(OUT, exist_ok=True)
+    fma_src, nofma_src = collect_sources(reference)
+    shim = '#include "%s"\n' % os.path.join(HERE, "ref_shim.h")
+    fma_cpp = os.path.join(OUT, "ref_kernels_fma.cpp")
+    nofma_cpp = os.path.join(OUT, "ref_kernels_nofma.cpp")
+    with open(fma_cpp, "w") as f:
+        f.write(shim + fma_src + WRAPPERS_FMA)
+    with open(nofma_cpp, "w") as f:
+        f.write(shim + nofma_src + WRAPPERS_NOFMA)
+    common = ["-O2", "-fPIC", "-fopenmp", "-march=x86-64-v3", "-fno-fast-math", "-w"]
+    objs = []
+    for src, contract in ((fma_cpp, "fast"), (nofma_cpp, "off")):
+        obj = src[:-4] + ".o"
+        subprocess.check_call([cxx, *common, f"-ffp-contract={contract}", "-c", src, "-o", obj])
+        objs.append(obj)
+    lib = os.path.join(OUT, "libdfsnn_ref.so")
+    subprocess.check_call([cxx, "-shared", "-fopenmp", *objs, "-o", lib])
+    print(f"build_ref: built {lib}")
+    return lib
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--cxx", default="g++")
+    args = ap.parse_args()
+    build(args.reference, args.cxx)

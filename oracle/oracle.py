@@ -1,0 +1,269 @@
+"""numpy front end of the LIF-FDE oracle (TEST INFRASTRUCTURE ONLY).
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference legs import
+this module, as the checker or as the timed CPU baseline.  It loads
+  * oracle/build/liboracle.so     -- the C restatement (oracle/lif_fde_oracle.c), and
+  * oracle/_ref/libdfsnn_ref.so   -- the reference's own kernel sources compiled for the
+                                     host by oracle/build_ref.py, when it was built.
+Arrays are time-major [T, N] float32, as the reference's autograd Functions pass them.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "build", "liboracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libdfsnn_ref.so")
+
+GL, TRAP, PRED, GL1 = 0, 1, 2, 3
+SCHEMES = {"gl": GL, "trap": TRAP, "predictor": PRED, "gl1": GL1}
+
+_f = ctypes.c_float
+_i = ctypes.c_int
+_i64 = ctypes.c_int64
+_p = ctypes.c_void_p
+
+_lib = None
+_ref = None
+
+
+def build():
+    """Compile the C restatement (make -C oracle)."""
+    subprocess.check_call(["make", "-s", "-C", HERE])
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        L.orc_single_forward.argtypes = [_i, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f, _f, _f]
+        L.orc_single_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f, _f, _f, _f]
+        L.orc_glmulti_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f]
+        L.orc_glmulti_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f]
+        L.orc_glmulti_param_grads.argtypes = [_p, _p, _p, _p, _p, _i, _i64]
+        L.orc_aligned_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f]
+        L.orc_aligned_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f, _f]
+        L.orc_aligned_param_grads.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i64]
+        L.orc_euler_forward.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i64] + [_f] * 8
+        L.orc_euler_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i64] + [_f] * 6
+        L.orc_num_threads.restype = _i
+        _lib = L
+    return _lib
+
+
+def ref_available():
+    return os.path.exists(REF_PATH)
+
+
+def ref():
+    """The reference's own kernels compiled for the host (None if not built)."""
+    global _ref
+    if _ref is None and ref_available():
+        R = ctypes.CDLL(REF_PATH)
+        for name in ("ref_gl_forward", "ref_trap_forward"):
+            getattr(R, name).argtypes = [_p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f]
+        R.ref_gl1_forward.argtypes = [_p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f]
+        R.ref_predictor_forward.argtypes = [_p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f, _f]
+        for name in ("ref_gl_backward", "ref_trap_backward"):
+            getattr(R, name).argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f]
+        R.ref_gl1_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f]
+        R.ref_predictor_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f, _f]
+        R.ref_glmulti_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f]
+        R.ref_glmulti_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f]
+        R.ref_aligned_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f]
+        R.ref_aligned_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f]
+        R.ref_euler_forward.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i] + [_f] * 8
+        R.ref_euler_backward.argtypes = [_p] * 10 + [_i, _i] + [_f] * 6
+        _ref = R
+    return _ref
+
+
+def num_threads():
+    return int(lib().orc_num_threads())
+
+
+def _c(a, dtype=np.float32):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _empty(T, N):
+    return np.empty((T, N), dtype=np.float32)
+
+
+# ---------------------------------------------------------------------------------------
+# single-order schemes (gl / trap / predictor / gl1)
+# ---------------------------------------------------------------------------------------
+def single_forward(scheme, x, v0, w, tau, beta, th, h_beta=1.0, gamma1=1.0, impl="oracle"):
+    x, v0, w = _c(x), _c(v0), _c(w)
+    T, N = x.shape
+    s, v = _empty(T, N), _empty(T, N)
+    if impl == "oracle":
+        lib().orc_single_forward(SCHEMES[scheme], _ptr(x), _ptr(v0), _ptr(w), _ptr(s), _ptr(v),
+                                 T, N, tau, beta, th, h_beta, gamma1)
+    else:
+        R = ref()
+        args = [_ptr(x), _ptr(v0), _ptr(w), _ptr(s), _ptr(v), T, N, tau, beta, th, 0.0]
+        if scheme == "gl":
+            R.ref_gl_forward(*args)
+        elif scheme == "trap":
+            R.ref_trap_forward(*args)
+        elif scheme == "gl1":
+            R.ref_gl1_forward(*args, h_beta)
+        else:
+            R.ref_predictor_forward(*args, h_beta, gamma1)
+    return s, v
+
+
+def single_backward(scheme, gS, gV, x, v0, w, tau, beta, th, sg, h_beta=1.0, gamma1=1.0,
+                    impl="oracle", spike=None, vseq=None):
+    """Reference backward (recomputes the forward, truncated history gradient)."""
+    gS, gV, x, v0, w = _c(gS), _c(gV), _c(x), _c(v0), _c(w)
+    T, N = x.shape
+    gx = _empty(T, N)
+    gv0 = np.empty(N, dtype=np.float32)
+    if impl == "oracle":
+        if spike is None or vseq is None:
+            spike, vseq = single_forward(scheme, x, v0, w, tau, beta, th, h_beta, gamma1)
+        spike, vseq = _c(spike), _c(vseq)
+        lib().orc_single_backward(SCHEMES[scheme], _ptr(gS), _ptr(gV), _ptr(spike), _ptr(vseq),
+                                  _ptr(w), _ptr(gx), _ptr(gv0), T, N, tau, beta, th, sg,
+                                  h_beta, gamma1)
+    else:
+        R = ref()
+        args = [_ptr(gS), _ptr(gV), _ptr(x), _ptr(v0), _ptr(w), _ptr(gx), _ptr(gv0), T, N,
+                tau, beta, th, sg]
+        if scheme == "gl":
+            R.ref_gl_backward(*args)
+        elif scheme == "trap":
+            R.ref_trap_backward(*args)
+        elif scheme == "gl1":
+            R.ref_gl1_backward(*args, h_beta)
+        else:
+            R.ref_predictor_backward(*args, h_beta, gamma1)
+    return gx, gv0
+
+
+# ---------------------------------------------------------------------------------------
+# library glmulti (LIFFDEGLMultiFunction)
+# ---------------------------------------------------------------------------------------
+def glmulti_forward(x, v0, scale, W, tau, th, impl="oracle"):
+    x, v0, scale, W = _c(x), _c(v0), _c(scale), _c(W)
+    T, N = x.shape
+    s, vpre, vhist, drift = (_empty(T, N) for _ in range(4))
+    fn = lib().orc_glmulti_forward if impl == "oracle" else ref().ref_glmulti_forward
+    fn(_ptr(x), _ptr(v0), _ptr(scale), _ptr(W), _ptr(s), _ptr(vpre), _ptr(vhist), _ptr(drift),
+       T, N, tau, th)
+    return {"spike": s, "vpre": vpre, "vhist": vhist, "drift": drift}
+
+
+def glmulti_backward(full, gS, scale, W, vpre, tau, th, sg, impl="oracle"):
+    gS, scale, W, vpre = _c(gS), _c(scale), _c(W), _c(vpre)
+    T, N = gS.shape
+    gx, gpre = _empty(T, N), _empty(T, N)
+    gv0 = np.empty(N, dtype=np.float32)
+    fn = lib().orc_glmulti_backward if impl == "oracle" else ref().ref_glmulti_backward
+    fn(int(bool(full)), _ptr(gS), _ptr(scale), _ptr(W), _ptr(vpre), _ptr(gx), _ptr(gv0),
+       _ptr(gpre), T, N, tau, th, sg)
+    return gx, gv0, gpre
+
+
+def glmulti_param_grads(gpre, drift, vhist):
+    """grad_scale = sum_n gpre*drift, grad_W = -gpre @ vhist^T, accumulated in double."""
+    gpre, drift, vhist = _c(gpre), _c(drift), _c(vhist)
+    T, N = gpre.shape
+    gs = np.empty(T, dtype=np.float64)
+    gW = np.empty((T, T), dtype=np.float64)
+    lib().orc_glmulti_param_grads(_ptr(gpre), _ptr(drift), _ptr(vhist), _ptr(gs), _ptr(gW), T, N)
+    return gs, gW
+
+
+def glmulti_step(x, v0, scale, W, gS, tau, th, sg, full, impl="oracle"):
+    """Forward + backward of LIFFDEGLMultiFunction; returns every output and gradient."""
+    fw = glmulti_forward(x, v0, scale, W, tau, th, impl)
+    gx, gv0, gpre = glmulti_backward(full, gS, scale, W, fw["vpre"], tau, th, sg, impl)
+    gs, gW = glmulti_param_grads(gpre, fw["drift"], fw["vhist"])
+    return dict(fw, gx=gx, gv0=gv0, gpre=gpre, gscale=gs, gW=gW)
+
+
+# ---------------------------------------------------------------------------------------
+# aligned glmulti (AlignedGLMulti of examples/*/aligned_glmulti.py)
+# ---------------------------------------------------------------------------------------
+def aligned_forward(x, v0, a, w, tau, th, impl="oracle"):
+    x, v0, a, w = _c(x), _c(v0), _c(a), _c(w)
+    T, N = x.shape
+    s, p, hist = _empty(T, N), _empty(T, N), _empty(T, N)
+    fn = lib().orc_aligned_forward if impl == "oracle" else ref().ref_aligned_forward
+    fn(_ptr(x), _ptr(v0), _ptr(a), _ptr(w), _ptr(s), _ptr(p), _ptr(hist), T, N, tau, th)
+    return {"spike": s, "pred": p, "hist": hist}
+
+
+def aligned_backward(g, a, w, p, tau, th, sg, rho=1.0, impl="oracle"):
+    g, a, w, p = _c(g), _c(a), _c(w), _c(p)
+    T, N = g.shape
+    gx, ga = _empty(T, N), _empty(T, N)
+    gv = np.empty(N, dtype=np.float32)
+    fn = lib().orc_aligned_backward if impl == "oracle" else ref().ref_aligned_backward
+    fn(_ptr(g), _ptr(a), _ptr(w), _ptr(p), _ptr(gx), _ptr(gv), _ptr(ga), T, N, tau, th, sg, rho)
+    return gx, gv, ga
+
+
+def aligned_param_grads(ga, hist, w, a):
+    ga, hist, w, a = _c(ga), _c(hist), _c(w), _c(a)
+    T, N = ga.shape
+    gs = np.empty(T, dtype=np.float64)
+    gw = np.empty((T, T), dtype=np.float64)
+    lib().orc_aligned_param_grads(_ptr(ga), _ptr(hist), _ptr(w), _ptr(a), _ptr(gs), _ptr(gw), T, N)
+    return gs, gw
+
+
+def aligned_step(x, v0, a, w, g, tau, th, sg, rho=1.0, impl="oracle"):
+    fw = aligned_forward(x, v0, a, w, tau, th, impl)
+    gx, gv, ga = aligned_backward(g, a, w, fw["pred"], tau, th, sg, rho, impl)
+    gs, gw = aligned_param_grads(ga, fw["hist"], w, a)
+    return dict(fw, gx=gx, gv0=gv, ga=ga, gscale=gs, gW=gw)
+
+
+# ---------------------------------------------------------------------------------------
+# direct LIF-like Euler (direct_euler_cupy.py)
+# ---------------------------------------------------------------------------------------
+def euler_forward(x, z0, in_scale, gain, bias, tau, th, step, reset_strength, sdt, impl="oracle"):
+    x, z0 = _c(x), _c(z0)
+    T, N = x.shape
+    s, zpre, sin_ = _empty(T, N), _empty(T, N), _empty(T, N)
+    zf = np.empty(N, dtype=np.float32)
+    fn = lib().orc_euler_forward if impl == "oracle" else ref().ref_euler_forward
+    fn(_ptr(x), _ptr(z0), _ptr(s), _ptr(zpre), _ptr(sin_), _ptr(zf), T, N, in_scale, gain, bias,
+       tau, th, step, reset_strength, sdt)
+    return {"spike": s, "zpre": zpre, "sin": sin_, "zfinal": zf}
+
+
+def euler_backward(gS, gzf, x, zpre, sin_, in_scale, gain, tau, step, sg, sdt, impl="oracle"):
+    gS, x, zpre, sin_ = _c(gS), _c(x), _c(zpre), _c(sin_)
+    T, N = x.shape
+    gx = _empty(T, N)
+    gz0 = np.empty(N, dtype=np.float32)
+    gzf_arr = None if gzf is None else _c(gzf)
+    if impl == "oracle":
+        g3 = np.empty(3, dtype=np.float64)
+        lib().orc_euler_backward(_ptr(gS), None if gzf_arr is None else _ptr(gzf_arr), _ptr(x),
+                                 _ptr(zpre), _ptr(sin_), _ptr(gx), _ptr(gz0), _ptr(g3), T, N,
+                                 in_scale, gain, tau, step, sg, sdt)
+    else:
+        g3f = np.zeros(3, dtype=np.float32)
+        if gzf_arr is None:
+            gzf_arr = np.zeros(N, dtype=np.float32)
+        base = g3f.ctypes.data
+        ref().ref_euler_backward(_ptr(gS), _ptr(gzf_arr), _ptr(x), _ptr(zpre), _ptr(sin_),
+                                 _ptr(gx), _ptr(gz0), ctypes.c_void_p(base),
+                                 ctypes.c_void_p(base + 4), ctypes.c_void_p(base + 8),
+                                 T, N, in_scale, gain, tau, step, sg, sdt)
+        g3 = g3f.astype(np.float64)
+    return gx, gz0, g3

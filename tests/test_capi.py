@@ -1,0 +1,97 @@
+"""The C-ABI library loads, exports every entry point of include/dfsnn_b200.h, and rejects
+bad arguments with status codes before touching the GPU (CPU-only checks)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from dfsnn_b200 import _capi
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "dfsnn_b200.h")
+
+
+def header_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(dfsnn_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def L():
+    return _capi.lib()
+
+
+def test_every_declared_symbol_is_exported(L):
+    names = header_functions()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(L, name), name
+        assert name in _capi.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_status_strings(L):
+    assert _capi.status_string(_capi.DFSNN_OK) == "ok"
+    for code in range(1, 8):
+        assert _capi.status_string(code) != "unknown status"
+    assert b"sm_100a" in L.dfsnn_version()
+
+
+def test_bits_words(L):
+    assert L.dfsnn_spike_bits_words(16, 1000) == 1000
+    assert L.dfsnn_spike_bits_words(33, 10) == 20
+    assert L.dfsnn_spike_bits_words(0, 10) == 0
+
+
+FAKE = ctypes.c_void_p(0x1000)   # never dereferenced: validation fails first
+
+
+def test_glmulti_validation(L):
+    f = L.dfsnn_glmulti_forward
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 0, 10, 2.0, 1.0, None) == _capi.DFSNN_ERR_SHAPE
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 4, -1, 2.0, 1.0, None) == _capi.DFSNN_ERR_SHAPE
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 257, 10, 2.0, 1.0, None) == _capi.DFSNN_ERR_T_LIMIT
+    assert f(None, FAKE, FAKE, FAKE, FAKE, 4, 10, 2.0, 1.0, None) == _capi.DFSNN_ERR_NULL
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 4, 10, 0.0, 1.0, None) == _capi.DFSNN_ERR_PARAM
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 4, 10, float("nan"), 1.0, None) == _capi.DFSNN_ERR_PARAM
+    # N == 0 is a valid empty call: nothing to launch
+    assert f(None, None, FAKE, FAKE, None, 4, 0, 2.0, 1.0, None) == _capi.DFSNN_OK
+    b = L.dfsnn_glmulti_backward
+    args = [FAKE] * 9 + [16, 100, 2.0, 1.0, 5.0, 1]
+    assert b(*args, None, 1 << 20, None) == _capi.DFSNN_ERR_WORKSPACE
+    assert b(*args, ctypes.c_void_p(0x1004), 1 << 20, None) == _capi.DFSNN_ERR_WORKSPACE
+    bad_t = [FAKE] * 9 + [33, 100, 2.0, 1.0, 5.0, 1]
+    assert b(*bad_t, FAKE, 1 << 20, None) == _capi.DFSNN_ERR_T_LIMIT
+    no_w = [FAKE] * 4 + [None] + [FAKE] * 4 + [16, 100, 2.0, 1.0, 5.0, 1]
+    assert b(*no_w, FAKE, 1 << 20, None) == _capi.DFSNN_ERR_NULL
+
+
+def test_single_validation(L):
+    f = L.dfsnn_single_forward
+    ok_args = [FAKE] * 6 + [16, 100, 2.0, 0.5, 1.0, 1.0, 1.0, None]
+    assert f(7, *ok_args) == _capi.DFSNN_ERR_SCHEME
+    assert f(-1, *ok_args) == _capi.DFSNN_ERR_SCHEME
+    assert f(0, *([FAKE] * 6 + [0, 100, 2.0, 0.5, 1.0, 1.0, 1.0, None])) == _capi.DFSNN_ERR_SHAPE
+    assert f(0, *([FAKE] * 5 + [None] + [16, 100, 2.0, 0.5, 1.0, 1.0, 1.0, None])) == _capi.DFSNN_ERR_NULL
+    g = L.dfsnn_single_backward
+    assert g(2, *([FAKE] * 7 + [16, 100, 0.0, 0.5, 1.0, 5.0, 1.0, 1.0, None])) == _capi.DFSNN_ERR_PARAM
+
+
+def test_aligned_and_euler_validation(L):
+    f = L.dfsnn_aligned_forward
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 33, 10, 2.0, 1.0, None) == _capi.DFSNN_ERR_T_LIMIT
+    e = L.dfsnn_direct_euler_backward
+    args = [FAKE] * 10 + [16, 100, 2.0, 1.0, 1.0, 1.0, 5.0, 1.0]
+    assert e(*args, FAKE, 8, None) == _capi.DFSNN_ERR_WORKSPACE
+    assert e(*([FAKE] * 9 + [None] + [16, 100, 2.0, 1.0, 1.0, 1.0, 5.0, 1.0]), FAKE, 1 << 20, None) \
+        == _capi.DFSNN_ERR_NULL
+
+
+def test_check_maps_to_reference_exception_types():
+    with pytest.raises(ValueError):
+        _capi.check(_capi.DFSNN_ERR_T_LIMIT, "x")
+    with pytest.raises(ValueError):
+        _capi.check(_capi.DFSNN_ERR_SHAPE, "x")
+    with pytest.raises(RuntimeError):
+        _capi.check(_capi.DFSNN_ERR_CUDA, "x")
+    _capi.check(_capi.DFSNN_OK, "x")

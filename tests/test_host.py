@@ -1,0 +1,134 @@
+"""Host-side logic on CPU: weight tables and glmulti schedule bit-identical to the
+reference's, gradient chain to the Softplus masses, LIFNeuronFDE mirror contract, no
+CPU fallback, and registration under the reference's module names."""
+import math
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from dfsnn_b200 import fde_kernels, integrate, neuron, schedule
+from dfsnn_b200 import aligned_glmulti as alg
+from oracle import oracle as O
+from parity import assert_bitwise, assert_close
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+TAU, TH, SG, H = 2.0, 1.0, 5.0, 0.1
+MULTI_BETA = [0.3, 0.4, 0.5]
+MASSES = [0.5, 0.5, 0.7]
+
+
+def tables():
+    return dict(np.load(os.path.join(GOLDEN, "torch_tables.npz")))
+
+
+def make_glmulti(T=16, **kw):
+    return neuron.LIFNeuronFDE(tau=TAU, threshold=TH, surrogate_grad_scale=SG,
+                               surrogate_function="arctan", beta=MULTI_BETA[0], T=T,
+                               method="glmulti", step_size=H, batchsize=4, step_mode="m",
+                               backend="cupy", multi_beta=MULTI_BETA, multi_coefficient=MASSES,
+                               learn_coefficient=True, coefficient_constraint="softplus",
+                               glmulti_history_grad="full", **kw)
+
+
+@pytest.mark.parametrize("method", ["gl", "trap", "predictor"])
+@pytest.mark.parametrize("beta", [0.3, 0.5, 0.7])
+@pytest.mark.parametrize("T", [8, 16, 20, 64, 256])
+def test_weight_tables_bitwise(method, beta, T):
+    ref = tables()[f"{method}_b{beta}_T{T}"]
+    got = getattr(schedule, f"{method}_weights")(beta, T).numpy()
+    assert_bitwise(got, ref, what=f"{method} beta={beta} T={T}")
+
+
+@pytest.mark.parametrize("T", [1, 8, 16, 32])
+def test_glmulti_schedule_bitwise(T):
+    d = tables()
+    n = make_glmulti(T)
+    with torch.no_grad():
+        terms = n._build_glmulti_schedule(T, torch.device("cpu"))
+    assert_bitwise(terms["scale"].contiguous().numpy(), d[f"glmulti_scale_T{T}"], what="scale")
+    assert_bitwise(terms["weights"].numpy(), d[f"glmulti_W_T{T}"], what="W")
+
+
+@pytest.mark.parametrize("case", ["spiking_T16", "config1_T16"])
+def test_glmulti_mass_gradient_chain(case):
+    """Reference LIFNeuronFDE (torch path, truncated history) gradient of the shared raw
+    masses == oracle (grad_scale, grad_W) pushed through this package's schedule."""
+    d = dict(np.load(os.path.join(GOLDEN, f"torch_glmulti_neuron_{case}.npz")))
+    T = d["x"].shape[0]
+    x = d["x"].reshape(T, -1)
+    N = x.shape[1]
+    n = make_glmulti(T)
+    terms = n._build_glmulti_schedule(T, torch.device("cpu"))
+    r = O.glmulti_step(x, np.zeros(N, np.float32), terms["scale"].detach().numpy(),
+                       terms["weights"].detach().numpy(), d["gS"].reshape(T, N), TAU, TH, SG, False)
+    assert (r["spike"] == d["spike"].reshape(T, N)).all()
+    torch.autograd.backward([terms["scale"], terms["weights"]],
+                            [torch.tensor(r["gscale"], dtype=torch.float32),
+                             torch.tensor(r["gW"], dtype=torch.float32)])
+    assert_close(n.multi_coefficient_raw.grad.numpy(), d["graw"], rtol=1e-4, what="grad raw")
+    assert_close(r["gx"], d["gx"].reshape(T, N), rtol=1e-4, what="gx")
+
+
+def test_state_dict_keys_match_reference():
+    d = tables()
+    assert sorted(make_glmulti().state_dict().keys()) == list(d["state_dict_keys_glmulti"])
+    gl = neuron.LIFNeuronFDE(method="gl", T=16, step_mode="m", backend="cupy")
+    assert sorted(gl.state_dict().keys()) == list(d["state_dict_keys_gl"])
+
+
+def test_shared_coefficient_and_validation():
+    raw = torch.nn.Parameter(torch.log(torch.expm1(torch.tensor(MASSES))))
+    a, b = make_glmulti(shared_multi_coefficient=raw), make_glmulti(shared_multi_coefficient=raw)
+    assert a.multi_coefficient_raw is b.multi_coefficient_raw
+    with pytest.raises(ValueError):
+        neuron.LIFNeuronFDE(method="glmulti", multi_beta=[0.3], multi_coefficient=[0.5, 0.5])
+    with pytest.raises(ValueError):
+        neuron.LIFNeuronFDE(method="nope")
+
+
+def test_no_cpu_fallback():
+    x = torch.zeros(8, 4)
+    with pytest.raises(RuntimeError):
+        fde_kernels.LIFFDEGLMultiFunction.apply(x, torch.zeros(4), torch.ones(8), torch.zeros(8, 8),
+                                                2.0, 1.0, 5.0, 1, True)
+    with pytest.raises(RuntimeError):
+        fde_kernels.LIFFDEGLFunction.apply(x, torch.zeros(4), torch.ones(9), 2.0, 0.5, 1.0, 0.0, 5.0)
+    with pytest.raises(RuntimeError):
+        make_glmulti(8)(torch.zeros(8, 2, 3))
+    with pytest.raises(NotImplementedError):
+        neuron.LIFNeuronFDE(method="gl", step_mode="s")(torch.zeros(2, 3))
+    with pytest.raises(NotImplementedError):
+        fde_kernels.LIFFDEVOGL1Function.apply(x)
+
+
+def test_reference_limits_raise_value_error():
+    x = torch.zeros(65, 4)
+    with pytest.raises(ValueError):
+        alg.AlignedGLMulti.apply(x, torch.zeros(4), torch.ones(65), torch.zeros(65, 65), 2.0, 1.0,
+                                 5.0, 1, True)
+    with pytest.raises(ValueError):
+        alg.AlignedGLMulti.apply(torch.zeros(4, 4), torch.zeros(4), torch.ones(4),
+                                 torch.zeros(4, 4), 2.0, 1.0, 5.0, 1, False)
+
+
+def test_integrate_registers_reference_module_names():
+    saved = {k: sys.modules.get(k) for k in (integrate.FDE_MODULE, integrate.EULER_MODULE)}
+    try:
+        integrate.install()
+        import importlib
+        m = importlib.import_module("spikeDE_dis.fde_cupy_kernels_all")
+        assert m is fde_kernels and m.CUPY_AVAILABLE
+        assert importlib.import_module("spikeDE_dis.direct_euler_cupy").lif_like_euler_cupy
+        original = fde_kernels.LIFFDEGLMultiFunction
+        integrate.rebind_aligned()
+        assert fde_kernels.LIFFDEGLMultiFunction is alg.AlignedGLMulti
+        fde_kernels.LIFFDEGLMultiFunction = original
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                sys.modules.pop(k, None)
+            else:
+                sys.modules[k] = v
