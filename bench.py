@@ -56,11 +56,24 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=1 << 22,
                     help="neurons of the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--only", default="",
+                    help="profiling: comma list of scheme:T (e.g. glmulti:16) instead of all")
+    ap.add_argument("--neurons", type=int, default=0,
+                    help="profiling: neurons per GPU instead of 16*128*64*64")
+    args = ap.parse_args()
+    global SHAPE, COMBOS
+    if args.only:
+        COMBOS = [(int(c.split(":")[1]), c.split(":")[0]) for c in args.only.split(",")]
+    if args.neurons:
+        SHAPE = (16, args.neurons // 16)
+    return args
+
+
+COMBOS = [(T, sch) for T in TS for sch in SCHEMES]
 
 
 def units_per_step(neurons):
-    return sum(T * neurons for T in TS for _ in SCHEMES)
+    return sum(T * neurons for T, _ in COMBOS)
 
 
 # -----------------------------------------------------------------------------------------
@@ -221,18 +234,17 @@ class ClockSampler:
 def make_layers(device):
     from dfsnn_b200.neuron import LIFNeuronFDE
     layers = {}
-    for T in TS:
-        for sch in SCHEMES:
-            kw = dict(tau=TAU, threshold=TH, surrogate_grad_scale=SG, surrogate_function="arctan",
-                      T=T, method=sch, step_size=H, batchsize=SHAPE[0], step_mode="m",
-                      backend="cupy")
-            if sch == "glmulti":
-                kw.update(beta=MULTI_BETA[0], multi_beta=MULTI_BETA, multi_coefficient=MASSES,
-                          learn_coefficient=True, coefficient_constraint="softplus",
-                          glmulti_history_grad="full")
-            else:
-                kw.update(beta=BETA, store_v_seq=True)
-            layers[(T, sch)] = LIFNeuronFDE(**kw).to(device)
+    for T, sch in COMBOS:
+        kw = dict(tau=TAU, threshold=TH, surrogate_grad_scale=SG, surrogate_function="arctan",
+                  T=T, method=sch, step_size=H, batchsize=SHAPE[0], step_mode="m",
+                  backend="cupy")
+        if sch == "glmulti":
+            kw.update(beta=MULTI_BETA[0], multi_beta=MULTI_BETA, multi_coefficient=MASSES,
+                      learn_coefficient=True, coefficient_constraint="softplus",
+                      glmulti_history_grad="full")
+        else:
+            kw.update(beta=BETA, store_v_seq=True)
+        layers[(T, sch)] = LIFNeuronFDE(**kw).to(device)
     return layers
 
 
@@ -275,10 +287,9 @@ def run_native(args):
 
     def step():
         mass_grads = []
-        for T in TS:
-            for sch in SCHEMES:
-                _, _, pg = layer_step(layers[(T, sch)], x16[:T], gS16[:T], gV16[:T], sch != "glmulti")
-                mass_grads += pg
+        for T, sch in COMBOS:
+            _, _, pg = layer_step(layers[(T, sch)], x16[:T], gS16[:T], gV16[:T], sch != "glmulti")
+            mass_grads += pg
         if world > 1 and mass_grads:
             flat = torch.cat([p.reshape(-1) for p in mass_grads])
             dist.all_reduce(flat)
@@ -377,19 +388,18 @@ def run_e2e(args, layers, x16, gS16, gV16, dev, world):
     def one():
         nonlocal h2d, d2h
         h2d = d2h = 0
-        for T in TS:
-            for sch in SCHEMES:
-                single = sch != "glmulti"
-                dx[:T].copy_(hx[:T], non_blocking=True)
-                dgS[:T].copy_(hgS[:T], non_blocking=True)
-                h2d += 2 * hx[:T].numel() * 4
-                if single:
-                    dgV[:T].copy_(hgV[:T], non_blocking=True)
-                    h2d += hx[:T].numel() * 4
-                gx, s, _ = layer_step(layers[(T, sch)], dx[:T], dgS[:T], dgV[:T], single)
-                out_s[:T].copy_(s, non_blocking=True)
-                out_g[:T].copy_(gx, non_blocking=True)
-                d2h += 2 * hx[:T].numel() * 4
+        for T, sch in COMBOS:
+            single = sch != "glmulti"
+            dx[:T].copy_(hx[:T], non_blocking=True)
+            dgS[:T].copy_(hgS[:T], non_blocking=True)
+            h2d += 2 * hx[:T].numel() * 4
+            if single:
+                dgV[:T].copy_(hgV[:T], non_blocking=True)
+                h2d += hx[:T].numel() * 4
+            gx, s, _ = layer_step(layers[(T, sch)], dx[:T], dgS[:T], dgV[:T], single)
+            out_s[:T].copy_(s, non_blocking=True)
+            out_g[:T].copy_(gx, non_blocking=True)
+            d2h += 2 * hx[:T].numel() * 4
 
     one()
     torch.cuda.synchronize()

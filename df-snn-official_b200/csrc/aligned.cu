@@ -10,8 +10,11 @@
 // The reference compiles these with --fmad=false: every product and sum here is a
 // separately rounded intrinsic, in the reference's order.
 // The forward writes only spikes (the reference also writes pred and hist: 12 B vs 4 B
-// per neuron-step); the backward recomputes them and reduces grad a / grad W in-kernel.
+// per neuron-step); the backward is the same persistent, bulk-staged design as the glmulti
+// backward (glmulti.cu), reducing grad a / grad W in-kernel.
+#include "bulk_pipe.cuh"
 #include "kernels.h"
+#include "pack2.cuh"
 #include "param_reduce.cuh"
 
 namespace dfsnn {
@@ -26,38 +29,37 @@ struct AlnArgs {
     float* gx;
     float* gv0;
     double* part;
+    unsigned int* err;
     int T;
     long long N;
     float tau, inv_tau, th, sg, rho;
 };
 
-// One forward step of aligned_forward.  Returns v_t; h is the history sum.
-template <int TB, bool TP2>
-__device__ __forceinline__ float aligned_step(float x, float v, const float* sW, const float* sA,
-                                              const float (&vh)[TB], int t, float tau, float inv_tau,
-                                              float th, float& pred, bool& fire, float& h) {
+// One forward step of aligned_forward (:11-14).  Returns v_t; h is the history sum.
+template <int TB, bool TP2, bool FAST>
+__device__ __forceinline__ float aligned_step(float x, float v, const float* sW, const float (&wr)[TB],
+                                              float a_t, const float (&vh)[TB], int t, float tau,
+                                              float inv_tau, float th, float& pred, bool& fire,
+                                              float& h) {
     const float d = div_tau<TP2>(__fsub_rn(x, v), tau, inv_tau);
     pred = __fadd_rn(v, d);
     fire = pred >= th;
     const float spike = fire ? 1.0f : 0.0f;
     h = 0.0f;
 #pragma unroll
-    for (int j = 0; j < t; ++j) h = __fadd_rn(h, __fmul_rn(sW[t * TB + j], vh[j]));
+    for (int j = 0; j < t; ++j) h = __fadd_rn(h, __fmul_rn(wgt<TB, FAST>(sW, wr, t, j), vh[j]));
     const float f = __fsub_rn(d, div_tau<TP2>(__fmul_rn(spike, th), tau, inv_tau));
-    return __fsub_rn(__fmul_rn(sA[t], f), h);
+    return __fsub_rn(__fmul_rn(a_t, f), h);
 }
 
-template <int TB, bool TP2>
-__global__ void __launch_bounds__(256) aln_fwd_reg(AlnArgs a) {
-    __shared__ float sW[TB * TB];
-    __shared__ float sA[TB];
+template <int TB, bool TP2, bool FAST>
+__device__ __forceinline__ void aln_fwd_body(const AlnArgs& a, const float* sW, const float* sA,
+                                             long long n) {
     const int T = a.T;
-    for (int e = threadIdx.x; e < T * T; e += blockDim.x) sW[(e / T) * TB + e % T] = a.W[e];
-    for (int e = threadIdx.x; e < T; e += blockDim.x) sA[e] = a.a[e];
-    __syncthreads();
-    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (n >= a.N) return;
     const long long N = a.N;
+    float wr[TB];
+#pragma unroll
+    for (int d = 0; d < TB; ++d) wr[d] = (FAST && d > 0) ? sW[d * TB] : 0.0f;
     float xr[TB];
 #pragma unroll
     for (int t = 0; t < TB; ++t)
@@ -69,7 +71,8 @@ __global__ void __launch_bounds__(256) aln_fwd_reg(AlnArgs a) {
         if (t < T) {
             float pred, h;
             bool fire;
-            v = aligned_step<TB, TP2>(xr[t], v, sW, sA, vh, t, a.tau, a.inv_tau, a.th, pred, fire, h);
+            v = aligned_step<TB, TP2, FAST>(xr[t], v, sW, wr, FAST ? sA[0] : sA[t], vh, t, a.tau,
+                                            a.inv_tau, a.th, pred, fire, h);
             vh[t] = v;
             st_stream(a.spike + t * N + n, fire ? 1.0f : 0.0f);
         }
@@ -77,13 +80,148 @@ __global__ void __launch_bounds__(256) aln_fwd_reg(AlnArgs a) {
 }
 
 template <int TB, bool TP2>
-__global__ void __launch_bounds__(256) aln_bwd_reg(AlnArgs a) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    float* sG = reinterpret_cast<float*>(smem_raw);   // adjoint r_t
-    float* sV = sG + TB * kLdn;                        // v_t
-    float* sE = sV + TB * kLdn;                        // r_t*(v_t+h_t)/a_t
+__global__ void __launch_bounds__(256) aln_fwd_reg(AlnArgs a) {
     __shared__ float sW[TB * TB];
     __shared__ float sA[TB];
+    const int T = a.T;
+    for (int e = threadIdx.x; e < TB * TB; e += blockDim.x) {
+        const int t = e / TB, i = e % TB;
+        sW[e] = (t < T && i < T) ? a.W[t * T + i] : 0.0f;
+    }
+    for (int e = threadIdx.x; e < TB; e += blockDim.x) sA[e] = e < T ? a.a[e] : 0.0f;
+    const bool fast = block_toeplitz(a.W, a.a, T);
+    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= a.N) return;
+    if (fast) aln_fwd_body<TB, TP2, true>(a, sW, sA, n);
+    else aln_fwd_body<TB, TP2, false>(a, sW, sA, n);
+}
+
+// Forward, T <= TB <= 16, two neurons per thread with packed fp32x2 (Toeplitz schedule;
+// a general W runs the scalar body per neuron).  The history sum h is accumulated negated,
+// h' = h' + round(-w*v), so v = round(a*f) - h is one packed add.
+template <int TB, bool TP2>
+__global__ void __launch_bounds__(256) aln_fwd_x2(AlnArgs a) {
+    __shared__ float sW[TB * TB];
+    __shared__ float sA[TB];
+    const int T = a.T;
+    for (int e = threadIdx.x; e < TB * TB; e += blockDim.x) {
+        const int t = e / TB, i = e % TB;
+        sW[e] = (t < T && i < T) ? a.W[t * T + i] : 0.0f;
+    }
+    for (int e = threadIdx.x; e < TB; e += blockDim.x) sA[e] = e < T ? a.a[e] : 0.0f;
+    const bool fast = block_toeplitz(a.W, a.a, T);
+    const long long n = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
+    if (n >= a.N) return;
+    if (!fast) {
+        aln_fwd_body<TB, TP2, false>(a, sW, sA, n);
+        aln_fwd_body<TB, TP2, false>(a, sW, sA, n + 1);
+        return;
+    }
+    const long long N = a.N;
+    float2 nw[TB];
+#pragma unroll
+    for (int d = 0; d < TB; ++d) nw[d] = f2(d > 0 ? -sW[d * TB] : 0.0f);
+    const float2 a2 = f2(sA[0]);
+    const float2 inv2 = f2(a.inv_tau);
+    const float2 mth = f2(-a.th);
+    float2 xr[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t)
+        if (t < T) xr[t] = ld2_stream(a.x + t * N + n);
+    float2 v = *reinterpret_cast<const float2*>(a.v0 + n);
+    float2 vh[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) {
+        if (t < T) {
+            const float2 d = div_tau2<TP2>(sub2(xr[t], v), a.tau, inv2);
+            const float2 pred = add2(v, d);
+            const float2 s = fire2(pred, a.th);
+            float2 hn = f2(-0.0f);                                   // -h
+#pragma unroll
+            for (int j = 0; j < t; ++j) hn = add2(hn, mul2(nw[t - j], vh[j]));
+            const float2 f = add2(d, div_tau2<TP2>(mul2(s, mth), a.tau, inv2));   // d - s*th/tau
+            v = add2(mul2(a2, f), hn);                               // a*f - h
+            vh[t] = v;
+            st2_stream(a.spike + t * N + n, s);
+        }
+    }
+}
+
+// Backward tile.  Stage X holds x_t, then v_t + h_t, then e_t = r_t (v_t + h_t) / a_t;
+// stage G holds grad_spike_t, then q_t (surrogate term), then the adjoint r_t.
+template <int TB, bool TP2, bool FAST>
+__device__ __forceinline__ void aln_bwd_tile(const AlnArgs& a, const float* sW, const float* sA,
+                                             const float (&wr)[TB], const float (&rw)[TB],
+                                             float zc, float one_m, float* X, float* G, float* V,
+                                             long long n0, int tid) {
+    const int T = a.T;
+    const long long N = a.N;
+    const long long n = n0 + tid;
+    const bool live = n < N;
+    float v = live ? a.v0[n] : 0.0f;
+    float vh[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) {
+        if (t < T) {
+            float pred, h;
+            bool fire;
+            v = aligned_step<TB, TP2, FAST>(X[t * kTile + tid], v, sW, wr, FAST ? sA[0] : sA[t],
+                                            vh, t, a.tau, a.inv_tau, a.th, pred, fire, h);
+            const float z = __fmul_rn(zc, __fsub_rn(pred, a.th));
+            const float den = __fmul_rn(2.0f, __fadd_rn(1.0f, __fmul_rn(z, z)));
+            G[t * kTile + tid] = __fdiv_rn(__fmul_rn(G[t * kTile + tid], a.sg), den);   // q_t
+            X[t * kTile + tid] = __fadd_rn(v, h);                                       // v_t + h_t
+        } else {
+            v = 0.0f;
+        }
+        if (!live) v = 0.0f;
+        vh[t] = v;
+        V[t * kTile + tid] = v;
+    }
+    float A[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) A[t] = 0.0f;
+#pragma unroll
+    for (int t = TB - 1; t >= 0; --t) {
+        float r = 0.0f, e = 0.0f;
+        if (t < T) {
+            const float a_t = FAST ? sA[0] : sA[t];
+            const float q = G[t * kTile + tid];
+            r = A[t];
+            const float ra = __fmul_rn(r, a_t);
+            if (live) st_stream(a.gx + t * N + n, div_tau<TP2>(__fadd_rn(q, ra), a.tau, a.inv_tau));
+            const float prev = __fsub_rn(__fmul_rn(q, one_m), div_tau<TP2>(ra, a.tau, a.inv_tau));
+            if (t) A[t - 1] = __fadd_rn(A[t - 1], prev);
+            else if (live) a.gv0[n] = prev;
+#pragma unroll
+            for (int j = 0; j < t; ++j) {
+                const float rwj = FAST ? rw[t - j] : __fmul_rn(a.rho, sW[t * TB + j]);
+                A[j] = __fsub_rn(A[j], __fmul_rn(rwj, r));
+            }
+            e = __fdiv_rn(__fmul_rn(r, X[t * kTile + tid]), a_t);
+        }
+        G[t * kTile + tid] = live ? r : 0.0f;
+        X[t * kTile + tid] = live ? e : 0.0f;
+    }
+}
+
+template <int TB>
+struct AlnBwdSmem {
+    static constexpr size_t kStageFloats = size_t(2) * TB * kTile;
+    static constexpr size_t kBytes = sizeof(float) * (2 * kStageFloats + size_t(TB) * kTile);
+    static_assert(size_t(kTile) * 20 * sizeof(double) <= kBytes, "reduction scratch must fit");
+};
+
+template <int TB, bool TP2, bool BULK>
+__global__ void __launch_bounds__(256) aln_bwd(AlnArgs a) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    float* base = reinterpret_cast<float*>(smem_raw);
+    float* stageX[2] = {base, base + AlnBwdSmem<TB>::kStageFloats};
+    float* stageG[2] = {base + TB * kTile, base + AlnBwdSmem<TB>::kStageFloats + TB * kTile};
+    float* V = base + 2 * AlnBwdSmem<TB>::kStageFloats;
+    __shared__ float sW[TB * TB];
+    __shared__ float sA[TB];
+    __shared__ __align__(8) uint64_t bars[2];
     const int T = a.T;
     const long long N = a.N;
     const int tid = threadIdx.x;
@@ -92,87 +230,83 @@ __global__ void __launch_bounds__(256) aln_bwd_reg(AlnArgs a) {
         sW[e] = (t < T && i < T) ? a.W[t * T + i] : 0.0f;
     }
     for (int e = tid; e < TB; e += blockDim.x) sA[e] = e < T ? a.a[e] : 1.0f;
-    TileAccumulator<TB, false> acc;
-    acc.init(tid);
-    const long long ntiles = (N + kTile - 1) / kTile;
+    BulkPipe<2> pipe;
+    pipe.bar = bars;
+    pipe.T = T;
+    pipe.N = N;
+    pipe.src[0] = a.x;
+    pipe.src[1] = a.g;
+    for (int s = 0; s < 2; ++s) { pipe.stage[s][0] = stageX[s]; pipe.stage[s][1] = stageG[s]; }
+    if (BULK && tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+    }
+    const bool fast = block_toeplitz(a.W, a.a, T);
+    float wr[TB], rw[TB];
+#pragma unroll
+    for (int d = 0; d < TB; ++d) {
+        wr[d] = (fast && d > 0) ? sW[d * TB] : 0.0f;
+        rw[d] = __fmul_rn(a.rho, wr[d]);                  // (rho * w) as the reference rounds it
+    }
     const float zc = __fmul_rn(kAlignedPiHalf, a.sg);
     const float one_m = __fsub_rn(1.0f, __fdiv_rn(1.0f, a.tau));      // 1 - 1/tau
-    __syncthreads();
-    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const long long n = tile * kTile + tid;
-        const bool live = n < N;
-        float xr[TB], gr[TB];
-#pragma unroll
-        for (int t = 0; t < TB; ++t) {
-            xr[t] = (live && t < T) ? ld_stream(a.x + t * N + n) : 0.0f;
-            gr[t] = (live && t < T) ? ld_stream(a.g + t * N + n) : 0.0f;
-        }
-        float v = live ? a.v0[n] : 0.0f;
-        float vh[TB], q[TB], vph[TB];
-#pragma unroll
-        for (int t = 0; t < TB; ++t) {
-            if (t < T) {
-                float pred, h;
-                bool fire;
-                v = aligned_step<TB, TP2>(xr[t], v, sW, sA, vh, t, a.tau, a.inv_tau, a.th, pred, fire, h);
-                const float z = __fmul_rn(zc, __fsub_rn(pred, a.th));
-                const float den = __fmul_rn(2.0f, __fadd_rn(1.0f, __fmul_rn(z, z)));
-                q[t] = __fdiv_rn(__fmul_rn(gr[t], a.sg), den);
-                vph[t] = __fadd_rn(v, h);
-            } else {
-                v = 0.0f;
-                q[t] = 0.0f;
-                vph[t] = 0.0f;
-            }
-            if (!live) v = 0.0f;
-            vh[t] = v;
-            sV[t * kLdn + tid] = v;
-        }
-        float A[TB];
-#pragma unroll
-        for (int t = 0; t < TB; ++t) A[t] = 0.0f;
-#pragma unroll
-        for (int t = TB - 1; t >= 0; --t) {
-            float r = 0.0f, e = 0.0f;
-            if (t < T) {
-                r = A[t];
-                const float ra = __fmul_rn(r, sA[t]);
-                if (live) st_stream(a.gx + t * N + n, div_tau<TP2>(__fadd_rn(q[t], ra), a.tau, a.inv_tau));
-                const float prev = __fsub_rn(__fmul_rn(q[t], one_m), div_tau<TP2>(ra, a.tau, a.inv_tau));
-                if (t) A[t - 1] = __fadd_rn(A[t - 1], prev);
-                else if (live) a.gv0[n] = prev;
-#pragma unroll
-                for (int j = 0; j < t; ++j) A[j] = __fsub_rn(A[j], __fmul_rn(__fmul_rn(a.rho, sW[t * TB + j]), r));
-                e = __fdiv_rn(__fmul_rn(r, vph[t]), sA[t]);
-            }
-            if (!live) { r = 0.0f; e = 0.0f; }
-            sG[t * kLdn + tid] = r;
-            sE[t * kLdn + tid] = e;
-        }
-        __syncthreads();
-        acc.accumulate(sG, sV, sE);
-        __syncthreads();
+    TileProduct<TB, false> prod;
+    prod.init(tid);
+    const long long ntiles = (N + kTile - 1) / kTile;
+    const long long first = blockIdx.x, stride = gridDim.x;
+    if (BULK && tid == 0) {
+        if (first < ntiles) pipe.issue(0, first);
+        if (first + stride < ntiles) pipe.issue(1, first + stride);
     }
-    acc.finish(reinterpret_cast<double*>(smem_raw), a.part + (size_t)blockIdx.x * ProdCfg<TB>::NOUT, tid);
+    bool failed = false;
+    int j = 0;
+    for (long long tile = first; tile < ntiles; tile += stride, ++j) {
+        const int s = BULK ? (j & 1) : 0;
+        float* X = stageX[s];
+        float* G = stageG[s];
+        if constexpr (BULK) {
+            const bool ok = mbar_wait_bounded(&bars[s], (uint32_t)((j >> 1) & 1));
+            if (__syncthreads_or(!ok)) { failed = true; break; }
+        } else {
+            const long long n = tile * kTile + tid;
+            for (int t = 0; t < T; ++t) {
+                X[t * kTile + tid] = n < N ? ld_stream(a.x + t * N + n) : 0.0f;
+                G[t * kTile + tid] = n < N ? ld_stream(a.g + t * N + n) : 0.0f;
+            }
+        }
+        if (fast) aln_bwd_tile<TB, TP2, true>(a, sW, sA, wr, rw, zc, one_m, X, G, V, tile * kTile, tid);
+        else aln_bwd_tile<TB, TP2, false>(a, sW, sA, wr, rw, zc, one_m, X, G, V, tile * kTile, tid);
+        __syncthreads();
+        prod.accumulate(G, V, X);
+        __syncthreads();
+        if (BULK && tid == 0 && tile + 2 * stride < ntiles) pipe.issue(s, tile + 2 * stride);
+    }
+    if (failed) {
+        if (tid == 0) {
+            atomicOr(a.err, 1u);
+            mbar_wait_bounded(&bars[j & 1], (uint32_t)((j >> 1) & 1));
+            if (first + (long long)(j + 1) * stride < ntiles)
+                mbar_wait_bounded(&bars[(j + 1) & 1], (uint32_t)(((j + 1) >> 1) & 1));
+        }
+        return;
+    }
+    prod.finish(reinterpret_cast<double*>(smem_raw), a.part + (size_t)blockIdx.x * ProdCfg<TB>::NOUT, tid);
 }
 
 namespace {
 
-template <int TB>
-size_t aln_smem() {
-    const size_t stage = ProdCfg<TB>::SMEM_BYTES;
-    const size_t red = size_t(kTile) * 20 * sizeof(double);
-    return stage > red ? stage : red;
-}
+int tb_of(int T) { return T <= 8 ? 8 : (T <= 16 ? 16 : 32); }
 
-template <int TB, bool TP2>
+template <int TB>
 int aln_grid_t(long long N) {
     int dev = 0, sms = 0, per = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const size_t smem = aln_smem<TB>();
-    cudaFuncSetAttribute(aln_bwd_reg<TB, TP2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, aln_bwd_reg<TB, TP2>, kTile, smem);
+    const size_t smem = AlnBwdSmem<TB>::kBytes;
+    auto k = aln_bwd<TB, false, true>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, kTile, smem);
     if (per < 1) per = 1;
     const long long ntiles = (N + kTile - 1) / kTile;
     long long g = (long long)sms * per;
@@ -180,24 +314,23 @@ int aln_grid_t(long long N) {
     return g < 1 ? 1 : (int)g;
 }
 
-template <int TB, bool TP2>
+template <int TB, bool TP2, bool BULK>
 cudaError_t aln_bwd_launch_t(const AlnArgs& a, int grid, cudaStream_t st) {
-    const size_t smem = aln_smem<TB>();
-    cudaError_t e = cudaFuncSetAttribute(aln_bwd_reg<TB, TP2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const size_t smem = AlnBwdSmem<TB>::kBytes;
+    auto k = aln_bwd<TB, TP2, BULK>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    aln_bwd_reg<TB, TP2><<<grid, kTile, smem, st>>>(a);
+    k<<<grid, kTile, smem, st>>>(a);
     return cudaGetLastError();
 }
 
-int tb_of(int T) { return T <= 8 ? 8 : (T <= 16 ? 16 : 32); }
-
 }  // namespace
 
-int aligned_bwd_blocks(int T, long long N, bool tau_pow2) {
+int aligned_bwd_blocks(int T, long long N, bool) {
     const int TB = tb_of(T);
-    if (TB == 8) return tau_pow2 ? aln_grid_t<8, true>(N) : aln_grid_t<8, false>(N);
-    if (TB == 16) return tau_pow2 ? aln_grid_t<16, true>(N) : aln_grid_t<16, false>(N);
-    return tau_pow2 ? aln_grid_t<32, true>(N) : aln_grid_t<32, false>(N);
+    if (TB == 8) return aln_grid_t<8>(N);
+    if (TB == 16) return aln_grid_t<16>(N);
+    return aln_grid_t<32>(N);
 }
 
 int aligned_part_stride(int T) {
@@ -212,6 +345,19 @@ cudaError_t aligned_forward_launch(const float* x, const float* v0, const float*
     AlnArgs a{};
     a.x = x; a.v0 = v0; a.a = a_; a.W = W; a.spike = spike; a.T = T; a.N = N; a.tau = tau;
     a.inv_tau = 1.0f / tau; a.th = th;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(v0) |
+                         reinterpret_cast<uintptr_t>(spike);
+    if (T <= 16 && (N % 2) == 0 && (al & 7u) == 0) {
+        const unsigned g2 = (unsigned)((N / 2 + 255) / 256);
+        if (T <= 8) {
+            if (tau_pow2) aln_fwd_x2<8, true><<<g2, 256, 0, st>>>(a);
+            else aln_fwd_x2<8, false><<<g2, 256, 0, st>>>(a);
+        } else {
+            if (tau_pow2) aln_fwd_x2<16, true><<<g2, 256, 0, st>>>(a);
+            else aln_fwd_x2<16, false><<<g2, 256, 0, st>>>(a);
+        }
+        return cudaGetLastError();
+    }
     const unsigned grid = (unsigned)((N + 255) / 256);
     const int TB = tb_of(T);
 #define DFSNN_AF(TBV)                                                    \
@@ -227,24 +373,27 @@ cudaError_t aligned_forward_launch(const float* x, const float* v0, const float*
 cudaError_t aligned_backward_launch(const float* g, const float* x, const float* v0,
                                     const float* a_, const float* W, float* gx, float* gv0,
                                     float* ga, float* gW, int T, long long N, float tau, float th,
-                                    float sg, float rho, bool tau_pow2, double* part, int nblocks,
-                                    cudaStream_t st) {
+                                    float sg, float rho, bool tau_pow2, double* part,
+                                    unsigned int* err, int nblocks, cudaStream_t st) {
     AlnArgs a{};
     a.x = x; a.v0 = v0; a.a = a_; a.W = W; a.g = g; a.gx = gx; a.gv0 = gv0; a.part = part;
-    a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau; a.th = th; a.sg = sg; a.rho = rho;
+    a.err = err; a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau; a.th = th; a.sg = sg;
+    a.rho = rho;
+    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(unsigned int), st);
+    if (e != cudaSuccess) return e;
+    const bool bulk = bulk_eligible(x, g, N);
     const int TB = tb_of(T);
-    cudaError_t e = cudaSuccess;
-#define DFSNN_AB(TBV)                                                                         \
-    if (TB == TBV) e = tau_pow2 ? aln_bwd_launch_t<TBV, true>(a, nblocks, st)                 \
-                                : aln_bwd_launch_t<TBV, false>(a, nblocks, st);
+#define DFSNN_AB(TBV)                                                                          \
+    if (TB == TBV) {                                                                           \
+        if (bulk) e = tau_pow2 ? aln_bwd_launch_t<TBV, true, true>(a, nblocks, st)             \
+                               : aln_bwd_launch_t<TBV, false, true>(a, nblocks, st);           \
+        else e = tau_pow2 ? aln_bwd_launch_t<TBV, true, false>(a, nblocks, st)                 \
+                          : aln_bwd_launch_t<TBV, false, false>(a, nblocks, st);               \
+    }
     DFSNN_AB(8) DFSNN_AB(16) DFSNN_AB(32)
 #undef DFSNN_AB
     if (e != cudaSuccess) return e;
-    if (ga || gW) {
-        const int nout = T + T * T;
-        param_finalize<<<(nout + 127) / 128, 128, 0, st>>>(part, nblocks, TB, T, ga, gW, 1);
-        e = cudaGetLastError();
-    }
+    if (ga || gW) e = launch_param_finalize(part, nblocks, TB, T, ga, gW, 1, err, st);
     return e;
 }
 

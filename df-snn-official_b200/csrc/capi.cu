@@ -39,6 +39,11 @@ int check_seq(int T, long long N, int tmax) {
 
 bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
 
+// Workspace of the persistent backward kernels: a 16-byte header holding the device error
+// word (set when a bounded wait in the kernel gives up; the reduced outputs are then NaN),
+// followed by one row of double partials per block.
+constexpr size_t kWsHeader = 16;
+
 }  // namespace
 
 extern "C" {
@@ -80,7 +85,7 @@ size_t dfsnn_glmulti_backward_workspace_size(int T, long long N, int full_histor
     const int b1 = dfsnn::glmulti_bwd_blocks(T, N, full_history != 0, true);
     const int b2 = dfsnn::glmulti_bwd_blocks(T, N, full_history != 0, false);
     const int b = b1 > b2 ? b1 : b2;
-    return (size_t)b * (size_t)dfsnn::glmulti_part_stride(T) * sizeof(double);
+    return kWsHeader + (size_t)b * (size_t)dfsnn::glmulti_part_stride(T) * sizeof(double);
 }
 
 int dfsnn_glmulti_backward(const float* grad_spike, const float* x, const float* v0,
@@ -97,13 +102,16 @@ int dfsnn_glmulti_backward(const float* grad_spike, const float* x, const float*
     const bool p2 = tau_is_pow2(tau);
     const size_t stride = (size_t)dfsnn::glmulti_part_stride(T) * sizeof(double);
     long long nb = dfsnn::glmulti_bwd_blocks(T, N, full_history != 0, p2);
-    const long long cap = (long long)(workspace_bytes / stride);
+    const long long cap =
+        workspace_bytes > kWsHeader ? (long long)((workspace_bytes - kWsHeader) / stride) : 0;
     if (cap < 1) return DFSNN_ERR_WORKSPACE;
     if (nb > cap) nb = cap;
+    char* ws = static_cast<char*>(workspace);
     return cuda_status(dfsnn::glmulti_backward_launch(
         grad_spike, x, v0, scale, weights, grad_x, grad_v0, grad_scale, grad_weights, T, N, tau,
-        threshold, surrogate_scale, full_history != 0, p2, static_cast<double*>(workspace),
-        (int)nb, (cudaStream_t)stream));
+        threshold, surrogate_scale, full_history != 0, p2,
+        reinterpret_cast<double*>(ws + kWsHeader), reinterpret_cast<unsigned int*>(ws), (int)nb,
+        (cudaStream_t)stream));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -125,7 +133,7 @@ size_t dfsnn_aligned_backward_workspace_size(int T, long long N) {
     const int b1 = dfsnn::aligned_bwd_blocks(T, N, true);
     const int b2 = dfsnn::aligned_bwd_blocks(T, N, false);
     const int b = b1 > b2 ? b1 : b2;
-    return (size_t)b * (size_t)dfsnn::aligned_part_stride(T) * sizeof(double);
+    return kWsHeader + (size_t)b * (size_t)dfsnn::aligned_part_stride(T) * sizeof(double);
 }
 
 int dfsnn_aligned_backward(const float* grad_spike, const float* x, const float* v0,
@@ -142,13 +150,15 @@ int dfsnn_aligned_backward(const float* grad_spike, const float* x, const float*
     const bool p2 = tau_is_pow2(tau);
     const size_t stride = (size_t)dfsnn::aligned_part_stride(T) * sizeof(double);
     long long nb = dfsnn::aligned_bwd_blocks(T, N, p2);
-    const long long cap = (long long)(workspace_bytes / stride);
+    const long long cap =
+        workspace_bytes > kWsHeader ? (long long)((workspace_bytes - kWsHeader) / stride) : 0;
     if (cap < 1) return DFSNN_ERR_WORKSPACE;
     if (nb > cap) nb = cap;
+    char* ws = static_cast<char*>(workspace);
     return cuda_status(dfsnn::aligned_backward_launch(
         grad_spike, x, v0, a, weights, grad_x, grad_v0, grad_a, grad_weights, T, N, tau,
-        threshold, surrogate_scale, rho, p2, static_cast<double*>(workspace), (int)nb,
-        (cudaStream_t)stream));
+        threshold, surrogate_scale, rho, p2, reinterpret_cast<double*>(ws + kWsHeader),
+        reinterpret_cast<unsigned int*>(ws), (int)nb, (cudaStream_t)stream));
 }
 
 // ---------------------------------------------------------------------------------------

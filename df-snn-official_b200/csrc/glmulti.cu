@@ -5,12 +5,21 @@
 //   backward = lif_fde_glmulti_backward_kernel (:1845-1875, truncated history) or
 //              lif_fde_glmulti_full_backward_kernel (:1877-1913, full history adjoint),
 //              followed by grad_scale = sum(grad_pre*drift) and grad_W = -grad_pre@v_hist^T.
-// Design (B200): the forward writes only the spikes (8 B per neuron-step instead of the
-// reference's 20 B: spike, v_pre, v_hist, drift).  The backward re-reads x and recomputes
-// the trajectory in registers (T <= 32) or shared memory (T <= 256), runs the reverse
-// sweep, and reduces grad_scale / grad_W inside the same persistent kernel, so neither
-// grad_pre nor v_hist nor drift ever reaches HBM.
+// Design (B200):
+//   * the forward writes only the spikes (8 B per neuron-step; the reference writes
+//     spike, v_pre, v_hist and drift, 20 B);
+//   * the backward is one persistent kernel per call: x and grad_spike tiles of 256
+//     neurons are staged in shared memory by double-buffered cp.async.bulk copies
+//     (mbarrier transaction counts), the trajectory is recomputed in registers, the
+//     reverse sweep writes grad_x, and grad_scale / grad_W are reduced from shared memory
+//     in the same kernel -- grad_pre, v_hist and drift never reach HBM;
+//   * the reference builds W as a Toeplitz matrix W[t,i] = c~[t-i]/c~[0] and a constant
+//     scale; each block detects that structure and then keeps the T-1 distinct weights and
+//     the scale in registers, so the history FMAs read no memory (general W falls back to
+//     shared-memory weights; results are bit-identical either way).
+#include "bulk_pipe.cuh"
 #include "kernels.h"
+#include "pack2.cuh"
 #include "param_reduce.cuh"
 
 namespace dfsnn {
@@ -25,6 +34,7 @@ struct GlmArgs {
     float* gx;            // [T, N] (backward)
     float* gv0;           // [N]    (backward)
     double* part;         // [gridDim.x, TB + TB*TB] (backward)
+    unsigned int* err;    // error word (backward)
     int T;
     long long N;
     float tau, inv_tau, th, sg;
@@ -33,17 +43,17 @@ struct GlmArgs {
 // ------------------------------------------------------------------------------------
 // forward, T <= TB <= 32: history in registers
 // ------------------------------------------------------------------------------------
-template <int TB, bool TP2>
-__global__ void __launch_bounds__(256) glm_fwd_reg(GlmArgs a) {
-    __shared__ float sW[TB * TB];
-    __shared__ float sScale[TB];
+template <int TB, bool TP2, bool FAST>
+__device__ __forceinline__ void glm_fwd_body(const GlmArgs& a, const float* sW,
+                                             const float* sScale, long long n) {
     const int T = a.T;
-    for (int e = threadIdx.x; e < T * T; e += blockDim.x) sW[(e / T) * TB + e % T] = a.W[e];
-    for (int e = threadIdx.x; e < T; e += blockDim.x) sScale[e] = a.scale[e];
-    __syncthreads();
-    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (n >= a.N) return;
     const long long N = a.N;
+    float wr[TB];
+    float sc = sScale[0];
+    if constexpr (FAST) {
+#pragma unroll
+        for (int d = 1; d < TB; ++d) wr[d] = sW[d * TB];
+    }
     float xr[TB];
 #pragma unroll
     for (int t = 0; t < TB; ++t)
@@ -56,12 +66,82 @@ __global__ void __launch_bounds__(256) glm_fwd_reg(GlmArgs a) {
             const float d = div_tau<TP2>(__fsub_rn(xr[t], v), a.tau, a.inv_tau);
             float hist = 0.0f;
 #pragma unroll
-            for (int i = 0; i < t; ++i) hist = __fmaf_rn(sW[t * TB + i], vh[i], hist);
-            const float p = __fmaf_rn(sScale[t], d, -hist);
+            for (int i = 0; i < t; ++i) hist = __fmaf_rn(wgt<TB, FAST>(sW, wr, t, i), vh[i], hist);
+            const float p = __fmaf_rn(FAST ? sc : sScale[t], d, -hist);
             const float s = (p >= a.th) ? 1.0f : 0.0f;
             v = __fsub_rn(p, s * a.th);
             vh[t] = v;
             st_stream(a.spike + t * N + n, s);
+        }
+    }
+}
+
+template <int TB, bool TP2>
+__global__ void __launch_bounds__(256) glm_fwd_reg(GlmArgs a) {
+    __shared__ float sW[TB * TB];
+    __shared__ float sScale[TB];
+    const int T = a.T;
+    for (int e = threadIdx.x; e < TB * TB; e += blockDim.x) {
+        const int t = e / TB, i = e % TB;
+        sW[e] = (t < T && i < T) ? a.W[t * T + i] : 0.0f;
+    }
+    for (int e = threadIdx.x; e < TB; e += blockDim.x) sScale[e] = e < T ? a.scale[e] : 0.0f;
+    const bool fast = block_toeplitz(a.W, a.scale, T);   // includes a block barrier
+    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= a.N) return;
+    if (fast) glm_fwd_body<TB, TP2, true>(a, sW, sScale, n);
+    else glm_fwd_body<TB, TP2, false>(a, sW, sScale, n);
+}
+
+// ------------------------------------------------------------------------------------
+// forward, T <= TB <= 16, two neurons per thread: with the Toeplitz structure the history
+// of both neurons advances with one packed FFMA2 per term (accumulated negated, so that
+// p = fma(scale, d, -hist) is a single FFMA2); a general W runs the scalar body per neuron.
+// Used when N is even and x / v0 / spike are 8-byte aligned.
+// ------------------------------------------------------------------------------------
+template <int TB, bool TP2>
+__global__ void __launch_bounds__(256) glm_fwd_x2(GlmArgs a) {
+    __shared__ float sW[TB * TB];
+    __shared__ float sScale[TB];
+    const int T = a.T;
+    for (int e = threadIdx.x; e < TB * TB; e += blockDim.x) {
+        const int t = e / TB, i = e % TB;
+        sW[e] = (t < T && i < T) ? a.W[t * T + i] : 0.0f;
+    }
+    for (int e = threadIdx.x; e < TB; e += blockDim.x) sScale[e] = e < T ? a.scale[e] : 0.0f;
+    const bool fast = block_toeplitz(a.W, a.scale, T);
+    const long long n = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
+    if (n >= a.N) return;
+    if (!fast) {
+        glm_fwd_body<TB, TP2, false>(a, sW, sScale, n);
+        glm_fwd_body<TB, TP2, false>(a, sW, sScale, n + 1);
+        return;
+    }
+    const long long N = a.N;
+    float2 nw[TB];
+#pragma unroll
+    for (int d = 0; d < TB; ++d) nw[d] = f2(d > 0 ? -sW[d * TB] : 0.0f);
+    const float2 sc2 = f2(sScale[0]);
+    const float2 inv2 = f2(a.inv_tau);
+    const float2 mth = f2(-a.th);
+    float2 xr[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t)
+        if (t < T) xr[t] = ld2_stream(a.x + t * N + n);
+    float2 v = *reinterpret_cast<const float2*>(a.v0 + n);
+    float2 vh[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) {
+        if (t < T) {
+            const float2 d = div_tau2<TP2>(sub2(xr[t], v), a.tau, inv2);
+            float2 hn = f2(-0.0f);                                  // -hist
+#pragma unroll
+            for (int i = 0; i < t; ++i) hn = fma2(nw[t - i], vh[i], hn);
+            const float2 p = fma2(sc2, d, hn);                       // scale*d - hist
+            const float2 s = fire2(p, a.th);
+            v = fma2(s, mth, p);
+            vh[t] = v;
+            st2_stream(a.spike + t * N + n, s);
         }
     }
 }
@@ -96,16 +176,100 @@ __global__ void __launch_bounds__(128) glm_fwd_smem(GlmArgs a) {
 }
 
 // ------------------------------------------------------------------------------------
-// backward, T <= TB <= 32: persistent, trajectory in registers, fused parameter grads
+// backward, T <= TB <= 32: persistent; tiles staged in shared memory (bulk copies when
+// BULK, else per-thread loads); trajectory in registers; fused parameter grads.
+// Shared layout per stage: X [TB][256] (x_t, then overwritten by drift d_t) and
+// G [TB][256] (grad_spike_t, then overwritten by grad_pre_t); plus V [TB][256] (v_t).
 // ------------------------------------------------------------------------------------
-template <int TB, bool FULL, bool TP2>
-__global__ void __launch_bounds__(256) glm_bwd_reg(GlmArgs a) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    float* sG = reinterpret_cast<float*>(smem_raw);
-    float* sV = sG + TB * kLdn;
-    float* sD = sV + TB * kLdn;
+template <int TB, bool FULL, bool TP2, bool FAST>
+__device__ __forceinline__ void glm_bwd_tile(const GlmArgs& a, const float* sW, const float* sScale,
+                                             const float (&wr)[TB], float sc, float* X, float* G,
+                                             float* V, long long n0, int tid) {
+    const int T = a.T;
+    const long long N = a.N;
+    const long long n = n0 + tid;
+    const bool live = n < N;
+    // forward recompute (bit-identical to the forward kernel)
+    float v = live ? a.v0[n] : 0.0f;
+    float vh[TB], sur[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) {
+        float d = 0.0f;
+        sur[t] = 0.0f;
+        if (t < T) {
+            d = div_tau<TP2>(__fsub_rn(X[t * kTile + tid], v), a.tau, a.inv_tau);
+            float hist = 0.0f;
+#pragma unroll
+            for (int i = 0; i < t; ++i) hist = __fmaf_rn(wgt<TB, FAST>(sW, wr, t, i), vh[i], hist);
+            const float p = __fmaf_rn(FAST ? sc : sScale[t], d, -hist);
+            const float s = (p >= a.th) ? 1.0f : 0.0f;
+            v = __fsub_rn(p, s * a.th);
+            sur[t] = surrogate_fma(__fsub_rn(p, a.th), a.sg);
+        } else {
+            v = 0.0f;
+        }
+        if (!live) { v = 0.0f; d = 0.0f; }
+        vh[t] = v;
+        V[t * kTile + tid] = v;
+        X[t * kTile + tid] = d;
+    }
+    // reverse sweep
+    if constexpr (FULL) {
+        float A[TB];
+#pragma unroll
+        for (int t = 0; t < TB; ++t) A[t] = 0.0f;
+        float ginit = 0.0f;
+#pragma unroll
+        for (int t = TB - 1; t >= 0; --t) {
+            float gp = 0.0f;
+            if (t < T) {
+                gp = __fmaf_rn(G[t * kTile + tid], sur[t], A[t]);
+                const float gd = __fmul_rn(gp, FAST ? sc : sScale[t]);
+                if (live) st_stream(a.gx + t * N + n, div_tau<TP2>(gd, a.tau, a.inv_tau));
+                const float prev = div_tau<TP2>(-gd, a.tau, a.inv_tau);
+                if (t == 0) ginit = __fadd_rn(ginit, prev);
+                else A[t - 1] = __fadd_rn(A[t - 1], prev);
+#pragma unroll
+                for (int i = 0; i < t; ++i) A[i] = __fmaf_rn(-wgt<TB, FAST>(sW, wr, t, i), gp, A[i]);
+            }
+            G[t * kTile + tid] = live ? gp : 0.0f;
+        }
+        if (live) a.gv0[n] = ginit;
+    } else {
+        float gvn = 0.0f;
+#pragma unroll
+        for (int t = TB - 1; t >= 0; --t) {
+            float gp = 0.0f;
+            if (t < T) {
+                const float s_t = FAST ? sc : sScale[t];
+                gp = __fmaf_rn(G[t * kTile + tid], sur[t], gvn);
+                if (live) st_stream(a.gx + t * N + n, div_tau<TP2>(__fmul_rn(gp, s_t), a.tau, a.inv_tau));
+                gvn = div_tau<TP2>(__fmul_rn(-gp, s_t), a.tau, a.inv_tau);
+            }
+            G[t * kTile + tid] = live ? gp : 0.0f;
+        }
+        if (live) a.gv0[n] = gvn;
+    }
+}
+
+template <int TB>
+struct GlmBwdSmem {
+    static constexpr size_t kStageFloats = size_t(2) * TB * kTile;      // X and G
+    static constexpr size_t kBytes = sizeof(float) * (2 * kStageFloats + size_t(TB) * kTile);
+    static_assert(size_t(kTile) * 20 * sizeof(double) <= kBytes,
+                  "reduction scratch must fit in the dynamic shared memory");
+};
+
+template <int TB, bool FULL, bool TP2, bool BULK>
+__global__ void __launch_bounds__(256) glm_bwd(GlmArgs a) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    float* base = reinterpret_cast<float*>(smem_raw);
+    float* stageX[2] = {base, base + GlmBwdSmem<TB>::kStageFloats};
+    float* stageG[2] = {base + TB * kTile, base + GlmBwdSmem<TB>::kStageFloats + TB * kTile};
+    float* V = base + 2 * GlmBwdSmem<TB>::kStageFloats;
     __shared__ float sW[TB * TB];
     __shared__ float sScale[TB];
+    __shared__ __align__(8) uint64_t bars[2];
     const int T = a.T;
     const long long N = a.N;
     const int tid = threadIdx.x;
@@ -114,98 +278,77 @@ __global__ void __launch_bounds__(256) glm_bwd_reg(GlmArgs a) {
         sW[e] = (t < T && i < T) ? a.W[t * T + i] : 0.0f;
     }
     for (int e = tid; e < TB; e += blockDim.x) sScale[e] = e < T ? a.scale[e] : 0.0f;
-    TileAccumulator<TB, true> acc;
-    acc.init(tid);
-    const long long ntiles = (a.N + kTile - 1) / kTile;
-    __syncthreads();
-    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const long long n = tile * kTile + tid;
-        const bool live = n < N;
-        float xr[TB], gs[TB];
-#pragma unroll
-        for (int t = 0; t < TB; ++t) {
-            xr[t] = (live && t < T) ? ld_stream(a.x + t * N + n) : 0.0f;
-            gs[t] = (live && t < T) ? ld_stream(a.gS + t * N + n) : 0.0f;
-        }
-        // forward recompute (bit-identical to the forward kernel)
-        float v = live ? a.v0[n] : 0.0f;
-        float vh[TB], sur[TB];
-#pragma unroll
-        for (int t = 0; t < TB; ++t) {
-            float d = 0.0f;
-            if (t < T) {
-                d = div_tau<TP2>(__fsub_rn(xr[t], v), a.tau, a.inv_tau);
-                float hist = 0.0f;
-#pragma unroll
-                for (int i = 0; i < t; ++i) hist = __fmaf_rn(sW[t * TB + i], vh[i], hist);
-                const float p = __fmaf_rn(sScale[t], d, -hist);
-                const float s = (p >= a.th) ? 1.0f : 0.0f;
-                v = __fsub_rn(p, s * a.th);
-                sur[t] = surrogate_fma(__fsub_rn(p, a.th), a.sg);
-            } else {
-                v = 0.0f;
-                sur[t] = 0.0f;
-            }
-            if (!live) { v = 0.0f; d = 0.0f; }
-            vh[t] = v;
-            sV[t * kLdn + tid] = v;
-            sD[t * kLdn + tid] = d;
-        }
-        // reverse sweep
-        if constexpr (FULL) {
-            float A[TB];
-#pragma unroll
-            for (int t = 0; t < TB; ++t) A[t] = 0.0f;
-            float ginit = 0.0f;
-#pragma unroll
-            for (int t = TB - 1; t >= 0; --t) {
-                float gp = 0.0f;
-                if (t < T) {
-                    gp = __fmaf_rn(gs[t], sur[t], A[t]);
-                    const float gd = __fmul_rn(gp, sScale[t]);
-                    if (live) st_stream(a.gx + t * N + n, div_tau<TP2>(gd, a.tau, a.inv_tau));
-                    const float prev = div_tau<TP2>(-gd, a.tau, a.inv_tau);
-                    if (t == 0) ginit = __fadd_rn(ginit, prev);
-                    else A[t - 1] = __fadd_rn(A[t - 1], prev);
-#pragma unroll
-                    for (int i = 0; i < t; ++i) A[i] = __fmaf_rn(-sW[t * TB + i], gp, A[i]);
-                }
-                if (!live) gp = 0.0f;
-                sG[t * kLdn + tid] = gp;
-            }
-            if (live) a.gv0[n] = ginit;
-        } else {
-            float gvn = 0.0f;
-#pragma unroll
-            for (int t = TB - 1; t >= 0; --t) {
-                float gp = 0.0f;
-                if (t < T) {
-                    gp = __fmaf_rn(gs[t], sur[t], gvn);
-                    if (live)
-                        st_stream(a.gx + t * N + n,
-                                  div_tau<TP2>(__fmul_rn(gp, sScale[t]), a.tau, a.inv_tau));
-                    gvn = div_tau<TP2>(__fmul_rn(-gp, sScale[t]), a.tau, a.inv_tau);
-                }
-                if (!live) gp = 0.0f;
-                sG[t * kLdn + tid] = gp;
-            }
-            if (live) a.gv0[n] = gvn;
-        }
-        __syncthreads();
-        acc.accumulate(sG, sV, sD);
-        __syncthreads();
+    BulkPipe<2> pipe;
+    pipe.bar = bars;
+    pipe.T = T;
+    pipe.N = N;
+    pipe.src[0] = a.x;
+    pipe.src[1] = a.gS;
+    for (int s = 0; s < 2; ++s) { pipe.stage[s][0] = stageX[s]; pipe.stage[s][1] = stageG[s]; }
+    if (BULK && tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
     }
-    acc.finish(reinterpret_cast<double*>(smem_raw), a.part + (size_t)blockIdx.x * ProdCfg<TB>::NOUT, tid);
+    const bool fast = block_toeplitz(a.W, a.scale, T);     // block barrier
+    float wr[TB];
+    const float sc = sScale[0];
+#pragma unroll
+    for (int d = 0; d < TB; ++d) wr[d] = (fast && d > 0) ? sW[d * TB] : 0.0f;
+    TileProduct<TB, true> prod;
+    prod.init(tid);
+    const long long ntiles = (N + kTile - 1) / kTile;
+    const long long first = blockIdx.x, stride = gridDim.x;
+    if (BULK && tid == 0) {
+        if (first < ntiles) pipe.issue(0, first);
+        if (first + stride < ntiles) pipe.issue(1, first + stride);
+    }
+    bool failed = false;
+    int j = 0;
+    for (long long tile = first; tile < ntiles; tile += stride, ++j) {
+        const int s = BULK ? (j & 1) : 0;
+        float* X = stageX[s];
+        float* G = stageG[s];
+        if constexpr (BULK) {
+            const bool ok = mbar_wait_bounded(&bars[s], (uint32_t)((j >> 1) & 1));
+            if (__syncthreads_or(!ok)) { failed = true; break; }
+        } else {
+            const long long n = tile * kTile + tid;
+            for (int t = 0; t < T; ++t) {
+                X[t * kTile + tid] = n < N ? ld_stream(a.x + t * N + n) : 0.0f;
+                G[t * kTile + tid] = n < N ? ld_stream(a.gS + t * N + n) : 0.0f;
+            }
+        }
+        if (fast) glm_bwd_tile<TB, FULL, TP2, true>(a, sW, sScale, wr, sc, X, G, V, tile * kTile, tid);
+        else glm_bwd_tile<TB, FULL, TP2, false>(a, sW, sScale, wr, sc, X, G, V, tile * kTile, tid);
+        __syncthreads();
+        prod.accumulate(G, V, X);
+        __syncthreads();
+        if (BULK && tid == 0 && tile + 2 * stride < ntiles) pipe.issue(s, tile + 2 * stride);
+    }
+    if (failed) {
+        if (tid == 0) {
+            atomicOr(a.err, 1u);
+            // let copies still in flight land before the block exits (bounded waits)
+            mbar_wait_bounded(&bars[j & 1], (uint32_t)((j >> 1) & 1));
+            if (first + (long long)(j + 1) * stride < ntiles)
+                mbar_wait_bounded(&bars[(j + 1) & 1], (uint32_t)(((j + 1) >> 1) & 1));
+        }
+        return;
+    }
+    prod.finish(reinterpret_cast<double*>(smem_raw), a.part + (size_t)blockIdx.x * ProdCfg<TB>::NOUT, tid);
 }
 
 // ------------------------------------------------------------------------------------
 // sum the per-block partials in a fixed order: gs (T) and gW (T x T, negated)
 // ------------------------------------------------------------------------------------
 __global__ void param_finalize(const double* part, int nblocks, int TB, int T, float* gscale,
-                               float* gW, int lower_only) {
+                               float* gW, int lower_only, const unsigned int* err) {
     const int nout = TB + TB * TB;
-    const int o = blockIdx.x * blockDim.x + threadIdx.x;
-    if (o >= T + T * T) return;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= T + T * T) return;
+    const int o = warp;
     int src;
     if (o < T) src = o;
     else {
@@ -213,13 +356,28 @@ __global__ void param_finalize(const double* part, int nblocks, int TB, int T, f
         src = TB + t * TB + i;
     }
     double s = 0.0;
-    for (int b = 0; b < nblocks; ++b) s += part[(size_t)b * nout + src];
+    for (int b = lane; b < nblocks; b += 32) s += part[(size_t)b * nout + src];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane != 0) return;
+    const bool bad = err && *err;
+    const float nan = __int_as_float(0x7fc00000);
     if (o < T) {
-        if (gscale) gscale[o] = (float)s;
+        if (gscale) gscale[o] = bad ? nan : (float)s;
     } else if (gW) {
         const int t = (o - T) / T, i = (o - T) % T;
-        gW[o - T] = (lower_only && i >= t) ? 0.0f : (float)(-s);
+        gW[o - T] = bad ? nan : ((lower_only && i >= t) ? 0.0f : (float)(-s));
     }
+}
+
+cudaError_t launch_param_finalize(const double* part, int nblocks, int TB, int T, float* gscale,
+                                  float* gW, int lower_only, const unsigned int* err,
+                                  cudaStream_t st) {
+    const int nout = T + T * T;
+    const int threads = 256;
+    const int blocks = (nout * 32 + threads - 1) / threads;
+    param_finalize<<<blocks, threads, 0, st>>>(part, nblocks, TB, T, gscale, gW, lower_only, err);
+    return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------------------------
@@ -229,36 +387,25 @@ namespace {
 
 int tb_bucket(int T) { return T <= 8 ? 8 : (T <= 16 ? 16 : 32); }
 
-template <int TB, bool FULL, bool TP2>
-size_t bwd_reg_smem() {
-    const size_t stage = ProdCfg<TB>::SMEM_BYTES;
-    const size_t red = size_t(kTile) * 20 * sizeof(double);
-    return stage > red ? stage : red;
-}
-
-template <int TB, bool FULL, bool TP2>
-cudaError_t launch_bwd_reg(const GlmArgs& a, int grid, cudaStream_t st) {
-    const size_t smem = bwd_reg_smem<TB, FULL, TP2>();
-    auto k = glm_bwd_reg<TB, FULL, TP2>;
+template <int TB, bool FULL, bool TP2, bool BULK>
+cudaError_t launch_bwd_t(const GlmArgs& a, int grid, cudaStream_t st) {
+    const size_t smem = GlmBwdSmem<TB>::kBytes;
+    auto k = glm_bwd<TB, FULL, TP2, BULK>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     k<<<grid, kTile, smem, st>>>(a);
     return cudaGetLastError();
 }
 
-template <int TB, bool TP2>
-int bwd_reg_grid_t(long long N, bool full) {
+template <int TB>
+int bwd_grid_t(long long N) {
     int dev = 0, sms = 0, per = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const size_t smem = bwd_reg_smem<TB, true, TP2>();
-    if (full) {
-        cudaFuncSetAttribute(glm_bwd_reg<TB, true, TP2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, glm_bwd_reg<TB, true, TP2>, kTile, smem);
-    } else {
-        cudaFuncSetAttribute(glm_bwd_reg<TB, false, TP2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, glm_bwd_reg<TB, false, TP2>, kTile, smem);
-    }
+    const size_t smem = GlmBwdSmem<TB>::kBytes;
+    auto k = glm_bwd<TB, true, false, true>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, kTile, smem);
     if (per < 1) per = 1;
     const long long ntiles = (N + kTile - 1) / kTile;
     long long g = (long long)sms * per;
@@ -268,11 +415,11 @@ int bwd_reg_grid_t(long long N, bool full) {
 
 }  // namespace
 
-int glmulti_bwd_blocks(int T, long long N, bool full, bool tau_pow2) {
+int glmulti_bwd_blocks(int T, long long N, bool, bool) {
     const int TB = tb_bucket(T);
-    if (TB == 8) return tau_pow2 ? bwd_reg_grid_t<8, true>(N, full) : bwd_reg_grid_t<8, false>(N, full);
-    if (TB == 16) return tau_pow2 ? bwd_reg_grid_t<16, true>(N, full) : bwd_reg_grid_t<16, false>(N, full);
-    return tau_pow2 ? bwd_reg_grid_t<32, true>(N, full) : bwd_reg_grid_t<32, false>(N, full);
+    if (TB == 8) return bwd_grid_t<8>(N);
+    if (TB == 16) return bwd_grid_t<16>(N);
+    return bwd_grid_t<32>(N);
 }
 
 int glmulti_part_stride(int T) {
@@ -287,6 +434,19 @@ cudaError_t glmulti_forward_launch(const float* x, const float* v0, const float*
     a.x = x; a.v0 = v0; a.scale = scale; a.W = W; a.spike = spike;
     a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau; a.th = th;
     if (N == 0) return cudaSuccess;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(v0) |
+                         reinterpret_cast<uintptr_t>(spike);
+    if (T <= 16 && (N % 2) == 0 && (al & 7u) == 0) {
+        const unsigned grid = (unsigned)((N / 2 + 255) / 256);
+        if (T <= 8) {
+            if (tau_pow2) glm_fwd_x2<8, true><<<grid, 256, 0, st>>>(a);
+            else glm_fwd_x2<8, false><<<grid, 256, 0, st>>>(a);
+        } else {
+            if (tau_pow2) glm_fwd_x2<16, true><<<grid, 256, 0, st>>>(a);
+            else glm_fwd_x2<16, false><<<grid, 256, 0, st>>>(a);
+        }
+        return cudaGetLastError();
+    }
     if (T <= 32) {
         const unsigned grid = (unsigned)((N + 255) / 256);
         const int TB = tb_bucket(T);
@@ -314,31 +474,41 @@ cudaError_t glmulti_forward_launch(const float* x, const float* v0, const float*
     return cudaGetLastError();
 }
 
+bool bulk_eligible(const void* p, const void* q, long long N) {
+    return (N % 4) == 0 && ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(q)) & 15u) == 0;
+}
+
 cudaError_t glmulti_backward_launch(const float* gS, const float* x, const float* v0,
                                     const float* scale, const float* W, float* gx, float* gv0,
                                     float* gscale, float* gW, int T, long long N, float tau,
                                     float th, float sg, bool full, bool tau_pow2, double* part,
-                                    int nblocks, cudaStream_t st) {
+                                    unsigned int* err, int nblocks, cudaStream_t st) {
     GlmArgs a{};
     a.x = x; a.v0 = v0; a.scale = scale; a.W = W; a.gS = gS; a.gx = gx; a.gv0 = gv0;
-    a.part = part; a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau; a.th = th; a.sg = sg;
-    cudaError_t e = cudaSuccess;
+    a.part = part; a.err = err; a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau;
+    a.th = th; a.sg = sg;
+    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(unsigned int), st);
+    if (e != cudaSuccess) return e;
+    const bool bulk = bulk_eligible(x, gS, N);
     const int TB = tb_bucket(T);
-#define DFSNN_BWD(TBV)                                                                       \
-    if (TB == TBV) {                                                                         \
-        if (full) e = tau_pow2 ? launch_bwd_reg<TBV, true, true>(a, nblocks, st)             \
-                               : launch_bwd_reg<TBV, true, false>(a, nblocks, st);           \
-        else e = tau_pow2 ? launch_bwd_reg<TBV, false, true>(a, nblocks, st)                 \
-                          : launch_bwd_reg<TBV, false, false>(a, nblocks, st);               \
+#define DFSNN_BWD(TBV)                                                                         \
+    if (TB == TBV) {                                                                           \
+        if (bulk) {                                                                            \
+            if (full) e = tau_pow2 ? launch_bwd_t<TBV, true, true, true>(a, nblocks, st)       \
+                                   : launch_bwd_t<TBV, true, false, true>(a, nblocks, st);     \
+            else e = tau_pow2 ? launch_bwd_t<TBV, false, true, true>(a, nblocks, st)           \
+                              : launch_bwd_t<TBV, false, false, true>(a, nblocks, st);         \
+        } else {                                                                               \
+            if (full) e = tau_pow2 ? launch_bwd_t<TBV, true, true, false>(a, nblocks, st)      \
+                                   : launch_bwd_t<TBV, true, false, false>(a, nblocks, st);    \
+            else e = tau_pow2 ? launch_bwd_t<TBV, false, true, false>(a, nblocks, st)          \
+                              : launch_bwd_t<TBV, false, false, false>(a, nblocks, st);        \
+        }                                                                                      \
     }
     DFSNN_BWD(8) DFSNN_BWD(16) DFSNN_BWD(32)
 #undef DFSNN_BWD
     if (e != cudaSuccess) return e;
-    if (gscale || gW) {
-        const int nout = T + T * T;
-        param_finalize<<<(nout + 127) / 128, 128, 0, st>>>(part, nblocks, TB, T, gscale, gW, 0);
-        e = cudaGetLastError();
-    }
+    if (gscale || gW) e = launch_param_finalize(part, nblocks, TB, T, gscale, gW, 0, err, st);
     return e;
 }
 

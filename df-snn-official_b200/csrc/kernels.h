@@ -19,9 +19,12 @@ cudaError_t glmulti_backward_launch(const float* gS, const float* x, const float
                                     const float* scale, const float* W, float* gx, float* gv0,
                                     float* gscale, float* gW, int T, long long N, float tau,
                                     float th, float sg, bool full, bool tau_pow2, double* part,
-                                    int nblocks, cudaStream_t st);
-__global__ void param_finalize(const double* part, int nblocks, int TB, int T, float* gscale,
-                               float* gW, int lower_only);
+                                    unsigned int* err, int nblocks, cudaStream_t st);
+cudaError_t launch_param_finalize(const double* part, int nblocks, int TB, int T, float* gscale,
+                                  float* gW, int lower_only, const unsigned int* err,
+                                  cudaStream_t st);
+// true when x/grad tiles can be staged with cp.async.bulk (16-byte rows)
+bool bulk_eligible(const void* p, const void* q, long long N);
 
 // aligned glmulti
 cudaError_t aligned_forward_launch(const float* x, const float* v0, const float* a,
@@ -32,8 +35,8 @@ int aligned_part_stride(int T);
 cudaError_t aligned_backward_launch(const float* g, const float* x, const float* v0,
                                     const float* a, const float* W, float* gx, float* gv0,
                                     float* ga, float* gW, int T, long long N, float tau, float th,
-                                    float sg, float rho, bool tau_pow2, double* part, int nblocks,
-                                    cudaStream_t st);
+                                    float sg, float rho, bool tau_pow2, double* part,
+                                    unsigned int* err, int nblocks, cudaStream_t st);
 
 // single-order schemes
 cudaError_t single_forward_launch(int scheme, const float* x, const float* v0, const float* w,

@@ -30,7 +30,44 @@ __device__ __forceinline__ float div_tau(float a, float tau, float inv_tau) {
     else return __fdiv_rn(a, tau);
 }
 
+// Block-wide check that W (row stride T) is Toeplitz on its strict lower triangle and that
+// scale is constant: W[t,i] == W[t-i,0] and scale[t] == scale[0], bitwise.  This is how the
+// reference builds every glmulti schedule (spikeDE_dis/neuron.py:1494-1514); kernels then
+// keep the T-1 distinct weights and the scale in registers.  Contains a block barrier.
+__device__ __forceinline__ bool block_toeplitz(const float* W, const float* scale, int T) {
+    int ok = 1;
+    for (int e = threadIdx.x; e < T * T; e += blockDim.x) {
+        const int t = e / T, i = e % T;
+        if (i < t && __float_as_uint(W[e]) != __float_as_uint(W[(t - i) * T])) ok = 0;
+    }
+    for (int t = threadIdx.x; t < T; t += blockDim.x)
+        if (__float_as_uint(scale[t]) != __float_as_uint(scale[0])) ok = 0;
+    return __syncthreads_and(ok) != 0;
+}
+
+// Weight of history term (t, i): registers wr[t-i] (Toeplitz) or shared sW[t*TB+i].
+template <int TB, bool FAST>
+__device__ __forceinline__ float wgt(const float* sW, const float (&wr)[TB], int t, int i) {
+    if constexpr (FAST) return wr[t - i];
+    else return sW[t * TB + i];
+}
+
 __device__ __forceinline__ float ld_stream(const float* p) { return __ldcs(p); }
 __device__ __forceinline__ void st_stream(float* p, float v) { __stcs(p, v); }
+
+// Grid for a grid-stride ("persistent") kernel: enough blocks to fill every SM at the
+// kernel's occupancy, never more than there are 256-neuron tiles.
+template <class K>
+inline unsigned persistent_grid(K kernel, int threads, size_t smem, long long N) {
+    int dev = 0, sms = 0, per = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, smem);
+    if (per < 1) per = 1;
+    const long long tiles = (N + threads - 1) / threads;
+    long long g = (long long)sms * per;
+    if (g > tiles) g = tiles;
+    return (unsigned)(g < 1 ? 1 : g);
+}
 
 }  // namespace dfsnn

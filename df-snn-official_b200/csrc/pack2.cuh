@@ -1,0 +1,55 @@
+// pack2.cuh -- two neurons per thread with Blackwell's packed fp32x2 arithmetic.
+//
+// sm_100 issues FFMA2/FADD2/FMUL2: one instruction applies the same IEEE fp32 operation,
+// rounded to nearest, to both halves of a float2.  Each half is therefore bit-identical to
+// the scalar operation the reference performs on that neuron.  Subtractions are written as
+// fma(b, -1, a) = round(a - b) and histories that enter with a minus sign are accumulated
+// negated (round-to-nearest is symmetric: round(-x) = -round(x)), so no separate negations
+// are issued.  Only the sign of an exact zero can differ from the scalar form.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace dfsnn {
+
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+// round(a - b) per half
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __ffma2_rn(b, f2(-1.0f), a); }
+
+// Kahan step on the term w*h (w, h per half) in the form used by the reference
+// (y = fma(w, h, -c); t = s + y; c = (t - s) - y; s = t), carrying cn = -c so that every
+// step is four packed instructions: y = fma(w,h,cn); t = s+y; d = round(s-t); cn = y+d.
+struct Kahan2 {
+    float2 s = make_float2(0.0f, 0.0f);
+    float2 cn = make_float2(-0.0f, -0.0f);
+    __device__ __forceinline__ void add(float2 w, float2 h) {
+        const float2 y = fma2(w, h, cn);
+        const float2 t = add2(s, y);
+        const float2 d = sub2(s, t);
+        cn = add2(y, d);
+        s = t;
+    }
+};
+
+// Per-half division by tau (IEEE) or product with 1/tau when tau is a power of two.
+template <bool TAU_POW2>
+__device__ __forceinline__ float2 div_tau2(float2 a, float tau, float2 inv_tau) {
+    if constexpr (TAU_POW2) return mul2(a, inv_tau);
+    else return make_float2(__fdiv_rn(a.x, tau), __fdiv_rn(a.y, tau));
+}
+
+__device__ __forceinline__ float2 ld2_stream(const float* p) {
+    return __ldcs(reinterpret_cast<const float2*>(p));
+}
+__device__ __forceinline__ void st2_stream(float* p, float2 v) {
+    __stcs(reinterpret_cast<float2*>(p), v);
+}
+
+// Spike of each half (p >= th) as 0/1 floats.
+__device__ __forceinline__ float2 fire2(float2 p, float th) {
+    return make_float2(p.x >= th ? 1.0f : 0.0f, p.y >= th ? 1.0f : 0.0f);
+}
+
+}  // namespace dfsnn

@@ -1,125 +1,145 @@
 // param_reduce.cuh -- block-level accumulation of the shared-parameter gradients
-//   gs[t]   = sum_n e[t,n]              (or sum_n g[t,n]*d[t,n])
-//   gW[t,i] = sum_n g[t,n] * v[i,n]     (all t, i < TB)
-// for the persistent glmulti / aligned backward kernels, replacing the reference's
+//   gs[t]   = sum_n g[t,n]*e[t,n]   (DIAG_PRODUCT)   or   sum_n e[t,n]
+//   gW[t,i] = sum_n g[t,n] * v[i,n]                 (all t, i < TB)
+// for the persistent glmulti / aligned backward kernels.  It replaces the reference's
 // torch.sum(grad_pre*drift) + torch.matmul(grad_pre, v_hist^T)
 // (fde_cupy_kernels_all.py:1999-2009) and aligned_scale + the ga@h^T GEMM
-// (aligned_glmulti.py:33-41, :141-144).  No atomics: each thread owns a 4x4 tile of the
-// TB x TB product (plus 4 gs entries on diagonal tiles) for a fixed slice of the 256
-// neurons of every tile; per-tile fp32 partials are folded into Kahan-compensated fp32
-// accumulators, and the block reduces its slices once at the end in double, in a fixed
-// order, writing one row of a [gridDim.x, TB + TB*TB] double partials array.
+// (aligned_glmulti.py:33-41, :141-144): the operands never leave shared memory.
+//
+// Operands are time-major [TB][256] tiles in shared memory.  Each thread owns a 4x4 block
+// of the TB x TB product for a fixed slice of the tile's neurons, read as float4 along the
+// neuron axis (lanes of a warp share the t-rows, so the g loads broadcast); diagonal blocks
+// also accumulate gs.  Per-tile fp32 partials are added to per-thread fp32 accumulators;
+// at the end the block reduces its slices in double, in a fixed order (deterministic, no
+// atomics), into one row [TB + TB*TB] of a per-block partials array.
 #pragma once
 #include "lif_common.cuh"
 
 namespace dfsnn {
 
-constexpr int kTile = 256;           // neurons per tile = threads per block
-constexpr int kLdn = kTile + 1;      // row stride of the time-major staging arrays
+constexpr int kTile = 256;   // neurons per tile = threads per block
 
 template <int TB>
 struct ProdCfg {
-    static constexpr int NTR = TB / 4;             // 4-row tiles along t (and along i)
-    static constexpr int NTILE = NTR * NTR;        // 4x4 output tiles
-    static constexpr int NSLICE = kTile / NTILE;   // neuron slices per tile
-    static constexpr int NPER = kTile / NSLICE;    // neurons per slice
-    static constexpr int NOUT = TB + TB * TB;      // gs then gW, row-major
-    static_assert(TB % 4 == 0 && NTILE <= kTile, "TB must be a multiple of 4, at most 32");
-    // staging arrays: g, v, d (or e), each [TB][kLdn] floats
-    static constexpr size_t SMEM_BYTES = size_t(3) * TB * kLdn * sizeof(float);
+    static constexpr int NTR = TB / 4;                  // 4-row blocks along t (and along i)
+    static constexpr int NSLICE = kTile / (NTR * NTR);  // neuron slices
+    static constexpr int NG = kTile / (4 * NSLICE);     // float4 neuron groups per slice
+    static constexpr int LANES_PER_SLICE = NTR;
+    static constexpr int SLICES_PER_WARP = 32 / NTR;
+    static constexpr int NOUT = TB + TB * TB;           // gs then gW, row-major
+    static_assert(TB % 4 == 0 && TB <= 32 && TB >= 8, "TB must be 8, 16 or 32");
 };
 
-// Kahan-compensated running sum of per-tile partials.
-struct KahanAcc {
-    float hi = 0.0f, lo = 0.0f;
-    __device__ __forceinline__ void add(float p) {
-        const float y = __fsub_rn(p, lo);
-        const float t = __fadd_rn(hi, y);
-        lo = __fsub_rn(__fsub_rn(t, hi), y);
-        hi = t;
-    }
-};
-
-// Per-thread accumulator of one 4x4 tile (+4 diagonal gs entries).
 template <int TB, bool DIAG_PRODUCT>
-struct TileAccumulator {
+struct TileProduct {
     using C = ProdCfg<TB>;
-    KahanAcc w[4][4];
-    KahanAcc s[4];
+    float acc[4][4];
+    float accs[4];
     int tr, tc, slice;
 
     __device__ __forceinline__ void init(int tid) {
-        const int tile = tid % C::NTILE;
-        slice = tid / C::NTILE;
-        tr = tile / C::NTR;
-        tc = tile % C::NTR;
+        const int lane = tid & 31, w = tid >> 5;
+        tc = lane % C::NTR;
+        tr = w % C::NTR;
+        slice = (w / C::NTR) * C::SLICES_PER_WARP + lane / C::NTR;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            accs[r] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[r][c] = 0.0f;
+        }
     }
 
-    // sG/sV/sE: time-major staging [TB][kLdn]; neurons of this tile are columns 0..255.
-    __device__ __forceinline__ void accumulate(const float* sG, const float* sV, const float* sE) {
-        float pw[4][4];
-        float ps[4];
+    // G, V, E: [TB][kTile] time-major tiles (rows t >= T and dead neurons hold zeros)
+    __device__ __forceinline__ void accumulate(const float* G, const float* V, const float* E) {
+        float pw[4][4], ps[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             ps[r] = 0.0f;
 #pragma unroll
             for (int c = 0; c < 4; ++c) pw[r][c] = 0.0f;
         }
-        const bool diag = (tr == tc);
-#pragma unroll 4
-        for (int j = 0; j < C::NPER; ++j) {
-            const int k = j * C::NSLICE + slice;
-            float g[4], v[4];
+        const bool diag = tr == tc;
+#pragma unroll 2
+        for (int jj = 0; jj < C::NG; ++jj) {
+            const int kb = 4 * (jj * C::NSLICE + slice);
+            float4 g[4], v[4];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) g[r] = sG[(4 * tr + r) * kLdn + k];
+            for (int r = 0; r < 4; ++r)
+                g[r] = *reinterpret_cast<const float4*>(G + (4 * tr + r) * kTile + kb);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) v[c] = sV[(4 * tc + c) * kLdn + k];
+            for (int c = 0; c < 4; ++c)
+                v[c] = *reinterpret_cast<const float4*>(V + (4 * tc + c) * kTile + kb);
 #pragma unroll
             for (int r = 0; r < 4; ++r)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) pw[r][c] = __fmaf_rn(g[r], v[c], pw[r][c]);
+                for (int c = 0; c < 4; ++c) {
+                    float p = pw[r][c];
+                    p = __fmaf_rn(g[r].x, v[c].x, p);
+                    p = __fmaf_rn(g[r].y, v[c].y, p);
+                    p = __fmaf_rn(g[r].z, v[c].z, p);
+                    p = __fmaf_rn(g[r].w, v[c].w, p);
+                    pw[r][c] = p;
+                }
             if (diag) {
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
-                    const float e = sE[(4 * tr + r) * kLdn + k];
-                    if constexpr (DIAG_PRODUCT) ps[r] = __fmaf_rn(g[r], e, ps[r]);
-                    else ps[r] = __fadd_rn(ps[r], e);
+                    const float4 e = *reinterpret_cast<const float4*>(E + (4 * tr + r) * kTile + kb);
+                    if constexpr (DIAG_PRODUCT) {
+                        float p = ps[r];
+                        p = __fmaf_rn(g[r].x, e.x, p);
+                        p = __fmaf_rn(g[r].y, e.y, p);
+                        p = __fmaf_rn(g[r].z, e.z, p);
+                        p = __fmaf_rn(g[r].w, e.w, p);
+                        ps[r] = p;
+                    } else {
+                        ps[r] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(ps[r], e.x), e.y), e.z), e.w);
+                    }
                 }
             }
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            if (diag) s[r].add(ps[r]);
+            accs[r] = __fadd_rn(accs[r], ps[r]);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) w[r][c].add(pw[r][c]);
+            for (int c = 0; c < 4; ++c) acc[r][c] = __fadd_rn(acc[r][c], pw[r][c]);
         }
     }
 
-    // Reduce all slices of the block in double, fixed order; write this block's partial
-    // row (NOUT doubles) to part.  red must hold NSLICE*NTILE*20 doubles of shared memory.
+    static __device__ __forceinline__ int owner(int otr, int otc, int sl) {
+        const int w = (sl / C::SLICES_PER_WARP) * C::NTR + otr;
+        const int lane = (sl % C::SLICES_PER_WARP) * C::NTR + otc;
+        return w * 32 + lane;
+    }
+
+    // Reduce all slices of the block in double, fixed order; write the block's partial row.
+    // red: kTile*20 doubles of shared memory (callers reuse their staging buffers).
     __device__ __forceinline__ void finish(double* red, double* part, int tid) {
         double* mine = red + (size_t)tid * 20;
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-                mine[r * 4 + c] = (double)w[r][c].hi + (double)(-w[r][c].lo);
-            mine[16 + r] = (double)s[r].hi + (double)(-s[r].lo);
+            for (int c = 0; c < 4; ++c) mine[r * 4 + c] = (double)acc[r][c];
+            mine[16 + r] = (double)accs[r];
         }
         __syncthreads();
         for (int o = tid; o < C::NOUT; o += blockDim.x) {
-            int t, i;
-            bool is_s = o < TB;
-            if (is_s) { t = o; i = o; } else { t = (o - TB) / TB; i = (o - TB) % TB; }
-            const int otr = t / 4, otc = i / 4, r = t % 4, c = i % 4;
+            const bool is_s = o < TB;
+            const int t = is_s ? o : (o - TB) / TB;
+            const int i = is_s ? o : (o - TB) % TB;
+            const int otr = t / 4, otc = is_s ? otr : i / 4, r = t % 4, c = i % 4;
             double sum = 0.0;
-            for (int sl = 0; sl < C::NSLICE; ++sl) {
-                const int th = sl * C::NTILE + (is_s ? (otr * C::NTR + otr) : (otr * C::NTR + otc));
-                sum += red[(size_t)th * 20 + (is_s ? 16 + r : r * 4 + c)];
-            }
+            for (int sl = 0; sl < C::NSLICE; ++sl)
+                sum += red[(size_t)owner(otr, otc, sl) * 20 + (is_s ? 16 + r : r * 4 + c)];
             part[o] = sum;
         }
     }
 };
+
+// Sum per-block partial rows [nblocks][TB + TB*TB] in a fixed order: one warp per output,
+// lanes stride over blocks, then a fixed shuffle tree.  gs -> gscale[T], -gW -> gW[T,T]
+// (strictly lower triangle only when lower_only).  A set error word poisons the outputs.
+__global__ void param_finalize(const double* part, int nblocks, int TB, int T, float* gscale,
+                               float* gW, int lower_only, const unsigned int* err);
 
 }  // namespace dfsnn

@@ -50,12 +50,17 @@ __global__ void __launch_bounds__(256) single_fwd_reg(SingleArgs a) {
     const int T = a.T;
     for (int e = threadIdx.x; e <= T; e += blockDim.x) sw[e] = a.w[e];
     __syncthreads();
-    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (n >= a.N) return;
     const long long N = a.N;
     const float trap_factor = __fmaf_rn(1.5f, a.beta, 0.5f);     // :346
     const float pred_scale = __fdiv_rn(a.h_beta, a.gamma1);       // :528
-    const float w_cur = sw[T];
+    // history weight of lag L = k - i is w[T - L] (k >= 1, i < k); keep the table in
+    // registers indexed by the (compile-time) lag so the Kahan loop reads no memory
+    float wr[TB + 1];
+#pragma unroll
+    for (int L = 0; L <= TB; ++L) wr[L] = (L <= T) ? sw[T - L] : 0.0f;
+    const float w_cur = wr[0];
+    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
     float xr[TB];
 #pragma unroll
     for (int t = 0; t < TB; ++t)
@@ -70,7 +75,7 @@ __global__ void __launch_bounds__(256) single_fwd_reg(SingleArgs a) {
             float sum = 0.0f, c = 0.0f;                            // Kahan, :52-63
 #pragma unroll
             for (int i = 0; i < k; ++i) {
-                const float y = __fmaf_rn(sw[T - k + i], hv[i], -c);
+                const float y = __fmaf_rn(wr[k - i], hv[i], -c);
                 const float t = __fadd_rn(sum, y);
                 c = __fsub_rn(__fsub_rn(t, sum), y);
                 sum = t;
@@ -140,11 +145,11 @@ __global__ void __launch_bounds__(kLongBlock) single_fwd_smem(SingleArgs a) {
 // ------------------------------------------------------------------------------------
 // backward: truncated reverse sweep from the saved membrane and spike bits (any T)
 // ------------------------------------------------------------------------------------
-template <int SCHEME, bool TP2>
+template <int SCHEME, bool TP2, class WFn>
 __device__ __forceinline__ void single_bwd_step(const SingleArgs& a, int t, float vt, bool fire,
                                                 float gst, float gvt, float& gv, float trap_factor,
                                                 float pred_scale, float w_cur, float* gx_out,
-                                                const float* sw) {
+                                                WFn lag_weight) {
     gv = __fadd_rn(gv, gvt);
     const float p = __fmaf_rn(fire ? 1.0f : 0.0f, a.th, vt);          // v + spike*theta
     const float surr = surrogate_fma(__fsub_rn(p, a.th), a.sg);
@@ -167,8 +172,7 @@ __device__ __forceinline__ void single_bwd_step(const SingleArgs& a, int t, floa
         const float gd = __fmul_rn(a.h_beta, gv);
         *gx_out = div_tau<TP2>(gd, a.tau, a.inv_tau);
         gvm = div_tau<TP2>(-gd, a.tau, a.inv_tau);
-        const int T = a.T;
-        for (int i = 0; i < t; ++i) gvm = __fmaf_rn(-sw[T - t + i], gv, gvm);
+        for (int i = 0; i < t; ++i) gvm = __fmaf_rn(-lag_weight(t - i), gv, gvm);
     }
     gv = gvm;
 }
@@ -197,13 +201,19 @@ __global__ void __launch_bounds__(256) single_bwd_reg(SingleArgs a) {
         }
     }
     const uint32_t bits = a.bits_in[n];
+    float wr[(SCHEME == kGL1) ? TB + 1 : 1];
+    if constexpr (SCHEME == kGL1) {
+#pragma unroll
+        for (int L = 0; L <= TB; ++L) wr[L] = (L <= T) ? sw[T - L] : 0.0f;
+    }
     float gv = 0.0f;
 #pragma unroll
     for (int t = TB - 1; t >= 0; --t) {
         if (t < T) {
             float gxt;
             single_bwd_step<SCHEME, TP2>(a, t, vr[t], (bits >> t) & 1u, gsr[t], gvr[t], gv,
-                                         trap_factor, pred_scale, w_cur, &gxt, sw);
+                                         trap_factor, pred_scale, w_cur, &gxt,
+                                         [&](int L) { return wr[(SCHEME == kGL1) ? L : 0]; });
             st_stream(a.gx + t * N + n, gxt);
         }
     }
@@ -233,7 +243,7 @@ __global__ void __launch_bounds__(256) single_bwd_loop(SingleArgs a) {
         const float gvt = ld_stream(a.gV + t * N + n);
         float gxt;
         single_bwd_step<SCHEME, TP2>(a, t, vt, (bits >> (t & 31)) & 1u, gst, gvt, gv, trap_factor,
-                                     pred_scale, w_cur, &gxt, sw);
+                                     pred_scale, w_cur, &gxt, [&](int L) { return sw[T - L]; });
         st_stream(a.gx + t * N + n, gxt);
     }
     a.gv0[n] = gv;

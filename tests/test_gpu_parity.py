@@ -41,15 +41,21 @@ def rng_inputs(seed, T, N, kind="spiking"):
             v0.astype(np.float32))
 
 
-def glmulti_tables(T, seed=0):
-    """A schedule with the reference's structure (Toeplitz, strictly lower) and one with
-    arbitrary entries (the Function accepts any [T,T])."""
-    d = np.load(os.path.join(GOLDEN, "torch_tables.npz"))
-    key = f"glmulti_W_T{T}"
-    if key in d:
-        return d[f"glmulti_scale_T{T}"], d[key]
+def glmulti_tables(T, seed=0, kind="toeplitz"):
+    """The schedule as the reference builds it (Toeplitz, strictly lower, constant scale)
+    or, with kind="general", arbitrary entries (the Function accepts any [T,T])."""
+    if kind == "toeplitz":
+        d = np.load(os.path.join(GOLDEN, "torch_tables.npz"))
+        key = f"glmulti_W_T{T}"
+        if key in d:
+            return d[f"glmulti_scale_T{T}"], d[key]
+        from dfsnn_b200 import schedule
+        basis = schedule.glmulti_basis([0.3, 0.4, 0.5], T)
+        terms = schedule.build_glmulti_schedule(torch.tensor([0.5, 0.5, 0.7]),
+                                                torch.tensor([0.3, 0.4, 0.5]), basis, 0.1, T)
+        return terms["scale"].contiguous().numpy().copy(), terms["weights"].numpy().copy()
     g = np.random.default_rng(seed)
-    scale = np.full(T, 0.22385544, np.float32)
+    scale = (0.22385544 + 0.01 * g.standard_normal(T)).astype(np.float32)
     W = np.tril(g.standard_normal((T, T)).astype(np.float32) * 0.05, -1)
     return scale, W
 
@@ -72,9 +78,10 @@ GLM_CASES = [(T, N) for T in (1, 2, 3, 7, 8, 13, 16, 17, 31, 32) for N in (1, 25
 @pytest.mark.parametrize("T,N", GLM_CASES)
 @pytest.mark.parametrize("full", [False, True])
 @pytest.mark.parametrize("tau", [2.0, 1.7])
-def test_glmulti_vs_oracle(T, N, full, tau):
+@pytest.mark.parametrize("kind", ["toeplitz", "general"])
+def test_glmulti_vs_oracle(T, N, full, tau, kind):
     x, gS, _, v0 = rng_inputs(T * 1000 + N, T, N)
-    scale, W = glmulti_tables(T)
+    scale, W = glmulti_tables(T, seed=T, kind=kind)
     r = O.glmulti_step(x, v0, scale, W, gS, tau, TH, SG, full)
     xt, v0t, st, Wt = cuda(x), cuda(v0), cuda(scale), cuda(W)
     xt.requires_grad_(True)
@@ -94,7 +101,7 @@ def test_glmulti_vs_oracle(T, N, full, tau):
 def test_glmulti_forward_long_T_vs_oracle():
     for T in (33, 64, 100, 256):
         x, _, _, v0 = rng_inputs(T, T, 777)
-        scale, W = glmulti_tables(T, seed=T)
+        scale, W = glmulti_tables(T, seed=T, kind="general")
         r = O.glmulti_forward(x, v0, scale, W, 2.0, TH)
         with torch.no_grad():
             s = fde_kernels.LIFFDEGLMultiFunction.apply(cuda(x), cuda(v0), cuda(scale), cuda(W),
@@ -155,8 +162,10 @@ def test_glmulti_empty_and_direct_capi():
     # direct C-ABI call on torch-owned buffers
     xx, _, _, v0 = rng_inputs(3, T, 513)
     out = torch.empty(T, 513, device=DEV)
-    code = L.dfsnn_glmulti_forward(_capi.ptr(cuda(xx)), _capi.ptr(cuda(v0)), _capi.ptr(cuda(scale)),
-                                   _capi.ptr(cuda(W)), _capi.ptr(out), T, 513, 2.0, TH, None)
+    # keep every buffer referenced until the asynchronous launch has completed
+    bufs = [cuda(xx), cuda(v0), cuda(scale), cuda(W)]
+    code = L.dfsnn_glmulti_forward(*[_capi.ptr(b) for b in bufs], _capi.ptr(out), T, 513, 2.0,
+                                   TH, None)
     torch.cuda.synchronize()
     assert code == 0
     assert_bitwise(cpu(out), O.glmulti_forward(xx, v0, scale, W, 2.0, TH)["spike"], what="spike")
@@ -167,9 +176,10 @@ def test_glmulti_empty_and_direct_capi():
 # -------------------------------------------------------------------------------------
 @pytest.mark.parametrize("T,N", [(T, N) for T in (1, 2, 5, 8, 11, 16, 24, 32) for N in (1, 300, 2049)])
 @pytest.mark.parametrize("tau", [2.0, 1.3])
-def test_aligned_vs_oracle(T, N, tau):
+@pytest.mark.parametrize("kind", ["toeplitz", "general"])
+def test_aligned_vs_oracle(T, N, tau, kind):
     x, gS, _, v0 = rng_inputs(T * 31 + N, T, N)
-    scale, W = glmulti_tables(T)
+    scale, W = glmulti_tables(T, seed=T, kind=kind)
     a = (scale * 4.0).astype(np.float32)
     r = O.aligned_step(x, v0, a, W, gS, tau, TH, SG, 1.0)
     xt, v0t, at, Wt = (cuda(z).requires_grad_(True) for z in (x, v0, a, W))
