@@ -16,7 +16,6 @@ N > 1 runs one process per GPU under torchrun: every rank processes its own 8.4M
 all-reduce per step.  Rank 0 prints one JSON line.
 """
 import argparse
-import datetime
 import json
 import math
 import os
@@ -267,6 +266,7 @@ def run_native(args):
     import torch
     import torch.distributed as dist
     from dfsnn_b200 import profiling
+    from dfsnn_b200.distributed import allreduce_flat, init_process_group
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -276,7 +276,7 @@ def run_native(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        init_process_group("nccl", timeout_s=300, device=dev)
     K, W = args.steps, max(args.warmup, 3)
     neurons = math.prod(SHAPE)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
@@ -290,9 +290,8 @@ def run_native(args):
         for T, sch in COMBOS:
             _, _, pg = layer_step(layers[(T, sch)], x16[:T], gS16[:T], gV16[:T], sch != "glmulti")
             mass_grads += pg
-        if world > 1 and mass_grads:
-            flat = torch.cat([p.reshape(-1) for p in mass_grads])
-            dist.all_reduce(flat)
+        if world > 1:
+            allreduce_flat(mass_grads)       # the one gradient exchange per step
         return mass_grads
 
     for _ in range(W):
