@@ -35,21 +35,26 @@ struct AlnArgs {
     float tau, inv_tau, th, sg, rho;
 };
 
-// One forward step of aligned_forward (:11-14).  Returns v_t; h is the history sum.
-template <int TB, bool TP2, bool FAST>
-__device__ __forceinline__ float aligned_step(float x, float v, const float* sW, const float (&wr)[TB],
-                                              float a_t, const float (&vh)[TB], int t, float tau,
-                                              float inv_tau, float th, float& pred, bool& fire,
-                                              float& h) {
+// One forward step of aligned_forward (:11-14) given the step's history sum h (accumulated
+// in push form by the caller, in the reference's term order).  Returns v_t.
+template <bool TP2>
+__device__ __forceinline__ float aligned_step(float x, float v, float a_t, float h, float tau,
+                                              float inv_tau, float th, float& pred, bool& fire) {
     const float d = div_tau<TP2>(__fsub_rn(x, v), tau, inv_tau);
     pred = __fadd_rn(v, d);
     fire = pred >= th;
     const float spike = fire ? 1.0f : 0.0f;
-    h = 0.0f;
-#pragma unroll
-    for (int j = 0; j < t; ++j) h = __fadd_rn(h, __fmul_rn(wgt<TB, FAST>(sW, wr, t, j), vh[j]));
     const float f = __fsub_rn(d, div_tau<TP2>(__fmul_rn(spike, th), tau, inv_tau));
     return __fsub_rn(__fmul_rn(a_t, f), h);
+}
+
+// Fold v_t into the history sums of all later steps: hs[u] += round(W[u,t] * v_t) (the
+// reference's sequential h += w*hist order, no fused multiply-add).
+template <int TB, bool FAST>
+__device__ __forceinline__ void aligned_push(float (&hs)[TB], const float* sW, const float (&wr)[TB],
+                                             int t, float v) {
+#pragma unroll
+    for (int u = t + 1; u < TB; ++u) hs[u] = __fadd_rn(hs[u], __fmul_rn(wgt<TB, FAST>(sW, wr, u, t), v));
 }
 
 template <int TB, bool TP2, bool FAST>
@@ -65,15 +70,17 @@ __device__ __forceinline__ void aln_fwd_body(const AlnArgs& a, const float* sW, 
     for (int t = 0; t < TB; ++t)
         if (t < T) xr[t] = ld_stream(a.x + t * N + n);
     float v = a.v0[n];
-    float vh[TB];
+    float hs[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) hs[t] = 0.0f;
 #pragma unroll
     for (int t = 0; t < TB; ++t) {
         if (t < T) {
-            float pred, h;
+            float pred;
             bool fire;
-            v = aligned_step<TB, TP2, FAST>(xr[t], v, sW, wr, FAST ? sA[0] : sA[t], vh, t, a.tau,
-                                            a.inv_tau, a.th, pred, fire, h);
-            vh[t] = v;
+            v = aligned_step<TP2>(xr[t], v, FAST ? sA[0] : sA[t], hs[t], a.tau, a.inv_tau, a.th,
+                                  pred, fire);
+            aligned_push<TB, FAST>(hs, sW, wr, t, v);
             st_stream(a.spike + t * N + n, fire ? 1.0f : 0.0f);
         }
     }
@@ -129,19 +136,19 @@ __global__ void __launch_bounds__(256) aln_fwd_x2(AlnArgs a) {
     for (int t = 0; t < TB; ++t)
         if (t < T) xr[t] = ld2_stream(a.x + t * N + n);
     float2 v = *reinterpret_cast<const float2*>(a.v0 + n);
-    float2 vh[TB];
+    float2 hn[TB];                                                   // -h, push form
+#pragma unroll
+    for (int t = 0; t < TB; ++t) hn[t] = f2(-0.0f);
 #pragma unroll
     for (int t = 0; t < TB; ++t) {
         if (t < T) {
             const float2 d = div_tau2<TP2>(sub2(xr[t], v), a.tau, inv2);
             const float2 pred = add2(v, d);
             const float2 s = fire2(pred, a.th);
-            float2 hn = f2(-0.0f);                                   // -h
-#pragma unroll
-            for (int j = 0; j < t; ++j) hn = add2(hn, mul2(nw[t - j], vh[j]));
             const float2 f = add2(d, div_tau2<TP2>(mul2(s, mth), a.tau, inv2));   // d - s*th/tau
-            v = add2(mul2(a2, f), hn);                               // a*f - h
-            vh[t] = v;
+            v = add2(mul2(a2, f), hn[t]);                            // a*f - h
+#pragma unroll
+            for (int u = t + 1; u < TB; ++u) hn[u] = add2(hn[u], mul2(nw[u - t], v));
             st2_stream(a.spike + t * N + n, s);
         }
     }
@@ -153,20 +160,24 @@ template <int TB, bool TP2, bool FAST>
 __device__ __forceinline__ void aln_bwd_tile(const AlnArgs& a, const float* sW, const float* sA,
                                              const float (&wr)[TB], const float (&rw)[TB],
                                              float zc, float one_m, float* X, float* G, float* V,
-                                             long long n0, int tid) {
+                                             const float* V0, long long n0, int tid) {
     const int T = a.T;
     const long long N = a.N;
     const long long n = n0 + tid;
     const bool live = n < N;
-    float v = live ? a.v0[n] : 0.0f;
-    float vh[TB];
+    float v = live ? V0[tid] : 0.0f;
+    float hs[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) hs[t] = 0.0f;
 #pragma unroll
     for (int t = 0; t < TB; ++t) {
         if (t < T) {
-            float pred, h;
+            float pred;
             bool fire;
-            v = aligned_step<TB, TP2, FAST>(X[t * kTile + tid], v, sW, wr, FAST ? sA[0] : sA[t],
-                                            vh, t, a.tau, a.inv_tau, a.th, pred, fire, h);
+            const float h = hs[t];
+            v = aligned_step<TP2>(X[t * kTile + tid], v, FAST ? sA[0] : sA[t], h, a.tau, a.inv_tau,
+                                  a.th, pred, fire);
+            aligned_push<TB, FAST>(hs, sW, wr, t, v);
             const float z = __fmul_rn(zc, __fsub_rn(pred, a.th));
             const float den = __fmul_rn(2.0f, __fadd_rn(1.0f, __fmul_rn(z, z)));
             G[t * kTile + tid] = __fdiv_rn(__fmul_rn(G[t * kTile + tid], a.sg), den);   // q_t
@@ -175,7 +186,6 @@ __device__ __forceinline__ void aln_bwd_tile(const AlnArgs& a, const float* sW, 
             v = 0.0f;
         }
         if (!live) v = 0.0f;
-        vh[t] = v;
         V[t * kTile + tid] = v;
     }
     float A[TB];
@@ -207,7 +217,8 @@ __device__ __forceinline__ void aln_bwd_tile(const AlnArgs& a, const float* sW, 
 
 template <int TB>
 struct AlnBwdSmem {
-    static constexpr size_t kStageFloats = size_t(2) * TB * kTile;
+    // per stage: X [TB][256], G [TB][256], v0 row [256]; then V [TB][256]
+    static constexpr size_t kStageFloats = size_t(2) * TB * kTile + kTile;
     static constexpr size_t kBytes = sizeof(float) * (2 * kStageFloats + size_t(TB) * kTile);
     static_assert(size_t(kTile) * 20 * sizeof(double) <= kBytes, "reduction scratch must fit");
 };
@@ -215,10 +226,9 @@ struct AlnBwdSmem {
 template <int TB, bool TP2, bool BULK>
 __global__ void __launch_bounds__(256) aln_bwd(AlnArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
+    constexpr size_t kSF = AlnBwdSmem<TB>::kStageFloats;
     float* base = reinterpret_cast<float*>(smem_raw);
-    float* stageX[2] = {base, base + AlnBwdSmem<TB>::kStageFloats};
-    float* stageG[2] = {base + TB * kTile, base + AlnBwdSmem<TB>::kStageFloats + TB * kTile};
-    float* V = base + 2 * AlnBwdSmem<TB>::kStageFloats;
+    float* V = base + 2 * kSF;
     __shared__ float sW[TB * TB];
     __shared__ float sA[TB];
     __shared__ __align__(8) uint64_t bars[2];
@@ -236,7 +246,12 @@ __global__ void __launch_bounds__(256) aln_bwd(AlnArgs a) {
     pipe.N = N;
     pipe.src[0] = a.x;
     pipe.src[1] = a.g;
-    for (int s = 0; s < 2; ++s) { pipe.stage[s][0] = stageX[s]; pipe.stage[s][1] = stageG[s]; }
+    pipe.row_src = a.v0;
+    for (int s = 0; s < 2; ++s) {
+        pipe.stage[s][0] = base + s * kSF;
+        pipe.stage[s][1] = base + s * kSF + TB * kTile;
+        pipe.row_stage[s] = base + s * kSF + 2 * TB * kTile;
+    }
     if (BULK && tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
@@ -263,8 +278,9 @@ __global__ void __launch_bounds__(256) aln_bwd(AlnArgs a) {
     int j = 0;
     for (long long tile = first; tile < ntiles; tile += stride, ++j) {
         const int s = BULK ? (j & 1) : 0;
-        float* X = stageX[s];
-        float* G = stageG[s];
+        float* X = base + s * kSF;
+        float* G = X + TB * kTile;
+        float* V0 = G + TB * kTile;
         if constexpr (BULK) {
             const bool ok = mbar_wait_bounded(&bars[s], (uint32_t)((j >> 1) & 1));
             if (__syncthreads_or(!ok)) { failed = true; break; }
@@ -274,9 +290,10 @@ __global__ void __launch_bounds__(256) aln_bwd(AlnArgs a) {
                 X[t * kTile + tid] = n < N ? ld_stream(a.x + t * N + n) : 0.0f;
                 G[t * kTile + tid] = n < N ? ld_stream(a.g + t * N + n) : 0.0f;
             }
+            V0[tid] = n < N ? a.v0[n] : 0.0f;
         }
-        if (fast) aln_bwd_tile<TB, TP2, true>(a, sW, sA, wr, rw, zc, one_m, X, G, V, tile * kTile, tid);
-        else aln_bwd_tile<TB, TP2, false>(a, sW, sA, wr, rw, zc, one_m, X, G, V, tile * kTile, tid);
+        if (fast) aln_bwd_tile<TB, TP2, true>(a, sW, sA, wr, rw, zc, one_m, X, G, V, V0, tile * kTile, tid);
+        else aln_bwd_tile<TB, TP2, false>(a, sW, sA, wr, rw, zc, one_m, X, G, V, V0, tile * kTile, tid);
         __syncthreads();
         prod.accumulate(G, V, X);
         __syncthreads();
@@ -381,7 +398,7 @@ cudaError_t aligned_backward_launch(const float* g, const float* x, const float*
     a.rho = rho;
     cudaError_t e = cudaMemsetAsync(err, 0, sizeof(unsigned int), st);
     if (e != cudaSuccess) return e;
-    const bool bulk = bulk_eligible(x, g, N);
+    const bool bulk = bulk_eligible(x, g, v0, N);
     const int TB = tb_of(T);
 #define DFSNN_AB(TBV)                                                                          \
     if (TB == TBV) {                                                                           \

@@ -64,13 +64,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return false;
 }
 
-// Two-stage pipeline of NARR input arrays, each staged as [T][kTileN] floats per stage.
+// Two-stage pipeline of NARR input arrays (each staged as [T][kTileN] floats per stage)
+// plus one optional single-row array (e.g. the initial membrane v0[N], staged as [kTileN]).
 template <int NARR>
 struct BulkPipe {
     static constexpr int kTileN = 256;
     uint64_t* bar;              // [2] mbarriers in shared memory
     float* stage[2][NARR];      // stage buffers
+    float* row_stage[2];        // single-row stage buffers (used when row_src != nullptr)
     const float* src[NARR];     // [T, N] global arrays
+    const float* row_src;       // [N] global array or nullptr
     int T;
     long long N;
 
@@ -80,11 +83,12 @@ struct BulkPipe {
         const long long len = (N - n0) < kTileN ? (N - n0) : kTileN;
         const uint32_t row_bytes = (uint32_t)(len * sizeof(float));
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&bar[s], row_bytes * (uint32_t)T * NARR);
+        mbar_arrive_expect_tx(&bar[s], row_bytes * ((uint32_t)T * NARR + (row_src ? 1u : 0u)));
         for (int a = 0; a < NARR; ++a)
             for (int t = 0; t < T; ++t)
                 bulk_copy_g2s(stage[s][a] + t * kTileN, src[a] + (long long)t * N + n0, row_bytes,
                               &bar[s]);
+        if (row_src) bulk_copy_g2s(row_stage[s], row_src + n0, row_bytes, &bar[s]);
     }
 };
 

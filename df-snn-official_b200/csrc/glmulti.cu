@@ -59,18 +59,21 @@ __device__ __forceinline__ void glm_fwd_body(const GlmArgs& a, const float* sW,
     for (int t = 0; t < TB; ++t)
         if (t < T) xr[t] = ld_stream(a.x + t * N + n);
     float v = a.v0[n];
-    float vh[TB];
+    // "push" form of the history: hs[u] accumulates sum_{i<u} W[u,i] v_i in the reference's
+    // term order (i = 0, 1, ...), each v_i being folded into every later sum as soon as it
+    // is known; the sums of different steps are independent chains (ILP), bit-identical.
+    float hs[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) hs[t] = 0.0f;
 #pragma unroll
     for (int t = 0; t < TB; ++t) {
         if (t < T) {
             const float d = div_tau<TP2>(__fsub_rn(xr[t], v), a.tau, a.inv_tau);
-            float hist = 0.0f;
-#pragma unroll
-            for (int i = 0; i < t; ++i) hist = __fmaf_rn(wgt<TB, FAST>(sW, wr, t, i), vh[i], hist);
-            const float p = __fmaf_rn(FAST ? sc : sScale[t], d, -hist);
+            const float p = __fmaf_rn(FAST ? sc : sScale[t], d, -hs[t]);
             const float s = (p >= a.th) ? 1.0f : 0.0f;
             v = __fsub_rn(p, s * a.th);
-            vh[t] = v;
+#pragma unroll
+            for (int u = t + 1; u < TB; ++u) hs[u] = __fmaf_rn(wgt<TB, FAST>(sW, wr, u, t), v, hs[u]);
             st_stream(a.spike + t * N + n, s);
         }
     }
@@ -129,18 +132,18 @@ __global__ void __launch_bounds__(256) glm_fwd_x2(GlmArgs a) {
     for (int t = 0; t < TB; ++t)
         if (t < T) xr[t] = ld2_stream(a.x + t * N + n);
     float2 v = *reinterpret_cast<const float2*>(a.v0 + n);
-    float2 vh[TB];
+    float2 hn[TB];                                                  // -history, push form
+#pragma unroll
+    for (int t = 0; t < TB; ++t) hn[t] = f2(-0.0f);
 #pragma unroll
     for (int t = 0; t < TB; ++t) {
         if (t < T) {
             const float2 d = div_tau2<TP2>(sub2(xr[t], v), a.tau, inv2);
-            float2 hn = f2(-0.0f);                                  // -hist
-#pragma unroll
-            for (int i = 0; i < t; ++i) hn = fma2(nw[t - i], vh[i], hn);
-            const float2 p = fma2(sc2, d, hn);                       // scale*d - hist
+            const float2 p = fma2(sc2, d, hn[t]);                    // scale*d - hist
             const float2 s = fire2(p, a.th);
             v = fma2(s, mth, p);
-            vh[t] = v;
+#pragma unroll
+            for (int u = t + 1; u < TB; ++u) hn[u] = fma2(nw[u - t], v, hn[u]);
             st2_stream(a.spike + t * N + n, s);
         }
     }
@@ -184,32 +187,32 @@ __global__ void __launch_bounds__(128) glm_fwd_smem(GlmArgs a) {
 template <int TB, bool FULL, bool TP2, bool FAST>
 __device__ __forceinline__ void glm_bwd_tile(const GlmArgs& a, const float* sW, const float* sScale,
                                              const float (&wr)[TB], float sc, float* X, float* G,
-                                             float* V, long long n0, int tid) {
+                                             float* V, const float* V0, long long n0, int tid) {
     const int T = a.T;
     const long long N = a.N;
     const long long n = n0 + tid;
     const bool live = n < N;
-    // forward recompute (bit-identical to the forward kernel)
-    float v = live ? a.v0[n] : 0.0f;
-    float vh[TB], sur[TB];
+    // forward recompute (bit-identical to the forward kernel; history in push form)
+    float v = live ? V0[tid] : 0.0f;
+    float hs[TB], sur[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) hs[t] = 0.0f;
 #pragma unroll
     for (int t = 0; t < TB; ++t) {
         float d = 0.0f;
         sur[t] = 0.0f;
         if (t < T) {
             d = div_tau<TP2>(__fsub_rn(X[t * kTile + tid], v), a.tau, a.inv_tau);
-            float hist = 0.0f;
-#pragma unroll
-            for (int i = 0; i < t; ++i) hist = __fmaf_rn(wgt<TB, FAST>(sW, wr, t, i), vh[i], hist);
-            const float p = __fmaf_rn(FAST ? sc : sScale[t], d, -hist);
+            const float p = __fmaf_rn(FAST ? sc : sScale[t], d, -hs[t]);
             const float s = (p >= a.th) ? 1.0f : 0.0f;
             v = __fsub_rn(p, s * a.th);
             sur[t] = surrogate_fma(__fsub_rn(p, a.th), a.sg);
+#pragma unroll
+            for (int u = t + 1; u < TB; ++u) hs[u] = __fmaf_rn(wgt<TB, FAST>(sW, wr, u, t), v, hs[u]);
         } else {
             v = 0.0f;
         }
         if (!live) { v = 0.0f; d = 0.0f; }
-        vh[t] = v;
         V[t * kTile + tid] = v;
         X[t * kTile + tid] = d;
     }
@@ -254,7 +257,8 @@ __device__ __forceinline__ void glm_bwd_tile(const GlmArgs& a, const float* sW, 
 
 template <int TB>
 struct GlmBwdSmem {
-    static constexpr size_t kStageFloats = size_t(2) * TB * kTile;      // X and G
+    // per stage: X [TB][256], G [TB][256], v0 row [256]; then V [TB][256]
+    static constexpr size_t kStageFloats = size_t(2) * TB * kTile + kTile;
     static constexpr size_t kBytes = sizeof(float) * (2 * kStageFloats + size_t(TB) * kTile);
     static_assert(size_t(kTile) * 20 * sizeof(double) <= kBytes,
                   "reduction scratch must fit in the dynamic shared memory");
@@ -263,10 +267,9 @@ struct GlmBwdSmem {
 template <int TB, bool FULL, bool TP2, bool BULK>
 __global__ void __launch_bounds__(256) glm_bwd(GlmArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
+    constexpr size_t kSF = GlmBwdSmem<TB>::kStageFloats;
     float* base = reinterpret_cast<float*>(smem_raw);
-    float* stageX[2] = {base, base + GlmBwdSmem<TB>::kStageFloats};
-    float* stageG[2] = {base + TB * kTile, base + GlmBwdSmem<TB>::kStageFloats + TB * kTile};
-    float* V = base + 2 * GlmBwdSmem<TB>::kStageFloats;
+    float* V = base + 2 * kSF;
     __shared__ float sW[TB * TB];
     __shared__ float sScale[TB];
     __shared__ __align__(8) uint64_t bars[2];
@@ -284,7 +287,12 @@ __global__ void __launch_bounds__(256) glm_bwd(GlmArgs a) {
     pipe.N = N;
     pipe.src[0] = a.x;
     pipe.src[1] = a.gS;
-    for (int s = 0; s < 2; ++s) { pipe.stage[s][0] = stageX[s]; pipe.stage[s][1] = stageG[s]; }
+    pipe.row_src = a.v0;
+    for (int s = 0; s < 2; ++s) {
+        pipe.stage[s][0] = base + s * kSF;
+        pipe.stage[s][1] = base + s * kSF + TB * kTile;
+        pipe.row_stage[s] = base + s * kSF + 2 * TB * kTile;
+    }
     if (BULK && tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
@@ -307,8 +315,9 @@ __global__ void __launch_bounds__(256) glm_bwd(GlmArgs a) {
     int j = 0;
     for (long long tile = first; tile < ntiles; tile += stride, ++j) {
         const int s = BULK ? (j & 1) : 0;
-        float* X = stageX[s];
-        float* G = stageG[s];
+        float* X = base + s * kSF;
+        float* G = X + TB * kTile;
+        float* V0 = G + TB * kTile;
         if constexpr (BULK) {
             const bool ok = mbar_wait_bounded(&bars[s], (uint32_t)((j >> 1) & 1));
             if (__syncthreads_or(!ok)) { failed = true; break; }
@@ -318,9 +327,10 @@ __global__ void __launch_bounds__(256) glm_bwd(GlmArgs a) {
                 X[t * kTile + tid] = n < N ? ld_stream(a.x + t * N + n) : 0.0f;
                 G[t * kTile + tid] = n < N ? ld_stream(a.gS + t * N + n) : 0.0f;
             }
+            V0[tid] = n < N ? a.v0[n] : 0.0f;
         }
-        if (fast) glm_bwd_tile<TB, FULL, TP2, true>(a, sW, sScale, wr, sc, X, G, V, tile * kTile, tid);
-        else glm_bwd_tile<TB, FULL, TP2, false>(a, sW, sScale, wr, sc, X, G, V, tile * kTile, tid);
+        if (fast) glm_bwd_tile<TB, FULL, TP2, true>(a, sW, sScale, wr, sc, X, G, V, V0, tile * kTile, tid);
+        else glm_bwd_tile<TB, FULL, TP2, false>(a, sW, sScale, wr, sc, X, G, V, V0, tile * kTile, tid);
         __syncthreads();
         prod.accumulate(G, V, X);
         __syncthreads();
@@ -474,8 +484,9 @@ cudaError_t glmulti_forward_launch(const float* x, const float* v0, const float*
     return cudaGetLastError();
 }
 
-bool bulk_eligible(const void* p, const void* q, long long N) {
-    return (N % 4) == 0 && ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(q)) & 15u) == 0;
+bool bulk_eligible(const void* p, const void* q, const void* r, long long N) {
+    return (N % 4) == 0 && ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(q) |
+                             reinterpret_cast<uintptr_t>(r)) & 15u) == 0;
 }
 
 cudaError_t glmulti_backward_launch(const float* gS, const float* x, const float* v0,
@@ -489,7 +500,7 @@ cudaError_t glmulti_backward_launch(const float* gS, const float* x, const float
     a.th = th; a.sg = sg;
     cudaError_t e = cudaMemsetAsync(err, 0, sizeof(unsigned int), st);
     if (e != cudaSuccess) return e;
-    const bool bulk = bulk_eligible(x, gS, N);
+    const bool bulk = bulk_eligible(x, gS, v0, N);
     const int TB = tb_bucket(T);
 #define DFSNN_BWD(TBV)                                                                         \
     if (TB == TBV) {                                                                           \

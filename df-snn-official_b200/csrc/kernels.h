@@ -23,8 +23,8 @@ cudaError_t glmulti_backward_launch(const float* gS, const float* x, const float
 cudaError_t launch_param_finalize(const double* part, int nblocks, int TB, int T, float* gscale,
                                   float* gW, int lower_only, const unsigned int* err,
                                   cudaStream_t st);
-// true when x/grad tiles can be staged with cp.async.bulk (16-byte rows)
-bool bulk_eligible(const void* p, const void* q, long long N);
+// true when the x / grad / v0 tiles can be staged with cp.async.bulk (16-byte rows)
+bool bulk_eligible(const void* p, const void* q, const void* r, long long N);
 
 // aligned glmulti
 cudaError_t aligned_forward_launch(const float* x, const float* v0, const float* a,

@@ -14,6 +14,7 @@
 // atomics), into one row [TB + TB*TB] of a per-block partials array.
 #pragma once
 #include "lif_common.cuh"
+#include "pack2.cuh"
 
 namespace dfsnn {
 
@@ -50,14 +51,16 @@ struct TileProduct {
         }
     }
 
-    // G, V, E: [TB][kTile] time-major tiles (rows t >= T and dead neurons hold zeros)
+    // G, V, E: [TB][kTile] time-major tiles (rows t >= T and dead neurons hold zeros).
+    // Each float4 group of neurons is reduced as two packed lanes (FFMA2): this is a sum
+    // over neurons whose order is free (the reference's torch.sum / cuBLAS fix none either).
     __device__ __forceinline__ void accumulate(const float* G, const float* V, const float* E) {
-        float pw[4][4], ps[4];
+        float2 pw[4][4], ps[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            ps[r] = 0.0f;
+            ps[r] = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) pw[r][c] = 0.0f;
+            for (int c = 0; c < 4; ++c) pw[r][c] = make_float2(0.0f, 0.0f);
         }
         const bool diag = tr == tc;
 #pragma unroll 2
@@ -71,38 +74,34 @@ struct TileProduct {
             for (int c = 0; c < 4; ++c)
                 v[c] = *reinterpret_cast<const float4*>(V + (4 * tc + c) * kTile + kb);
 #pragma unroll
-            for (int r = 0; r < 4; ++r)
+            for (int r = 0; r < 4; ++r) {
+                const float2 g01 = make_float2(g[r].x, g[r].y), g23 = make_float2(g[r].z, g[r].w);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    float p = pw[r][c];
-                    p = __fmaf_rn(g[r].x, v[c].x, p);
-                    p = __fmaf_rn(g[r].y, v[c].y, p);
-                    p = __fmaf_rn(g[r].z, v[c].z, p);
-                    p = __fmaf_rn(g[r].w, v[c].w, p);
-                    pw[r][c] = p;
+                    pw[r][c] = fma2(g01, make_float2(v[c].x, v[c].y), pw[r][c]);
+                    pw[r][c] = fma2(g23, make_float2(v[c].z, v[c].w), pw[r][c]);
                 }
+            }
             if (diag) {
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     const float4 e = *reinterpret_cast<const float4*>(E + (4 * tr + r) * kTile + kb);
                     if constexpr (DIAG_PRODUCT) {
-                        float p = ps[r];
-                        p = __fmaf_rn(g[r].x, e.x, p);
-                        p = __fmaf_rn(g[r].y, e.y, p);
-                        p = __fmaf_rn(g[r].z, e.z, p);
-                        p = __fmaf_rn(g[r].w, e.w, p);
-                        ps[r] = p;
+                        ps[r] = fma2(make_float2(g[r].x, g[r].y), make_float2(e.x, e.y), ps[r]);
+                        ps[r] = fma2(make_float2(g[r].z, g[r].w), make_float2(e.z, e.w), ps[r]);
                     } else {
-                        ps[r] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(ps[r], e.x), e.y), e.z), e.w);
+                        ps[r] = add2(ps[r], make_float2(e.x, e.y));
+                        ps[r] = add2(ps[r], make_float2(e.z, e.w));
                     }
                 }
             }
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            accs[r] = __fadd_rn(accs[r], ps[r]);
+            accs[r] = __fadd_rn(accs[r], __fadd_rn(ps[r].x, ps[r].y));
 #pragma unroll
-            for (int c = 0; c < 4; ++c) acc[r][c] = __fadd_rn(acc[r][c], pw[r][c]);
+            for (int c = 0; c < 4; ++c)
+                acc[r][c] = __fadd_rn(acc[r][c], __fadd_rn(pw[r][c].x, pw[r][c].y));
         }
     }
 
