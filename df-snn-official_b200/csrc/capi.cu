@@ -46,6 +46,10 @@ constexpr size_t kWsHeader = 16;
 
 }  // namespace
 
+namespace dfsnn {
+int record_cuda_error(cudaError_t e) { return cuda_status(e); }
+}  // namespace dfsnn
+
 extern "C" {
 
 const char* dfsnn_status_string(int status) {

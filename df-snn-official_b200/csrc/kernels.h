@@ -48,6 +48,9 @@ cudaError_t single_backward_launch(int scheme, const float* gS, const float* gV,
                                    int T, long long N, float tau, float beta, float th, float sg,
                                    float h_beta, float gamma1, bool tau_pow2, cudaStream_t st);
 
+// Store e as the calling thread's dfsnn_last_cuda_error() value; returns DFSNN_ERR_CUDA.
+int record_cuda_error(cudaError_t e);
+
 // direct LIF-like Euler
 int euler_bwd_blocks(long long N);
 cudaError_t euler_forward_launch(const float* x, const float* z0, const float* in_scale,

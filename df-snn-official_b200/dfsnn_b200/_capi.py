@@ -38,6 +38,8 @@ SIGNATURES = {
     "dfsnn_glmulti_backward_workspace_size": (_sz, [_i, _ll, _i]),
     "dfsnn_glmulti_backward": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _ll, _f, _f, _f, _i,
                                     _p, _sz, _p]),
+    "dfsnn_glmulti_backward_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _ll, _f, _f,
+                                            _f, _i, _p]),
     "dfsnn_aligned_forward": (_i, [_p, _p, _p, _p, _p, _i, _ll, _f, _f, _p]),
     "dfsnn_aligned_backward_workspace_size": (_sz, [_i, _ll]),
     "dfsnn_aligned_backward": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _ll, _f, _f, _f, _f,

@@ -81,6 +81,20 @@ int dfsnn_glmulti_backward(const float* grad_spike, const float* x, const float*
                            int full_history, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* Same computation and results as dfsnn_glmulti_backward, for callers that cannot allocate
+ * device memory when the backward runs (a host callback, a runtime that owns all device
+ * memory, an allocation-free serving loop).  No counterpart in the reference: it has no
+ * workspace argument; its scratch (error word + per-block partial sums) is a 1.1 MB
+ * file-scope device array that every device loading the library keeps until exit.
+ * Limit: T <= 16 (DFSNN_ERR_T_LIMIT above).  All calls share that array: calls whose work
+ * overlaps on the GPU (other streams or host threads) race.  The first call on a device
+ * looks up the array's address; make it before any stream capture.  Allocates nothing. */
+int dfsnn_glmulti_backward_noalloc(const float* grad_spike, const float* x, const float* v0,
+                                   const float* scale, const float* weights, float* grad_x,
+                                   float* grad_v0, float* grad_scale, float* grad_weights, int T,
+                                   long long N, float tau, float threshold,
+                                   float surrogate_scale, int full_history, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * Aligned distributed-order GL (AlignedGLMulti, examples/cnn128/aligned_glmulti.py)
  * ------------------------------------------------------------------------------- */
