@@ -17,10 +17,14 @@
 //     scale; each block detects that structure and then keeps the T-1 distinct weights and
 //     the scale in registers, so the history FMAs read no memory (general W falls back to
 //     shared-memory weights; results are bit-identical either way).
+#include <atomic>
+#include <cmath>
+
 #include "bulk_pipe.cuh"
 #include "kernels.h"
 #include "pack2.cuh"
 #include "param_reduce.cuh"
+#include "tma.cuh"
 
 namespace dfsnn {
 
@@ -350,6 +354,321 @@ __global__ void __launch_bounds__(256) glm_bwd(GlmArgs a) {
 }
 
 // ------------------------------------------------------------------------------------
+// backward, T in {8, 16} exactly: warp-tiled persistent kernel, two neurons per lane.
+// Each warp owns a fixed, strided set of 64-neuron tiles and stages them itself -- three
+// TMA box copies per tile (x and grad_spike as [T x 64] boxes, v0 as a [1 x 64] box;
+// neurons past N read as zeros) into its own two stages, one mbarrier per stage -- so the
+// tile loop has no block barrier.  Lane l carries neurons 2l and 2l+1 as the halves of
+// float2 values and advances both with packed fp32x2 instructions (each half performs
+// exactly the scalar operation of the reference on its neuron).  With T a compile-time
+// constant the steps carry no bounds tests.  The drift overwrites x in the stage, grad_x
+// overwrites grad_spike and grad_v0 overwrites v0 (written back by TMA stores that clip
+// at N); grad_pre and v go to the warp's GP and V rows.  grad_scale is accumulated per
+// lane; grad_W per lane as a 4x4 block of the T x T product over one slice of the tile's
+// neurons.  GP and V rows are padded to 72 floats, which makes the product's float4 reads
+// free of bank conflicts.
+// ------------------------------------------------------------------------------------
+struct alignas(64) GlmTmaMaps {
+    CUtensorMap x;    // [T, N], boxes T x 64 (loads)
+    CUtensorMap g;    // [T, N] grad_spike
+    CUtensorMap v0;   // [1, N], boxes 1 x 64
+    CUtensorMap gx;   // [T, N] grad_x (stores)
+    CUtensorMap gv0;  // [1, N] grad_v0
+};
+
+template <int T>
+struct WarpBwdCfg {
+    static constexpr int kWarps = 8;
+    static constexpr int TN = 64;                        // neurons per warp tile
+    static constexpr int RS = 72;                        // padded GP / V row stride (floats)
+    static constexpr int STAGE = 2 * T * TN + TN;        // dense X rows, G rows, v0 row
+    static constexpr int PER_WARP = 2 * STAGE + 2 * T * RS;   // two stages + GP + V rows
+    static constexpr size_t kBytes = sizeof(float) * kWarps * PER_WARP + 128;  // + alignment
+    static constexpr uint32_t kTxBytes = sizeof(float) * STAGE;
+    static constexpr int kMinBlocks = T <= 8 ? 2 : 1;    // blocks per SM the registers allow
+    static constexpr int NRED = 16 + T;                  // doubles per thread in the reduction
+    static constexpr int TBLK = T / 4;                   // 4-row blocks along t (and along i)
+    static constexpr int LANES_PER_SLICE = TBLK * TBLK;
+    static constexpr int NSLICES = 32 / LANES_PER_SLICE;
+    static constexpr int GROUPS = TN / (4 * NSLICES);    // float4 neuron groups per lane
+    static_assert(T == 8 || T == 16, "warp-tiled backward covers T = 8 and T = 16");
+    static_assert((sizeof(float) * STAGE) % 128 == 0 && (sizeof(float) * PER_WARP) % 128 == 0,
+                  "TMA destinations must stay 128-byte aligned");
+    static_assert(sizeof(double) * 32 * kWarps * NRED <= kBytes - 128, "reduction scratch");
+};
+
+// Arm stage X of this warp and copy its tile (lane 0).  The stage's previous contents
+// were fenced against the async proxy when its grad_x / grad_v0 store was issued; the
+// store must have finished reading the stage before the new copies land.
+template <int T>
+__device__ __forceinline__ void warp_load(float* X, uint64_t* bar, const GlmTmaMaps& m,
+                                          long long n0) {
+    constexpr int TN = WarpBwdCfg<T>::TN;
+    bulk_wait_read_all();
+    mbar_arrive_expect_tx(bar, WarpBwdCfg<T>::kTxBytes);
+    tma_load_rows(X, &m.x, (int)n0, bar);
+    tma_load_rows(X + T * TN, &m.g, (int)n0, bar);
+    tma_load_rows(X + 2 * T * TN, &m.v0, (int)n0, bar);
+}
+
+// Store the tile's grad_x rows (in G) and grad_v0 row (in V0) with TMA (columns past N
+// are clipped by the tensor maps).  All lanes fence their generic writes of the stage.
+template <int T>
+__device__ __forceinline__ void warp_store(float* X, const GlmTmaMaps& m, long long n0, int lane) {
+    constexpr int TN = WarpBwdCfg<T>::TN;
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_rows(&m.gx, X + T * TN, (int)n0);
+        tma_store_rows(&m.gv0, X + 2 * T * TN, (int)n0);
+        bulk_commit();
+    }
+}
+
+// sg / b per half: div_markstein in packed form, or the IEEE division (SLOW)
+template <bool SLOW>
+__device__ __forceinline__ float2 surrogate_quot2(float2 sg2, float2 b) {
+    if constexpr (SLOW) {
+        return make_float2(__fdiv_rn(sg2.x, b.x), __fdiv_rn(sg2.y, b.y));
+    } else {
+        const float2 nb = pmul2(b, f2(-1.0f));
+        const float2 y0 = make_float2(rcp_approx(b.x), rcp_approx(b.y));
+        const float2 y = pfma2(pfma2(nb, y0, f2(1.0f)), y0, y0);
+        const float2 q0 = pmul2(sg2, y);
+        return pfma2(pfma2(nb, q0, sg2), y, q0);
+    }
+}
+
+// Negated history weight of term (t, i) for both halves: registers (Toeplitz) or shared.
+template <int T, bool FAST>
+__device__ __forceinline__ float2 nwgt2(const float* sW, const float2 (&nw)[T], int t, int i) {
+    if constexpr (FAST) return nw[t - i];
+    else return f2(-sW[t * T + i]);
+}
+
+// Reverse sweep of one tile given the surrogate denominators b_t of the forward pass
+// (SLOW: some lane met a denominator outside div_markstein's range; uniform per warp).
+template <int T, bool FULL, bool TP2, bool FAST, bool SLOW>
+__device__ __forceinline__ void glm_bwd_warp_reverse(const GlmArgs& a, const float* sW,
+                                                     const float* sScale, const float2 (&nw)[T],
+                                                     float sc, const float* X, float* G,
+                                                     float* V0, float* GP,
+                                                     const float2 (&bden)[T], float2 (&gsa)[T]) {
+    constexpr int RS = WarpBwdCfg<T>::RS;
+    constexpr int TN = WarpBwdCfg<T>::TN;
+    const int c2 = 2 * (threadIdx.x & 31);
+    const float2 sg2 = f2(a.sg), inv2 = f2(a.inv_tau);
+    if constexpr (FULL) {
+        float2 A[T];
+#pragma unroll
+        for (int t = 0; t < T; ++t) A[t] = f2(0.0f);
+        float2 ginit = f2(0.0f);
+#pragma unroll
+        for (int t = T - 1; t >= 0; --t) {
+            const float2 sur = surrogate_quot2<SLOW>(sg2, bden[t]);
+            const float2 gs = *reinterpret_cast<const float2*>(G + t * TN + c2);
+            const float2 gp = pfma2(gs, sur, A[t]);
+            const float2 gd = pmul2(gp, f2(FAST ? sc : sScale[t]));
+            const float2 gx = TP2 ? pmul2(gd, inv2)
+                                  : make_float2(__fdiv_rn(gd.x, a.tau), __fdiv_rn(gd.y, a.tau));
+            *reinterpret_cast<float2*>(G + t * TN + c2) = gx;
+            // the reference's (-gd)/tau is -gx exactly (round-to-nearest is symmetric)
+            if (t == 0) ginit = psub2(ginit, gx);
+            else A[t - 1] = psub2(A[t - 1], gx);
+#pragma unroll
+            for (int i = 0; i < t; ++i) A[i] = pfma2(nwgt2<T, FAST>(sW, nw, t, i), gp, A[i]);
+            *reinterpret_cast<float2*>(GP + t * RS + c2) = gp;
+            gsa[t] = pfma2(gp, *reinterpret_cast<const float2*>(X + t * TN + c2), gsa[t]);
+        }
+        *reinterpret_cast<float2*>(V0 + c2) = ginit;
+    } else {
+        float2 gvn = f2(0.0f);
+#pragma unroll
+        for (int t = T - 1; t >= 0; --t) {
+            const float2 sur = surrogate_quot2<SLOW>(sg2, bden[t]);
+            const float2 gs = *reinterpret_cast<const float2*>(G + t * TN + c2);
+            const float2 gp = pfma2(gs, sur, gvn);
+            const float2 gd = pmul2(gp, f2(FAST ? sc : sScale[t]));
+            const float2 gx = TP2 ? pmul2(gd, inv2)
+                                  : make_float2(__fdiv_rn(gd.x, a.tau), __fdiv_rn(gd.y, a.tau));
+            *reinterpret_cast<float2*>(G + t * TN + c2) = gx;
+            gvn = make_float2(-gx.x, -gx.y);    // ((-gp)*s_t)/tau, exactly
+            *reinterpret_cast<float2*>(GP + t * RS + c2) = gp;
+            gsa[t] = pfma2(gp, *reinterpret_cast<const float2*>(X + t * TN + c2), gsa[t]);
+        }
+        *reinterpret_cast<float2*>(V0 + c2) = gvn;
+    }
+}
+
+// One tile: forward recompute of both halves (v -> V rows, drift -> X, surrogate
+// denominators b = 2*(1 + u*u), u = (pi/2*sg)*(p - th) kept in registers, as
+// surrogate_fma evaluates them), then the reverse sweep.
+template <int T, bool FULL, bool TP2, bool FAST>
+__device__ __forceinline__ void glm_bwd_warp_tile(const GlmArgs& a, const float* sW,
+                                                  const float* sScale, const float2 (&nw)[T],
+                                                  float sc, float* X, float* G, float* V0,
+                                                  float* GP, float* Vs, float2 (&gsa)[T]) {
+    constexpr int RS = WarpBwdCfg<T>::RS;
+    constexpr int TN = WarpBwdCfg<T>::TN;
+    const int c2 = 2 * (threadIdx.x & 31);
+    const float th = a.th;
+    const float2 th2 = f2(th), inv2 = f2(a.inv_tau), ksg2 = f2(__fmul_rn(kPiHalf, a.sg));
+    float2 v = *reinterpret_cast<const float2*>(V0 + c2);
+    float2 hn[T], bden[T];            // hn = -history (push form), exact negation
+    bool bad = false;
+#pragma unroll
+    for (int t = 0; t < T; ++t) hn[t] = f2(-0.0f);
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const float2 xs = *reinterpret_cast<const float2*>(X + t * TN + c2);
+        const float2 xm = psub2(xs, v);
+        const float2 d = TP2 ? pmul2(xm, inv2)
+                             : make_float2(__fdiv_rn(xm.x, a.tau), __fdiv_rn(xm.y, a.tau));
+        const float2 p = pfma2(f2(FAST ? sc : sScale[t]), d, hn[t]);   // scale*d - hist
+        // v = p - s*th with s*th exactly th or 0: the surrogate's p - th, or p
+        const float2 z = psub2(p, th2);
+        v = make_float2(p.x >= th ? z.x : p.x, p.y >= th ? z.y : p.y);
+        const float2 u = pmul2(ksg2, z);
+        const float2 b = pmul2(f2(2.0f), pfma2(u, u, f2(1.0f)));
+        bden[t] = b;
+        bad |= !(b.x <= 0x1p64f) || !(b.y <= 0x1p64f);
+#pragma unroll
+        for (int w = t + 1; w < T; ++w) hn[w] = pfma2(nwgt2<T, FAST>(sW, nw, w, t), v, hn[w]);
+        *reinterpret_cast<float2*>(Vs + t * RS + c2) = v;
+        *reinterpret_cast<float2*>(X + t * TN + c2) = d;
+    }
+    if (__any_sync(0xffffffffu, bad))
+        glm_bwd_warp_reverse<T, FULL, TP2, FAST, true>(a, sW, sScale, nw, sc, X, G, V0, GP, bden, gsa);
+    else
+        glm_bwd_warp_reverse<T, FULL, TP2, FAST, false>(a, sW, sScale, nw, sc, X, G, V0, GP, bden, gsa);
+}
+
+// pw[r][c] += sum over this lane's neurons of GP[t] * V[i], t = tr + TBLK*r,
+// i = tc + TBLK*c; each float4 group of neurons enters as two packed halves.
+template <int T>
+__device__ __forceinline__ void warp_product(const float* GP, const float* Vs, int lane,
+                                             float2 (&pw)[4][4]) {
+    using C = WarpBwdCfg<T>;
+    constexpr int RS = C::RS;
+    const int tr = lane % C::TBLK, tc = (lane / C::TBLK) % C::TBLK, sl = lane / C::LANES_PER_SLICE;
+#pragma unroll
+    for (int jj = 0; jj < C::GROUPS; ++jj) {
+        const int kb = 4 * (sl * C::GROUPS + jj);
+        float4 g[4], v[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            g[r] = *reinterpret_cast<const float4*>(GP + (tr + C::TBLK * r) * RS + kb);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            v[c] = *reinterpret_cast<const float4*>(Vs + (tc + C::TBLK * c) * RS + kb);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const float2 g01 = make_float2(g[r].x, g[r].y), g23 = make_float2(g[r].z, g[r].w);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                pw[r][c] = fma2(g01, make_float2(v[c].x, v[c].y), pw[r][c]);
+                pw[r][c] = fma2(g23, make_float2(v[c].z, v[c].w), pw[r][c]);
+            }
+        }
+    }
+}
+
+template <int T, bool FULL, bool TP2>
+__global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
+    glm_bwd_w(GlmArgs a, const __grid_constant__ GlmTmaMaps m) {
+    using C = WarpBwdCfg<T>;
+    constexpr int RS = C::RS;
+    constexpr int TN = C::TN;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    __shared__ float sW[T * T];
+    __shared__ float sScale[T];
+    __shared__ __align__(8) uint64_t bars[C::kWarps][2];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const long long N = a.N;
+    for (int e = tid; e < T * T; e += blockDim.x) sW[e] = a.W[e];
+    for (int e = tid; e < T; e += blockDim.x) sScale[e] = a.scale[e];
+    if (lane == 0) {
+        mbar_init(&bars[warp][0], 1);
+        mbar_init(&bars[warp][1], 1);
+        fence_mbar_init();
+    }
+    const bool fast = block_toeplitz(a.W, a.scale, T);     // block barrier
+    unsigned char* aligned_smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    float* wbase = reinterpret_cast<float*>(aligned_smem) + warp * C::PER_WARP;
+    float* GP = wbase + 2 * C::STAGE;
+    float* Vs = GP + T * RS;
+    float2 nw[T];
+    const float sc = sScale[0];
+#pragma unroll
+    for (int d = 0; d < T; ++d) nw[d] = f2((fast && d > 0) ? -sW[d * T] : 0.0f);
+    float2 pw[4][4];
+    float2 gsa[T];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) pw[r][c] = f2(0.0f);
+#pragma unroll
+    for (int t = 0; t < T; ++t) gsa[t] = f2(0.0f);
+    const long long ntiles = (N + TN - 1) / TN;
+    const long long first = (long long)blockIdx.x * C::kWarps + warp;
+    const long long stride = (long long)gridDim.x * C::kWarps;
+    if (lane == 0 && first < ntiles) warp_load<T>(wbase, &bars[warp][0], m, first * TN);
+    bool failed = false;
+    int j = 0;
+    for (long long tile = first; tile < ntiles; tile += stride, ++j) {
+        const int s = j & 1;
+        float* X = wbase + s * C::STAGE;
+        float* G = X + T * TN;
+        float* V0 = X + 2 * T * TN;
+        const bool ok = mbar_wait_bounded(&bars[warp][s], (uint32_t)((j >> 1) & 1));
+        if (__any_sync(0xffffffffu, !ok)) { failed = true; break; }
+        if (lane == 0 && tile + stride < ntiles)
+            warp_load<T>(wbase + (s ^ 1) * C::STAGE, &bars[warp][s ^ 1], m, (tile + stride) * TN);
+        // lanes past N compute on zero-filled inputs; the stores clip them
+        if (fast) glm_bwd_warp_tile<T, FULL, TP2, true>(a, sW, sScale, nw, sc, X, G, V0, GP, Vs, gsa);
+        else glm_bwd_warp_tile<T, FULL, TP2, false>(a, sW, sScale, nw, sc, X, G, V0, GP, Vs, gsa);
+        __syncwarp();
+        warp_product<T>(GP, Vs, lane, pw);
+        warp_store<T>(X, m, tile * TN, lane);
+    }
+    if (lane == 0) {
+        if (failed) {
+            atomicOr(a.err, 1u);
+            // let the copies still in flight into this warp's stage land (bounded wait)
+            mbar_wait_bounded(&bars[warp][j & 1], (uint32_t)((j >> 1) & 1));
+        }
+        bulk_wait_all();   // stores complete before the stages are reused below
+    }
+    // block reduction in double, fixed order, into this block's partial row
+    __syncthreads();
+    double* red = reinterpret_cast<double*>(aligned_smem);
+    double* mine = red + (size_t)tid * C::NRED;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) mine[r * 4 + c] = (double)pw[r][c].x + (double)pw[r][c].y;
+#pragma unroll
+    for (int t = 0; t < T; ++t) mine[16 + t] = (double)gsa[t].x + (double)gsa[t].y;
+    __syncthreads();
+    double* part = a.part + (size_t)blockIdx.x * (T + T * T);
+    for (int o = tid; o < T + T * T; o += blockDim.x) {
+        double sum = 0.0;
+        if (o < T) {
+            for (int q = 0; q < C::kWarps * 32; ++q) sum += red[(size_t)q * C::NRED + 16 + o];
+        } else {
+            const int t = (o - T) / T, i = (o - T) % T;
+            const int r = t / C::TBLK, c = i / C::TBLK;
+            const int l0 = (t % C::TBLK) + C::TBLK * (i % C::TBLK);
+            for (int w = 0; w < C::kWarps; ++w)
+                for (int sl = 0; sl < C::NSLICES; ++sl)
+                    sum += red[(size_t)(w * 32 + sl * C::LANES_PER_SLICE + l0) * C::NRED + r * 4 + c];
+        }
+        part[o] = sum;
+    }
+}
+
+// ------------------------------------------------------------------------------------
 // sum the per-block partials in a fixed order: gs (T) and gW (T x T, negated)
 // ------------------------------------------------------------------------------------
 __global__ void param_finalize(const double* part, int nblocks, int TB, int T, float* gscale,
@@ -397,6 +716,8 @@ namespace {
 
 int tb_bucket(int T) { return T <= 8 ? 8 : (T <= 16 ? 16 : 32); }
 
+constexpr int kMaxDevices = 64;
+
 template <int TB, bool FULL, bool TP2, bool BULK>
 cudaError_t launch_bwd_t(const GlmArgs& a, int grid, cudaStream_t st) {
     const size_t smem = GlmBwdSmem<TB>::kBytes;
@@ -407,20 +728,64 @@ cudaError_t launch_bwd_t(const GlmArgs& a, int grid, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+template <int T, bool FULL, bool TP2>
+cudaError_t launch_bwd_w(const GlmArgs& a, const GlmTmaMaps& m, int grid, cudaStream_t st) {
+    const size_t smem = WarpBwdCfg<T>::kBytes;
+    auto k = glm_bwd_w<T, FULL, TP2>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k<<<grid, 256, smem, st>>>(a, m);
+    return cudaGetLastError();
+}
+
+// tensor maps of the warp-tiled backward, false when the arrays do not meet the TMA rules
+bool glm_tma_maps(GlmTmaMaps* m, const float* x, const float* gS, const float* v0, float* gx,
+                  float* gv0, int T, long long N) {
+    const int bn = 64;   // WarpBwdCfg<T>::TN
+    return encode_rows_map(&m->x, x, N, T, bn) && encode_rows_map(&m->g, gS, N, T, bn) &&
+           encode_rows_map(&m->v0, v0, N, 1, bn) && encode_rows_map(&m->gx, gx, N, T, bn) &&
+           encode_rows_map(&m->gv0, gv0, N, 1, bn);
+}
+
+// resident blocks per device of a backward kernel (SMs x occupancy), cached per device
+template <class K>
+int resident_blocks(K k, size_t smem, int slot) {
+    static std::atomic<int> cache[kMaxDevices][8];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const bool cacheable = dev >= 0 && dev < kMaxDevices;
+    if (cacheable) {
+        const int got = cache[dev][slot].load(std::memory_order_relaxed);
+        if (got > 0) return got;
+    }
+    int sms = 0, per = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, 256, smem);
+    if (per < 1) per = 1;
+    if (sms < 1) sms = 1;
+    const int r = sms * per;
+    if (cacheable) cache[dev][slot].store(r, std::memory_order_relaxed);
+    return r;
+}
+
 template <int TB>
 int bwd_grid_t(long long N) {
-    int dev = 0, sms = 0, per = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const size_t smem = GlmBwdSmem<TB>::kBytes;
-    auto k = glm_bwd<TB, true, false, true>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, kTile, smem);
-    if (per < 1) per = 1;
+    int res;
+    if constexpr (TB == 8 || TB == 16)
+        res = resident_blocks(glm_bwd_w<TB, true, false>, WarpBwdCfg<TB>::kBytes, TB == 8 ? 0 : 1);
+    else
+        res = resident_blocks(glm_bwd<TB, true, false, true>, GlmBwdSmem<TB>::kBytes, 2);
     const long long ntiles = (N + kTile - 1) / kTile;
-    long long g = (long long)sms * per;
+    long long g = res;
     if (g > ntiles) g = ntiles;
     return g < 1 ? 1 : (int)g;
+}
+
+// sg within the range where surrogate_fast is exact
+bool surrogate_fast_ok(float sg) {
+    const float m = std::fabs(sg);
+    return m >= 0x1p-60f && m <= 0x1p60f;
 }
 
 }  // namespace
@@ -502,6 +867,21 @@ cudaError_t glmulti_backward_launch(const float* gS, const float* x, const float
     if (e != cudaSuccess) return e;
     const bool bulk = bulk_eligible(x, gS, v0, N);
     const int TB = tb_bucket(T);
+    GlmTmaMaps maps;
+    if ((T == 8 || T == 16) && surrogate_fast_ok(sg) && glm_tma_maps(&maps, x, gS, v0, gx, gv0, T, N)) {
+#define DFSNN_BWDW(TV)                                                                          \
+        if (T == TV) {                                                                          \
+            if (full) e = tau_pow2 ? launch_bwd_w<TV, true, true>(a, maps, nblocks, st)         \
+                                   : launch_bwd_w<TV, true, false>(a, maps, nblocks, st);       \
+            else e = tau_pow2 ? launch_bwd_w<TV, false, true>(a, maps, nblocks, st)             \
+                              : launch_bwd_w<TV, false, false>(a, maps, nblocks, st);           \
+        }
+        DFSNN_BWDW(8) DFSNN_BWDW(16)
+#undef DFSNN_BWDW
+        if (e != cudaSuccess) return e;
+        if (gscale || gW) e = launch_param_finalize(part, nblocks, TB, T, gscale, gW, 0, err, st);
+        return e;
+    }
 #define DFSNN_BWD(TBV)                                                                         \
     if (TB == TBV) {                                                                           \
         if (bulk) {                                                                            \

@@ -22,6 +22,39 @@ __device__ __forceinline__ float surrogate_fma(float z, float sg) {
     return __fdiv_rn(sg, __fmul_rn(2.0f, __fmaf_rn(u, u, 1.0f)));
 }
 
+// Correctly rounded a / b without the general IEEE division sequence, by Markstein's
+// FMA-corrected quotient (P. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990; Theorem 8.10 of his
+// "IA-64 and Elementary Functions", 2000): with y = RN(1/b) and a quotient q0 within one
+// ulp of a/b, the remainder r = a - b*q0 is exact in one FMA and RN(q0 + r*y) = RN(a/b).
+// y comes from the hardware reciprocal approximation refined by one Newton step.  Valid
+// when a, b, 1/b and a/b stay in the normal range (callers guarantee 2 <= b <= 2^64 and
+// 2^-60 <= |a| <= 2^60 and take __fdiv_rn otherwise); the tests compare it bit for bit
+// with __fdiv_rn over every b mantissa.
+__device__ __forceinline__ float rcp_approx(float b) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+    return y;
+}
+
+__device__ __forceinline__ float div_markstein(float a, float b) {
+    const float y0 = rcp_approx(b);
+    const float y = __fmaf_rn(__fmaf_rn(-b, y0, 1.0f), y0, y0);
+    const float q0 = __fmul_rn(a, y);
+    return __fmaf_rn(__fmaf_rn(-b, q0, a), y, q0);
+}
+
+// surrogate_fma with the quotient by div_markstein (sg checked on the host to lie in
+// [2^-60, 2^60] in magnitude); 1+u*u >= 1 so only a huge or NaN denominator takes the
+// IEEE division.  Bit-identical to surrogate_fma.
+__device__ __forceinline__ float surrogate_fast(float z, float sg) {
+    const float u = __fmul_rn(__fmul_rn(kPiHalf, sg), z);
+    const float b = __fmul_rn(2.0f, __fmaf_rn(u, u, 1.0f));
+    float q = div_markstein(sg, b);
+    if (!(b <= 0x1p64f)) q = __fdiv_rn(sg, b);
+    return q;
+}
+
 // Division by tau.  The reference divides (IEEE).  When tau is a power of two the
 // quotient equals the product with 1/tau exactly, so the kernels may multiply instead.
 template <bool TAU_POW2>

@@ -79,6 +79,26 @@ def lib():
     return _lib
 
 
+_WS_CACHE = {}
+
+
+def workspace_bytes(kind, device, T, N, full=0):
+    """Workspace size of a backward entry point (cached: the query consults the occupancy
+    API, which costs host time on every call)."""
+    key = (kind, device.index, T, N, full)
+    got = _WS_CACHE.get(key)
+    if got is None:
+        L = lib()
+        if kind == "glmulti":
+            got = int(L.dfsnn_glmulti_backward_workspace_size(T, N, full))
+        elif kind == "aligned":
+            got = int(L.dfsnn_aligned_backward_workspace_size(T, N))
+        else:
+            got = int(L.dfsnn_direct_euler_backward_workspace_size(N))
+        _WS_CACHE[key] = got
+    return got
+
+
 def status_string(code):
     return lib().dfsnn_status_string(code).decode()
 

@@ -63,7 +63,7 @@ class AlignedGLMulti(torch.autograd.Function):
         launches = 2 if (gs is not None or gw is not None) else 1
         with torch.cuda.device(g.device):
             L = _capi.lib()
-            ws_bytes = L.dfsnn_aligned_backward_workspace_size(T, N)
+            ws_bytes = _capi.workspace_bytes("aligned", g.device, T, N)
             ws = torch.empty(max(int(ws_bytes), 8), dtype=torch.uint8, device=g.device)
         with torch.cuda.device(g.device), _prof.native_call(
                 "aligned_backward", launches, _prof.glmulti_backward_bytes(T, N), g.device):

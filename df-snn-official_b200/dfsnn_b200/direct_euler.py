@@ -52,7 +52,7 @@ class DirectLIFLikeEulerCuPyFunction(torch.autograd.Function):
         g3 = torch.empty(3, device=x.device, dtype=torch.float32)
         with torch.cuda.device(x.device):
             L = _capi.lib()
-            ws_bytes = L.dfsnn_direct_euler_backward_workspace_size(N)
+            ws_bytes = _capi.workspace_bytes("euler", x.device, 0, N)
             ws = torch.empty(max(int(ws_bytes), 8), dtype=torch.uint8, device=x.device)
         with torch.cuda.device(x.device), _prof.native_call(
                 "euler_backward", 2, _prof.euler_backward_bytes(T, N), x.device):

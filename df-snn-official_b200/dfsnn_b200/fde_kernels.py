@@ -196,7 +196,7 @@ class LIFFDEGLMultiFunction(torch.autograd.Function):
         launches = 2 if (grad_scale is not None or grad_weights is not None) else 1
         with torch.cuda.device(x.device):
             L = _capi.lib()
-            ws_bytes = L.dfsnn_glmulti_backward_workspace_size(T, N, full)
+            ws_bytes = _capi.workspace_bytes("glmulti", x.device, T, N, full)
             ws = torch.empty(max(int(ws_bytes), 8), dtype=torch.uint8, device=x.device)
         with torch.cuda.device(x.device), _prof.native_call(
                 "glmulti_backward", launches, _prof.glmulti_backward_bytes(T, N), x.device):

@@ -183,7 +183,12 @@ class LIFNeuronFDE(nn.Module):
         if T != self.T:
             raise ValueError(f"glmulti was initialized for T={self.T}, got T={T}")
         basis = self._glmulti_basis.to(device=device, dtype=torch.float32)
-        return _sched.build_glmulti_schedule(coefficient, self.multi_beta, basis, self.h, T)
+        key = (device.type, device.index)
+        cache = self.__dict__.setdefault("_h_pow_cache", {})
+        if key not in cache:
+            cache[key] = _sched.h_pow_neg_beta(self.h, self.multi_beta, device)
+        return _sched.build_glmulti_schedule(coefficient, self.multi_beta, basis, self.h, T,
+                                             h_pow=cache[key])
 
     def _compute_weights(self, T, device, dtype):
         beta = self._beta_value()

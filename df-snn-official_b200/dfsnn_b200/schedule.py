@@ -28,13 +28,21 @@ def softplus_masses(raw):
     return F.softplus(raw)
 
 
-def glmulti_c_tilde(coefficient, multi_beta, basis, h):
+def h_pow_neg_beta(h, multi_beta, device):
+    """h^-beta exactly as _get_glmulti_weights evaluates it (torch.pow of a 0-dim h tensor on
+    the given device).  Constant for a neuron: callers cache it instead of paying the
+    host-to-device copy of h on every forward."""
+    beta = multi_beta.to(device=device, dtype=torch.float32)
+    return torch.pow(torch.tensor(h, device=device, dtype=torch.float32), -beta)
+
+
+def glmulti_c_tilde(coefficient, multi_beta, basis, h, h_pow=None):
     """c~ (length T+1) and 1/c~_0 exactly as _get_glmulti_weights computes them."""
     device = basis.device
-    beta = multi_beta.to(device=device, dtype=torch.float32)
     coefficient = coefficient.to(device=device, dtype=torch.float32)
-    hh = torch.tensor(h, device=device, dtype=torch.float32)
-    weighted_h = coefficient * torch.pow(hh, -beta)
+    if h_pow is None:
+        h_pow = h_pow_neg_beta(h, multi_beta, device)
+    weighted_h = coefficient * h_pow
     c_tilde = torch.sum(weighted_h.unsqueeze(1) * basis, dim=0)
     return c_tilde, 1.0 / c_tilde[0]
 
@@ -54,9 +62,9 @@ def _lag_index(T, device):
     return got
 
 
-def build_glmulti_schedule(coefficient, multi_beta, basis, h, T):
+def build_glmulti_schedule(coefficient, multi_beta, basis, h, T, h_pow=None):
     """{'scale': [T], 'weights': [T,T]} of LIFNeuronFDE._build_glmulti_schedule."""
-    c_tilde, c0_inv = glmulti_c_tilde(coefficient, multi_beta, basis, h)
+    c_tilde, c0_inv = glmulti_c_tilde(coefficient, multi_beta, basis, h, h_pow)
     lag, mask = _lag_index(T, c_tilde.device)
     weights = torch.where(mask, c_tilde[lag] * c0_inv, torch.zeros((), device=c_tilde.device))
     return {"scale": c0_inv.expand(T), "weights": weights}

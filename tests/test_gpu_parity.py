@@ -72,7 +72,8 @@ def cpu(t):
 # library glmulti
 # -------------------------------------------------------------------------------------
 GLM_CASES = [(T, N) for T in (1, 2, 3, 7, 8, 13, 16, 17, 31, 32) for N in (1, 255, 1000)] + \
-            [(16, 4099), (8, 70001), (32, 5000)]
+            [(16, 4099), (8, 70001), (32, 5000)] + \
+            [(T, N) for T in (8, 16) for N in (4, 32, 36, 4100, 70000, 100000)]
 
 
 @pytest.mark.parametrize("T,N", GLM_CASES)
