@@ -10,6 +10,7 @@
 // bits: O(T) per neuron, no recompute, bit-identical surrogate inputs (v_t + s_t*theta).
 #include "kernels.h"
 #include "lif_common.cuh"
+#include "pack2.cuh"
 
 namespace dfsnn {
 
@@ -91,6 +92,75 @@ __global__ void __launch_bounds__(256) single_fwd_reg(SingleArgs a) {
         }
     }
     a.bits[n] = bits;
+}
+
+// ------------------------------------------------------------------------------------
+// forward, T in {8, 16} exactly, two neurons per thread (n, n+1): both Kahan chains advance
+// with packed fp32x2 instructions (inline PTX, so no compiler pass can rewrite the
+// compensation).  The history is summed negated (weights -w) for the schemes that use
+// -hist, which makes every update a single packed operation; round-to-nearest is
+// symmetric, so only the sign of an exact zero can differ from the scalar kernel.
+// Used when N is even and x / v0 / spike / v / bits are 8-byte aligned.
+// ------------------------------------------------------------------------------------
+template <int SCHEME, int T, bool TP2>
+__global__ void __launch_bounds__(256) single_fwd_x2(SingleArgs a) {
+    __shared__ float sw[T + 1];
+    for (int e = threadIdx.x; e <= T; e += blockDim.x) sw[e] = a.w[e];
+    __syncthreads();
+    const long long N = a.N;
+    const long long n = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
+    if (n >= N) return;
+    constexpr bool NEG = SCHEME != kPRED;
+    float2 wr[T + 1];
+#pragma unroll
+    for (int L = 1; L <= T; ++L) wr[L] = f2(NEG ? -sw[T - L] : sw[T - L]);
+    const float th = a.th;
+    const float2 th2 = f2(th), inv2 = f2(a.inv_tau), ninv2 = f2(-a.inv_tau);
+    const float2 tf2 = f2(__fmaf_rn(1.5f, a.beta, 0.5f));                 // :346
+    const float2 ps2 = f2(__fdiv_rn(a.h_beta, a.gamma1));                 // :528
+    const float2 wc2 = f2(sw[T]), hb2 = f2(a.h_beta);
+    float2 xr[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) xr[t] = ld2_stream(a.x + t * N + n);
+    float2 v = *reinterpret_cast<const float2*>(a.v0 + n);
+    float2 hv[T];
+    uint32_t b0 = 0, b1 = 0;
+#pragma unroll
+    for (int k = 0; k < T; ++k) {
+        const float2 xm = psub2(xr[k], v);
+        const float2 dv = TP2 ? pmul2(xm, inv2)
+                              : make_float2(__fdiv_rn(xm.x, a.tau), __fdiv_rn(xm.y, a.tau));
+        float2 s = f2(0.0f), cn = f2(-0.0f);       // Kahan sum (negated when NEG), cn = -c
+#pragma unroll
+        for (int i = 0; i < k; ++i) {
+            const float2 y = pfma2(wr[k - i], hv[i], cn);
+            // the running sum is formed by two scalar adds: with a packed add here the
+            // optimised code was seen to lose the compensation in some chains (the GPU
+            // suite compares every instantiation of this kernel bit for bit)
+            const float2 t = make_float2(__fadd_rn(s.x, y.x), __fadd_rn(s.y, y.y));
+            cn = padd2(y, psub2(s, t));
+            s = t;
+        }
+        float2 p;
+        if constexpr (SCHEME == kGL) p = padd2(dv, s);                          // dv - hist
+        else if constexpr (SCHEME == kGL1) p = pfma2(hb2, dv, s);               // fma(hb, dv, -hist)
+        else if constexpr (SCHEME == kTRAP) p = padd2(v, pfma2(tf2, dv, s));    // v + fma(tf, dv, -hist)
+        else p = pfma2(ps2, pfma2(wc2, dv, s), v);                              // predictor
+        // v = p - spike*th with spike*th exactly th or 0
+        const float2 z = psub2(p, th2);
+        const bool f0 = p.x >= th, f1 = p.y >= th;
+        v = make_float2(f0 ? z.x : p.x, f1 ? z.y : p.y);
+        if constexpr (SCHEME == kPRED)
+            hv[k] = TP2 ? pmul2(v, ninv2)
+                        : make_float2(__fdiv_rn(-v.x, a.tau), __fdiv_rn(-v.y, a.tau));
+        else
+            hv[k] = v;
+        b0 |= (f0 ? 1u : 0u) << k;
+        b1 |= (f1 ? 1u : 0u) << k;
+        st2_stream(a.spike + k * N + n, make_float2(f0 ? 1.0f : 0.0f, f1 ? 1.0f : 0.0f));
+        st2_stream(a.v + k * N + n, v);
+    }
+    *reinterpret_cast<uint2*>(a.bits + n) = make_uint2(b0, b1);
 }
 
 // ------------------------------------------------------------------------------------
@@ -262,9 +332,21 @@ SingleArgs make_args(int T, long long N, float tau, float beta, float th, float 
     return a;
 }
 
+bool aligned8_all(const void* p, const void* q, const void* r, const void* s, const void* t) {
+    return ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(q) |
+             reinterpret_cast<uintptr_t>(r) | reinterpret_cast<uintptr_t>(s) |
+             reinterpret_cast<uintptr_t>(t)) & 7u) == 0;
+}
+
 template <int SCHEME, bool TP2>
 cudaError_t fwd_dispatch(const SingleArgs& a, cudaStream_t st) {
     const int T = a.T;
+    if ((T == 8 || T == 16) && (a.N % 2) == 0 && aligned8_all(a.x, a.v0, a.spike, a.v, a.bits)) {
+        const unsigned grid = (unsigned)((a.N / 2 + 255) / 256);
+        if (T == 8) single_fwd_x2<SCHEME, 8, TP2><<<grid, 256, 0, st>>>(a);
+        else single_fwd_x2<SCHEME, 16, TP2><<<grid, 256, 0, st>>>(a);
+        return cudaGetLastError();
+    }
     if (T <= 32) {
         const unsigned grid = (unsigned)((a.N + 255) / 256);
         if (T <= 8) single_fwd_reg<SCHEME, 8, TP2><<<grid, 256, 0, st>>>(a);

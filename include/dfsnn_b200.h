@@ -170,6 +170,19 @@ int dfsnn_direct_euler_backward(const float* grad_spike, const float* grad_z_fin
                                 float spike_update_dt, void* workspace, size_t workspace_bytes,
                                 void* stream);
 
+/* ---- self-check (no reference counterpart) ----------------------------------------
+ * The backward kernels divide the arctan surrogate's numerator by its denominator with an
+ * FMA-corrected reciprocal (Markstein) instead of the IEEE division sequence.  This entry
+ * point compares that quotient bit for bit with __fdiv_rn on the device: for each of the
+ * n_numerators numerators a[k] (device array) and every float denominator b with biased
+ * exponent in [exp_lo, exp_hi] (all 2^23 mantissas per exponent; b = 2 has exponent 128),
+ * plus the refined reciprocal against __frcp_rn for every mantissa.  mismatches (device,
+ * 2 x unsigned long long) receives {quotient mismatches, reciprocal mismatches}; it is
+ * zeroed by the call.  Exponents outside [128, 191] (b < 2 or b > 2^64, where the kernels
+ * take the IEEE division) are rejected with DFSNN_ERR_PARAM. */
+int dfsnn_check_surrogate_quotient(const float* a, int n_numerators, int exp_lo, int exp_hi,
+                                   unsigned long long* mismatches, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -95,3 +95,12 @@ def test_check_maps_to_reference_exception_types():
     with pytest.raises(RuntimeError):
         _capi.check(_capi.DFSNN_ERR_CUDA, "x")
     _capi.check(_capi.DFSNN_OK, "x")
+
+
+def test_quotient_check_validates_before_launch():
+    L = _capi.lib()
+    fake = ctypes.c_void_p(16)
+    assert L.dfsnn_check_surrogate_quotient(None, 1, 128, 128, fake, None) == _capi.DFSNN_ERR_NULL
+    assert L.dfsnn_check_surrogate_quotient(fake, 1, 127, 128, fake, None) == _capi.DFSNN_ERR_PARAM
+    assert L.dfsnn_check_surrogate_quotient(fake, 1, 128, 192, fake, None) == _capi.DFSNN_ERR_PARAM
+    assert L.dfsnn_check_surrogate_quotient(fake, 0, 128, 128, fake, None) == _capi.DFSNN_ERR_PARAM

@@ -248,7 +248,8 @@ def run_single(method, x, v0, w, tau, beta, gS, gV, h=0.1):
 
 @pytest.mark.parametrize("method", ["gl", "trap", "predictor", "gl1"])
 @pytest.mark.parametrize("T,N", [(1, 50), (5, 999), (8, 1000), (16, 4099), (20, 512), (32, 300),
-                                 (33, 300), (64, 1000), (100, 257), (256, 130)])
+                                 (33, 300), (64, 1000), (100, 257), (256, 130), (8, 2), (16, 2),
+                                 (16, 4100), (8, 70002), (16, 70000)])
 @pytest.mark.parametrize("tau", [2.0, 0.7])
 def test_single_vs_oracle(method, T, N, tau):
     beta = 0.7 if T != 64 else 0.5
