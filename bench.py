@@ -173,13 +173,15 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic(kernel, T):
-    """DRAM bytes per launch from the committed ncu summary, if one covers this kernel."""
+def ncu_traffic(kernel, Ts):
+    """DRAM bytes per launch from the committed ncu summary (profiles/ncu_traffic.json),
+    averaged over the step counts the bench runs (each T runs equally often), or None."""
     path = os.path.join(REPO, "profiles", "ncu_traffic.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        return d.get(f"{kernel}_T{T}")
+        vals = [d[f"{kernel}_T{T}"] for T in Ts]
+        return sum(vals) / len(vals)
     except Exception:
         return None
 
@@ -331,7 +333,7 @@ def run_native(args):
                     "unit": "GB/s", "frac": achieved / peak if achieved else None,
                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
                     "algorithmic_bytes_per_launch": d["bytes_per_call"],
-                    "traffic": ncu_traffic(name, 16)}
+                    "traffic": ncu_traffic(name, sorted({T for T, _ in COMBOS}))}
     kernels = {k: {"calls_per_step": v["calls"] / K, "ms_per_call": round(v["ms_per_call"], 4),
                    "gbs": round(v["gbs"], 1) if v["gbs"] else None,
                    "frac_of_hbm": round(v["gbs"] / peak, 4) if v["gbs"] else None}
