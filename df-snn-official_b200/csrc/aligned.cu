@@ -331,6 +331,83 @@ int aln_grid_t(long long N) {
     return g < 1 ? 1 : (int)g;
 }
 
+// ------------------------------------------------------------------------------------
+// 32 < T <= 64: one thread per neuron, history in shared memory ([T][64] floats per block;
+// the backward's adjoint sums another [T][64]).  Pull-form history in the reference's
+// order (h += w*hist, separately rounded).  The backward writes v_t, the adjoint r_t (ga)
+// and e_t = r_t*(v_t + h_t)/a_t to [T, N] scratch for param_long.
+// ------------------------------------------------------------------------------------
+constexpr int kAlnLongThreads = 64;
+
+template <bool TP2>
+__global__ void __launch_bounds__(kAlnLongThreads) aln_fwd_long(AlnArgs a) {
+    extern __shared__ float sh[];
+    const long long n = (long long)blockIdx.x * kAlnLongThreads + threadIdx.x;
+    if (n >= a.N) return;
+    const long long N = a.N;
+    const int T = a.T;
+    float* vh = sh + threadIdx.x;
+    float v = a.v0[n];
+    for (int t = 0; t < T; ++t) {
+        const float* wrow = a.W + (size_t)t * T;
+        float h = 0.0f;
+        for (int j = 0; j < t; ++j) h = __fadd_rn(h, __fmul_rn(__ldg(wrow + j), vh[j * kAlnLongThreads]));
+        float pred;
+        bool fire;
+        v = aligned_step<TP2>(ld_stream(a.x + t * N + n), v, __ldg(a.a + t), h, a.tau, a.inv_tau,
+                              a.th, pred, fire);
+        vh[t * kAlnLongThreads] = v;
+        st_stream(a.spike + t * N + n, fire ? 1.0f : 0.0f);
+    }
+}
+
+template <bool TP2>
+__global__ void __launch_bounds__(kAlnLongThreads) aln_bwd_long(AlnArgs a, float* Vs, float* Es,
+                                                                float* Rs) {
+    extern __shared__ float sh[];
+    const long long n = (long long)blockIdx.x * kAlnLongThreads + threadIdx.x;
+    if (n >= a.N) return;
+    const long long N = a.N;
+    const int T = a.T;
+    float* vh = sh + threadIdx.x;
+    float* A = sh + (size_t)T * kAlnLongThreads + threadIdx.x;
+    const float zc = __fmul_rn(kAlignedPiHalf, a.sg);
+    const float one_m = __fsub_rn(1.0f, __fdiv_rn(1.0f, a.tau));
+    float v = a.v0[n];
+    for (int t = 0; t < T; ++t) {
+        const float* wrow = a.W + (size_t)t * T;
+        float h = 0.0f;
+        for (int j = 0; j < t; ++j) h = __fadd_rn(h, __fmul_rn(__ldg(wrow + j), vh[j * kAlnLongThreads]));
+        float pred;
+        bool fire;
+        v = aligned_step<TP2>(ld_stream(a.x + t * N + n), v, __ldg(a.a + t), h, a.tau, a.inv_tau,
+                              a.th, pred, fire);
+        vh[t * kAlnLongThreads] = v;
+        const float z = __fmul_rn(zc, __fsub_rn(pred, a.th));
+        const float den = __fmul_rn(2.0f, __fadd_rn(1.0f, __fmul_rn(z, z)));
+        Rs[t * N + n] = __fdiv_rn(__fmul_rn(ld_stream(a.g + t * N + n), a.sg), den);   // q_t
+        Es[t * N + n] = __fadd_rn(v, h);                                               // v_t + h_t
+        Vs[t * N + n] = v;
+        A[t * kAlnLongThreads] = 0.0f;
+    }
+    for (int t = T - 1; t >= 0; --t) {
+        const float a_t = __ldg(a.a + t);
+        const float q = Rs[t * N + n];
+        const float r = A[t * kAlnLongThreads];
+        const float ra = __fmul_rn(r, a_t);
+        st_stream(a.gx + t * N + n, div_tau<TP2>(__fadd_rn(q, ra), a.tau, a.inv_tau));
+        const float prev = __fsub_rn(__fmul_rn(q, one_m), div_tau<TP2>(ra, a.tau, a.inv_tau));
+        if (t) A[(t - 1) * kAlnLongThreads] = __fadd_rn(A[(t - 1) * kAlnLongThreads], prev);
+        else a.gv0[n] = prev;
+        const float* wrow = a.W + (size_t)t * T;
+        for (int j = 0; j < t; ++j)
+            A[j * kAlnLongThreads] = __fsub_rn(A[j * kAlnLongThreads],
+                                               __fmul_rn(__fmul_rn(a.rho, __ldg(wrow + j)), r));
+        Rs[t * N + n] = r;
+        Es[t * N + n] = __fdiv_rn(__fmul_rn(r, Es[t * N + n]), a_t);
+    }
+}
+
 template <int TB, bool TP2, bool BULK>
 cudaError_t aln_bwd_launch_t(const AlnArgs& a, int grid, cudaStream_t st) {
     const size_t smem = AlnBwdSmem<TB>::kBytes;
@@ -351,8 +428,39 @@ int aligned_bwd_blocks(int T, long long N, bool) {
 }
 
 int aligned_part_stride(int T) {
+    if (T > 32) return T + T * T;
     const int TB = tb_of(T);
     return TB + TB * TB;
+}
+
+cudaError_t aligned_backward_long_launch(const float* g, const float* x, const float* v0,
+                                         const float* a_, const float* W, float* gx, float* gv0,
+                                         float* ga, float* gW, int T, long long N, float tau,
+                                         float th, float sg, float rho, bool tau_pow2,
+                                         double* part, int slices, float* scratch,
+                                         unsigned int* err, cudaStream_t st) {
+    AlnArgs a{};
+    a.x = x; a.v0 = v0; a.a = a_; a.W = W; a.g = g; a.gx = gx; a.gv0 = gv0;
+    a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau; a.th = th; a.sg = sg; a.rho = rho;
+    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(unsigned int), st);
+    if (e != cudaSuccess) return e;
+    float* Vs = scratch;
+    float* Es = scratch + (size_t)T * N;
+    float* Rs = scratch + 2 * (size_t)T * N;
+    if (N > 0) {
+        const size_t smem = sizeof(float) * 2 * (size_t)T * kAlnLongThreads;
+        const unsigned grid = (unsigned)((N + kAlnLongThreads - 1) / kAlnLongThreads);
+        auto k = tau_pow2 ? aln_bwd_long<true> : aln_bwd_long<false>;
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        k<<<grid, kAlnLongThreads, smem, st>>>(a, Vs, Es, Rs);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    if (!ga && !gW) return cudaSuccess;
+    e = param_long_launch(Rs, Vs, Es, T, N, false, part, slices, st);
+    if (e != cudaSuccess) return e;
+    return launch_param_finalize(part, slices, T, T, ga, gW, 1, err, st);
 }
 
 cudaError_t aligned_forward_launch(const float* x, const float* v0, const float* a_,
@@ -373,6 +481,15 @@ cudaError_t aligned_forward_launch(const float* x, const float* v0, const float*
             if (tau_pow2) aln_fwd_x2<16, true><<<g2, 256, 0, st>>>(a);
             else aln_fwd_x2<16, false><<<g2, 256, 0, st>>>(a);
         }
+        return cudaGetLastError();
+    }
+    if (T > 32) {
+        const unsigned gl = (unsigned)((N + kAlnLongThreads - 1) / kAlnLongThreads);
+        const size_t smem = sizeof(float) * (size_t)T * kAlnLongThreads;
+        auto k = tau_pow2 ? aln_fwd_long<true> : aln_fwd_long<false>;
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        k<<<gl, kAlnLongThreads, smem, st>>>(a);
         return cudaGetLastError();
     }
     const unsigned grid = (unsigned)((N + 255) / 256);

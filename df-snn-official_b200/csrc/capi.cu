@@ -84,8 +84,31 @@ int dfsnn_glmulti_forward(const float* x, const float* v0, const float* scale,
                                                      (cudaStream_t)stream));
 }
 
+}  // extern "C"
+
+namespace {
+
+// Long-history layout (T > 32): header, `slices` partial rows of T + T*T doubles, then three
+// [T, N] float scratch arrays, each starting on a 256-byte boundary.
+size_t long_part_bytes(int T, long long N) {
+    return (size_t)dfsnn::param_long_slices(T, N) * (size_t)(T + T * T) * sizeof(double);
+}
+size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
+size_t long_workspace_bytes(int T, long long N) {
+    return round256(kWsHeader + long_part_bytes(T, N)) + 3 * round256((size_t)T * N * sizeof(float));
+}
+
+int glmulti_backward_limit(int full_history) {
+    return full_history ? DFSNN_MAX_T_FULL : DFSNN_MAX_T;
+}
+
+}  // namespace
+
+extern "C" {
+
 size_t dfsnn_glmulti_backward_workspace_size(int T, long long N, int full_history) {
-    if (T < 1 || T > DFSNN_MAX_T_FULL || N < 0) return 0;
+    if (T < 1 || T > glmulti_backward_limit(full_history) || N < 0) return 0;
+    if (T > 32) return long_workspace_bytes(T, N);
     const int b1 = dfsnn::glmulti_bwd_blocks(T, N, full_history != 0, true);
     const int b2 = dfsnn::glmulti_bwd_blocks(T, N, full_history != 0, false);
     const int b = b1 > b2 ? b1 : b2;
@@ -98,19 +121,29 @@ int dfsnn_glmulti_backward(const float* grad_spike, const float* x, const float*
                            long long N, float tau, float threshold, float surrogate_scale,
                            int full_history, void* workspace, size_t workspace_bytes,
                            void* stream) {
-    if (int s = check_seq(T, N, DFSNN_MAX_T_FULL)) return s;
+    if (int s = check_seq(T, N, glmulti_backward_limit(full_history))) return s;
     if (!scale || !weights) return DFSNN_ERR_NULL;
     if (N > 0 && (!grad_spike || !x || !v0 || !grad_x || !grad_v0)) return DFSNN_ERR_NULL;
     if (!valid_tau(tau) || !finite(threshold) || !finite(surrogate_scale)) return DFSNN_ERR_PARAM;
     if (!workspace || !aligned8(workspace)) return DFSNN_ERR_WORKSPACE;
     const bool p2 = tau_is_pow2(tau);
+    char* ws = static_cast<char*>(workspace);
+    if (T > 32) {
+        if (workspace_bytes < long_workspace_bytes(T, N)) return DFSNN_ERR_WORKSPACE;
+        const size_t scratch_off = round256(kWsHeader + long_part_bytes(T, N));
+        return cuda_status(dfsnn::glmulti_backward_long_launch(
+            grad_spike, x, v0, scale, weights, grad_x, grad_v0, grad_scale, grad_weights, T, N,
+            tau, threshold, surrogate_scale, full_history != 0, p2,
+            reinterpret_cast<double*>(ws + kWsHeader), dfsnn::param_long_slices(T, N),
+            reinterpret_cast<float*>(ws + scratch_off), reinterpret_cast<unsigned int*>(ws),
+            (cudaStream_t)stream));
+    }
     const size_t stride = (size_t)dfsnn::glmulti_part_stride(T) * sizeof(double);
     long long nb = dfsnn::glmulti_bwd_blocks(T, N, full_history != 0, p2);
     const long long cap =
         workspace_bytes > kWsHeader ? (long long)((workspace_bytes - kWsHeader) / stride) : 0;
     if (cap < 1) return DFSNN_ERR_WORKSPACE;
     if (nb > cap) nb = cap;
-    char* ws = static_cast<char*>(workspace);
     return cuda_status(dfsnn::glmulti_backward_launch(
         grad_spike, x, v0, scale, weights, grad_x, grad_v0, grad_scale, grad_weights, T, N, tau,
         threshold, surrogate_scale, full_history != 0, p2,
@@ -134,6 +167,7 @@ int dfsnn_aligned_forward(const float* x, const float* v0, const float* a,
 
 size_t dfsnn_aligned_backward_workspace_size(int T, long long N) {
     if (T < 1 || T > DFSNN_MAX_T_FULL || N < 0) return 0;
+    if (T > 32) return long_workspace_bytes(T, N);
     const int b1 = dfsnn::aligned_bwd_blocks(T, N, true);
     const int b2 = dfsnn::aligned_bwd_blocks(T, N, false);
     const int b = b1 > b2 ? b1 : b2;
@@ -152,13 +186,22 @@ int dfsnn_aligned_backward(const float* grad_spike, const float* x, const float*
         return DFSNN_ERR_PARAM;
     if (!workspace || !aligned8(workspace)) return DFSNN_ERR_WORKSPACE;
     const bool p2 = tau_is_pow2(tau);
+    char* ws = static_cast<char*>(workspace);
+    if (T > 32) {
+        if (workspace_bytes < long_workspace_bytes(T, N)) return DFSNN_ERR_WORKSPACE;
+        const size_t scratch_off = round256(kWsHeader + long_part_bytes(T, N));
+        return cuda_status(dfsnn::aligned_backward_long_launch(
+            grad_spike, x, v0, a, weights, grad_x, grad_v0, grad_a, grad_weights, T, N, tau,
+            threshold, surrogate_scale, rho, p2, reinterpret_cast<double*>(ws + kWsHeader),
+            dfsnn::param_long_slices(T, N), reinterpret_cast<float*>(ws + scratch_off),
+            reinterpret_cast<unsigned int*>(ws), (cudaStream_t)stream));
+    }
     const size_t stride = (size_t)dfsnn::aligned_part_stride(T) * sizeof(double);
     long long nb = dfsnn::aligned_bwd_blocks(T, N, p2);
     const long long cap =
         workspace_bytes > kWsHeader ? (long long)((workspace_bytes - kWsHeader) / stride) : 0;
     if (cap < 1) return DFSNN_ERR_WORKSPACE;
     if (nb > cap) nb = cap;
-    char* ws = static_cast<char*>(workspace);
     return cuda_status(dfsnn::aligned_backward_launch(
         grad_spike, x, v0, a, weights, grad_x, grad_v0, grad_a, grad_weights, T, N, tau,
         threshold, surrogate_scale, rho, p2, reinterpret_cast<double*>(ws + kWsHeader),

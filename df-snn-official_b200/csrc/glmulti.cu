@@ -669,6 +669,67 @@ __global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
 }
 
 // ------------------------------------------------------------------------------------
+// backward, 32 < T <= 256 (full history T <= 64): one thread per neuron, history in shared
+// memory ([T][64] floats per block; the full-history adjoint sums another [T][64]).  The
+// recompute is the forward's pull-form sum (glm_fwd_smem), the reverse sweep is the
+// reference's loop; v_t, the drift and grad_pre go to [T, N] scratch for param_long.
+// ------------------------------------------------------------------------------------
+constexpr int kLongThreads = 64;
+
+template <bool FULL, bool TP2>
+__global__ void __launch_bounds__(kLongThreads) glm_bwd_long(GlmArgs a, float* Vs, float* Ds,
+                                                             float* Gs) {
+    extern __shared__ float sh[];
+    const long long n = (long long)blockIdx.x * kLongThreads + threadIdx.x;
+    if (n >= a.N) return;
+    const long long N = a.N;
+    const int T = a.T;
+    float* vh = sh + threadIdx.x;
+    float* A = sh + (size_t)T * kLongThreads + threadIdx.x;
+    float v = a.v0[n];
+    for (int t = 0; t < T; ++t) {
+        const float d = div_tau<TP2>(__fsub_rn(ld_stream(a.x + t * N + n), v), a.tau, a.inv_tau);
+        const float* wrow = a.W + (size_t)t * T;
+        float hist = 0.0f;
+        for (int i = 0; i < t; ++i) hist = __fmaf_rn(__ldg(wrow + i), vh[i * kLongThreads], hist);
+        const float p = __fmaf_rn(__ldg(a.scale + t), d, -hist);
+        const float z = __fsub_rn(p, a.th);
+        v = (p >= a.th) ? z : p;                     // p - spike*th, spike*th exactly th or 0
+        vh[t * kLongThreads] = v;
+        Vs[t * N + n] = v;
+        Ds[t * N + n] = d;
+        Gs[t * N + n] = surrogate_fma(z, a.sg);
+    }
+    if constexpr (FULL) {
+        for (int t = 0; t < T; ++t) A[t * kLongThreads] = 0.0f;
+        float ginit = 0.0f;
+        for (int t = T - 1; t >= 0; --t) {
+            const float gp = __fmaf_rn(ld_stream(a.gS + t * N + n), Gs[t * N + n], A[t * kLongThreads]);
+            Gs[t * N + n] = gp;
+            const float gd = __fmul_rn(gp, __ldg(a.scale + t));
+            const float gx = div_tau<TP2>(gd, a.tau, a.inv_tau);
+            st_stream(a.gx + t * N + n, gx);
+            if (t == 0) ginit = __fsub_rn(ginit, gx);            // + (-gd)/tau == -gx exactly
+            else A[(t - 1) * kLongThreads] = __fsub_rn(A[(t - 1) * kLongThreads], gx);
+            const float* wrow = a.W + (size_t)t * T;
+            for (int i = 0; i < t; ++i)
+                A[i * kLongThreads] = __fmaf_rn(-__ldg(wrow + i), gp, A[i * kLongThreads]);
+        }
+        a.gv0[n] = ginit;
+    } else {
+        float gvn = 0.0f;
+        for (int t = T - 1; t >= 0; --t) {
+            const float gp = __fmaf_rn(ld_stream(a.gS + t * N + n), Gs[t * N + n], gvn);
+            Gs[t * N + n] = gp;
+            const float gx = div_tau<TP2>(__fmul_rn(gp, __ldg(a.scale + t)), a.tau, a.inv_tau);
+            st_stream(a.gx + t * N + n, gx);
+            gvn = -gx;                                            // ((-gp)*s)/tau, exactly
+        }
+        a.gv0[n] = gvn;
+    }
+}
+
+// ------------------------------------------------------------------------------------
 // sum the per-block partials in a fixed order: gs (T) and gW (T x T, negated)
 // ------------------------------------------------------------------------------------
 __global__ void param_finalize(const double* part, int nblocks, int TB, int T, float* gscale,
@@ -798,8 +859,40 @@ int glmulti_bwd_blocks(int T, long long N, bool, bool) {
 }
 
 int glmulti_part_stride(int T) {
+    if (T > 32) return T + T * T;
     const int TB = tb_bucket(T);
     return TB + TB * TB;
+}
+
+cudaError_t glmulti_backward_long_launch(const float* gS, const float* x, const float* v0,
+                                         const float* scale, const float* W, float* gx,
+                                         float* gv0, float* gscale, float* gW, int T, long long N,
+                                         float tau, float th, float sg, bool full, bool tau_pow2,
+                                         double* part, int slices, float* scratch,
+                                         unsigned int* err, cudaStream_t st) {
+    GlmArgs a{};
+    a.x = x; a.v0 = v0; a.scale = scale; a.W = W; a.gS = gS; a.gx = gx; a.gv0 = gv0;
+    a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau; a.th = th; a.sg = sg;
+    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(unsigned int), st);
+    if (e != cudaSuccess) return e;
+    float* Vs = scratch;
+    float* Ds = scratch + (size_t)T * N;
+    float* Gs = scratch + 2 * (size_t)T * N;
+    if (N > 0) {
+        const size_t smem = sizeof(float) * (size_t)(full ? 2 : 1) * T * kLongThreads;
+        const unsigned grid = (unsigned)((N + kLongThreads - 1) / kLongThreads);
+        auto k = full ? (tau_pow2 ? glm_bwd_long<true, true> : glm_bwd_long<true, false>)
+                      : (tau_pow2 ? glm_bwd_long<false, true> : glm_bwd_long<false, false>);
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        k<<<grid, kLongThreads, smem, st>>>(a, Vs, Ds, Gs);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    if (!gscale && !gW) return cudaSuccess;
+    e = param_long_launch(Gs, Vs, Ds, T, N, true, part, slices, st);
+    if (e != cudaSuccess) return e;
+    return launch_param_finalize(part, slices, T, T, gscale, gW, 0, err, st);
 }
 
 cudaError_t glmulti_forward_launch(const float* x, const float* v0, const float* scale,

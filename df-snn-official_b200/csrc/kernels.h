@@ -23,6 +23,24 @@ cudaError_t glmulti_backward_launch(const float* gS, const float* x, const float
 cudaError_t launch_param_finalize(const double* part, int nblocks, int TB, int T, float* gscale,
                                   float* gW, int lower_only, const unsigned int* err,
                                   cudaStream_t st);
+// long-history backward (32 < T <= 256; full history T <= 64): scratch holds three [T, N]
+// float arrays (v, drift, grad_pre); part holds `slices` rows of T + T*T doubles
+cudaError_t glmulti_backward_long_launch(const float* gS, const float* x, const float* v0,
+                                         const float* scale, const float* W, float* gx,
+                                         float* gv0, float* gscale, float* gW, int T, long long N,
+                                         float tau, float th, float sg, bool full, bool tau_pow2,
+                                         double* part, int slices, float* scratch,
+                                         unsigned int* err, cudaStream_t st);
+cudaError_t aligned_backward_long_launch(const float* g, const float* x, const float* v0,
+                                         const float* a_, const float* W, float* gx, float* gv0,
+                                         float* ga, float* gW, int T, long long N, float tau,
+                                         float th, float sg, float rho, bool tau_pow2,
+                                         double* part, int slices, float* scratch,
+                                         unsigned int* err, cudaStream_t st);
+// gs / gW partial rows from [T, N] scratch (param_long.cu)
+int param_long_slices(int T, long long N);
+cudaError_t param_long_launch(const float* G, const float* V, const float* E, int T, long long N,
+                              bool diag_product, double* part, int slices, cudaStream_t st);
 // true when the x / grad / v0 tiles can be staged with cp.async.bulk (16-byte rows)
 bool bulk_eligible(const void* p, const void* q, const void* r, long long N);
 

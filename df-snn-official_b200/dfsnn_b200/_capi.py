@@ -19,7 +19,7 @@ DFSNN_ERR_SCHEME = 6
 DFSNN_ERR_PARAM = 7
 
 MAX_T = 256
-MAX_T_FULL = 32
+MAX_T_FULL = 64
 
 GL, TRAP, PREDICTOR, GL1 = 0, 1, 2, 3
 

@@ -30,8 +30,6 @@ class AlignedGLMulti(torch.autograd.Function):
     def forward(ctx, x, v, a, w, tau, th, sg, batch, full=False):
         if not full or not 0 < x.shape[0] <= 64:
             raise ValueError("Requires full history and 1<=T<=64")
-        if x.shape[0] > _capi.MAX_T_FULL:
-            raise ValueError(f"aligned glmulti on B200 currently supports T <= {_capi.MAX_T_FULL}")
         if not x.is_cuda:
             raise RuntimeError("AlignedGLMulti requires CUDA tensors")
         CALLS["forward"] += 1

@@ -166,8 +166,6 @@ class LIFFDEGLMultiFunction(torch.autograd.Function):
             raise ValueError("Full glmulti history gradients currently support T <= 64")
         if scale_f32.shape != (T,) or weights_f32.shape != (T, T):
             raise ValueError("glmulti scale/weights must have shapes [T] and [T,T]")
-        if T > _capi.MAX_T_FULL and any(ctx.needs_input_grad[:4]):
-            raise ValueError(f"glmulti backward on B200 currently supports T <= {_capi.MAX_T_FULL}")
         spike = torch.empty_like(x_f32)
         with torch.cuda.device(x_f32.device), _prof.native_call(
                 "glmulti_forward", 1, _prof.glmulti_forward_bytes(T, N), x_f32.device):

@@ -42,7 +42,7 @@ extern "C" {
 #define DFSNN_ERR_PARAM 7       /* tau == 0 or a non-finite scalar parameter */
 
 #define DFSNN_MAX_T 256         /* forward / truncated limit (reference: 256-entry locals) */
-#define DFSNN_MAX_T_FULL 32     /* full-history glmulti and aligned backward (reference: 64) */
+#define DFSNN_MAX_T_FULL 64     /* full-history glmulti backward and aligned glmulti (as the reference) */
 
 /* scheme ids of the single-order family */
 #define DFSNN_GL 0
@@ -66,14 +66,17 @@ int dfsnn_glmulti_forward(const float* x, const float* v0, const float* scale,
                           const float* weights, float* spike, int T, long long N, float tau,
                           float threshold, void* stream);
 
-/* Bytes of device workspace dfsnn_glmulti_backward needs (8-byte aligned). */
+/* Bytes of device workspace dfsnn_glmulti_backward needs (8-byte aligned); 0 when T is
+ * outside the limit for this history mode. */
 size_t dfsnn_glmulti_backward_workspace_size(int T, long long N, int full_history);
 
 /* Replaces LIFFDEGLMultiFunction.backward (fde_cupy_kernels_all.py:1973-2011): the
  * lif_fde_glmulti_backward_kernel (:1845-1875, full_history=0) or
  * lif_fde_glmulti_full_backward_kernel (:1877-1913, full_history=1) launch, then
  * grad_scale[t] = sum_n grad_pre*drift and grad_weights = -grad_pre @ v_hist^T (full T x T).
- * grad_scale / grad_weights may be NULL (not needed).  T <= DFSNN_MAX_T_FULL. */
+ * grad_scale / grad_weights may be NULL (not needed).  T <= DFSNN_MAX_T_FULL with
+ * full_history (the reference's limit), T <= DFSNN_MAX_T without.  For T > 32 the workspace
+ * also holds three [T, N] float arrays (v, drift, grad_pre) for the parameter reduction. */
 int dfsnn_glmulti_backward(const float* grad_spike, const float* x, const float* v0,
                            const float* scale, const float* weights, float* grad_x,
                            float* grad_v0, float* grad_scale, float* grad_weights, int T,

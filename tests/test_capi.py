@@ -60,8 +60,15 @@ def test_glmulti_validation(L):
     args = [FAKE] * 9 + [16, 100, 2.0, 1.0, 5.0, 1]
     assert b(*args, None, 1 << 20, None) == _capi.DFSNN_ERR_WORKSPACE
     assert b(*args, ctypes.c_void_p(0x1004), 1 << 20, None) == _capi.DFSNN_ERR_WORKSPACE
-    bad_t = [FAKE] * 9 + [33, 100, 2.0, 1.0, 5.0, 1]
+    bad_t = [FAKE] * 9 + [65, 100, 2.0, 1.0, 5.0, 1]        # full history: T <= 64
     assert b(*bad_t, FAKE, 1 << 20, None) == _capi.DFSNN_ERR_T_LIMIT
+    bad_t = [FAKE] * 9 + [257, 100, 2.0, 1.0, 5.0, 0]       # truncated: T <= 256
+    assert b(*bad_t, FAKE, 1 << 20, None) == _capi.DFSNN_ERR_T_LIMIT
+    assert L.dfsnn_glmulti_backward_workspace_size(65, 100, 1) == 0
+    assert L.dfsnn_glmulti_backward_workspace_size(65, 100, 0) > 3 * 65 * 100 * 4
+    long_ws = L.dfsnn_glmulti_backward_workspace_size(64, 100, 1)
+    ok_t = [FAKE] * 9 + [64, 100, 2.0, 1.0, 5.0, 1]         # too small a workspace: rejected
+    assert b(*ok_t, FAKE, long_ws - 1, None) == _capi.DFSNN_ERR_WORKSPACE
     no_w = [FAKE] * 4 + [None] + [FAKE] * 4 + [16, 100, 2.0, 1.0, 5.0, 1]
     assert b(*no_w, FAKE, 1 << 20, None) == _capi.DFSNN_ERR_NULL
 
@@ -79,7 +86,8 @@ def test_single_validation(L):
 
 def test_aligned_and_euler_validation(L):
     f = L.dfsnn_aligned_forward
-    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 33, 10, 2.0, 1.0, None) == _capi.DFSNN_ERR_T_LIMIT
+    assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 65, 10, 2.0, 1.0, None) == _capi.DFSNN_ERR_T_LIMIT
+    assert L.dfsnn_aligned_backward_workspace_size(65, 10) == 0
     e = L.dfsnn_direct_euler_backward
     args = [FAKE] * 10 + [16, 100, 2.0, 1.0, 1.0, 1.0, 5.0, 1.0]
     assert e(*args, FAKE, 8, None) == _capi.DFSNN_ERR_WORKSPACE

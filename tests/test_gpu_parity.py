@@ -143,13 +143,36 @@ def test_glmulti_on_side_stream():
     assert_bitwise(cpu(xt.grad), r["gx"], what="gx")
 
 
-def test_glmulti_backward_T_limit_raises():
-    x = torch.zeros(33, 10, device=DEV, requires_grad=True)
+@pytest.mark.parametrize("T,full", [(65, True), (257, False)])
+def test_glmulti_T_limit_raises(T, full):
+    """Full history is limited to T <= 64 (as the reference); any history to T <= 256."""
+    x = torch.zeros(T, 10, device=DEV, requires_grad=True)
     with pytest.raises(ValueError):
         fde_kernels.LIFFDEGLMultiFunction.apply(x, torch.zeros(10, device=DEV),
-                                                torch.ones(33, device=DEV),
-                                                torch.zeros(33, 33, device=DEV), 2.0, TH, SG, 1,
-                                                False)
+                                                torch.ones(T, device=DEV),
+                                                torch.zeros(T, T, device=DEV), 2.0, TH, SG, 1,
+                                                full)
+
+
+@pytest.mark.parametrize("T,N,full", [(33, 1000, True), (48, 4099, True), (64, 2000, True),
+                                      (33, 1000, False), (64, 2000, False), (100, 777, False),
+                                      (256, 500, False)])
+@pytest.mark.parametrize("tau", [2.0, 1.7])
+@pytest.mark.parametrize("kind", ["toeplitz", "general"])
+def test_glmulti_long_history_vs_oracle(T, N, full, tau, kind):
+    """32 < T: shared-memory history kernels and the tiled parameter reduction."""
+    x, gS, _, v0 = rng_inputs(T * 1000 + N + 7, T, N)
+    scale, W = glmulti_tables(T, seed=T + 1, kind=kind)
+    r = O.glmulti_step(x, v0, scale, W, gS, tau, TH, SG, full)
+    xt, v0t, st, Wt = (cuda(z).requires_grad_(True) for z in (x, v0, scale, W))
+    s = fde_kernels.LIFFDEGLMultiFunction.apply(xt, v0t, st, Wt, tau, TH, SG, 1, full)
+    s.backward(cuda(gS))
+    torch.cuda.synchronize()
+    assert_bitwise(cpu(s), r["spike"], what="spike")
+    assert_bitwise(cpu(xt.grad), r["gx"], what="gx")
+    assert_bitwise(cpu(v0t.grad), r["gv0"], what="gv0")
+    assert_close(cpu(st.grad), r["gscale"], what="grad_scale")
+    assert_close(cpu(Wt.grad), r["gW"], what="grad_W")
 
 
 def test_glmulti_empty_and_direct_capi():
@@ -175,7 +198,8 @@ def test_glmulti_empty_and_direct_capi():
 # -------------------------------------------------------------------------------------
 # aligned glmulti
 # -------------------------------------------------------------------------------------
-@pytest.mark.parametrize("T,N", [(T, N) for T in (1, 2, 5, 8, 11, 16, 24, 32) for N in (1, 300, 2049)])
+@pytest.mark.parametrize("T,N", [(T, N) for T in (1, 2, 5, 8, 11, 16, 24, 32) for N in (1, 300, 2049)]
+                         + [(33, 300), (40, 2049), (64, 1000)])
 @pytest.mark.parametrize("tau", [2.0, 1.3])
 @pytest.mark.parametrize("kind", ["toeplitz", "general"])
 def test_aligned_vs_oracle(T, N, tau, kind):
