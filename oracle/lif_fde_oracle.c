@@ -410,6 +410,19 @@ void orc_euler_backward(const float* gS, const float* gzf, const float* x, const
     free(part);
 }
 
+/* Set the OpenMP thread count of the calling thread's later parallel regions (the oracle's and
+ * those of any library sharing this OpenMP runtime, e.g. the host build of the reference
+ * kernels).  Launchers such as torchrun export OMP_NUM_THREADS=1; the CPU baseline overrides it
+ * with every host thread it may use. */
+void orc_set_num_threads(int n) {
+#ifdef _OPENMP
+    extern void omp_set_num_threads(int);
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 /* Number of OpenMP threads the oracle runs with (for the cpu_baseline "cores" field). */
 int orc_num_threads(void) {
 #ifdef _OPENMP

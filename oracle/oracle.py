@@ -51,6 +51,8 @@ def lib():
         L.orc_euler_forward.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i64] + [_f] * 8
         L.orc_euler_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i64] + [_f] * 6
         L.orc_num_threads.restype = _i
+        L.orc_set_num_threads.argtypes = [_i]
+        L.orc_set_num_threads.restype = None
         _lib = L
     return _lib
 
@@ -84,6 +86,11 @@ def ref():
 
 def num_threads():
     return int(lib().orc_num_threads())
+
+
+def set_num_threads(n):
+    """OpenMP threads for the oracle and the host build of the reference kernels."""
+    lib().orc_set_num_threads(int(n))
 
 
 def _c(a, dtype=np.float32):
