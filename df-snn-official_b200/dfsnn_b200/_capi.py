@@ -54,6 +54,8 @@ SIGNATURES = {
     "dfsnn_direct_euler_backward": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _ll, _f, _f,
                                          _f, _f, _f, _f, _p, _sz, _p]),
     "dfsnn_check_surrogate_quotient": (_i, [_p, _i, _i, _i, _p, _p]),
+    "dfsnn_glmulti_schedule_forward": (_i, [_p, _p, _p, _i, _i, _i, _p, _p, _p, _p]),
+    "dfsnn_glmulti_schedule_backward": (_i, [_p, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p]),
 }
 
 _lib = None

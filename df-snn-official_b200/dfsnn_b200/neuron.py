@@ -163,10 +163,27 @@ class LIFNeuronFDE(nn.Module):
         b = self.get_beta()
         return b.detach().item() if isinstance(b, torch.Tensor) else b
 
+    def _reset_state(self, like):
+        """A tensor shaped like `like` holding v_reset (float32 unless `like` says otherwise).
+
+        The reference allocates and fills a fresh tensor on every reset and after every glmulti
+        forward (one [N] fill each).  Here one filled tensor per shape is kept and handed out
+        again while nobody has written to it (its version counter is unchanged); a tensor that
+        was modified in place is replaced by a new one, never refilled, so tensors saved for a
+        backward are never touched."""
+        key = (tuple(like.shape), like.device, like.dtype)
+        cache = self.__dict__.setdefault("_reset_cache", {})
+        got = cache.get(key)
+        if got is not None and got[0]._version == got[1]:
+            return got[0]
+        t = torch.full_like(like, float(self.v_reset)).detach()
+        cache[key] = (t, t._version)
+        return t
+
     def reset(self):
         self.k = 0
         if isinstance(self.v, torch.Tensor):
-            self.v = torch.full_like(self.v, self.v_reset).detach()
+            self.v = self._reset_state(self.v)
         else:
             self.v = self.v_reset
         if self.store_v_seq:
@@ -174,12 +191,22 @@ class LIFNeuronFDE(nn.Module):
 
     # -- schedules ---------------------------------------------------------------------
     def _build_glmulti_schedule(self, T, device):
-        coefficient = self.get_multi_coefficient()
+        # Softplus-constrained (or unconstrained) masses: one native launch per direction
+        # (GLMultiScheduleFunction, bit-identical forward); softmax keeps PyTorch's chain.
+        fused = device.type == "cuda" and (self.coefficient_constraint != "softmax"
+                                           or not self.learn_coefficient)
+        if fused:
+            if self.learn_coefficient and self.coefficient_constraint == "softplus":
+                src, constraint = self.multi_coefficient_raw, 1
+            else:
+                src, constraint = self.multi_coefficient, 0
+        else:
+            src = self.get_multi_coefficient()
         if torch.is_grad_enabled() and self.learn_coefficient:
             update = self._coefficient_forward_count % self.coefficient_update_interval == 0
             self._coefficient_forward_count += 1
             if not update:
-                coefficient = coefficient.detach()
+                src = src.detach()
         if T != self.T:
             raise ValueError(f"glmulti was initialized for T={self.T}, got T={T}")
         basis = self._glmulti_basis.to(device=device, dtype=torch.float32)
@@ -187,7 +214,11 @@ class LIFNeuronFDE(nn.Module):
         cache = self.__dict__.setdefault("_h_pow_cache", {})
         if key not in cache:
             cache[key] = _sched.h_pow_neg_beta(self.h, self.multi_beta, device)
-        return _sched.build_glmulti_schedule(coefficient, self.multi_beta, basis, self.h, T,
+        if fused:
+            scale, weights = _sched.GLMultiScheduleFunction.apply(
+                src.to(device), basis, cache[key], constraint)
+            return {"scale": scale, "weights": weights}
+        return _sched.build_glmulti_schedule(src, self.multi_beta, basis, self.h, T,
                                              h_pow=cache[key])
 
     def _compute_weights(self, T, device, dtype):
@@ -228,7 +259,7 @@ class LIFNeuronFDE(nn.Module):
         x_flat = x_seq.flatten(1)
         if isinstance(self.v, torch.Tensor) and self.v.shape == x_seq[0].shape:
             return x_flat, self.v.flatten().float()
-        return x_flat, torch.full_like(x_flat[0], float(self.v_reset), dtype=torch.float32)
+        return x_flat, self._reset_state(x_flat[0].float())
 
     def _multi_step_forward_glmulti(self, x_seq):
         T = x_seq.shape[0]
@@ -238,7 +269,7 @@ class LIFNeuronFDE(nn.Module):
             x_flat, v_init, terms["scale"], terms["weights"], float(self.get_tau()),
             float(self.threshold), float(self.surrogate_grad_scale), x_seq.shape[1],
             self.glmulti_history_grad == "full")
-        self.v = torch.full_like(x_seq[0], float(self.v_reset)).detach()
+        self.v = self._reset_state(x_seq[0])
         self.k = T
         return spike_flat.reshape_as(x_seq)
 

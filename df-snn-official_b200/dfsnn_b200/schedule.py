@@ -70,6 +70,52 @@ def build_glmulti_schedule(coefficient, multi_beta, basis, h, T, h_pow=None):
     return {"scale": c0_inv.expand(T), "weights": weights}
 
 
+class GLMultiScheduleFunction(torch.autograd.Function):
+    """(scale[T], W[T,T]) of build_glmulti_schedule in one native launch per direction.
+
+    src is the raw Softplus parameter (constraint 1) or the masses themselves (constraint 0);
+    basis [J, T+1] and h_pow [J] as above.  The forward is bit-identical to the PyTorch chain
+    above (same fp32 operations); the backward returns grad_src accumulated in double."""
+
+    @staticmethod
+    def forward(ctx, src, basis, h_pow, constraint):
+        from . import _capi
+        src_f = src.detach().float().contiguous()
+        basis_f = basis.float().contiguous()
+        hp = h_pow.float().contiguous()
+        J, T1 = basis_f.shape
+        T = T1 - 1
+        dev = src_f.device
+        scale = torch.empty(T, device=dev, dtype=torch.float32)
+        W = torch.empty((T, T), device=dev, dtype=torch.float32)
+        ct = torch.empty(T + 1, device=dev, dtype=torch.float32)
+        with torch.cuda.device(dev):
+            code = _capi.lib().dfsnn_glmulti_schedule_forward(
+                _capi.ptr(src_f), _capi.ptr(basis_f), _capi.ptr(hp), J, T, int(constraint),
+                _capi.ptr(scale), _capi.ptr(W), _capi.ptr(ct), _capi.stream_of(src_f))
+        _capi.check(code, "glmulti schedule forward")
+        ctx.save_for_backward(src_f, basis_f, hp, ct)
+        ctx.constraint = int(constraint)
+        ctx.src_dtype = src.dtype
+        return scale, W
+
+    @staticmethod
+    def backward(ctx, grad_scale, grad_W):
+        from . import _capi
+        src_f, basis_f, hp, ct = ctx.saved_tensors
+        J, T1 = basis_f.shape
+        gs = None if grad_scale is None else grad_scale.float().contiguous()
+        gw = None if grad_W is None else grad_W.float().contiguous()
+        grad = torch.empty(J, device=src_f.device, dtype=torch.float32)
+        with torch.cuda.device(src_f.device):
+            code = _capi.lib().dfsnn_glmulti_schedule_backward(
+                _capi.ptr(src_f), _capi.ptr(basis_f), _capi.ptr(hp), _capi.ptr(ct),
+                _capi.ptr(gs), _capi.ptr(gw), J, T1 - 1, ctx.constraint, _capi.ptr(grad),
+                _capi.stream_of(src_f))
+        _capi.check(code, "glmulti schedule backward")
+        return grad.to(ctx.src_dtype), None, None, None
+
+
 def gl_weights(beta_val, T, device=None, dtype=torch.float32):
     c = torch.zeros(T + 1, device=device, dtype=dtype)
     c[0] = 1

@@ -66,6 +66,24 @@ int dfsnn_glmulti_forward(const float* x, const float* v0, const float* scale,
                           const float* weights, float* spike, int T, long long N, float tau,
                           float threshold, void* stream);
 
+/* glmulti schedule (LIFNeuronFDE._get_glmulti_weights + _build_glmulti_schedule,
+ * neuron.py:1461-1514) in one launch: masses m = softplus(raw) (constraint 1) or raw
+ * (constraint 0), c~[k] = sum_j m_j h_pow[j] basis[j][k] (k = 0..T), scale[t] = 1/c~[0],
+ * weights[t][i] = c~[t-i]/c~[0] for i < t, else 0.  Same fp32 operations as the reference's
+ * PyTorch chain, so scale and weights are bit-identical to it.  basis is [J][T+1], c_tilde
+ * (T+1 floats) is kept for the backward.  J <= 16, T <= DFSNN_MAX_T. */
+int dfsnn_glmulti_schedule_forward(const float* raw, const float* basis, const float* h_pow,
+                                   int J, int T, int constraint, float* scale, float* weights,
+                                   float* c_tilde, void* stream);
+
+/* Gradient of the schedule with respect to raw (J floats) given grad_scale [T] and
+ * grad_weights [T][T] (either may be NULL = zero); upper-triangle entries of grad_weights
+ * are ignored (the reference's torch.where discards them).  Accumulated in double. */
+int dfsnn_glmulti_schedule_backward(const float* raw, const float* basis, const float* h_pow,
+                                    const float* c_tilde, const float* grad_scale,
+                                    const float* grad_weights, int J, int T, int constraint,
+                                    float* grad_raw, void* stream);
+
 /* Bytes of device workspace dfsnn_glmulti_backward needs (8-byte aligned); 0 when T is
  * outside the limit for this history mode. */
 size_t dfsnn_glmulti_backward_workspace_size(int T, long long N, int full_history);

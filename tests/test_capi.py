@@ -112,3 +112,16 @@ def test_quotient_check_validates_before_launch():
     assert L.dfsnn_check_surrogate_quotient(fake, 1, 127, 128, fake, None) == _capi.DFSNN_ERR_PARAM
     assert L.dfsnn_check_surrogate_quotient(fake, 1, 128, 192, fake, None) == _capi.DFSNN_ERR_PARAM
     assert L.dfsnn_check_surrogate_quotient(fake, 0, 128, 128, fake, None) == _capi.DFSNN_ERR_PARAM
+
+
+def test_schedule_validation_before_launch():
+    L = _capi.lib()
+    F = ctypes.c_void_p(16)
+    f, b = L.dfsnn_glmulti_schedule_forward, L.dfsnn_glmulti_schedule_backward
+    assert f(None, F, F, 3, 16, 1, F, F, F, None) == _capi.DFSNN_ERR_NULL
+    assert f(F, F, F, 0, 16, 1, F, F, F, None) == _capi.DFSNN_ERR_SHAPE
+    assert f(F, F, F, 17, 16, 1, F, F, F, None) == _capi.DFSNN_ERR_SHAPE
+    assert f(F, F, F, 3, 257, 1, F, F, F, None) == _capi.DFSNN_ERR_T_LIMIT
+    assert f(F, F, F, 3, 16, 2, F, F, F, None) == _capi.DFSNN_ERR_PARAM
+    assert b(F, F, F, F, None, None, 3, 16, 1, None, None) == _capi.DFSNN_ERR_NULL
+    assert b(F, F, F, F, None, None, 3, 0, 1, F, None) == _capi.DFSNN_ERR_SHAPE
