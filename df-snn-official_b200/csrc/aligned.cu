@@ -12,10 +12,13 @@
 // The forward writes only spikes (the reference also writes pred and hist: 12 B vs 4 B
 // per neuron-step); the backward is the same persistent, bulk-staged design as the glmulti
 // backward (glmulti.cu), reducing grad a / grad W in-kernel.
+#include <atomic>
+
 #include "bulk_pipe.cuh"
 #include "kernels.h"
 #include "pack2.cuh"
 #include "param_reduce.cuh"
+#include "warp_tile.cuh"
 
 namespace dfsnn {
 
@@ -103,9 +106,10 @@ __global__ void __launch_bounds__(256) aln_fwd_reg(AlnArgs a) {
     else aln_fwd_body<TB, TP2, false>(a, sW, sA, n);
 }
 
-// Forward, T <= TB <= 16, two neurons per thread with packed fp32x2 (Toeplitz schedule;
-// a general W runs the scalar body per neuron).  The history sum h is accumulated negated,
-// h' = h' + round(-w*v), so v = round(a*f) - h is one packed add.
+// Forward, T <= TB <= 16, two neurons per thread (Toeplitz schedule; a general W runs the
+// scalar body per neuron).  Products are packed; every sum that consumes a product is a
+// per-half scalar add (pack2.cuh).  The history sum h is accumulated negated,
+// h' = h' + round(-w*v), so v = round(a*f) - h is an add.
 template <int TB, bool TP2>
 __global__ void __launch_bounds__(256) aln_fwd_x2(AlnArgs a) {
     __shared__ float sW[TB * TB];
@@ -142,13 +146,14 @@ __global__ void __launch_bounds__(256) aln_fwd_x2(AlnArgs a) {
 #pragma unroll
     for (int t = 0; t < TB; ++t) {
         if (t < T) {
-            const float2 d = div_tau2<TP2>(sub2(xr[t], v), a.tau, inv2);
-            const float2 pred = add2(v, d);
+            // sums that consume a product are per-half scalar ops (pack2.cuh)
+            const float2 d = div_tau2<TP2>(ssub2(xr[t], v), a.tau, inv2);
+            const float2 pred = sadd2(v, d);
             const float2 s = fire2(pred, a.th);
-            const float2 f = add2(d, div_tau2<TP2>(mul2(s, mth), a.tau, inv2));   // d - s*th/tau
-            v = add2(mul2(a2, f), hn[t]);                            // a*f - h
+            const float2 f = sadd2(d, div_tau2<TP2>(smul2(s, mth), a.tau, inv2));   // d - s*th/tau
+            v = sadd2(pmul2(a2, f), hn[t]);                          // a*f - h
 #pragma unroll
-            for (int u = t + 1; u < TB; ++u) hn[u] = add2(hn[u], mul2(nw[u - t], v));
+            for (int u = t + 1; u < TB; ++u) hn[u] = sadd2(hn[u], pmul2(nw[u - t], v));
             st2_stream(a.spike + t * N + n, s);
         }
     }
@@ -311,22 +316,216 @@ __global__ void __launch_bounds__(256) aln_bwd(AlnArgs a) {
     prod.finish(reinterpret_cast<double*>(smem_raw), a.part + (size_t)blockIdx.x * ProdCfg<TB>::NOUT, tid);
 }
 
+// ------------------------------------------------------------------------------------
+// backward, T in {8, 16} exactly: the warp-tiled persistent design of glm_bwd_w
+// (warp_tile.cuh) with the aligned arithmetic: every product and sum separately rounded
+// (packed fp32x2 per neuron pair), IEEE divisions for the surrogate term and for e_t.
+// Stage X holds x_t, then v_t + h_t; G holds grad_spike_t, then grad_x_t; V0 holds v0,
+// then grad_v0.  GP receives the adjoint r_t, V the membrane v_t.
+// ------------------------------------------------------------------------------------
+// Reverse sweep of one aligned tile (SLOW: IEEE division for the surrogate term q_t).
+template <int T, bool TP2, bool FAST, bool SLOW>
+__device__ __forceinline__ void aln_bwd_warp_reverse(const AlnArgs& a, const float* sW,
+                                                     const float* sA, const float* sInvA,
+                                                     const float2 (&rw)[T], const float* X,
+                                                     float* G, float* V0, float* GP,
+                                                     const float2 (&den)[T], float2 (&gsa)[T]) {
+    constexpr int RS = WarpBwdCfg<T>::RS;
+    constexpr int TN = WarpBwdCfg<T>::TN;
+    const int c2 = 2 * (threadIdx.x & 31);
+    const float2 inv2 = f2(a.inv_tau), sg2 = f2(a.sg);
+    const float2 one_m2 = f2(__fsub_rn(1.0f, __fdiv_rn(1.0f, a.tau)));
+    float2 A[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) A[t] = f2(0.0f);
+#pragma unroll
+    for (int t = T - 1; t >= 0; --t) {
+        const float2 a2 = f2(FAST ? sA[0] : sA[t]);
+        const float2 gnum = pmul2(*reinterpret_cast<const float2*>(G + t * TN + c2), sg2);
+        const float2 q = quot2<SLOW>(gnum, den[t]);                     // (g*sg)/den, exact
+        const float2 r = A[t];
+        const float2 ra = pmul2(r, a2);
+        const float2 qa = sadd2(q, ra);
+        const float2 gx = TP2 ? pmul2(qa, inv2)
+                              : make_float2(__fdiv_rn(qa.x, a.tau), __fdiv_rn(qa.y, a.tau));
+        *reinterpret_cast<float2*>(G + t * TN + c2) = gx;
+        const float2 rat = TP2 ? pmul2(ra, inv2)
+                               : make_float2(__fdiv_rn(ra.x, a.tau), __fdiv_rn(ra.y, a.tau));
+        const float2 prev = ssub2(pmul2(q, one_m2), rat);
+        if (t) A[t - 1] = sadd2(A[t - 1], prev);
+        else *reinterpret_cast<float2*>(V0 + c2) = prev;
+#pragma unroll
+        for (int j = 0; j < t; ++j) {
+            const float2 rwj = FAST ? rw[t - j] : f2(__fmul_rn(a.rho, sW[t * T + j]));
+            A[j] = ssub2(A[j], pmul2(rwj, r));
+        }
+        *reinterpret_cast<float2*>(GP + t * RS + c2) = r;
+        // e_t = r_t (v_t + h_t) / a_t feeds only the grad_a reduction: product with the
+        // correctly rounded reciprocal of a_t (within an ulp of the quotient per term)
+        const float2 rx = pmul2(r, *reinterpret_cast<const float2*>(X + t * TN + c2));
+        gsa[t] = sadd2(gsa[t], pmul2(rx, f2(FAST ? sInvA[0] : sInvA[t])));
+    }
+}
+
+// One aligned tile: forward recompute (v -> V rows, v + h -> X, surrogate denominators in
+// registers), then the reverse sweep with the fast or the IEEE surrogate quotient.
+template <int T, bool TP2, bool FAST>
+__device__ __forceinline__ void aln_bwd_warp_tile(const AlnArgs& a, const float* sW, const float* sA,
+                                                  const float* sInvA, const float2 (&wr)[T],
+                                                  const float2 (&rw)[T], float* X, float* G,
+                                                  float* V0, float* GP, float* Vs,
+                                                  float2 (&gsa)[T]) {
+    constexpr int RS = WarpBwdCfg<T>::RS;
+    constexpr int TN = WarpBwdCfg<T>::TN;
+    const int c2 = 2 * (threadIdx.x & 31);
+    const float th = a.th;
+    const float2 th2 = f2(th), inv2 = f2(a.inv_tau), zc2 = f2(__fmul_rn(kAlignedPiHalf, a.sg));
+    const float sg = a.sg;
+    const float2 thr_tau = f2(div_tau<TP2>(th, a.tau, a.inv_tau));   // spike*th/tau for spike = 1
+    float2 v = *reinterpret_cast<const float2*>(V0 + c2);
+    float2 hs[T], den[T];
+    bool bad = false;
+#pragma unroll
+    for (int t = 0; t < T; ++t) hs[t] = f2(0.0f);
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const float2 a2 = f2(FAST ? sA[0] : sA[t]);
+        const float2 xs = *reinterpret_cast<const float2*>(X + t * TN + c2);
+        const float2 xm = ssub2(xs, v);
+        const float2 d = TP2 ? pmul2(xm, inv2)
+                             : make_float2(__fdiv_rn(xm.x, a.tau), __fdiv_rn(xm.y, a.tau));
+        const float2 pred = sadd2(v, d);
+        // f = d - spike*th/tau; spike*th/tau is exactly thr_tau or 0 (and d - 0 == d)
+        const float2 dm = ssub2(d, thr_tau);
+        const float2 f = make_float2(pred.x >= th ? dm.x : d.x, pred.y >= th ? dm.y : d.y);
+        const float2 h = hs[t];
+        v = ssub2(pmul2(a2, f), h);
+#pragma unroll
+        for (int u = t + 1; u < T; ++u) {
+            const float2 w = FAST ? wr[u - t] : f2(sW[u * T + t]);
+            hs[u] = sadd2(hs[u], pmul2(w, v));
+        }
+        const float2 z = pmul2(zc2, ssub2(pred, th2));
+        const float2 dn = pmul2(f2(2.0f), sadd2(f2(1.0f), pmul2(z, z)));
+        den[t] = dn;
+        const float2 g = *reinterpret_cast<const float2*>(G + t * TN + c2);
+        bad |= !(dn.x <= 0x1p64f) || !(dn.y <= 0x1p64f) ||
+               !quot_num_ok(__fmul_rn(g.x, sg)) || !quot_num_ok(__fmul_rn(g.y, sg));
+        *reinterpret_cast<float2*>(Vs + t * RS + c2) = v;
+        *reinterpret_cast<float2*>(X + t * TN + c2) = sadd2(v, h);     // v_t + h_t
+    }
+    if (__any_sync(0xffffffffu, bad))
+        aln_bwd_warp_reverse<T, TP2, FAST, true>(a, sW, sA, sInvA, rw, X, G, V0, GP, den, gsa);
+    else
+        aln_bwd_warp_reverse<T, TP2, FAST, false>(a, sW, sA, sInvA, rw, X, G, V0, GP, den, gsa);
+}
+
+template <int T, bool TP2>
+__global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
+    aln_bwd_w(AlnArgs a, const __grid_constant__ TileMaps m) {
+    using C = WarpBwdCfg<T>;
+    constexpr int RS = C::RS;
+    constexpr int TN = C::TN;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    __shared__ float sW[T * T];
+    __shared__ float sA[T];
+    __shared__ float sInvA[T];
+    __shared__ __align__(8) uint64_t bars[C::kWarps][2];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const long long N = a.N;
+    for (int e = tid; e < T * T; e += blockDim.x) sW[e] = a.W[e];
+    for (int e = tid; e < T; e += blockDim.x) {
+        sA[e] = a.a[e];
+        sInvA[e] = __frcp_rn(a.a[e]);
+    }
+    if (lane == 0) {
+        mbar_init(&bars[warp][0], 1);
+        mbar_init(&bars[warp][1], 1);
+        fence_mbar_init();
+    }
+    const bool fast = block_toeplitz(a.W, a.a, T);     // block barrier
+    unsigned char* aligned_smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    float* wbase = reinterpret_cast<float*>(aligned_smem) + warp * C::PER_WARP;
+    float* GP = wbase + 2 * C::STAGE;
+    float* Vs = GP + T * RS;
+    float2 wr[T], rw[T];
+#pragma unroll
+    for (int d = 0; d < T; ++d) {
+        const float w = (fast && d > 0) ? sW[d * T] : 0.0f;
+        wr[d] = f2(w);
+        rw[d] = f2(__fmul_rn(a.rho, w));                // (rho * w) as the reference rounds it
+    }
+    float2 pw[4][4];
+    float2 gsa[T];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) pw[r][c] = f2(0.0f);
+#pragma unroll
+    for (int t = 0; t < T; ++t) gsa[t] = f2(0.0f);
+    const long long ntiles = (N + TN - 1) / TN;
+    const long long first = (long long)blockIdx.x * C::kWarps + warp;
+    const long long stride = (long long)gridDim.x * C::kWarps;
+    if (lane == 0 && first < ntiles) warp_load<T>(wbase, &bars[warp][0], m, first * TN);
+    bool failed = false;
+    int j = 0;
+    for (long long tile = first; tile < ntiles; tile += stride, ++j) {
+        const int s = j & 1;
+        float* X = wbase + s * C::STAGE;
+        float* G = X + T * TN;
+        float* V0 = X + 2 * T * TN;
+        const bool ok = mbar_wait_bounded(&bars[warp][s], (uint32_t)((j >> 1) & 1));
+        if (__any_sync(0xffffffffu, !ok)) { failed = true; break; }
+        if (lane == 0 && tile + stride < ntiles)
+            warp_load<T>(wbase + (s ^ 1) * C::STAGE, &bars[warp][s ^ 1], m, (tile + stride) * TN);
+        // lanes past N compute on zero-filled inputs (finite); the stores clip them
+        if (fast) aln_bwd_warp_tile<T, TP2, true>(a, sW, sA, sInvA, wr, rw, X, G, V0, GP, Vs, gsa);
+        else aln_bwd_warp_tile<T, TP2, false>(a, sW, sA, sInvA, wr, rw, X, G, V0, GP, Vs, gsa);
+        __syncwarp();
+        warp_product<T>(GP, Vs, lane, pw);
+        warp_store<T>(X, m, tile * TN, lane);
+    }
+    if (lane == 0) {
+        if (failed) {
+            atomicOr(a.err, 1u);
+            mbar_wait_bounded(&bars[warp][j & 1], (uint32_t)((j >> 1) & 1));
+        }
+        bulk_wait_all();
+    }
+    warp_tiles_finish<T>(pw, gsa, aligned_smem, a.part, tid);
+}
+
 namespace {
 
 int tb_of(int T) { return T <= 8 ? 8 : (T <= 16 ? 16 : 32); }
 
-template <int TB>
-int aln_grid_t(long long N) {
+template <class K>
+int aln_resident(K k, size_t smem) {
     int dev = 0, sms = 0, per = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const size_t smem = AlnBwdSmem<TB>::kBytes;
-    auto k = aln_bwd<TB, false, true>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, kTile, smem);
     if (per < 1) per = 1;
+    return (sms < 1 ? 1 : sms) * per;
+}
+
+template <int TB>
+int aln_grid_t(long long N) {
+    static std::atomic<int> cached[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int res = (dev >= 0 && dev < 64) ? cached[dev].load(std::memory_order_relaxed) : 0;
+    if (res <= 0) {
+        if constexpr (TB == 8 || TB == 16)
+            res = aln_resident(aln_bwd_w<TB, false>, WarpBwdCfg<TB>::kBytes);
+        else
+            res = aln_resident(aln_bwd<TB, false, true>, AlnBwdSmem<TB>::kBytes);
+        if (dev >= 0 && dev < 64) cached[dev].store(res, std::memory_order_relaxed);
+    }
     const long long ntiles = (N + kTile - 1) / kTile;
-    long long g = (long long)sms * per;
+    long long g = res;
     if (g > ntiles) g = ntiles;
     return g < 1 ? 1 : (int)g;
 }
@@ -515,8 +714,21 @@ cudaError_t aligned_backward_launch(const float* g, const float* x, const float*
     a.rho = rho;
     cudaError_t e = cudaMemsetAsync(err, 0, sizeof(unsigned int), st);
     if (e != cudaSuccess) return e;
-    const bool bulk = bulk_eligible(x, g, v0, N);
     const int TB = tb_of(T);
+    TileMaps maps;
+    if ((T == 8 || T == 16) && encode_tile_maps(&maps, x, g, v0, gx, gv0, T, N)) {
+        auto k = T == 8 ? (tau_pow2 ? aln_bwd_w<8, true> : aln_bwd_w<8, false>)
+                        : (tau_pow2 ? aln_bwd_w<16, true> : aln_bwd_w<16, false>);
+        const size_t smem = T == 8 ? WarpBwdCfg<8>::kBytes : WarpBwdCfg<16>::kBytes;
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        k<<<nblocks, 256, smem, st>>>(a, maps);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        if (ga || gW) e = launch_param_finalize(part, nblocks, TB, T, ga, gW, 1, err, st);
+        return e;
+    }
+    const bool bulk = bulk_eligible(x, g, v0, N);
 #define DFSNN_AB(TBV)                                                                          \
     if (TB == TBV) {                                                                           \
         if (bulk) e = tau_pow2 ? aln_bwd_launch_t<TBV, true, true>(a, nblocks, st)             \

@@ -25,6 +25,7 @@
 #include "pack2.cuh"
 #include "param_reduce.cuh"
 #include "tma.cuh"
+#include "warp_tile.cuh"
 
 namespace dfsnn {
 
@@ -368,77 +369,6 @@ __global__ void __launch_bounds__(256) glm_bwd(GlmArgs a) {
 // neurons.  GP and V rows are padded to 72 floats, which makes the product's float4 reads
 // free of bank conflicts.
 // ------------------------------------------------------------------------------------
-struct alignas(64) GlmTmaMaps {
-    CUtensorMap x;    // [T, N], boxes T x 64 (loads)
-    CUtensorMap g;    // [T, N] grad_spike
-    CUtensorMap v0;   // [1, N], boxes 1 x 64
-    CUtensorMap gx;   // [T, N] grad_x (stores)
-    CUtensorMap gv0;  // [1, N] grad_v0
-};
-
-template <int T>
-struct WarpBwdCfg {
-    static constexpr int kWarps = 8;
-    static constexpr int TN = 64;                        // neurons per warp tile
-    static constexpr int RS = 72;                        // padded GP / V row stride (floats)
-    static constexpr int STAGE = 2 * T * TN + TN;        // dense X rows, G rows, v0 row
-    static constexpr int PER_WARP = 2 * STAGE + 2 * T * RS;   // two stages + GP + V rows
-    static constexpr size_t kBytes = sizeof(float) * kWarps * PER_WARP + 128;  // + alignment
-    static constexpr uint32_t kTxBytes = sizeof(float) * STAGE;
-    static constexpr int kMinBlocks = T <= 8 ? 2 : 1;    // blocks per SM the registers allow
-    static constexpr int NRED = 16 + T;                  // doubles per thread in the reduction
-    static constexpr int TBLK = T / 4;                   // 4-row blocks along t (and along i)
-    static constexpr int LANES_PER_SLICE = TBLK * TBLK;
-    static constexpr int NSLICES = 32 / LANES_PER_SLICE;
-    static constexpr int GROUPS = TN / (4 * NSLICES);    // float4 neuron groups per lane
-    static_assert(T == 8 || T == 16, "warp-tiled backward covers T = 8 and T = 16");
-    static_assert((sizeof(float) * STAGE) % 128 == 0 && (sizeof(float) * PER_WARP) % 128 == 0,
-                  "TMA destinations must stay 128-byte aligned");
-    static_assert(sizeof(double) * 32 * kWarps * NRED <= kBytes - 128, "reduction scratch");
-};
-
-// Arm stage X of this warp and copy its tile (lane 0).  The stage's previous contents
-// were fenced against the async proxy when its grad_x / grad_v0 store was issued; the
-// store must have finished reading the stage before the new copies land.
-template <int T>
-__device__ __forceinline__ void warp_load(float* X, uint64_t* bar, const GlmTmaMaps& m,
-                                          long long n0) {
-    constexpr int TN = WarpBwdCfg<T>::TN;
-    bulk_wait_read_all();
-    mbar_arrive_expect_tx(bar, WarpBwdCfg<T>::kTxBytes);
-    tma_load_rows(X, &m.x, (int)n0, bar);
-    tma_load_rows(X + T * TN, &m.g, (int)n0, bar);
-    tma_load_rows(X + 2 * T * TN, &m.v0, (int)n0, bar);
-}
-
-// Store the tile's grad_x rows (in G) and grad_v0 row (in V0) with TMA (columns past N
-// are clipped by the tensor maps).  All lanes fence their generic writes of the stage.
-template <int T>
-__device__ __forceinline__ void warp_store(float* X, const GlmTmaMaps& m, long long n0, int lane) {
-    constexpr int TN = WarpBwdCfg<T>::TN;
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-        tma_store_rows(&m.gx, X + T * TN, (int)n0);
-        tma_store_rows(&m.gv0, X + 2 * T * TN, (int)n0);
-        bulk_commit();
-    }
-}
-
-// sg / b per half: div_markstein in packed form, or the IEEE division (SLOW)
-template <bool SLOW>
-__device__ __forceinline__ float2 surrogate_quot2(float2 sg2, float2 b) {
-    if constexpr (SLOW) {
-        return make_float2(__fdiv_rn(sg2.x, b.x), __fdiv_rn(sg2.y, b.y));
-    } else {
-        const float2 nb = pmul2(b, f2(-1.0f));
-        const float2 y0 = make_float2(rcp_approx(b.x), rcp_approx(b.y));
-        const float2 y = pfma2(pfma2(nb, y0, f2(1.0f)), y0, y0);
-        const float2 q0 = pmul2(sg2, y);
-        return pfma2(pfma2(nb, q0, sg2), y, q0);
-    }
-}
-
 // Negated history weight of term (t, i) for both halves: registers (Toeplitz) or shared.
 template <int T, bool FAST>
 __device__ __forceinline__ float2 nwgt2(const float* sW, const float2 (&nw)[T], int t, int i) {
@@ -465,7 +395,7 @@ __device__ __forceinline__ void glm_bwd_warp_reverse(const GlmArgs& a, const flo
         float2 ginit = f2(0.0f);
 #pragma unroll
         for (int t = T - 1; t >= 0; --t) {
-            const float2 sur = surrogate_quot2<SLOW>(sg2, bden[t]);
+            const float2 sur = quot2<SLOW>(sg2, bden[t]);
             const float2 gs = *reinterpret_cast<const float2*>(G + t * TN + c2);
             const float2 gp = pfma2(gs, sur, A[t]);
             const float2 gd = pmul2(gp, f2(FAST ? sc : sScale[t]));
@@ -473,8 +403,8 @@ __device__ __forceinline__ void glm_bwd_warp_reverse(const GlmArgs& a, const flo
                                   : make_float2(__fdiv_rn(gd.x, a.tau), __fdiv_rn(gd.y, a.tau));
             *reinterpret_cast<float2*>(G + t * TN + c2) = gx;
             // the reference's (-gd)/tau is -gx exactly (round-to-nearest is symmetric)
-            if (t == 0) ginit = psub2(ginit, gx);
-            else A[t - 1] = psub2(A[t - 1], gx);
+            if (t == 0) ginit = ssub2(ginit, gx);                 // gx is a product: scalar
+            else A[t - 1] = ssub2(A[t - 1], gx);
 #pragma unroll
             for (int i = 0; i < t; ++i) A[i] = pfma2(nwgt2<T, FAST>(sW, nw, t, i), gp, A[i]);
             *reinterpret_cast<float2*>(GP + t * RS + c2) = gp;
@@ -485,7 +415,7 @@ __device__ __forceinline__ void glm_bwd_warp_reverse(const GlmArgs& a, const flo
         float2 gvn = f2(0.0f);
 #pragma unroll
         for (int t = T - 1; t >= 0; --t) {
-            const float2 sur = surrogate_quot2<SLOW>(sg2, bden[t]);
+            const float2 sur = quot2<SLOW>(sg2, bden[t]);
             const float2 gs = *reinterpret_cast<const float2*>(G + t * TN + c2);
             const float2 gp = pfma2(gs, sur, gvn);
             const float2 gd = pmul2(gp, f2(FAST ? sc : sScale[t]));
@@ -543,39 +473,9 @@ __device__ __forceinline__ void glm_bwd_warp_tile(const GlmArgs& a, const float*
         glm_bwd_warp_reverse<T, FULL, TP2, FAST, false>(a, sW, sScale, nw, sc, X, G, V0, GP, bden, gsa);
 }
 
-// pw[r][c] += sum over this lane's neurons of GP[t] * V[i], t = tr + TBLK*r,
-// i = tc + TBLK*c; each float4 group of neurons enters as two packed halves.
-template <int T>
-__device__ __forceinline__ void warp_product(const float* GP, const float* Vs, int lane,
-                                             float2 (&pw)[4][4]) {
-    using C = WarpBwdCfg<T>;
-    constexpr int RS = C::RS;
-    const int tr = lane % C::TBLK, tc = (lane / C::TBLK) % C::TBLK, sl = lane / C::LANES_PER_SLICE;
-#pragma unroll
-    for (int jj = 0; jj < C::GROUPS; ++jj) {
-        const int kb = 4 * (sl * C::GROUPS + jj);
-        float4 g[4], v[4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-            g[r] = *reinterpret_cast<const float4*>(GP + (tr + C::TBLK * r) * RS + kb);
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-            v[c] = *reinterpret_cast<const float4*>(Vs + (tc + C::TBLK * c) * RS + kb);
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const float2 g01 = make_float2(g[r].x, g[r].y), g23 = make_float2(g[r].z, g[r].w);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                pw[r][c] = fma2(g01, make_float2(v[c].x, v[c].y), pw[r][c]);
-                pw[r][c] = fma2(g23, make_float2(v[c].z, v[c].w), pw[r][c]);
-            }
-        }
-    }
-}
-
 template <int T, bool FULL, bool TP2>
 __global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
-    glm_bwd_w(GlmArgs a, const __grid_constant__ GlmTmaMaps m) {
+    glm_bwd_w(GlmArgs a, const __grid_constant__ TileMaps m) {
     using C = WarpBwdCfg<T>;
     constexpr int RS = C::RS;
     constexpr int TN = C::TN;
@@ -640,32 +540,7 @@ __global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
         }
         bulk_wait_all();   // stores complete before the stages are reused below
     }
-    // block reduction in double, fixed order, into this block's partial row
-    __syncthreads();
-    double* red = reinterpret_cast<double*>(aligned_smem);
-    double* mine = red + (size_t)tid * C::NRED;
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) mine[r * 4 + c] = (double)pw[r][c].x + (double)pw[r][c].y;
-#pragma unroll
-    for (int t = 0; t < T; ++t) mine[16 + t] = (double)gsa[t].x + (double)gsa[t].y;
-    __syncthreads();
-    double* part = a.part + (size_t)blockIdx.x * (T + T * T);
-    for (int o = tid; o < T + T * T; o += blockDim.x) {
-        double sum = 0.0;
-        if (o < T) {
-            for (int q = 0; q < C::kWarps * 32; ++q) sum += red[(size_t)q * C::NRED + 16 + o];
-        } else {
-            const int t = (o - T) / T, i = (o - T) % T;
-            const int r = t / C::TBLK, c = i / C::TBLK;
-            const int l0 = (t % C::TBLK) + C::TBLK * (i % C::TBLK);
-            for (int w = 0; w < C::kWarps; ++w)
-                for (int sl = 0; sl < C::NSLICES; ++sl)
-                    sum += red[(size_t)(w * 32 + sl * C::LANES_PER_SLICE + l0) * C::NRED + r * 4 + c];
-        }
-        part[o] = sum;
-    }
+    warp_tiles_finish<T>(pw, gsa, aligned_smem, a.part, tid);
 }
 
 // ------------------------------------------------------------------------------------
@@ -790,7 +665,7 @@ cudaError_t launch_bwd_t(const GlmArgs& a, int grid, cudaStream_t st) {
 }
 
 template <int T, bool FULL, bool TP2>
-cudaError_t launch_bwd_w(const GlmArgs& a, const GlmTmaMaps& m, int grid, cudaStream_t st) {
+cudaError_t launch_bwd_w(const GlmArgs& a, const TileMaps& m, int grid, cudaStream_t st) {
     const size_t smem = WarpBwdCfg<T>::kBytes;
     auto k = glm_bwd_w<T, FULL, TP2>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -799,14 +674,6 @@ cudaError_t launch_bwd_w(const GlmArgs& a, const GlmTmaMaps& m, int grid, cudaSt
     return cudaGetLastError();
 }
 
-// tensor maps of the warp-tiled backward, false when the arrays do not meet the TMA rules
-bool glm_tma_maps(GlmTmaMaps* m, const float* x, const float* gS, const float* v0, float* gx,
-                  float* gv0, int T, long long N) {
-    const int bn = 64;   // WarpBwdCfg<T>::TN
-    return encode_rows_map(&m->x, x, N, T, bn) && encode_rows_map(&m->g, gS, N, T, bn) &&
-           encode_rows_map(&m->v0, v0, N, 1, bn) && encode_rows_map(&m->gx, gx, N, T, bn) &&
-           encode_rows_map(&m->gv0, gv0, N, 1, bn);
-}
 
 // resident blocks per device of a backward kernel (SMs x occupancy), cached per device
 template <class K>
@@ -960,8 +827,8 @@ cudaError_t glmulti_backward_launch(const float* gS, const float* x, const float
     if (e != cudaSuccess) return e;
     const bool bulk = bulk_eligible(x, gS, v0, N);
     const int TB = tb_bucket(T);
-    GlmTmaMaps maps;
-    if ((T == 8 || T == 16) && surrogate_fast_ok(sg) && glm_tma_maps(&maps, x, gS, v0, gx, gv0, T, N)) {
+    TileMaps maps;
+    if ((T == 8 || T == 16) && surrogate_fast_ok(sg) && encode_tile_maps(&maps, x, gS, v0, gx, gv0, T, N)) {
 #define DFSNN_BWDW(TV)                                                                          \
         if (T == TV) {                                                                          \
             if (full) e = tau_pow2 ? launch_bwd_w<TV, true, true>(a, maps, nblocks, st)         \

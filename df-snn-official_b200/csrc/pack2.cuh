@@ -18,9 +18,15 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a
 // round(a - b) per half
 __device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __ffma2_rn(b, f2(-1.0f), a); }
 
-// The same operations as inline PTX (fma/add/sub/mul .rn.f32x2, sm_100+).  The optimizer
-// treats each as an opaque instruction, so no pass can contract or reassociate across
-// them: the form used by the chains whose exactness depends on operation order.
+// The same operations as inline PTX (fma/add/sub/mul .rn.f32x2, sm_100+).
+//
+// Rule for every packed kernel here: a packed product never feeds a packed sum.  GPU probes
+// (2^17 neuron pairs) showed that a packed multiply whose result is consumed by a packed
+// add/sub can be fused into one packed FMA by the optimised code -- for the intrinsics and
+// for these .rn PTX forms alike, depending on context -- which changes the rounding.  Such
+// sums are written with the per-half scalar helpers below (sadd2/ssub2), which are never
+// contracted.  A packed Kahan chain whose running sum is a packed add was also seen to lose
+// its compensation; that add is scalar too (single_order.cu).
 __device__ __forceinline__ unsigned long long pk(float2 a) {
     unsigned long long r;
     asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a.x), "f"(a.y));
@@ -52,20 +58,17 @@ __device__ __forceinline__ float2 pmul2(float2 a, float2 b) {
     return upk(d);
 }
 
-// Kahan step on the term w*h (w, h per half) in the form used by the reference
-// (y = fma(w, h, -c); t = s + y; c = (t - s) - y; s = t), carrying cn = -c so that every
-// step is four packed instructions: y = fma(w,h,cn); t = s+y; d = round(s-t); cn = y+d.
-struct Kahan2 {
-    float2 s = make_float2(0.0f, 0.0f);
-    float2 cn = make_float2(-0.0f, -0.0f);
-    __device__ __forceinline__ void add(float2 w, float2 h) {
-        const float2 y = fma2(w, h, cn);
-        const float2 t = add2(s, y);
-        const float2 d = sub2(s, t);
-        cn = add2(y, d);
-        s = t;
-    }
-};
+// per-half scalar operations (separately rounded, never contracted)
+__device__ __forceinline__ float2 sadd2(float2 a, float2 b) {
+    return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+}
+__device__ __forceinline__ float2 ssub2(float2 a, float2 b) {
+    return make_float2(__fsub_rn(a.x, b.x), __fsub_rn(a.y, b.y));
+}
+__device__ __forceinline__ float2 smul2(float2 a, float2 b) {
+    return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
+}
+
 
 // Per-half division by tau (IEEE) or product with 1/tau when tau is a power of two.
 template <bool TAU_POW2>

@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(256) single_fwd_x2(SingleArgs a) {
             s = t;
         }
         float2 p;
-        if constexpr (SCHEME == kGL) p = padd2(dv, s);                          // dv - hist
+        if constexpr (SCHEME == kGL) p = sadd2(dv, s);                          // dv - hist (dv is a product)
         else if constexpr (SCHEME == kGL1) p = pfma2(hb2, dv, s);               // fma(hb, dv, -hist)
         else if constexpr (SCHEME == kTRAP) p = padd2(v, pfma2(tf2, dv, s));    // v + fma(tf, dv, -hist)
         else p = pfma2(ps2, pfma2(wc2, dv, s), v);                              // predictor

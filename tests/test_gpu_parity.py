@@ -199,7 +199,8 @@ def test_glmulti_empty_and_direct_capi():
 # aligned glmulti
 # -------------------------------------------------------------------------------------
 @pytest.mark.parametrize("T,N", [(T, N) for T in (1, 2, 5, 8, 11, 16, 24, 32) for N in (1, 300, 2049)]
-                         + [(33, 300), (40, 2049), (64, 1000)])
+                         + [(33, 300), (40, 2049), (64, 1000)]
+                         + [(T, N) for T in (8, 16) for N in (4, 64, 4096, 70000)])
 @pytest.mark.parametrize("tau", [2.0, 1.3])
 @pytest.mark.parametrize("kind", ["toeplitz", "general"])
 def test_aligned_vs_oracle(T, N, tau, kind):
