@@ -59,6 +59,9 @@ def parse():
                     help="profiling: comma list of scheme:T (e.g. glmulti:16) instead of all")
     ap.add_argument("--neurons", type=int, default=0,
                     help="profiling: neurons per GPU instead of 16*128*64*64")
+    ap.add_argument("--workload", choices=("layers", "cnn128"), default="layers",
+                    help="layers: the LIFNeuronFDE layer step (default); cnn128: synthetic "
+                         "CNN128 training step, data-parallel, samples/s")
     args = ap.parse_args()
     global SHAPE, COMBOS
     if args.only:
@@ -459,8 +462,159 @@ def run_e2e(args, layers, x16, gS16, gV16, dev, world):
             "overlap": "h2d, compute and d2h on separate streams"}
 
 
+# -----------------------------------------------------------------------------------------
+# CNN128 synthetic training (the network configuration of the examples, data-parallel)
+# -----------------------------------------------------------------------------------------
+CNN_T, CNN_B, CNN_CLASSES = 16, 16, 11
+
+
+def make_cnn128(dev):
+    """The CNN128 topology of the reference examples (examples/cnn128/cnn128_aligned.py:8-40):
+    five blocks Conv2d(3x3, 128, no bias) -> BatchNorm2d -> LIFNeuronFDE -> MaxPool2d(2), then
+    Flatten, Dropout(0.5), Linear(2048, 512), LIF, Dropout(0.5), Linear(512, 256), LIF,
+    Linear(256, classes); every LIF layer is glmulti with aligned semantics (installed as
+    the examples do), full-history gradient and one shared Softplus mass parameter.  Frame
+    layers run on all T frames at once (the reference loops over frames: same math), batch
+    norm per frame as in the reference; output = mean over time."""
+    import torch
+    import torch.nn as nn
+    from dfsnn_b200 import aligned_glmulti
+    from dfsnn_b200.neuron import LIFNeuronFDE
+    aligned_glmulti.install("native")
+    raw = nn.Parameter(torch.log(torch.expm1(torch.tensor(MASSES))))
+
+    def neuron(name):
+        return LIFNeuronFDE(tau=2.0, threshold=1.0, surrogate_grad_scale=5.0,
+                            surrogate_function="arctan", beta=MULTI_BETA[0], T=CNN_T,
+                            method="glmulti", step_size=0.1, batchsize=CNN_B, name=name,
+                            backend="cupy", step_mode="m", multi_beta=MULTI_BETA,
+                            multi_coefficient=MASSES, learn_coefficient=True,
+                            coefficient_constraint="softplus", shared_multi_coefficient=raw,
+                            coefficient_update_interval=1, glmulti_history_grad="full")
+
+    class CNN128(nn.Module):
+        def __init__(self):
+            super().__init__()
+            blocks = []
+            for i in range(5):
+                blocks += [("frames", nn.Conv2d(2 if i == 0 else 128, 128, 3, padding=1, bias=False)),
+                           ("per_frame", nn.BatchNorm2d(128)), ("lif", neuron(f"conv{i}")),
+                           ("frames", nn.MaxPool2d(2))]
+            blocks += [("frames", nn.Flatten()), ("frames", nn.Dropout(0.5)),
+                       ("frames", nn.Linear(128 * 4 * 4, 512)), ("lif", neuron("fc0")),
+                       ("frames", nn.Dropout(0.5)), ("frames", nn.Linear(512, 256)),
+                       ("lif", neuron("fc1")), ("frames", nn.Linear(256, CNN_CLASSES))]
+            self.kinds = [k for k, _ in blocks]
+            self.layers = nn.ModuleList([m for _, m in blocks])
+
+        def forward(self, x):
+            T, B = x.shape[:2]
+            for kind, layer in zip(self.kinds, self.layers):
+                if kind == "lif":
+                    x = layer(x)
+                elif kind == "per_frame":
+                    x = torch.stack([layer(f) for f in x])
+                else:
+                    y = layer(x.flatten(0, 1))
+                    x = y.reshape((T, B) + tuple(y.shape[1:]))
+            return x.mean(0)
+
+        def reset(self):
+            for m in self.modules():
+                if isinstance(m, LIFNeuronFDE):
+                    m.reset()
+
+    return CNN128().to(dev)
+
+
+def run_cnn128(args):
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+    from dfsnn_b200 import profiling
+    from dfsnn_b200.distributed import init_process_group
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        init_process_group("nccl", timeout_s=300, device=dev)
+    K, W = args.steps, max(args.warmup, 3)
+    torch.manual_seed(1234 + rank)
+    model = make_cnn128(dev)
+    net = model
+    if world > 1:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local],
+                                                        broadcast_buffers=False)
+    opt = torch.optim.SGD(model.parameters(), lr=1e-3, momentum=0.9)
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    # synthetic event frames: Bernoulli(0.05) spike counts scaled by Poisson(1), 11 classes
+    shape = (CNN_T, CNN_B, 2, 128, 128)
+    frames = (torch.rand(shape, device=dev, generator=g) < 0.05).float() * \
+        torch.poisson(torch.ones(shape, device=dev), generator=g)
+    labels = torch.randint(0, CNN_CLASSES, (CNN_B,), device=dev, generator=g)
+
+    def step():
+        model.reset()
+        out = net(frames)
+        loss = F.cross_entropy(out, labels)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+        return loss
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with profiling.NativeCallTimer() as timer:
+        start.record()
+        for _ in range(K):
+            loss = step()
+        end.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    summary = timer.summary()
+    if rank == 0:
+        line = {
+            "metric": "CNN128 synthetic training samples/s", "value": world * CNN_B * K / (ms / 1e3),
+            "unit": "samples/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "CNN128 (5x conv128-BN-LIF-pool, fc512-LIF, fc256-LIF, fc11) "
+                       "training step, SGD, LIFNeuronFDE glmulti aligned full history, shared "
+                       "Softplus masses, T=16, B=16 per GPU, frames [16,16,2,128,128] "
+                       "Bernoulli(0.05)*Poisson(1), 11 classes",
+                       "parallelism": f"dp{world}" + (" (DDP, NCCL)" if world > 1 else "")},
+            "lif_kernels": {k: {"calls_per_step": v["calls"] / K,
+                                "ms_per_call": round(v["ms_per_call"], 4)}
+                            for k, v in summary.items()},
+            "lif_ms_per_step": round(sum(v["ms_total"] for v in summary.values()) / K, 3),
+            "loss": float(loss.item()),
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "cnn128":
+        return run_cnn128(args) if args.impl == "native" else 0
     if args.impl == "reference":
         return run_reference(args)
     return run_native(args)
