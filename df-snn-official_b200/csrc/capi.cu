@@ -220,7 +220,7 @@ int dfsnn_single_forward(int scheme, const float* x, const float* v0, const floa
                          float* spike, float* v_seq, unsigned int* spike_bits, int T,
                          long long N, float tau, float beta, float threshold, float h_beta,
                          float gamma_beta_plus_1, void* stream) {
-    if (scheme < DFSNN_GL || scheme > DFSNN_GL1) return DFSNN_ERR_SCHEME;
+    if (scheme < DFSNN_GL || scheme > DFSNN_PREDICTOR1) return DFSNN_ERR_SCHEME;
     if (int s = check_seq(T, N, DFSNN_MAX_T)) return s;
     if (!weights) return DFSNN_ERR_NULL;
     if (N > 0 && (!x || !v0 || !spike || !v_seq || !spike_bits)) return DFSNN_ERR_NULL;
@@ -252,6 +252,24 @@ int dfsnn_single_backward(int scheme, const float* grad_spike, const float* grad
         scheme, grad_spike, grad_v, v_seq, reinterpret_cast<const uint32_t*>(spike_bits), weights,
         grad_x, grad_v0, T, N, tau, beta, threshold, surrogate_scale, h_beta, gamma_beta_plus_1,
         tau_is_pow2(tau), (cudaStream_t)stream));
+}
+
+int dfsnn_single_recompute_backward(int scheme, const float* grad_spike, const float* grad_v,
+                                    const float* x, const float* v0, const float* weights,
+                                    float* grad_x, float* grad_v0, int T, long long N, float tau,
+                                    float threshold, float surrogate_scale, float h_beta,
+                                    void* stream) {
+    if (scheme != DFSNN_TRAP1 && scheme != DFSNN_PREDICTOR1) return DFSNN_ERR_SCHEME;
+    if (int s = check_seq(T, N, DFSNN_MAX_T)) return s;
+    if (!weights) return DFSNN_ERR_NULL;
+    if (N > 0 && (!grad_spike || !grad_v || !x || !v0 || !grad_x || !grad_v0))
+        return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(threshold) || !finite(surrogate_scale) || !finite(h_beta))
+        return DFSNN_ERR_PARAM;
+    return cuda_status(dfsnn::single1_backward_launch(scheme, grad_spike, grad_v, x, v0, weights,
+                                                      grad_x, grad_v0, T, N, tau, threshold,
+                                                      surrogate_scale, h_beta, tau_is_pow2(tau),
+                                                      (cudaStream_t)stream));
 }
 
 // ---------------------------------------------------------------------------------------

@@ -7,7 +7,7 @@
 
 namespace dfsnn {
 
-enum Scheme { kGL = 0, kTRAP = 1, kPRED = 2, kGL1 = 3 };
+enum Scheme { kGL = 0, kTRAP = 1, kPRED = 2, kGL1 = 3, kTRAP1 = 4, kPRED1 = 5 };
 
 // library glmulti
 cudaError_t glmulti_forward_launch(const float* x, const float* v0, const float* scale,
@@ -65,6 +65,12 @@ cudaError_t single_backward_launch(int scheme, const float* gS, const float* gV,
                                    const uint32_t* bits, const float* w, float* gx, float* gv0,
                                    int T, long long N, float tau, float beta, float th, float sg,
                                    float h_beta, float gamma1, bool tau_pow2, cudaStream_t st);
+
+// TRAP1 / PREDICTOR1 backward: recomputes the trajectory from x and v0 as the reference does
+cudaError_t single1_backward_launch(int scheme, const float* gS, const float* gV, const float* x,
+                                    const float* v0, const float* w, float* gx, float* gv0,
+                                    int T, long long N, float tau, float th, float sg,
+                                    float h_beta, bool tau_pow2, cudaStream_t st);
 
 // Store e as the calling thread's dfsnn_last_cuda_error() value; returns DFSNN_ERR_CUDA.
 int record_cuda_error(cudaError_t e);

@@ -38,6 +38,9 @@ __device__ __forceinline__ float single_update(float v, float dv, float hist, fl
                                                float pred_scale, float w_cur, float h_beta) {
     if constexpr (SCHEME == kGL) return __fsub_rn(dv, hist);                         // :66
     else if constexpr (SCHEME == kGL1) return __fmaf_rn(h_beta, dv, -hist);          // :213
+    else if constexpr (SCHEME == kTRAP1) return __fsub_rn(__fmaf_rn(h_beta, dv, v), hist);  // :2059
+    else if constexpr (SCHEME == kPRED1)
+        return __fmaf_rn(h_beta, __fmaf_rn(w_cur, dv, hist), v);                     // :2326
     else if constexpr (SCHEME == kTRAP) return __fadd_rn(v, __fmaf_rn(trap_factor, dv, -hist));  // :372
     else return __fmaf_rn(pred_scale, __fmaf_rn(w_cur, dv, hist), v);                // :528
 }
@@ -85,7 +88,7 @@ __global__ void __launch_bounds__(256) single_fwd_reg(SingleArgs a) {
             const bool fire = p >= a.th;
             const float s = fire ? 1.0f : 0.0f;
             v = __fsub_rn(p, s * a.th);
-            hv[k] = (SCHEME == kPRED) ? div_tau<TP2>(-v, a.tau, a.inv_tau) : v;
+            hv[k] = (SCHEME == kPRED || SCHEME == kPRED1) ? div_tau<TP2>(-v, a.tau, a.inv_tau) : v;
             bits |= (fire ? 1u : 0u) << k;
             st_stream(a.spike + k * N + n, s);
             st_stream(a.v + k * N + n, v);
@@ -110,7 +113,7 @@ __global__ void __launch_bounds__(256) single_fwd_x2(SingleArgs a) {
     const long long N = a.N;
     const long long n = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
     if (n >= N) return;
-    constexpr bool NEG = SCHEME != kPRED;
+    constexpr bool NEG = SCHEME != kPRED && SCHEME != kPRED1;
     float2 wr[T + 1];
 #pragma unroll
     for (int L = 1; L <= T; ++L) wr[L] = f2(NEG ? -sw[T - L] : sw[T - L]);
@@ -144,13 +147,15 @@ __global__ void __launch_bounds__(256) single_fwd_x2(SingleArgs a) {
         float2 p;
         if constexpr (SCHEME == kGL) p = sadd2(dv, s);                          // dv - hist (dv is a product)
         else if constexpr (SCHEME == kGL1) p = pfma2(hb2, dv, s);               // fma(hb, dv, -hist)
+        else if constexpr (SCHEME == kTRAP1) p = padd2(pfma2(hb2, dv, v), s);   // fma(hb, dv, v) - hist
+        else if constexpr (SCHEME == kPRED1) p = pfma2(hb2, pfma2(wc2, dv, s), v);
         else if constexpr (SCHEME == kTRAP) p = padd2(v, pfma2(tf2, dv, s));    // v + fma(tf, dv, -hist)
         else p = pfma2(ps2, pfma2(wc2, dv, s), v);                              // predictor
         // v = p - spike*th with spike*th exactly th or 0
         const float2 z = psub2(p, th2);
         const bool f0 = p.x >= th, f1 = p.y >= th;
         v = make_float2(f0 ? z.x : p.x, f1 ? z.y : p.y);
-        if constexpr (SCHEME == kPRED)
+        if constexpr (SCHEME == kPRED || SCHEME == kPRED1)
             hv[k] = TP2 ? pmul2(v, ninv2)
                         : make_float2(__fdiv_rn(-v.x, a.tau), __fdiv_rn(-v.y, a.tau));
         else
@@ -201,7 +206,7 @@ __global__ void __launch_bounds__(kLongBlock) single_fwd_smem(SingleArgs a) {
         const bool fire = p >= a.th;
         const float s = fire ? 1.0f : 0.0f;
         v = __fsub_rn(p, s * a.th);
-        hv[k * kLongBlock] = (SCHEME == kPRED) ? div_tau<TP2>(-v, a.tau, a.inv_tau) : v;
+        hv[k * kLongBlock] = (SCHEME == kPRED || SCHEME == kPRED1) ? div_tau<TP2>(-v, a.tau, a.inv_tau) : v;
         bits |= (fire ? 1u : 0u) << (k & 31);
         st_stream(a.spike + k * N + n, s);
         st_stream(a.v + k * N + n, v);
@@ -320,6 +325,74 @@ __global__ void __launch_bounds__(256) single_bwd_loop(SingleArgs a) {
 }
 
 // ------------------------------------------------------------------------------------
+// TRAP1 / PREDICTOR1 backward (fde_cupy_kernels_all.py:2072-2161, :2337-2432).  The
+// reference recomputes the trajectory here with a plain fused multiply-add history sum --
+// not the forward's Kahan sum, so its membranes and spikes may differ from the forward's --
+// and the reverse step's history term touches only the current gradient.  Both are
+// reproduced operation by operation: one thread per neuron, the recomputed membranes (and
+// PREDICTOR1's history derivatives -v/tau) in shared memory [T][64], spikes as bits.
+// ------------------------------------------------------------------------------------
+constexpr int kS1Threads = 64;
+
+template <int SCHEME, bool TP2>
+__global__ void __launch_bounds__(kS1Threads) single1_bwd(SingleArgs a) {
+    extern __shared__ float sh[];
+    const int T = a.T;
+    const int tid = threadIdx.x;
+    const int wpad = (T + 1 + 3) & ~3;
+    float* sw = sh;                                            // [T+1] weights
+    float* hbw = sh + wpad;                                    // [T+1] h_beta * w (PREDICTOR1)
+    float* VL = sh + 2 * wpad;                                 // [T][64] recomputed v
+    float* HV = (SCHEME == kPRED1) ? VL + (size_t)T * kS1Threads : VL;   // [T][64] history
+    uint32_t* SB = reinterpret_cast<uint32_t*>(HV + (size_t)T * kS1Threads);   // [8][64] spikes
+    for (int e = tid; e <= T; e += blockDim.x) {
+        sw[e] = a.w[e];
+        hbw[e] = __fmul_rn(a.h_beta, a.w[e]);
+    }
+    __syncthreads();
+    const long long n = (long long)blockIdx.x * kS1Threads + tid;
+    if (n >= a.N) return;
+    const long long N = a.N;
+    const float hb = a.h_beta, th = a.th;
+    for (int wdx = 0; wdx < (T + 31) / 32; ++wdx) SB[wdx * kS1Threads + tid] = 0u;
+    float v = a.v0[n];
+    for (int k = 0; k < T; ++k) {
+        const float dv = div_tau<TP2>(__fsub_rn(ld_stream(a.x + k * N + n), v), a.tau, a.inv_tau);
+        float hist = 0.0f;
+        for (int i = 0; i < k; ++i) hist = __fmaf_rn(sw[T - k + i], HV[i * kS1Threads + tid], hist);
+        const float p = SCHEME == kTRAP1 ? __fsub_rn(__fmaf_rn(hb, dv, v), hist)
+                                         : __fmaf_rn(hb, __fmaf_rn(sw[T], dv, hist), v);
+        const bool fire = p >= th;
+        const float vn = fire ? __fsub_rn(p, th) : p;           // p - spike*th
+        VL[k * kS1Threads + tid] = vn;
+        if constexpr (SCHEME == kPRED1) HV[k * kS1Threads + tid] = div_tau<TP2>(-vn, a.tau, a.inv_tau);
+        if (fire) SB[(k >> 5) * kS1Threads + tid] |= 1u << (k & 31);
+        v = vn;
+    }
+    const float m1 = SCHEME == kTRAP1 ? __fsub_rn(1.0f, div_tau<TP2>(hb, a.tau, a.inv_tau))
+                                      : __fsub_rn(1.0f, div_tau<TP2>(hbw[T], a.tau, a.inv_tau));
+    const float gxs = SCHEME == kTRAP1 ? hb : hbw[T];           // h_beta (* w_T)
+    float gv = 0.0f;
+    for (int t = T - 1; t >= 0; --t) {
+        gv = __fadd_rn(gv, ld_stream(a.gV + t * N + n));
+        const float vl = VL[t * kS1Threads + tid];
+        const bool fire = (SB[(t >> 5) * kS1Threads + tid] >> (t & 31)) & 1u;
+        const float pp = fire ? __fadd_rn(vl, th) : vl;         // v + spike*th
+        gv = __fmaf_rn(ld_stream(a.gS + t * N + n), surrogate_fma(__fsub_rn(pp, th), a.sg), gv);
+        st_stream(a.gx + t * N + n, div_tau<TP2>(__fmul_rn(gxs, gv), a.tau, a.inv_tau));
+        float gvm = __fmul_rn(gv, m1);
+        if constexpr (SCHEME == kTRAP1) {
+            for (int i = 0; i < t; ++i) gvm = __fmaf_rn(-sw[T - t + i], gv, gvm);
+        } else {
+            for (int i = 0; i < t; ++i)
+                gvm = __fsub_rn(gvm, div_tau<TP2>(__fmul_rn(hbw[T - t + i], gv), a.tau, a.inv_tau));
+        }
+        gv = gvm;
+    }
+    a.gv0[n] = gv;
+}
+
+// ------------------------------------------------------------------------------------
 // host launchers
 // ------------------------------------------------------------------------------------
 namespace {
@@ -385,6 +458,8 @@ cudaError_t fwd_scheme(int scheme, const SingleArgs& a, cudaStream_t st) {
         case kTRAP: return fwd_dispatch<kTRAP, TP2>(a, st);
         case kPRED: return fwd_dispatch<kPRED, TP2>(a, st);
         case kGL1: return fwd_dispatch<kGL1, TP2>(a, st);
+        case kTRAP1: return fwd_dispatch<kTRAP1, TP2>(a, st);
+        case kPRED1: return fwd_dispatch<kPRED1, TP2>(a, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -420,6 +495,37 @@ cudaError_t single_backward_launch(int scheme, const float* gS, const float* gV,
     SingleArgs a = make_args(T, N, tau, beta, th, sg, h_beta, gamma1);
     a.gS = gS; a.gV = gV; a.vs = v; a.bits_in = bits; a.w = w; a.gx = gx; a.gv0 = gv0;
     return tau_pow2 ? bwd_scheme<true>(scheme, a, st) : bwd_scheme<false>(scheme, a, st);
+}
+
+cudaError_t single1_backward_launch(int scheme, const float* gS, const float* gV, const float* x,
+                                    const float* v0, const float* w, float* gx, float* gv0,
+                                    int T, long long N, float tau, float th, float sg,
+                                    float h_beta, bool tau_pow2, cudaStream_t st) {
+    if (N == 0) return cudaSuccess;
+    SingleArgs a = make_args(T, N, tau, 0.0f, th, sg, h_beta, 1.0f);
+    a.x = x; a.v0 = v0; a.w = w; a.gS = gS; a.gV = gV; a.gx = gx; a.gv0 = gv0;
+    const int wpad = (T + 1 + 3) & ~3;
+    const int arrays = scheme == kPRED1 ? 2 : 1;
+    const size_t smem = sizeof(float) * (2 * (size_t)wpad + (size_t)arrays * T * kS1Threads) +
+                        sizeof(uint32_t) * 8 * kS1Threads;
+    const unsigned grid = (unsigned)((N + kS1Threads - 1) / kS1Threads);
+    cudaError_t e;
+#define DFSNN_S1(SCH, P2)                                                                    \
+    {                                                                                        \
+        auto k = single1_bwd<SCH, P2>;                                                       \
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+        if (e != cudaSuccess) return e;                                                      \
+        k<<<grid, kS1Threads, smem, st>>>(a);                                                \
+    }
+    if (scheme == kTRAP1) {
+        if (tau_pow2) DFSNN_S1(kTRAP1, true) else DFSNN_S1(kTRAP1, false)
+    } else if (scheme == kPRED1) {
+        if (tau_pow2) DFSNN_S1(kPRED1, true) else DFSNN_S1(kPRED1, false)
+    } else {
+        return cudaErrorInvalidValue;
+    }
+#undef DFSNN_S1
+    return cudaGetLastError();
 }
 
 }  // namespace dfsnn

@@ -21,7 +21,7 @@ DFSNN_ERR_PARAM = 7
 MAX_T = 256
 MAX_T_FULL = 64
 
-GL, TRAP, PREDICTOR, GL1 = 0, 1, 2, 3
+GL, TRAP, PREDICTOR, GL1, TRAP1, PREDICTOR1 = 0, 1, 2, 3, 4, 5
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
@@ -48,6 +48,8 @@ SIGNATURES = {
     "dfsnn_single_forward": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _ll, _f, _f, _f, _f, _f, _p]),
     "dfsnn_single_backward": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _i, _ll, _f, _f, _f, _f, _f,
                                    _f, _p]),
+    "dfsnn_single_recompute_backward": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _i, _ll, _f, _f, _f,
+                                             _f, _p]),
     "dfsnn_direct_euler_forward": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _ll, _f, _f, _f, _f, _f,
                                         _p]),
     "dfsnn_direct_euler_backward_workspace_size": (_sz, [_ll]),

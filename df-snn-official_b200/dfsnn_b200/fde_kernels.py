@@ -8,7 +8,7 @@ neuron.py gates on it (:1995); it is True because the native path never needs Cu
 missing native library raises on first use rather than falling back to the CPU.
 
 Native here: LIFFDEGLFunction, LIFFDEGL1Function, LIFFDETRAPFunction,
-LIFFDEPREDICTORFunction, LIFFDEGLMultiFunction.  The remaining reference Functions of the
+LIFFDEPREDICTORFunction, LIFFDETRAP1Function, LIFFDEPREDICTOR1Function, LIFFDEGLMultiFunction.  The remaining reference Functions of the
 module are outside this hot path and raise NotImplementedError.
 """
 import math
@@ -52,7 +52,10 @@ def _single_forward(ctx, scheme, name, x_seq, v_init, weights, tau, beta, v_thre
             _capi.ptr(v_seq), _capi.ptr(bits), T, N, tau_f, beta_f, float(v_threshold),
             float(h_beta), float(gamma1), _capi.stream_of(x))
     _capi.check(code, name + ".forward")
-    ctx.save_for_backward(v_seq, bits, w)
+    if scheme in (_capi.TRAP1, _capi.PREDICTOR1):
+        ctx.save_for_backward(x, v0, w)       # their backward recomputes, as the reference's
+    else:
+        ctx.save_for_backward(v_seq, bits, w)
     ctx.scheme = scheme
     ctx.name = name
     ctx.consts = (tau_f, beta_f, float(v_threshold), float(surrogate_grad_scale), float(h_beta),
@@ -61,7 +64,26 @@ def _single_forward(ctx, scheme, name, x_seq, v_init, weights, tau, beta, v_thre
     return spike, v_seq
 
 
+def _single_recompute_backward(ctx, grad_spike_seq, grad_v_seq):
+    x, v0, w = ctx.saved_tensors
+    T, N = ctx.T, ctx.N
+    gS = torch.zeros_like(x) if grad_spike_seq is None else grad_spike_seq.float().contiguous()
+    gV = torch.zeros_like(x) if grad_v_seq is None else grad_v_seq.float().contiguous()
+    grad_x = torch.empty((T, N), dtype=torch.float32, device=x.device)
+    grad_v0 = torch.empty(N, dtype=torch.float32, device=x.device)
+    tau, beta, th, sg, h_beta, gamma1 = ctx.consts
+    with torch.cuda.device(x.device), _prof.native_call(
+            "single_backward", 1, _prof.single1_backward_bytes(T, N), x.device):
+        code = _capi.lib().dfsnn_single_recompute_backward(
+            ctx.scheme, _capi.ptr(gS), _capi.ptr(gV), _capi.ptr(x), _capi.ptr(v0), _capi.ptr(w),
+            _capi.ptr(grad_x), _capi.ptr(grad_v0), T, N, tau, th, sg, h_beta, _capi.stream_of(x))
+    _capi.check(code, ctx.name + ".backward")
+    return grad_x, grad_v0
+
+
 def _single_backward(ctx, grad_spike_seq, grad_v_seq):
+    if ctx.scheme in (_capi.TRAP1, _capi.PREDICTOR1):
+        return _single_recompute_backward(ctx, grad_spike_seq, grad_v_seq)
     v_seq, bits, w = ctx.saved_tensors
     T, N = ctx.T, ctx.N
     gS = (torch.zeros_like(v_seq) if grad_spike_seq is None
@@ -208,6 +230,41 @@ class LIFFDEGLMultiFunction(torch.autograd.Function):
                 None, None, None, None, None)
 
 
+class LIFFDETRAP1Function(torch.autograd.Function):
+    """TRAP1 (fde_cupy_kernels_all.py:2163-2276): v + h_beta*dv - hist with h_beta = 1**beta."""
+
+    @staticmethod
+    def forward(ctx, x_seq, v_init, trap_weights, tau, beta, v_threshold, v_reset,
+                surrogate_grad_scale):
+        beta_value = beta if isinstance(beta, float) else float(beta.item() if isinstance(
+            beta, torch.Tensor) else beta)
+        h_beta = math.pow(1.0, beta_value)                     # as the reference (:2190)
+        return _single_forward(ctx, _capi.TRAP1, "LIFFDETRAP1Function", x_seq, v_init,
+                               trap_weights, tau, beta, v_threshold, surrogate_grad_scale,
+                               h_beta=h_beta)
+
+    @staticmethod
+    def backward(ctx, grad_spike_seq, grad_v_seq):
+        gx, gv = _single_backward(ctx, grad_spike_seq, grad_v_seq)
+        return gx, gv, None, None, None, None, None, None
+
+
+class LIFFDEPREDICTOR1Function(torch.autograd.Function):
+    """PREDICTOR1 (fde_cupy_kernels_all.py:2434-2545): v + h_beta*(w_T*dv + hist)."""
+
+    @staticmethod
+    def forward(ctx, x_seq, v_init, predictor_weights, tau, beta, v_threshold, v_reset,
+                surrogate_grad_scale, h_beta, gamma_beta_plus_1):
+        return _single_forward(ctx, _capi.PREDICTOR1, "LIFFDEPREDICTOR1Function", x_seq, v_init,
+                               predictor_weights, tau, beta, v_threshold, surrogate_grad_scale,
+                               h_beta=h_beta, gamma1=gamma_beta_plus_1)
+
+    @staticmethod
+    def backward(ctx, grad_spike_seq, grad_v_seq):
+        gx, gv = _single_backward(ctx, grad_spike_seq, grad_v_seq)
+        return gx, gv, None, None, None, None, None, None, None, None
+
+
 # ---------------------------------------------------------------------------------------
 # reference Functions outside this hot path
 # ---------------------------------------------------------------------------------------
@@ -215,13 +272,11 @@ def _not_native(name):
     def apply(*args, **kwargs):
         raise NotImplementedError(
             f"{name} is not part of the B200 LIF-FDE hot path (native: GL, GL1, TRAP, "
-            "PREDICTOR, GLMULTI, aligned GLMULTI, direct Euler)")
+            "PREDICTOR, TRAP1, PREDICTOR1, GLMULTI, aligned GLMULTI, direct Euler)")
 
     return type(name, (), {"apply": staticmethod(apply)})
 
 
-LIFFDETRAP1Function = _not_native("LIFFDETRAP1Function")
-LIFFDEPREDICTOR1Function = _not_native("LIFFDEPREDICTOR1Function")
 LIFEulerFunction = _not_native("LIFEulerFunction")
 LIFFDEVOPREDICTORFunction = _not_native("LIFFDEVOPREDICTORFunction")
 LIFFDEFAGL1Function = _not_native("LIFFDEFAGL1Function")

@@ -2,7 +2,7 @@
 
 Same constructor signature, parameters/buffers (state_dict keys) and multi-step forward
 contract as spikeDE_dis.neuron.LIFNeuronFDE (spikeDE_dis/neuron.py:1058-2270) for the
-schemes of the hot path -- glmulti, gl, gl1, trap, predictor -- dispatching to the
+schemes of the hot path -- glmulti, gl, gl1, trap, predictor, trap1, predictor1 -- dispatching to the
 autograd Functions of dfsnn_b200.fde_kernels exactly as the reference's
 _multi_step_forward_glmulti_cupy (:1992-2007) and _multi_step_forward_cupy (:2091-2270)
 dispatch to fde_cupy_kernels_all.  Functions are looked up on the module at call time, so
@@ -21,7 +21,7 @@ import torch.nn.functional as F
 from . import fde_kernels as _kernels
 from . import schedule as _sched
 
-_NATIVE_METHODS = ("glmulti", "gl", "gl1", "trap", "predictor")
+_NATIVE_METHODS = ("glmulti", "gl", "gl1", "trap", "predictor", "trap1", "predictor1")
 _ALL_METHODS = ("gl", "gl1", "fagl1", "vogl1", "predictor", "predictor1", "vopredictor", "trap",
                 "trap1", "euler", "glmulti")
 
@@ -225,9 +225,9 @@ class LIFNeuronFDE(nn.Module):
         beta = self._beta_value()
         if self.method in ("gl", "gl1"):
             return _sched.gl_weights(beta, T, device, dtype)
-        if self.method == "trap":
+        if self.method in ("trap", "trap1"):                   # neuron.py:1431-1436
             return _sched.trap_weights(beta, T, device, dtype)
-        if self.method == "predictor":
+        if self.method in ("predictor", "predictor1"):
             return _sched.predictor_weights(beta, T, device, dtype)
         return None
 
@@ -307,6 +307,14 @@ class LIFNeuronFDE(nn.Module):
         elif self.method == "trap":
             s, v = K.LIFFDETRAPFunction.apply(x_flat, v_flat, self.weights, tau, beta,
                                               self.threshold, v_reset, self.surrogate_grad_scale)
+        elif self.method == "trap1":
+            s, v = K.LIFFDETRAP1Function.apply(x_flat, v_flat, self.weights, tau, beta,
+                                               self.threshold, v_reset, self.surrogate_grad_scale)
+        elif self.method == "predictor1":
+            h_beta, gamma1 = _sched.predictor_constants(beta, self.h)
+            s, v = K.LIFFDEPREDICTOR1Function.apply(x_flat, v_flat, self.weights, tau, beta,
+                                                    self.threshold, v_reset,
+                                                    self.surrogate_grad_scale, h_beta, gamma1)
         else:
             h_beta, gamma1 = _sched.predictor_constants(beta, self.h)
             s, v = K.LIFFDEPREDICTORFunction.apply(x_flat, v_flat, self.weights, tau, beta,

@@ -97,6 +97,10 @@ def single_backward_bytes(T, N):
     return N * (16 * T + 4 + 4 * ((T + 31) // 32))   # grad_s, grad_v, v, bits in; grad_x, grad_v0 out
 
 
+def single1_backward_bytes(T, N):
+    return N * (16 * T + 8)                      # grad_s, grad_v, x in; grad_x out; v0 in, grad_v0 out
+
+
 def euler_forward_bytes(T, N):
     return N * (8 * T + 8)                       # x in, spikes out; z0 in, z_final out
 

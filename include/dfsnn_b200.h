@@ -49,6 +49,8 @@ extern "C" {
 #define DFSNN_TRAP 1
 #define DFSNN_PREDICTOR 2
 #define DFSNN_GL1 3
+#define DFSNN_TRAP1 4        /* LIFFDETRAP1Function (fde_cupy_kernels_all.py:2018-2276) */
+#define DFSNN_PREDICTOR1 5   /* LIFFDEPREDICTOR1Function (:2278-2545) */
 
 const char* dfsnn_status_string(int status);
 int dfsnn_last_cuda_error(void);
@@ -148,11 +150,25 @@ size_t dfsnn_spike_bits_words(int T, long long N);
  * (fde_cupy_kernels_all.py:24-75, :327-381, :479-539, :170-260; launched from the Functions'
  * forward at :658-698, :843-882, :933-975, :749-793).  weights = the reversed table of T+1 entries.
  * Writes spike[T,N], v_seq[T,N] and the spike bitmask the backward consumes.
- * h_beta / gamma_beta_plus_1 are used by PREDICTOR (both) and GL1 (h_beta). */
+ * h_beta / gamma_beta_plus_1 are used by PREDICTOR (both) and GL1 (h_beta).  Schemes
+ * DFSNN_TRAP1 / DFSNN_PREDICTOR1 replace lif_fde_trap1_forward_kernel (:2018-2070) and
+ * lif_fde_predictor1_forward_kernel (:2278-2335) (h_beta used by both; TRAP1's Function
+ * passes h_beta = 1).  Their spike_bits output is written but their backward does not use it. */
 int dfsnn_single_forward(int scheme, const float* x, const float* v0, const float* weights,
                          float* spike, float* v_seq, unsigned int* spike_bits, int T,
                          long long N, float tau, float beta, float threshold, float h_beta,
                          float gamma_beta_plus_1, void* stream);
+
+/* Replaces lif_fde_trap1_backward_kernel (:2072-2161, launched :2225-2276) and
+ * lif_fde_predictor1_backward_kernel (:2337-2432, launched :2497-2545) (scheme DFSNN_TRAP1 or
+ * DFSNN_PREDICTOR1): like the reference, recomputes the trajectory from x and v0 with a plain
+ * fused multiply-add history sum (not the forward's Kahan sum) before the reverse sweep.
+ * grad_v is the upstream gradient of v_seq.  T <= DFSNN_MAX_T. */
+int dfsnn_single_recompute_backward(int scheme, const float* grad_spike, const float* grad_v,
+                                    const float* x, const float* v0, const float* weights,
+                                    float* grad_x, float* grad_v0, int T, long long N, float tau,
+                                    float threshold, float surrogate_scale, float h_beta,
+                                    void* stream);
 
 /* Replaces the lif_fde_{gl,trap,predictor,gl1}_backward_kernel launches (:77-163,
  * :383-472, :541-637, :262-320; launched from :700-732, :884-916, :977-1010, :795-827):

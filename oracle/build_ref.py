@@ -33,6 +33,20 @@ LIB_KERNELS = [
     "predictor_forward_kernel_code", "predictor_backward_kernel_code",
     "vo_gl1_forward_kernel_code",
     "glmulti_backward_kernel_code", "glmulti_full_backward_kernel_code",
+    "trap1_forward_kernel_code", "trap1_backward_kernel_code",
+    "predictor1_forward_kernel_code", "predictor1_backward_kernel_code",
+]
+
+# Statements whose fused multiply-add NVRTC forms but GCC does not (see collect_sources).
+NVRTC_CONTRACTIONS = [
+    ("hist += trap_weights[weight_idx] * v_seq_local[hist_idx];",
+     "hist = fmaf(trap_weights[weight_idx], v_seq_local[hist_idx], hist);"),
+    ("grad_v_mem -= c_rev[weight_idx] * grad_v;",
+     "grad_v_mem = fmaf(-c_rev[weight_idx], grad_v, grad_v_mem);"),
+    ("grad_v_mem -= trap_weights[weight_idx] * grad_v;",
+     "grad_v_mem = fmaf(-trap_weights[weight_idx], grad_v, grad_v_mem);"),
+    ("hist_integral += predictor_weights[weight_idx] * hist_dv;",
+     "hist_integral = fmaf(predictor_weights[weight_idx], hist_dv, hist_integral);"),
 ]
 
 # Host launchers (this repository's code): one OpenMP loop over global thread indices.
@@ -84,6 +98,25 @@ void ref_predictor_backward(const float* gs, const float* gv, const float* x, co
                             const float* w, float* gx, float* gv0, int T, int N, float tau,
                             float beta, float th, float sg, float h_beta, float gamma1) {
     DFSNN_REF_LOOP(N, lif_fde_predictor_backward_kernel(gs, gv, x, v0, w, gx, gv0, T, N, tau, beta, th, sg, h_beta, gamma1));
+}
+void ref_trap1_forward(const float* x, const float* v0, const float* w, float* s, float* v,
+                       int T, int N, float tau, float beta, float th, float v_reset, float h_beta) {
+    DFSNN_REF_LOOP(N, lif_fde_trap1_forward_kernel(x, v0, w, s, v, T, N, tau, beta, th, v_reset, h_beta));
+}
+void ref_trap1_backward(const float* gs, const float* gv, const float* x, const float* v0,
+                        const float* w, float* gx, float* gv0, int T, int N, float tau, float beta,
+                        float th, float sg, float h_beta) {
+    DFSNN_REF_LOOP(N, lif_fde_trap1_backward_kernel(gs, gv, x, v0, w, gx, gv0, T, N, tau, beta, th, sg, h_beta));
+}
+void ref_predictor1_forward(const float* x, const float* v0, const float* w, float* s, float* v,
+                            int T, int N, float tau, float beta, float th, float v_reset,
+                            float h_beta, float gamma1) {
+    DFSNN_REF_LOOP(N, lif_fde_predictor1_forward_kernel(x, v0, w, s, v, T, N, tau, beta, th, v_reset, h_beta, gamma1));
+}
+void ref_predictor1_backward(const float* gs, const float* gv, const float* x, const float* v0,
+                             const float* w, float* gx, float* gv0, int T, int N, float tau,
+                             float beta, float th, float sg, float h_beta, float gamma1) {
+    DFSNN_REF_LOOP(N, lif_fde_predictor1_backward_kernel(gs, gv, x, v0, w, gx, gv0, T, N, tau, beta, th, sg, h_beta, gamma1));
 }
 void ref_glmulti_forward(const float* x, const float* v0, const float* scale, const float* W,
                          float* s, float* vpre, float* vhist, float* drift, int T, int N,
@@ -170,6 +203,13 @@ def collect_sources(reference):
     import spikeDE_dis.fde_cupy_kernels_all as lib  # noqa: E402
     import aligned_glmulti as alg  # noqa: E402
     fma_parts = [getattr(lib, name) for name in LIB_KERNELS]
+    # NVRTC (--fmad=true) contracts every a += b*c / a -= b*c; GCC's -ffp-contract=fast leaves
+    # these loop statements of the GL1 / TRAP1 / PREDICTOR1 backward unfused (found by stepping
+    # one neuron through both), so the host build writes NVRTC's contraction out.
+    for i, part in enumerate(fma_parts):
+        for old, new in NVRTC_CONTRACTIONS:
+            part = part.replace(old, new)
+        fma_parts[i] = part
     euler_path = os.path.join(reference, "spikeDE_dis", "direct_euler_cupy.py")
     fma_parts.append(_function_local_string(euler_path, "_get_forward_kernel"))
     fma_parts.append(_function_local_string(euler_path, "_get_backward_kernel"))

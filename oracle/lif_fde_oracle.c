@@ -44,7 +44,9 @@ static inline float surr_fma(float z, float sg) {
  * w is the reversed weight table of T+1 entries (c_rev / trap_w / pred_w); at step k
  * the history term i<k uses w[T-k+i].
  * ---------------------------------------------------------------------------------- */
-enum { ORC_GL = 0, ORC_TRAP = 1, ORC_PRED = 2, ORC_GL1 = 3 };
+enum { ORC_GL = 0, ORC_TRAP = 1, ORC_PRED = 2, ORC_GL1 = 3, ORC_TRAP1 = 4, ORC_PRED1 = 5 };
+/* TRAP1 (fde_cupy_kernels_all.py:2018-2070) and PREDICTOR1 (:2278-2335) share the Kahan
+ * forward; their updates are v + h_beta*dv - hist and v + h_beta*(w_T*dv + hist). */
 
 static void single_forward_one(int scheme, const float* x, float v, const float* w,
                                float* spike, float* vseq, float* hv, int T, int64_t N, int64_t n,
@@ -68,12 +70,14 @@ static void single_forward_one(int scheme, const float* x, float v, const float*
         if (scheme == ORC_GL)        p = dv - hist;                              /* :66 */
         else if (scheme == ORC_GL1)  p = fmaf(h_beta, dv, -hist);                /* gl1 :213 */
         else if (scheme == ORC_TRAP) p = v + fmaf(trap_factor, dv, -hist);       /* :372 */
+        else if (scheme == ORC_TRAP1) p = fmaf(h_beta, dv, v) - hist;            /* :2059 */
+        else if (scheme == ORC_PRED1) p = fmaf(h_beta, fmaf(w[T], dv, hist), v); /* :2326 */
         else                         p = fmaf(pred_scale, fmaf(w[T], dv, hist), v); /* :528 */
         const float s = (p >= th) ? 1.0f : 0.0f;
         const float vn = p - s * th;
         spike[(int64_t)k * N + n] = s;
         vseq[(int64_t)k * N + n] = vn;
-        hv[k] = (scheme == ORC_PRED) ? (-vn) / tau : vn;        /* predictor history: -v/tau */
+        hv[k] = (scheme == ORC_PRED || scheme == ORC_PRED1) ? (-vn) / tau : vn;   /* -v/tau */
         v = vn;
     }
 }
@@ -130,6 +134,61 @@ void orc_single_backward(int scheme, const float* gS, const float* gV, const flo
             }
             if (t > 0) gv = gvm; else gv0[n] = gvm;
         }
+    }
+}
+
+/* TRAP1 / PREDICTOR1 backward (fde_cupy_kernels_all.py:2072-2161, :2337-2432): the reference
+ * recomputes the trajectory with a plain fused multiply-add history sum (not the forward's
+ * Kahan sum), then runs a reverse sweep whose history term touches only the current step's
+ * gradient.  Restated operation by operation. */
+void orc_single1_backward(int scheme, const float* gS, const float* gV, const float* x,
+                          const float* v0, const float* w, float* gx, float* gv0, int T,
+                          int64_t N, float tau, float th, float sg, float h_beta) {
+    #pragma omp parallel
+    {
+        float* vl = (float*)malloc(sizeof(float) * (size_t)(T > 0 ? T : 1));
+        float* hv = (float*)malloc(sizeof(float) * (size_t)(T > 0 ? T : 1));
+        float* sp = (float*)malloc(sizeof(float) * (size_t)(T > 0 ? T : 1));
+        #pragma omp for schedule(static)
+        for (int64_t n = 0; n < N; ++n) {
+            float v = v0[n];
+            for (int k = 0; k < T; ++k) {                        /* :2103-2124, :2371-2395 */
+                const float dv = (x[(int64_t)k * N + n] - v) / tau;
+                float hist = 0.0f;
+                for (int i = 0; i < k; ++i) hist = fmaf(w[T - k + i], hv[i], hist);
+                const float p = (scheme == ORC_TRAP1) ? fmaf(h_beta, dv, v) - hist
+                                                      : fmaf(h_beta, fmaf(w[T], dv, hist), v);
+                const float s = (p >= th) ? 1.0f : 0.0f;
+                const float vn = p - s * th;
+                vl[k] = vn;
+                sp[k] = s;
+                hv[k] = (scheme == ORC_TRAP1) ? vn : (-vn) / tau;
+                v = vn;
+            }
+            float gv = 0.0f;
+            for (int t = T - 1; t >= 0; --t) {                   /* :2128-2157, :2399-2428 */
+                const int64_t o = (int64_t)t * N + n;
+                gv = gv + gV[o];
+                const float pp = fmaf(sp[t], th, vl[t]);
+                gv = fmaf(gS[o], surr_fma(pp - th, sg), gv);
+                float gvm;
+                if (scheme == ORC_TRAP1) {
+                    gx[o] = (h_beta * gv) / tau;
+                    gvm = gv * (1.0f - h_beta / tau);
+                    for (int i = 0; i < t; ++i) gvm = fmaf(-w[T - t + i], gv, gvm);
+                } else {
+                    const float hw = h_beta * w[T];
+                    gx[o] = (hw * gv) / tau;
+                    gvm = gv * (1.0f - hw / tau);
+                    for (int i = 0; i < t; ++i) gvm = gvm - ((h_beta * w[T - t + i]) * gv) / tau;
+                }
+                gv = gvm;
+            }
+            gv0[n] = gv;
+        }
+        free(vl);
+        free(hv);
+        free(sp);
     }
 }
 

@@ -17,8 +17,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "build", "liboracle.so")
 REF_PATH = os.path.join(HERE, "_ref", "libdfsnn_ref.so")
 
-GL, TRAP, PRED, GL1 = 0, 1, 2, 3
-SCHEMES = {"gl": GL, "trap": TRAP, "predictor": PRED, "gl1": GL1}
+GL, TRAP, PRED, GL1, TRAP1, PRED1 = 0, 1, 2, 3, 4, 5
+SCHEMES = {"gl": GL, "trap": TRAP, "predictor": PRED, "gl1": GL1, "trap1": TRAP1,
+           "predictor1": PRED1}
+RECOMPUTE_BACKWARD = ("trap1", "predictor1")   # backward recomputes with a plain sum
 
 _f = ctypes.c_float
 _i = ctypes.c_int
@@ -42,6 +44,7 @@ def lib():
         L = ctypes.CDLL(LIB_PATH)
         L.orc_single_forward.argtypes = [_i, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f, _f, _f]
         L.orc_single_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f, _f, _f, _f]
+        L.orc_single1_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f, _f]
         L.orc_glmulti_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f]
         L.orc_glmulti_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f]
         L.orc_glmulti_param_grads.argtypes = [_p, _p, _p, _p, _p, _i, _i64]
@@ -74,6 +77,10 @@ def ref():
             getattr(R, name).argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f]
         R.ref_gl1_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f]
         R.ref_predictor_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f, _f]
+        R.ref_trap1_forward.argtypes = [_p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f]
+        R.ref_trap1_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f]
+        R.ref_predictor1_forward.argtypes = [_p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f, _f]
+        R.ref_predictor1_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f, _f]
         R.ref_glmulti_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f]
         R.ref_glmulti_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f]
         R.ref_aligned_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f]
@@ -106,7 +113,7 @@ def _empty(T, N):
 
 
 # ---------------------------------------------------------------------------------------
-# single-order schemes (gl / trap / predictor / gl1)
+# single-order schemes (gl / trap / predictor / gl1 / trap1 / predictor1)
 # ---------------------------------------------------------------------------------------
 def single_forward(scheme, x, v0, w, tau, beta, th, h_beta=1.0, gamma1=1.0, impl="oracle"):
     x, v0, w = _c(x), _c(v0), _c(w)
@@ -124,6 +131,10 @@ def single_forward(scheme, x, v0, w, tau, beta, th, h_beta=1.0, gamma1=1.0, impl
             R.ref_trap_forward(*args)
         elif scheme == "gl1":
             R.ref_gl1_forward(*args, h_beta)
+        elif scheme == "trap1":
+            R.ref_trap1_forward(*args, h_beta)
+        elif scheme == "predictor1":
+            R.ref_predictor1_forward(*args, h_beta, gamma1)
         else:
             R.ref_predictor_forward(*args, h_beta, gamma1)
     return s, v
@@ -136,7 +147,10 @@ def single_backward(scheme, gS, gV, x, v0, w, tau, beta, th, sg, h_beta=1.0, gam
     T, N = x.shape
     gx = _empty(T, N)
     gv0 = np.empty(N, dtype=np.float32)
-    if impl == "oracle":
+    if impl == "oracle" and scheme in RECOMPUTE_BACKWARD:
+        lib().orc_single1_backward(SCHEMES[scheme], _ptr(gS), _ptr(gV), _ptr(x), _ptr(v0), _ptr(w),
+                                   _ptr(gx), _ptr(gv0), T, N, tau, th, sg, h_beta)
+    elif impl == "oracle":
         if spike is None or vseq is None:
             spike, vseq = single_forward(scheme, x, v0, w, tau, beta, th, h_beta, gamma1)
         spike, vseq = _c(spike), _c(vseq)
@@ -153,6 +167,10 @@ def single_backward(scheme, gS, gV, x, v0, w, tau, beta, th, sg, h_beta=1.0, gam
             R.ref_trap_backward(*args)
         elif scheme == "gl1":
             R.ref_gl1_backward(*args, h_beta)
+        elif scheme == "trap1":
+            R.ref_trap1_backward(*args, h_beta)
+        elif scheme == "predictor1":
+            R.ref_predictor1_backward(*args, h_beta, gamma1)
         else:
             R.ref_predictor_backward(*args, h_beta, gamma1)
     return gx, gv0

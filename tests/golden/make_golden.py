@@ -163,12 +163,14 @@ def kernel_fixtures(T, N, seed):
     crev = c[::-1].copy()
     hb = np.float32(H ** beta)
     g1 = np.float32(math.exp(math.lgamma(beta + 1.0)))
-    for scheme in ("gl", "trap", "predictor"):
-        s, v = oracle.single_forward(scheme, x, v0, crev, TAU, beta, TH, hb, g1, impl="ref")
-        gx, gv0 = oracle.single_backward(scheme, gS, gV, x, v0, crev, TAU, beta, TH, SG, hb, g1,
+    for scheme in ("gl", "trap", "predictor", "gl1", "trap1", "predictor1"):
+        # TRAP1 receives h_beta = 1**beta = 1 from its Function (fde_cupy_kernels_all.py:2190)
+        hbs = np.float32(1.0) if scheme == "trap1" else hb
+        s, v = oracle.single_forward(scheme, x, v0, crev, TAU, beta, TH, hbs, g1, impl="ref")
+        gx, gv0 = oracle.single_backward(scheme, gS, gV, x, v0, crev, TAU, beta, TH, SG, hbs, g1,
                                          impl="ref")
         _save(f"kern_{scheme}_T{T}.npz", x=x, v0=v0, w=crev, gS=gS, gV=gV, beta=np.float32(beta),
-              h_beta=hb, gamma1=g1, spike=s, v=v, gx=gx, gv0=gv0)
+              h_beta=hbs, gamma1=g1, spike=s, v=v, gx=gx, gv0=gv0)
     scale, W = glmulti_schedule(T)
     for full in (0, 1):
         fw = oracle.glmulti_forward(x, v0, scale, W, TAU, TH, impl="ref")

@@ -239,17 +239,21 @@ def test_aligned_history_rho():
 # single-order schemes
 # -------------------------------------------------------------------------------------
 SCHEME_FN = {"gl": fde_kernels.LIFFDEGLFunction, "trap": fde_kernels.LIFFDETRAPFunction,
-             "predictor": fde_kernels.LIFFDEPREDICTORFunction, "gl1": fde_kernels.LIFFDEGL1Function}
+             "predictor": fde_kernels.LIFFDEPREDICTORFunction, "gl1": fde_kernels.LIFFDEGL1Function,
+             "trap1": fde_kernels.LIFFDETRAP1Function,
+             "predictor1": fde_kernels.LIFFDEPREDICTOR1Function}
+BASE_TABLE = {"gl1": "gl", "trap1": "trap", "predictor1": "predictor"}
 
 
 def single_weights(method, beta, T):
     d = np.load(os.path.join(GOLDEN, "torch_tables.npz"))
-    key = f"{'gl' if method == 'gl1' else method}_b{beta}_T{T}"
+    base = BASE_TABLE.get(method, method)
+    key = f"{base}_b{beta}_T{T}"
     if key in d:
         return d[key]
     from dfsnn_b200 import schedule
-    fn = {"gl": schedule.gl_weights, "gl1": schedule.gl_weights, "trap": schedule.trap_weights,
-          "predictor": schedule.predictor_weights}[method]
+    fn = {"gl": schedule.gl_weights, "trap": schedule.trap_weights,
+          "predictor": schedule.predictor_weights}[base]
     return fn(beta, T).numpy()
 
 
@@ -258,9 +262,9 @@ def run_single(method, x, v0, w, tau, beta, gS, gV, h=0.1):
     xt, v0t = cuda(x).requires_grad_(True), cuda(v0).requires_grad_(True)
     wt = cuda(w)
     fn = SCHEME_FN[method]
-    if method == "gl":
-        s, v = fn.apply(xt, v0t, wt, tau, beta, TH, 0.0, SG)
-    elif method == "trap":
+    if method in ("gl", "trap", "trap1"):
+        if method == "trap1":
+            hb = 1.0                                   # the Function passes 1**beta
         s, v = fn.apply(xt, v0t, wt, tau, beta, TH, 0.0, SG)
     elif method == "gl1":
         s, v = fn.apply(xt, v0t, wt, tau, beta, h, TH, 0.0, SG)
@@ -271,7 +275,7 @@ def run_single(method, x, v0, w, tau, beta, gS, gV, h=0.1):
     return cpu(s), cpu(v), cpu(xt.grad), cpu(v0t.grad), hb, g1
 
 
-@pytest.mark.parametrize("method", ["gl", "trap", "predictor", "gl1"])
+@pytest.mark.parametrize("method", ["gl", "trap", "predictor", "gl1", "trap1", "predictor1"])
 @pytest.mark.parametrize("T,N", [(1, 50), (5, 999), (8, 1000), (16, 4099), (20, 512), (32, 300),
                                  (33, 300), (64, 1000), (100, 257), (256, 130), (8, 2), (16, 2),
                                  (16, 4100), (8, 70002), (16, 70000)])
