@@ -220,9 +220,9 @@ int dfsnn_single_forward(int scheme, const float* x, const float* v0, const floa
                          float* spike, float* v_seq, unsigned int* spike_bits, int T,
                          long long N, float tau, float beta, float threshold, float h_beta,
                          float gamma_beta_plus_1, void* stream) {
-    if (scheme < DFSNN_GL || scheme > DFSNN_PREDICTOR1) return DFSNN_ERR_SCHEME;
+    if (scheme < DFSNN_GL || scheme > DFSNN_EULER_LIF) return DFSNN_ERR_SCHEME;
     if (int s = check_seq(T, N, DFSNN_MAX_T)) return s;
-    if (!weights) return DFSNN_ERR_NULL;
+    if (!weights && scheme != DFSNN_EULER_LIF) return DFSNN_ERR_NULL;
     if (N > 0 && (!x || !v0 || !spike || !v_seq || !spike_bits)) return DFSNN_ERR_NULL;
     if (!valid_tau(tau) || !finite(beta) || !finite(threshold) || !finite(h_beta) ||
         !finite(gamma_beta_plus_1))
@@ -240,9 +240,10 @@ int dfsnn_single_backward(int scheme, const float* grad_spike, const float* grad
                           long long N, float tau, float beta, float threshold,
                           float surrogate_scale, float h_beta, float gamma_beta_plus_1,
                           void* stream) {
-    if (scheme < DFSNN_GL || scheme > DFSNN_GL1) return DFSNN_ERR_SCHEME;
+    if ((scheme < DFSNN_GL || scheme > DFSNN_GL1) && scheme != DFSNN_EULER_LIF)
+        return DFSNN_ERR_SCHEME;                  // TRAP1 / PREDICTOR1: recompute backward
     if (int s = check_seq(T, N, DFSNN_MAX_T)) return s;
-    if (!weights) return DFSNN_ERR_NULL;
+    if (!weights && scheme != DFSNN_EULER_LIF) return DFSNN_ERR_NULL;
     if (N > 0 && (!grad_spike || !grad_v || !v_seq || !spike_bits || !grad_x || !grad_v0))
         return DFSNN_ERR_NULL;
     if (!valid_tau(tau) || !finite(beta) || !finite(threshold) || !finite(surrogate_scale) ||

@@ -7,7 +7,7 @@
 
 namespace dfsnn {
 
-enum Scheme { kGL = 0, kTRAP = 1, kPRED = 2, kGL1 = 3, kTRAP1 = 4, kPRED1 = 5 };
+enum Scheme { kGL = 0, kTRAP = 1, kPRED = 2, kGL1 = 3, kTRAP1 = 4, kPRED1 = 5, kEULER = 6 };
 
 // library glmulti
 cudaError_t glmulti_forward_launch(const float* x, const float* v0, const float* scale,

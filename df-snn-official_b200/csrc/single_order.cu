@@ -243,6 +243,9 @@ __device__ __forceinline__ void single_bwd_step(const SingleArgs& a, int t, floa
         const float q = div_tau<TP2>(gdc, a.tau, a.inv_tau);
         *gx_out = q;
         gvm = __fsub_rn(gv, q);
+    } else if constexpr (SCHEME == kEULER) {                            // LIFEuler :2645-2647
+        *gx_out = div_tau<TP2>(gv, a.tau, a.inv_tau);
+        gvm = __fmul_rn(gv, __fsub_rn(1.0f, __fdiv_rn(1.0f, a.tau)));
     } else {                                                            // GL1 :296-312
         const float gd = __fmul_rn(a.h_beta, gv);
         *gx_out = div_tau<TP2>(gd, a.tau, a.inv_tau);
@@ -322,6 +325,33 @@ __global__ void __launch_bounds__(256) single_bwd_loop(SingleArgs a) {
         st_stream(a.gx + t * N + n, gxt);
     }
     a.gv0[n] = gv;
+}
+
+// ------------------------------------------------------------------------------------
+// LIFEuler forward (fde_cupy_kernels_all.py:2546-2584): v + (x - v)/tau, no history; one
+// neuron per thread, streaming, spike bitmask for the backward as for the other schemes.
+// ------------------------------------------------------------------------------------
+template <bool TP2>
+__global__ void __launch_bounds__(256) euler_lif_fwd(SingleArgs a) {
+    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= a.N) return;
+    const long long N = a.N;
+    const int T = a.T;
+    float v = a.v0[n];
+    uint32_t word = 0;
+    for (int k = 0; k < T; ++k) {
+        const float dv = div_tau<TP2>(__fsub_rn(ld_stream(a.x + k * N + n), v), a.tau, a.inv_tau);
+        const float p = __fadd_rn(v, dv);
+        const bool fire = p >= a.th;
+        v = fire ? __fsub_rn(p, a.th) : p;                   // p - spike*th
+        st_stream(a.spike + k * N + n, fire ? 1.0f : 0.0f);
+        st_stream(a.v + k * N + n, v);
+        word |= (fire ? 1u : 0u) << (k & 31);
+        if ((k & 31) == 31 || k == T - 1) {
+            a.bits[(k >> 5) * N + n] = word;
+            word = 0;
+        }
+    }
 }
 
 // ------------------------------------------------------------------------------------
@@ -414,6 +444,10 @@ bool aligned8_all(const void* p, const void* q, const void* r, const void* s, co
 template <int SCHEME, bool TP2>
 cudaError_t fwd_dispatch(const SingleArgs& a, cudaStream_t st) {
     const int T = a.T;
+    if constexpr (SCHEME == kEULER) {
+        euler_lif_fwd<TP2><<<(unsigned)((a.N + 255) / 256), 256, 0, st>>>(a);
+        return cudaGetLastError();
+    }
     if ((T == 8 || T == 16) && (a.N % 2) == 0 && aligned8_all(a.x, a.v0, a.spike, a.v, a.bits)) {
         const unsigned grid = (unsigned)((a.N / 2 + 255) / 256);
         if (T == 8) single_fwd_x2<SCHEME, 8, TP2><<<grid, 256, 0, st>>>(a);
@@ -460,6 +494,7 @@ cudaError_t fwd_scheme(int scheme, const SingleArgs& a, cudaStream_t st) {
         case kGL1: return fwd_dispatch<kGL1, TP2>(a, st);
         case kTRAP1: return fwd_dispatch<kTRAP1, TP2>(a, st);
         case kPRED1: return fwd_dispatch<kPRED1, TP2>(a, st);
+        case kEULER: return fwd_dispatch<kEULER, TP2>(a, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -471,6 +506,7 @@ cudaError_t bwd_scheme(int scheme, const SingleArgs& a, cudaStream_t st) {
         case kTRAP: return bwd_dispatch<kTRAP, TP2>(a, st);
         case kPRED: return bwd_dispatch<kPRED, TP2>(a, st);
         case kGL1: return bwd_dispatch<kGL1, TP2>(a, st);
+        case kEULER: return bwd_dispatch<kEULER, TP2>(a, st);
         default: return cudaErrorInvalidValue;
     }
 }

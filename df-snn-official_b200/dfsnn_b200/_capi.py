@@ -21,7 +21,7 @@ DFSNN_ERR_PARAM = 7
 MAX_T = 256
 MAX_T_FULL = 64
 
-GL, TRAP, PREDICTOR, GL1, TRAP1, PREDICTOR1 = 0, 1, 2, 3, 4, 5
+GL, TRAP, PREDICTOR, GL1, TRAP1, PREDICTOR1, EULER_LIF = 0, 1, 2, 3, 4, 5, 6
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int

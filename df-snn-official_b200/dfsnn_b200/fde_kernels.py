@@ -8,7 +8,8 @@ neuron.py gates on it (:1995); it is True because the native path never needs Cu
 missing native library raises on first use rather than falling back to the CPU.
 
 Native here: LIFFDEGLFunction, LIFFDEGL1Function, LIFFDETRAPFunction,
-LIFFDEPREDICTORFunction, LIFFDETRAP1Function, LIFFDEPREDICTOR1Function, LIFFDEGLMultiFunction.  The remaining reference Functions of the
+LIFFDEPREDICTORFunction, LIFFDETRAP1Function, LIFFDEPREDICTOR1Function, LIFEulerFunction,
+LIFFDEGLMultiFunction.  The remaining reference Functions of the
 module are outside this hot path and raise NotImplementedError.
 """
 import math
@@ -35,8 +36,9 @@ def _single_forward(ctx, scheme, name, x_seq, v_init, weights, tau, beta, v_thre
     T, N = x_seq.shape
     x = x_seq.float().contiguous()
     v0 = v_init.float().contiguous()
-    w = weights.float().contiguous()
-    if w.numel() < T + 1:
+    w = (torch.zeros(1, dtype=torch.float32, device=x.device) if weights is None
+         else weights.float().contiguous())
+    if weights is not None and w.numel() < T + 1:
         # The reference kernels read entries [0, T] of the table (a longer table built for a
         # larger neuron T is read the same way).
         raise ValueError(f"{name}: weight table needs at least T+1 = {T + 1} entries, got {w.numel()}")
@@ -265,6 +267,20 @@ class LIFFDEPREDICTOR1Function(torch.autograd.Function):
         return gx, gv, None, None, None, None, None, None, None, None
 
 
+class LIFEulerFunction(torch.autograd.Function):
+    """Plain LIF, explicit Euler, no history (fde_cupy_kernels_all.py:2657-2756)."""
+
+    @staticmethod
+    def forward(ctx, x_seq, v_init, tau, v_threshold, v_reset, surrogate_grad_scale):
+        return _single_forward(ctx, _capi.EULER_LIF, "LIFEulerFunction", x_seq, v_init, None, tau,
+                               0.0, v_threshold, surrogate_grad_scale)
+
+    @staticmethod
+    def backward(ctx, grad_spike_seq, grad_v_seq):
+        gx, gv = _single_backward(ctx, grad_spike_seq, grad_v_seq)
+        return gx, gv, None, None, None, None
+
+
 # ---------------------------------------------------------------------------------------
 # reference Functions outside this hot path
 # ---------------------------------------------------------------------------------------
@@ -272,12 +288,11 @@ def _not_native(name):
     def apply(*args, **kwargs):
         raise NotImplementedError(
             f"{name} is not part of the B200 LIF-FDE hot path (native: GL, GL1, TRAP, "
-            "PREDICTOR, TRAP1, PREDICTOR1, GLMULTI, aligned GLMULTI, direct Euler)")
+            "PREDICTOR, TRAP1, PREDICTOR1, LIF Euler, GLMULTI, aligned GLMULTI, direct Euler)")
 
     return type(name, (), {"apply": staticmethod(apply)})
 
 
-LIFEulerFunction = _not_native("LIFEulerFunction")
 LIFFDEVOPREDICTORFunction = _not_native("LIFFDEVOPREDICTORFunction")
 LIFFDEFAGL1Function = _not_native("LIFFDEFAGL1Function")
 LIFFDEFAGL1TorchFunction = _not_native("LIFFDEFAGL1TorchFunction")

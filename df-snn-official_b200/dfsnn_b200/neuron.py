@@ -21,7 +21,7 @@ import torch.nn.functional as F
 from . import fde_kernels as _kernels
 from . import schedule as _sched
 
-_NATIVE_METHODS = ("glmulti", "gl", "gl1", "trap", "predictor", "trap1", "predictor1")
+_NATIVE_METHODS = ("glmulti", "gl", "gl1", "trap", "predictor", "trap1", "predictor1", "euler")
 _ALL_METHODS = ("gl", "gl1", "fagl1", "vogl1", "predictor", "predictor1", "vopredictor", "trap",
                 "trap1", "euler", "glmulti")
 
@@ -307,6 +307,9 @@ class LIFNeuronFDE(nn.Module):
         elif self.method == "trap":
             s, v = K.LIFFDETRAPFunction.apply(x_flat, v_flat, self.weights, tau, beta,
                                               self.threshold, v_reset, self.surrogate_grad_scale)
+        elif self.method == "euler":                             # neuron.py:2247-2255
+            s, v = K.LIFEulerFunction.apply(x_flat, v_flat, tau, self.threshold, v_reset,
+                                            self.surrogate_grad_scale)
         elif self.method == "trap1":
             s, v = K.LIFFDETRAP1Function.apply(x_flat, v_flat, self.weights, tau, beta,
                                                self.threshold, v_reset, self.surrogate_grad_scale)

@@ -51,6 +51,7 @@ extern "C" {
 #define DFSNN_GL1 3
 #define DFSNN_TRAP1 4        /* LIFFDETRAP1Function (fde_cupy_kernels_all.py:2018-2276) */
 #define DFSNN_PREDICTOR1 5   /* LIFFDEPREDICTOR1Function (:2278-2545) */
+#define DFSNN_EULER_LIF 6    /* LIFEulerFunction (:2546-2756): no history; weights may be NULL */
 
 const char* dfsnn_status_string(int status);
 int dfsnn_last_cuda_error(void);
@@ -153,7 +154,8 @@ size_t dfsnn_spike_bits_words(int T, long long N);
  * h_beta / gamma_beta_plus_1 are used by PREDICTOR (both) and GL1 (h_beta).  Schemes
  * DFSNN_TRAP1 / DFSNN_PREDICTOR1 replace lif_fde_trap1_forward_kernel (:2018-2070) and
  * lif_fde_predictor1_forward_kernel (:2278-2335) (h_beta used by both; TRAP1's Function
- * passes h_beta = 1).  Their spike_bits output is written but their backward does not use it. */
+ * passes h_beta = 1).  Their spike_bits output is written but their backward does not use it.
+ * DFSNN_EULER_LIF replaces lif_euler_forward_kernel (:2546-2584); weights may be NULL. */
 int dfsnn_single_forward(int scheme, const float* x, const float* v0, const float* weights,
                          float* spike, float* v_seq, unsigned int* spike_bits, int T,
                          long long N, float tau, float beta, float threshold, float h_beta,
@@ -170,7 +172,8 @@ int dfsnn_single_recompute_backward(int scheme, const float* grad_spike, const f
                                     float threshold, float surrogate_scale, float h_beta,
                                     void* stream);
 
-/* Replaces the lif_fde_{gl,trap,predictor,gl1}_backward_kernel launches (:77-163,
+/* Replaces the lif_fde_{gl,trap,predictor,gl1}_backward_kernel and lif_euler_backward_kernel
+ * (:2586-2654) launches (:77-163,
  * :383-472, :541-637, :262-320; launched from :700-732, :884-916, :977-1010, :795-827):
  * truncated reverse sweep, from the saved v_seq and
  * spike bitmask instead of a recompute. */

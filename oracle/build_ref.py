@@ -35,6 +35,7 @@ LIB_KERNELS = [
     "glmulti_backward_kernel_code", "glmulti_full_backward_kernel_code",
     "trap1_forward_kernel_code", "trap1_backward_kernel_code",
     "predictor1_forward_kernel_code", "predictor1_backward_kernel_code",
+    "euler_forward_kernel_code", "euler_backward_kernel_code",
 ]
 
 # Statements whose fused multiply-add NVRTC forms but GCC does not (see collect_sources).
@@ -117,6 +118,14 @@ void ref_predictor1_backward(const float* gs, const float* gv, const float* x, c
                              const float* w, float* gx, float* gv0, int T, int N, float tau,
                              float beta, float th, float sg, float h_beta, float gamma1) {
     DFSNN_REF_LOOP(N, lif_fde_predictor1_backward_kernel(gs, gv, x, v0, w, gx, gv0, T, N, tau, beta, th, sg, h_beta, gamma1));
+}
+void ref_lifeuler_forward(const float* x, const float* v0, float* s, float* v, int T, int N,
+                          float tau, float th, float v_reset) {
+    DFSNN_REF_LOOP(N, lif_euler_forward_kernel(x, v0, s, v, T, N, tau, th, v_reset));
+}
+void ref_lifeuler_backward(const float* gs, const float* gv, const float* x, const float* v0,
+                           float* gx, float* gv0, int T, int N, float tau, float th, float sg) {
+    DFSNN_REF_LOOP(N, lif_euler_backward_kernel(gs, gv, x, v0, gx, gv0, T, N, tau, th, sg));
 }
 void ref_glmulti_forward(const float* x, const float* v0, const float* scale, const float* W,
                          float* s, float* vpre, float* vhist, float* drift, int T, int N,

@@ -44,7 +44,9 @@ static inline float surr_fma(float z, float sg) {
  * w is the reversed weight table of T+1 entries (c_rev / trap_w / pred_w); at step k
  * the history term i<k uses w[T-k+i].
  * ---------------------------------------------------------------------------------- */
-enum { ORC_GL = 0, ORC_TRAP = 1, ORC_PRED = 2, ORC_GL1 = 3, ORC_TRAP1 = 4, ORC_PRED1 = 5 };
+enum { ORC_GL = 0, ORC_TRAP = 1, ORC_PRED = 2, ORC_GL1 = 3, ORC_TRAP1 = 4, ORC_PRED1 = 5,
+       ORC_EULER = 6 };
+/* EULER = LIFEulerFunction (fde_cupy_kernels_all.py:2546-2756): v + dv, no history term. */
 /* TRAP1 (fde_cupy_kernels_all.py:2018-2070) and PREDICTOR1 (:2278-2335) share the Kahan
  * forward; their updates are v + h_beta*dv - hist and v + h_beta*(w_T*dv + hist). */
 
@@ -56,7 +58,7 @@ static void single_forward_one(int scheme, const float* x, float v, const float*
     for (int k = 0; k < T; ++k) {
         const float dv = (x[(int64_t)k * N + n] - v) / tau;    /* (-v + x)/tau */
         float hist = 0.0f;
-        if (k > 0) {                                            /* Kahan, :52-63 */
+        if (k > 0 && scheme != ORC_EULER) {                     /* Kahan, :52-63 */
             float sum = 0.0f, c = 0.0f;
             for (int i = 0; i < k; ++i) {
                 const float y = fmaf(w[T - k + i], hv[i], -c);
@@ -72,6 +74,7 @@ static void single_forward_one(int scheme, const float* x, float v, const float*
         else if (scheme == ORC_TRAP) p = v + fmaf(trap_factor, dv, -hist);       /* :372 */
         else if (scheme == ORC_TRAP1) p = fmaf(h_beta, dv, v) - hist;            /* :2059 */
         else if (scheme == ORC_PRED1) p = fmaf(h_beta, fmaf(w[T], dv, hist), v); /* :2326 */
+        else if (scheme == ORC_EULER) p = v + dv;                                 /* :2571 */
         else                         p = fmaf(pred_scale, fmaf(w[T], dv, hist), v); /* :528 */
         const float s = (p >= th) ? 1.0f : 0.0f;
         const float vn = p - s * th;
@@ -126,6 +129,9 @@ void orc_single_backward(int scheme, const float* gS, const float* gV, const flo
                 const float gdc = (gv * pred_scale) * w[T];
                 gx[o] = gdc / tau;
                 gvm = gv - gdc / tau;
+            } else if (scheme == ORC_EULER) {                    /* :2645-2647 */
+                gx[o] = gv / tau;
+                gvm = gv * (1.0f - 1.0f / tau);
             } else {                                             /* GL1 :296-312 */
                 const float gd = h_beta * gv;
                 gx[o] = gd / tau;

@@ -17,9 +17,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "build", "liboracle.so")
 REF_PATH = os.path.join(HERE, "_ref", "libdfsnn_ref.so")
 
-GL, TRAP, PRED, GL1, TRAP1, PRED1 = 0, 1, 2, 3, 4, 5
+GL, TRAP, PRED, GL1, TRAP1, PRED1, EULER = 0, 1, 2, 3, 4, 5, 6
 SCHEMES = {"gl": GL, "trap": TRAP, "predictor": PRED, "gl1": GL1, "trap1": TRAP1,
-           "predictor1": PRED1}
+           "predictor1": PRED1, "euler": EULER}
 RECOMPUTE_BACKWARD = ("trap1", "predictor1")   # backward recomputes with a plain sum
 
 _f = ctypes.c_float
@@ -81,6 +81,8 @@ def ref():
         R.ref_trap1_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f]
         R.ref_predictor1_forward.argtypes = [_p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f, _f]
         R.ref_predictor1_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f, _f]
+        R.ref_lifeuler_forward.argtypes = [_p, _p, _p, _p, _i, _i, _f, _f, _f]
+        R.ref_lifeuler_backward.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f]
         R.ref_glmulti_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f]
         R.ref_glmulti_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f]
         R.ref_aligned_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f]
@@ -122,6 +124,8 @@ def single_forward(scheme, x, v0, w, tau, beta, th, h_beta=1.0, gamma1=1.0, impl
     if impl == "oracle":
         lib().orc_single_forward(SCHEMES[scheme], _ptr(x), _ptr(v0), _ptr(w), _ptr(s), _ptr(v),
                                  T, N, tau, beta, th, h_beta, gamma1)
+    elif scheme == "euler":
+        ref().ref_lifeuler_forward(_ptr(x), _ptr(v0), _ptr(s), _ptr(v), T, N, tau, th, 0.0)
     else:
         R = ref()
         args = [_ptr(x), _ptr(v0), _ptr(w), _ptr(s), _ptr(v), T, N, tau, beta, th, 0.0]
@@ -157,6 +161,9 @@ def single_backward(scheme, gS, gV, x, v0, w, tau, beta, th, sg, h_beta=1.0, gam
         lib().orc_single_backward(SCHEMES[scheme], _ptr(gS), _ptr(gV), _ptr(spike), _ptr(vseq),
                                   _ptr(w), _ptr(gx), _ptr(gv0), T, N, tau, beta, th, sg,
                                   h_beta, gamma1)
+    elif scheme == "euler":
+        ref().ref_lifeuler_backward(_ptr(gS), _ptr(gV), _ptr(x), _ptr(v0), _ptr(gx), _ptr(gv0),
+                                    T, N, tau, th, sg)
     else:
         R = ref()
         args = [_ptr(gS), _ptr(gV), _ptr(x), _ptr(v0), _ptr(w), _ptr(gx), _ptr(gv0), T, N,

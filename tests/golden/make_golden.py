@@ -163,7 +163,7 @@ def kernel_fixtures(T, N, seed):
     crev = c[::-1].copy()
     hb = np.float32(H ** beta)
     g1 = np.float32(math.exp(math.lgamma(beta + 1.0)))
-    for scheme in ("gl", "trap", "predictor", "gl1", "trap1", "predictor1"):
+    for scheme in ("gl", "trap", "predictor", "gl1", "trap1", "predictor1", "euler"):
         # TRAP1 receives h_beta = 1**beta = 1 from its Function (fde_cupy_kernels_all.py:2190)
         hbs = np.float32(1.0) if scheme == "trap1" else hb
         s, v = oracle.single_forward(scheme, x, v0, crev, TAU, beta, TH, hbs, g1, impl="ref")

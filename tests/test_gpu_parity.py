@@ -241,11 +241,14 @@ def test_aligned_history_rho():
 SCHEME_FN = {"gl": fde_kernels.LIFFDEGLFunction, "trap": fde_kernels.LIFFDETRAPFunction,
              "predictor": fde_kernels.LIFFDEPREDICTORFunction, "gl1": fde_kernels.LIFFDEGL1Function,
              "trap1": fde_kernels.LIFFDETRAP1Function,
-             "predictor1": fde_kernels.LIFFDEPREDICTOR1Function}
+             "predictor1": fde_kernels.LIFFDEPREDICTOR1Function,
+             "euler": fde_kernels.LIFEulerFunction}
 BASE_TABLE = {"gl1": "gl", "trap1": "trap", "predictor1": "predictor"}
 
 
 def single_weights(method, beta, T):
+    if method == "euler":
+        return np.zeros(T + 1, np.float32)       # no history term (the Function takes no table)
     d = np.load(os.path.join(GOLDEN, "torch_tables.npz"))
     base = BASE_TABLE.get(method, method)
     key = f"{base}_b{beta}_T{T}"
@@ -262,7 +265,9 @@ def run_single(method, x, v0, w, tau, beta, gS, gV, h=0.1):
     xt, v0t = cuda(x).requires_grad_(True), cuda(v0).requires_grad_(True)
     wt = cuda(w)
     fn = SCHEME_FN[method]
-    if method in ("gl", "trap", "trap1"):
+    if method == "euler":
+        s, v = fn.apply(xt, v0t, tau, TH, 0.0, SG)
+    elif method in ("gl", "trap", "trap1"):
         if method == "trap1":
             hb = 1.0                                   # the Function passes 1**beta
         s, v = fn.apply(xt, v0t, wt, tau, beta, TH, 0.0, SG)
@@ -275,7 +280,8 @@ def run_single(method, x, v0, w, tau, beta, gS, gV, h=0.1):
     return cpu(s), cpu(v), cpu(xt.grad), cpu(v0t.grad), hb, g1
 
 
-@pytest.mark.parametrize("method", ["gl", "trap", "predictor", "gl1", "trap1", "predictor1"])
+@pytest.mark.parametrize("method", ["gl", "trap", "predictor", "gl1", "trap1", "predictor1",
+                                    "euler"])
 @pytest.mark.parametrize("T,N", [(1, 50), (5, 999), (8, 1000), (16, 4099), (20, 512), (32, 300),
                                  (33, 300), (64, 1000), (100, 257), (256, 130), (8, 2), (16, 2),
                                  (16, 4100), (8, 70002), (16, 70000)])

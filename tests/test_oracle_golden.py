@@ -80,7 +80,8 @@ def test_aligned_vs_reference_torch(case):
     assert_close(r["gW"], d["gw"], what="grad w")
 
 
-@pytest.mark.parametrize("method", ["gl", "trap", "predictor", "gl1", "trap1", "predictor1"])
+@pytest.mark.parametrize("method", ["gl", "trap", "predictor", "gl1", "trap1", "predictor1",
+                                    "euler"])
 def test_single_vs_reference_kernels_bitwise(method):
     d = load(f"kern_{method}_T16.npz")
     beta = float(d["beta"])
