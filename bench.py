@@ -59,9 +59,10 @@ def parse():
                     help="profiling: comma list of scheme:T (e.g. glmulti:16) instead of all")
     ap.add_argument("--neurons", type=int, default=0,
                     help="profiling: neurons per GPU instead of 16*128*64*64")
-    ap.add_argument("--workload", choices=("layers", "cnn128"), default="layers",
+    ap.add_argument("--workload", choices=("layers", "cnn128", "history"), default="layers",
                     help="layers: the LIFNeuronFDE layer step (default); cnn128: synthetic "
-                         "CNN128 training step, data-parallel, samples/s")
+                         "CNN128 training step, data-parallel, samples/s; history: the "
+                         "VO-GL1 / FAGL1 / VO-PREDICTOR Functions with per-sample tables")
     args = ap.parse_args()
     global SHAPE, COMBOS
     if args.only:
@@ -611,10 +612,147 @@ def run_cnn128(args):
     return 0
 
 
+HIST_KINDS = ("vogl1", "fagl1", "vopred")
+
+
+def history_tables(T, B, dev, g):
+    """Per-sample tables as LIFNeuronFDE builds them: VO-GL1 / VO-PREDICTOR from a beta[T, B]
+    schedule in (0.2, 0.8); FAGL1 rows = GL coefficients (beta 0.5) x a positive attention."""
+    from dfsnn_b200 import schedule
+    beta = 0.2 + 0.6 * torch_rand((T, B), dev, g)
+    vo = schedule.build_vogl1_schedule(beta, H)
+    vp = schedule.build_vopredictor_schedule(beta, H)
+    att = 0.5 + torch_rand((T, B, T), dev, g)
+    gl = schedule.build_vogl1_schedule(beta.new_full((T,), 0.5), H)["weights"]
+    return {"vogl1": (vo["scale"], vo["weights"]), "vopred": (vp["scale"], vp["weights"]),
+            "fagl1": (None, (gl[:, None, :] * att).contiguous())}
+
+
+def torch_rand(shape, dev, g):
+    import torch
+    return torch.rand(shape, device=dev, generator=g)
+
+
+def run_history(args):
+    """One step: VO-GL1 (full history), FAGL1 (full history) and VO-PREDICTOR, each forward +
+    backward with gradients for x, scale and weights, at T = 8 and 16 on [T, N] inputs with
+    per-sample tables (B = 16 samples of N/16 neurons)."""
+    import torch
+    import torch.distributed as dist
+    from dfsnn_b200 import fde_kernels as fk
+    from dfsnn_b200 import profiling
+    from dfsnn_b200.distributed import allreduce_flat, init_process_group
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        init_process_group("nccl", timeout_s=300, device=dev)
+    K, W = args.steps, max(args.warmup, 3)
+    B = SHAPE[0]
+    neurons = math.prod(SHAPE)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    x16 = torch.randn((16, neurons), device=dev, generator=g).mul_(0.5).add_(0.3)
+    gS16 = torch.randn((16, neurons), device=dev, generator=g)
+    tabs = {T: history_tables(T, B, dev, g) for T in TS}
+    for T in TS:
+        for kind in HIST_KINDS:
+            sc, Wt = tabs[T][kind]
+            tabs[T][kind] = (None if sc is None else sc.detach().requires_grad_(True),
+                             Wt.detach().requires_grad_(True))
+    v0 = torch.zeros(neurons, device=dev)
+    hb = H ** 0.5
+
+    def step():
+        pgrads = []
+        for T in TS:
+            for kind in HIST_KINDS:
+                sc, Wt = tabs[T][kind]
+                x = x16[:T].detach().requires_grad_(True)
+                if kind == "vogl1":
+                    s = fk.LIFFDEVOGL1Function.apply(x, v0, sc, Wt, TAU, TH, SG, B, True)
+                    ins = [x, sc, Wt]
+                elif kind == "fagl1":
+                    s = fk.LIFFDEFAGL1Function.apply(x, v0, Wt, TAU, hb, TH, SG, B, True)
+                    ins = [x, Wt]
+                else:
+                    s = fk.LIFFDEVOPREDICTORFunction.apply(x, v0, sc, Wt, TAU, TH, SG, 0.25, B)
+                    ins = [x, sc, Wt]
+                res = torch.autograd.grad([s], ins, [gS16[:T]])
+                pgrads += list(res[1:])
+        if world > 1:
+            allreduce_flat(pgrads)
+        return pgrads
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with profiling.NativeCallTimer() as timer:
+        start.record()
+        for _ in range(K):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    units = sum(TS) * neurons * len(HIST_KINDS)
+    summary = timer.summary()
+    peak, peak_src = measured_hbm_peak()
+    dom = max(summary.items(), key=lambda kv: kv[1]["ms_total"]) if summary else None
+    roofline = None
+    if dom is not None:
+        name, d = dom
+        roofline = {"bound": "hbm", "kernel": name, "achieved": d["gbs"], "peak": peak,
+                    "unit": "GB/s", "frac": d["gbs"] / peak if d["gbs"] else None,
+                    "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
+                    "algorithmic_bytes_per_launch": d["bytes_per_call"], "traffic": None}
+    if rank == 0:
+        line = {
+            "metric": "LIF-FDE history-table Functions neuron-timesteps/s fwd+bwd",
+            "value": world * K * units / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "LIFFDEVOGL1Function (full history), LIFFDEFAGL1Function "
+                       "(full history), LIFFDEVOPREDICTORFunction fwd+bwd with grads of x, scale "
+                       "and weights; per-sample tables, B=16, x [T, 8,388,608] ~N(0.3,0.5^2), "
+                       "T=8 and 16", "neurons_per_gpu": neurons, "T": list(TS),
+                       "l2": "inputs larger than L2 (no flush)",
+                       "parallelism": f"dp{world}" + (" (one NCCL all-reduce of the table grads "
+                                                      "per step)" if world > 1 else "")},
+            "gpu_launches": timer.total_launches(),
+            "roofline": roofline,
+            "kernels": {k: {"calls_per_step": v["calls"] / K,
+                            "ms_per_call": round(v["ms_per_call"], 4),
+                            "gbs": round(v["gbs"], 1) if v["gbs"] else None,
+                            "frac_of_hbm": round(v["gbs"] / peak, 4) if v["gbs"] else None}
+                        for k, v in summary.items()},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.workload == "cnn128":
         return run_cnn128(args) if args.impl == "native" else 0
+    if args.workload == "history":
+        return run_history(args) if args.impl == "native" else 0
     if args.impl == "reference":
         return run_reference(args)
     return run_native(args)

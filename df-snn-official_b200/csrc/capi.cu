@@ -273,6 +273,169 @@ int dfsnn_single_recompute_backward(int scheme, const float* grad_spike, const f
                                                       (cudaStream_t)stream));
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// VO-GL1 / FAGL1 / VO-PREDICTOR
+// ---------------------------------------------------------------------------------------
+namespace {
+
+// Workspace: grad_pre [T, N] floats, then the partial rows (B*chunks rows of T + T*T
+// doubles), then the summed rows ((per_batch ? B : 1) of them), each on a 256-byte boundary.
+struct HistWs {
+    size_t gpre, part, msum, total;
+    int chunks;
+};
+
+HistWs hist_ws(int T, long long N, int B, int per_batch) {
+    HistWs w;
+    const size_t R = (size_t)T + (size_t)T * T;
+    w.chunks = dfsnn::param_rows_chunks(T, N, B);
+    w.gpre = 0;
+    w.part = round256((size_t)T * (size_t)N * sizeof(float));
+    w.msum = w.part + round256((size_t)B * w.chunks * R * sizeof(double));
+    w.total = w.msum + round256((size_t)(per_batch ? B : 1) * R * sizeof(double));
+    return w;
+}
+
+int check_hist(int T, long long N, int B, int per_batch, int tmax) {
+    if (int s = check_seq(T, N, tmax)) return s;
+    if (B < 1 || N % B != 0) return DFSNN_ERR_SHAPE;
+    if (per_batch != 0 && per_batch != 1) return DFSNN_ERR_PARAM;
+    return DFSNN_OK;
+}
+
+int hist_forward(int kind, const float* x, const float* v0, const float* scale,
+                 const float* weights, int batch, int per_batch, float* spike, float* v_pre,
+                 float* hsrc, float* drift, int T, long long N, float tau, float threshold,
+                 float h_beta, float residual_mix, int tmax, void* stream) {
+    if (int s = check_hist(T, N, batch, per_batch, tmax)) return s;
+    if (!weights || (kind != dfsnn::kFAGL1 && !scale)) return DFSNN_ERR_NULL;
+    if (N > 0 && (!x || !v0 || !spike || !v_pre || !hsrc || (kind == dfsnn::kVOGL1 && !drift)))
+        return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(threshold) || !finite(h_beta) || !finite(residual_mix))
+        return DFSNN_ERR_PARAM;
+    return cuda_status(dfsnn::hfam_forward_launch(kind, x, v0, scale, h_beta, weights, batch,
+                                                  per_batch != 0, spike, v_pre, hsrc, drift, T,
+                                                  N, tau, threshold, residual_mix,
+                                                  tau_is_pow2(tau), (cudaStream_t)stream));
+}
+
+// V: the saved sequence the weight gradient pairs with grad_pre; E: the drift (VO-GL1's
+// grad_scale), NULL otherwise
+int hist_backward(int kind, int full, const float* grad_spike, const float* scale,
+                  const float* weights, const float* v_pre, const float* V, const float* E,
+                  int batch, int per_batch, float* grad_x, float* grad_v0, float* grad_scale,
+                  float* grad_weights, int T, long long N, float tau, float threshold,
+                  float surrogate_scale, float h_beta, float residual_mix, int tmax,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+    if (full != 0 && full != 1) return DFSNN_ERR_PARAM;
+    if (int s = check_hist(T, N, batch, per_batch, full ? DFSNN_MAX_T_FULL : tmax)) return s;
+    if (!weights || (kind != dfsnn::kFAGL1 && !scale)) return DFSNN_ERR_NULL;
+    const bool params = grad_scale || grad_weights;
+    if (N > 0 && (!grad_spike || !v_pre || !grad_x || !grad_v0)) return DFSNN_ERR_NULL;
+    if (N > 0 && params && (!V || (grad_scale && kind == dfsnn::kVOGL1 && !E)))
+        return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(threshold) || !finite(surrogate_scale) || !finite(h_beta) ||
+        !finite(residual_mix))
+        return DFSNN_ERR_PARAM;
+    const HistWs w = hist_ws(T, N, batch, per_batch);
+    if (!workspace || !aligned8(workspace) || workspace_bytes < w.total) return DFSNN_ERR_WORKSPACE;
+    char* ws = static_cast<char*>(workspace);
+    float* gpre = reinterpret_cast<float*>(ws + w.gpre);
+    double* part = reinterpret_cast<double*>(ws + w.part);
+    double* msum = reinterpret_cast<double*>(ws + w.msum);
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool p2 = tau_is_pow2(tau);
+    cudaError_t e = dfsnn::hfam_backward_launch(kind, full != 0, grad_spike, scale, h_beta,
+                                                weights, batch, per_batch != 0, v_pre, grad_x,
+                                                grad_v0, gpre, T, N, tau, threshold,
+                                                surrogate_scale, residual_mix, p2, st);
+    if (e != cudaSuccess || !params) return cuda_status(e);
+    if (N > 0) {
+        const int diag = (kind == dfsnn::kVOGL1 && grad_scale) ? dfsnn::kDiagProduct
+                                                               : dfsnn::kDiagNone;
+        e = dfsnn::param_rows_launch(gpre, V, E, T, N, batch, diag, part, w.chunks, true, st);
+    } else {
+        e = cudaMemsetAsync(part, 0, (size_t)batch * w.chunks * (T + (size_t)T * T) * sizeof(double), st);
+    }
+    if (e != cudaSuccess) return cuda_status(e);
+    return cuda_status(dfsnn::hfam_param_finalize(kind, part, w.chunks, batch, per_batch != 0, T,
+                                                  weights, scale, msum, grad_scale, grad_weights,
+                                                  st));
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t dfsnn_history_backward_workspace_size(int T, long long N, int batch, int per_batch) {
+    if (T < 1 || T > DFSNN_MAX_T || N < 0 || batch < 1 || N % batch != 0) return 0;
+    if (per_batch != 0 && per_batch != 1) return 0;
+    return hist_ws(T, N, batch, per_batch).total;
+}
+
+int dfsnn_vo_gl1_forward(const float* x, const float* v0, const float* scale,
+                         const float* weights, int batch, int per_batch, float* spike,
+                         float* v_pre, float* v_hist, float* drift, int T, long long N, float tau,
+                         float threshold, void* stream) {
+    return hist_forward(dfsnn::kVOGL1, x, v0, scale, weights, batch, per_batch, spike, v_pre,
+                        v_hist, drift, T, N, tau, threshold, 1.0f, 0.0f, DFSNN_MAX_T, stream);
+}
+
+int dfsnn_fa_gl1_forward(const float* x, const float* v0, const float* weights, int batch,
+                         int per_batch, float* spike, float* v_pre, float* v_hist, int T,
+                         long long N, float tau, float h_beta, float threshold, void* stream) {
+    return hist_forward(dfsnn::kFAGL1, x, v0, nullptr, weights, batch, per_batch, spike, v_pre,
+                        v_hist, nullptr, T, N, tau, threshold, h_beta, 0.0f, DFSNN_MAX_T_FULL,
+                        stream);
+}
+
+int dfsnn_vo_predictor_forward(const float* x, const float* v0, const float* scale,
+                               const float* weights, int batch, int per_batch, float* spike,
+                               float* v_pre, float* drift, int T, long long N, float tau,
+                               float threshold, float residual_mix, void* stream) {
+    return hist_forward(dfsnn::kVOPRED, x, v0, scale, weights, batch, per_batch, spike, v_pre,
+                        drift, nullptr, T, N, tau, threshold, 1.0f, residual_mix, DFSNN_MAX_T,
+                        stream);
+}
+
+int dfsnn_vo_gl1_backward(const float* grad_spike, const float* scale, const float* weights,
+                          const float* v_pre, const float* v_hist, const float* drift, int batch,
+                          int per_batch, float* grad_x, float* grad_v0, float* grad_scale,
+                          float* grad_weights, int T, long long N, float tau, float threshold,
+                          float surrogate_scale, int full_history, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    return hist_backward(dfsnn::kVOGL1, full_history, grad_spike, scale, weights, v_pre, v_hist,
+                         drift, batch, per_batch, grad_x, grad_v0, grad_scale, grad_weights, T, N,
+                         tau, threshold, surrogate_scale, 1.0f, 0.0f, DFSNN_MAX_T, workspace,
+                         workspace_bytes, stream);
+}
+
+int dfsnn_fa_gl1_backward(const float* grad_spike, const float* weights, const float* v_pre,
+                          const float* v_hist, int batch, int per_batch, float* grad_x,
+                          float* grad_v0, float* grad_weights, int T, long long N, float tau,
+                          float h_beta, float threshold, float surrogate_scale, int full_history,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+    return hist_backward(dfsnn::kFAGL1, full_history, grad_spike, nullptr, weights, v_pre, v_hist,
+                         nullptr, batch, per_batch, grad_x, grad_v0, nullptr, grad_weights, T, N,
+                         tau, threshold, surrogate_scale, h_beta, 0.0f, DFSNN_MAX_T_FULL,
+                         workspace, workspace_bytes, stream);
+}
+
+int dfsnn_vo_predictor_backward(const float* grad_spike, const float* scale,
+                                const float* weights, const float* v_pre, const float* drift,
+                                int batch, int per_batch, float* grad_x, float* grad_v0,
+                                float* grad_scale, float* grad_weights, int T, long long N,
+                                float tau, float threshold, float surrogate_scale,
+                                float residual_mix, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+    return hist_backward(dfsnn::kVOPRED, 0, grad_spike, scale, weights, v_pre, drift, nullptr,
+                         batch, per_batch, grad_x, grad_v0, grad_scale, grad_weights, T, N, tau,
+                         threshold, surrogate_scale, 1.0f, residual_mix, DFSNN_MAX_T, workspace,
+                         workspace_bytes, stream);
+}
+
 // ---------------------------------------------------------------------------------------
 // direct LIF-like Euler
 // ---------------------------------------------------------------------------------------

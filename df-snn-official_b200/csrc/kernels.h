@@ -41,6 +41,30 @@ cudaError_t aligned_backward_long_launch(const float* g, const float* x, const f
 int param_long_slices(int T, long long N);
 cudaError_t param_long_launch(const float* G, const float* V, const float* E, int T, long long N,
                               bool diag_product, double* part, int slices, cudaStream_t st);
+// Per-sample rows: B samples of N/B neurons, `chunks` rows per sample (row b*chunks + c),
+// each [T + T*T] doubles = {d[t], M[t][i]}.  diag: what d holds.
+enum DiagMode { kDiagNone = 0, kDiagSum = 1, kDiagProduct = 2 };
+int param_rows_chunks(int T, long long N, int B);
+cudaError_t param_rows_launch(const float* G, const float* V, const float* E, int T, long long N,
+                              int B, int diag, double* part, int chunks, bool small_ok,
+                              cudaStream_t st);
+
+// VO-GL1 / FAGL1 / VO-PREDICTOR (hfam.cu): per-neuron history kernels with shared or
+// per-sample (scale, weights) tables
+enum HistKind { kVOGL1 = 0, kFAGL1 = 1, kVOPRED = 2 };
+cudaError_t hfam_forward_launch(int kind, const float* x, const float* v0, const float* scale,
+                                float h_beta, const float* W, int B, bool per_batch, float* spike,
+                                float* vpre, float* hsrc, float* drift, int T, long long N,
+                                float tau, float th, float rm, bool tau_pow2, cudaStream_t st);
+cudaError_t hfam_backward_launch(int kind, bool full, const float* gS, const float* scale,
+                                 float h_beta, const float* W, int B, bool per_batch,
+                                 const float* vpre, float* gx, float* gv0, float* gpre, int T,
+                                 long long N, float tau, float th, float sg, float rm,
+                                 bool tau_pow2, cudaStream_t st);
+// gscale / gW from the summed rows (either may be NULL); msum holds (per_batch ? B : 1) rows
+cudaError_t hfam_param_finalize(int kind, const double* part, int chunks, int B, bool per_batch,
+                                int T, const float* W, const float* scale, double* msum,
+                                float* gscale, float* gW, cudaStream_t st);
 // true when the x / grad / v0 tiles can be staged with cp.async.bulk (16-byte rows)
 bool bulk_eligible(const void* p, const void* q, const void* r, long long N);
 

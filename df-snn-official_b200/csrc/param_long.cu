@@ -1,16 +1,27 @@
-// param_long.cu -- shared-parameter gradients of the long-history backward kernels (T > 32):
-//   gs[t]   = sum_n G[t,n] * E[t,n]   (DIAG_PRODUCT)   or   sum_n E[t,n]
-//   gW[t,i] = sum_n G[t,n] * V[i,n]
-// from [T, N] scratch arrays written by the backward sweep, i.e. the reference's
-// torch.sum(grad_pre*drift) + torch.matmul(grad_pre, v_hist^T) (fde_cupy_kernels_all.py:
-// 1999-2009) and aligned_scale + ga@h^T (aligned_glmulti.py:33-41, :141-144).
+// param_long.cu -- parameter-gradient reductions over [T, N] scratch arrays written by a
+// backward sweep:
+//   d[t]    = sum_n G[t,n] * E[t,n]   (kDiagProduct)   or   sum_n E[t,n]   (kDiagSum)
+//   M[t,i]  = sum_n G[t,n] * V[i,n]
+// i.e. the reference's torch.sum(grad_pre*drift) + torch.matmul(grad_pre, v_hist^T)
+// (fde_cupy_kernels_all.py:1999-2009), aligned_scale + ga@h^T (aligned_glmulti.py:33-41,
+// :141-144), and the per-sample sums / einsums of the VO-GL1, FAGL1 and VO-PREDICTOR
+// Functions (fde_cupy_kernels_all.py:1829-1838, :1478-1497, :1167-1181).
 //
-// Grid (slices, tiles, tiles): block (s, bt, bi) reduces neuron slice s into the 64 x 64
-// output tile (bt, bi); each of its 256 threads owns a 4 x 4 block of the tile.  Chunks of
-// 32 neurons are staged through shared memory, multiplied in fp32 and folded into double
-// accumulators per chunk.  Every block writes its part of the slice's partial row
-// [T + T*T] (double); param_finalize sums the rows in a fixed order -- deterministic, no
-// atomics.
+// Neurons are split into B samples of F consecutive neurons and each sample into `chunks`
+// segments; block row s = b*chunks + c reduces segment c of sample b and writes partial row
+// s of [T + T*T] doubles (d, then M row-major).  Nothing crosses a sample boundary, so a
+// caller sums the rows of one sample for per-sample results or all rows for shared ones,
+// in a fixed order -- deterministic, no atomics.
+//
+// Two kernels:
+//  * param_long: any T.  Grid (rows, tiles, tiles); block (s, bt, bi) computes the 64 x 64
+//    output tile (bt, bi), each of its 256 threads a 4 x 4 block, from chunks of 32 neurons
+//    staged through shared memory, multiplied in fp32 and folded into doubles per chunk.
+//  * param_small<T> (T = 8, 16): one block per row computes all T x T outputs.  Threads form
+//    groups of (T/4)^2, each thread a 4 x 4 block of M; the groups split every 256-neuron
+//    chunk by 4-neuron quads (LDS.128 of each G and V row), and the group results are summed
+//    in a fixed order at the end.  About one shared-memory wavefront per neuron, so the
+//    kernel runs at the speed of its global loads.
 #include "kernels.h"
 #include "lif_common.cuh"
 
@@ -18,32 +29,42 @@ namespace dfsnn {
 
 namespace {
 
-constexpr int kLT = 64;      // output tile edge
-constexpr int kLK = 32;      // neurons per chunk
+constexpr int kLT = 64;      // output tile edge (param_long)
+constexpr int kLK = 32;      // neurons per chunk (param_long)
 
-template <bool DIAG_PRODUCT>
+struct Segment {
+    long long nb, ne;        // neuron range [nb, ne) of this block row
+};
+
+__device__ __forceinline__ Segment row_segment(long long F, int chunks, long long per) {
+    const long long b = blockIdx.x / chunks, c = blockIdx.x % chunks;
+    const long long s0 = b * F + c * per;
+    const long long send = b * F + F;
+    return {s0, (s0 + per) < send ? (s0 + per) : send};
+}
+
+template <int DIAG>
 __global__ void __launch_bounds__(256) param_long(const float* G, const float* V, const float* E,
-                                                  int T, long long N, long long per_slice,
-                                                  double* part) {
+                                                  int T, long long N, long long F, int chunks,
+                                                  long long per, double* part) {
     __shared__ float sG[kLT][kLK + 1];
     __shared__ float sV[kLT][kLK + 1];
     __shared__ float sE[kLT][kLK + 1];
     const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
     const int t0 = blockIdx.y * kLT, i0 = blockIdx.z * kLT;
-    const bool diag = blockIdx.y == blockIdx.z;
-    const long long nb = (long long)blockIdx.x * per_slice;
-    const long long ne = (nb + per_slice) < N ? (nb + per_slice) : N;
+    const bool diag = DIAG != kDiagNone && blockIdx.y == blockIdx.z;
+    const Segment sg = row_segment(F, chunks, per);
     double acc[4][4], accs = 0.0;
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[r][c] = 0.0;
-    for (long long k0 = nb; k0 < ne; k0 += kLK) {
+    for (long long k0 = sg.nb; k0 < sg.ne; k0 += kLK) {
         // stage rows t0.. of G (and E on the diagonal) and rows i0.. of V, zeros outside
         for (int e = tid; e < kLT * kLK; e += 256) {
             const int row = e / kLK, k = e % kLK;
             const long long n = k0 + k;
-            const bool okn = n < ne;
+            const bool okn = n < sg.ne;
             sG[row][k] = (okn && t0 + row < T) ? G[(long long)(t0 + row) * N + n] : 0.0f;
             sV[row][k] = (okn && i0 + row < T) ? V[(long long)(i0 + row) * N + n] : 0.0f;
             if (diag) sE[row][k] = (okn && t0 + row < T) ? E[(long long)(t0 + row) * N + n] : 0.0f;
@@ -70,7 +91,8 @@ __global__ void __launch_bounds__(256) param_long(const float* G, const float* V
             const int row = 4 * ty + tx;
 #pragma unroll 8
             for (int k = 0; k < kLK; ++k)
-                ps = DIAG_PRODUCT ? __fmaf_rn(sG[row][k], sE[row][k], ps) : __fadd_rn(ps, sE[row][k]);
+                ps = DIAG == kDiagProduct ? __fmaf_rn(sG[row][k], sE[row][k], ps)
+                                          : __fadd_rn(ps, sE[row][k]);
             accs += (double)ps;
         }
 #pragma unroll
@@ -90,7 +112,130 @@ __global__ void __launch_bounds__(256) param_long(const float* G, const float* V
             if (i < T) row[T + t * T + i] = acc[r][c];
         }
     }
-    if (diag && tx < 4 && t0 + 4 * ty + tx < T) row[t0 + 4 * ty + tx] = accs;
+    if (blockIdx.y == blockIdx.z && tx < 4 && t0 + 4 * ty + tx < T)
+        row[t0 + 4 * ty + tx] = diag ? accs : 0.0;
+}
+
+// ---- small T -------------------------------------------------------------------------
+template <int T>
+struct SmallCfg {
+    static constexpr int kK = 256;                  // neurons per chunk
+    static constexpr int kRS = kK + 8;              // padded row: LDS.128 rows 8 banks apart
+    static constexpr int kGS = (T / 4) * (T / 4);   // threads per group
+    static constexpr int kNG = 256 / kGS;           // groups per block
+    static constexpr int kQ = kK / 4;               // quads per chunk
+    static constexpr int kStage = 3 * T * kRS * 4;
+    static constexpr int kReduce = kNG * (T * T + T) * 8;
+    static constexpr int kBytes = kStage > kReduce ? kStage : kReduce;
+};
+
+template <int T, int DIAG>
+__global__ void __launch_bounds__(256) param_small(const float* __restrict__ G,
+                                                   const float* __restrict__ V,
+                                                   const float* __restrict__ E, long long N,
+                                                   long long F, int chunks, long long per,
+                                                   double* part) {
+    using C = SmallCfg<T>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* sG = reinterpret_cast<float*>(smem);
+    float* sV = sG + T * C::kRS;
+    float* sE = sV + T * C::kRS;
+    const int tid = threadIdx.x;
+    const int grp = tid / C::kGS, lt = tid % C::kGS;
+    const int ty = lt / (T / 4), tx = lt % (T / 4);
+    // diagonal term: thread lt of a group owns rows lt, lt + kGS, ... (T / kGS of them)
+    constexpr int kDR = (T + C::kGS - 1) / C::kGS;
+    const Segment sg = row_segment(F, chunks, per);
+    double acc[4][4], dacc[kDR];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = 0.0;
+#pragma unroll
+    for (int r = 0; r < kDR; ++r) dacc[r] = 0.0;
+    for (long long k0 = sg.nb; k0 < sg.ne; k0 += C::kK) {
+        {
+            const long long n = k0 + tid;
+            const bool ok = n < sg.ne;
+#pragma unroll
+            for (int t = 0; t < T; ++t) {
+                sG[t * C::kRS + tid] = ok ? ld_stream(G + (long long)t * N + n) : 0.0f;
+                sV[t * C::kRS + tid] = ok ? ld_stream(V + (long long)t * N + n) : 0.0f;
+                if (DIAG != kDiagNone)
+                    sE[t * C::kRS + tid] = ok ? ld_stream(E + (long long)t * N + n) : 0.0f;
+            }
+        }
+        __syncthreads();
+        float pc[4][4], pd[kDR];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) pc[r][c] = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kDR; ++r) pd[r] = 0.0f;
+        for (int q = grp; q < C::kQ; q += C::kNG) {
+            float4 g[4], v[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+                g[r] = *reinterpret_cast<const float4*>(sG + (4 * ty + r) * C::kRS + 4 * q);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                v[c] = *reinterpret_cast<const float4*>(sV + (4 * tx + c) * C::kRS + 4 * q);
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    pc[r][c] = __fmaf_rn(g[r].x, v[c].x, pc[r][c]);
+                    pc[r][c] = __fmaf_rn(g[r].y, v[c].y, pc[r][c]);
+                    pc[r][c] = __fmaf_rn(g[r].z, v[c].z, pc[r][c]);
+                    pc[r][c] = __fmaf_rn(g[r].w, v[c].w, pc[r][c]);
+                }
+            if (DIAG != kDiagNone) {
+#pragma unroll
+                for (int r = 0; r < kDR; ++r) {
+                    const int t = lt + r * C::kGS;
+                    if (t < T) {
+                        const float4 e = *reinterpret_cast<const float4*>(sE + t * C::kRS + 4 * q);
+                        if (DIAG == kDiagProduct) {
+                            const float4 gg = *reinterpret_cast<const float4*>(sG + t * C::kRS + 4 * q);
+                            pd[r] = __fmaf_rn(gg.x, e.x, pd[r]);
+                            pd[r] = __fmaf_rn(gg.y, e.y, pd[r]);
+                            pd[r] = __fmaf_rn(gg.z, e.z, pd[r]);
+                            pd[r] = __fmaf_rn(gg.w, e.w, pd[r]);
+                        } else {
+                            pd[r] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(pd[r], e.x), e.y), e.z), e.w);
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[r][c] += (double)pc[r][c];
+#pragma unroll
+        for (int r = 0; r < kDR; ++r) dacc[r] += (double)pd[r];
+        __syncthreads();
+    }
+    // fixed-order sum over the groups: red[g][0..T) = d, red[g][T..) = M
+    double* red = reinterpret_cast<double*>(smem);
+    constexpr int kRow = T * T + T;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) red[grp * kRow + T + (4 * ty + r) * T + 4 * tx + c] = acc[r][c];
+#pragma unroll
+    for (int r = 0; r < kDR; ++r) {
+        const int t = lt + r * C::kGS;
+        if (t < T) red[grp * kRow + t] = dacc[r];
+    }
+    __syncthreads();
+    double* out = part + (size_t)blockIdx.x * kRow;
+    for (int e = tid; e < kRow; e += 256) {
+        double s = 0.0;
+        for (int g = 0; g < C::kNG; ++g) s += red[g * kRow + e];
+        out[e] = s;
+    }
 }
 
 }  // namespace
@@ -105,13 +250,55 @@ int param_long_slices(int T, long long N) {
 
 cudaError_t param_long_launch(const float* G, const float* V, const float* E, int T, long long N,
                               bool diag_product, double* part, int slices, cudaStream_t st) {
-    const int tiles = (T + kLT - 1) / kLT;
-    long long per = (N + slices - 1) / slices;
+    return param_rows_launch(G, V, E, T, N, 1, diag_product ? kDiagProduct : kDiagSum, part,
+                             slices, false, st);
+}
+
+int param_rows_chunks(int T, long long N, int B) {
+    const long long F = N / (B < 1 ? 1 : B);
+    long long target, cap;
+    if (T == 8 || T == 16) {
+        target = 148 * 8;
+        cap = (F + SmallCfg<8>::kK - 1) / SmallCfg<8>::kK;
+    } else {
+        const int tiles = (T + kLT - 1) / kLT;
+        target = 2368 / (tiles * tiles);
+        cap = (F + 8191) / 8192;
+    }
+    long long c = (target + B - 1) / B;
+    if (c > cap) c = cap;
+    return c < 1 ? 1 : (int)c;
+}
+
+cudaError_t param_rows_launch(const float* G, const float* V, const float* E, int T, long long N,
+                              int B, int diag, double* part, int chunks, bool small_ok,
+                              cudaStream_t st) {
+    if (N <= 0 || B < 1) return cudaSuccess;
+    const long long F = N / B;
+    long long per = (F + chunks - 1) / chunks;
+    const dim3 rows((unsigned)((long long)B * chunks));
+    if (small_ok && (T == 8 || T == 16)) {
+        per = (per + 3) / 4 * 4;
+#define DFSNN_SMALL(TV, DV)                                                                   \
+        if (T == TV && diag == DV) {                                                          \
+            auto k = param_small<TV, DV>;                                                     \
+            const int bytes = SmallCfg<TV>::kBytes;                                           \
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); \
+            if (e != cudaSuccess) return e;                                                   \
+            k<<<rows, 256, bytes, st>>>(G, V, E, N, F, chunks, per, part);                    \
+            return cudaGetLastError();                                                        \
+        }
+        DFSNN_SMALL(8, kDiagNone) DFSNN_SMALL(8, kDiagSum) DFSNN_SMALL(8, kDiagProduct)
+        DFSNN_SMALL(16, kDiagNone) DFSNN_SMALL(16, kDiagSum) DFSNN_SMALL(16, kDiagProduct)
+#undef DFSNN_SMALL
+    }
     per = (per + kLK - 1) / kLK * kLK;
     if (per < kLK) per = kLK;
-    const dim3 grid((unsigned)slices, (unsigned)tiles, (unsigned)tiles);
-    if (diag_product) param_long<true><<<grid, 256, 0, st>>>(G, V, E, T, N, per, part);
-    else param_long<false><<<grid, 256, 0, st>>>(G, V, E, T, N, per, part);
+    const int tiles = (T + kLT - 1) / kLT;
+    const dim3 grid(rows.x, (unsigned)tiles, (unsigned)tiles);
+    if (diag == kDiagProduct) param_long<kDiagProduct><<<grid, 256, 0, st>>>(G, V, E, T, N, F, chunks, per, part);
+    else if (diag == kDiagSum) param_long<kDiagSum><<<grid, 256, 0, st>>>(G, V, E, T, N, F, chunks, per, part);
+    else param_long<kDiagNone><<<grid, 256, 0, st>>>(G, V, E, T, N, F, chunks, per, part);
     return cudaGetLastError();
 }
 

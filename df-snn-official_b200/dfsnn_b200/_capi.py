@@ -58,6 +58,17 @@ SIGNATURES = {
     "dfsnn_check_surrogate_quotient": (_i, [_p, _i, _i, _i, _p, _p]),
     "dfsnn_glmulti_schedule_forward": (_i, [_p, _p, _p, _i, _i, _i, _p, _p, _p, _p]),
     "dfsnn_glmulti_schedule_backward": (_i, [_p, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p]),
+    "dfsnn_vo_gl1_forward": (_i, [_p, _p, _p, _p, _i, _i, _p, _p, _p, _p, _i, _ll, _f, _f, _p]),
+    "dfsnn_fa_gl1_forward": (_i, [_p, _p, _p, _i, _i, _p, _p, _p, _i, _ll, _f, _f, _f, _p]),
+    "dfsnn_vo_predictor_forward": (_i, [_p, _p, _p, _p, _i, _i, _p, _p, _p, _i, _ll, _f, _f, _f,
+                                        _p]),
+    "dfsnn_history_backward_workspace_size": (_sz, [_i, _ll, _i, _i]),
+    "dfsnn_vo_gl1_backward": (_i, [_p, _p, _p, _p, _p, _p, _i, _i, _p, _p, _p, _p, _i, _ll, _f,
+                                   _f, _f, _i, _p, _sz, _p]),
+    "dfsnn_fa_gl1_backward": (_i, [_p, _p, _p, _p, _i, _i, _p, _p, _p, _i, _ll, _f, _f, _f, _f,
+                                   _i, _p, _sz, _p]),
+    "dfsnn_vo_predictor_backward": (_i, [_p, _p, _p, _p, _p, _i, _i, _p, _p, _p, _p, _i, _ll, _f,
+                                         _f, _f, _f, _p, _sz, _p]),
 }
 
 _lib = None
@@ -100,6 +111,16 @@ def workspace_bytes(kind, device, T, N, full=0):
             got = int(L.dfsnn_aligned_backward_workspace_size(T, N))
         else:
             got = int(L.dfsnn_direct_euler_backward_workspace_size(N))
+        _WS_CACHE[key] = got
+    return got
+
+
+def history_workspace_bytes(device, T, N, B, per_batch):
+    """Workspace of the VO-GL1 / FAGL1 / VO-PREDICTOR backward entry points (cached)."""
+    key = ("history", device.index, T, N, B, per_batch)
+    got = _WS_CACHE.get(key)
+    if got is None:
+        got = int(lib().dfsnn_history_backward_workspace_size(T, N, B, per_batch))
         _WS_CACHE[key] = got
     return got
 

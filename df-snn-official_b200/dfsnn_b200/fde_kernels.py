@@ -7,10 +7,10 @@ gradient arities, dtype behaviour and exceptions, backed by the sm_100a C ABI
 neuron.py gates on it (:1995); it is True because the native path never needs CuPy, and a
 missing native library raises on first use rather than falling back to the CPU.
 
-Native here: LIFFDEGLFunction, LIFFDEGL1Function, LIFFDETRAPFunction,
-LIFFDEPREDICTORFunction, LIFFDETRAP1Function, LIFFDEPREDICTOR1Function, LIFEulerFunction,
-LIFFDEGLMultiFunction.  The remaining reference Functions of the
-module are outside this hot path and raise NotImplementedError.
+Every Function of the module is native: LIFFDEGLFunction, LIFFDEGL1Function,
+LIFFDETRAPFunction, LIFFDEPREDICTORFunction, LIFFDETRAP1Function, LIFFDEPREDICTOR1Function,
+LIFEulerFunction, LIFFDEGLMultiFunction, LIFFDEVOGL1Function, LIFFDEFAGL1Function,
+LIFFDEFAGL1TorchFunction and LIFFDEVOPREDICTORFunction.
 """
 import math
 
@@ -282,18 +282,284 @@ class LIFEulerFunction(torch.autograd.Function):
 
 
 # ---------------------------------------------------------------------------------------
-# reference Functions outside this hot path
+# history-table Functions with shared or per-sample parameters
+# (fde_cupy_kernels_all.py:1098-1198, :1379-1587, :1751-1843)
 # ---------------------------------------------------------------------------------------
-def _not_native(name):
-    def apply(*args, **kwargs):
-        raise NotImplementedError(
-            f"{name} is not part of the B200 LIF-FDE hot path (native: GL, GL1, TRAP, "
-            "PREDICTOR, TRAP1, PREDICTOR1, LIF Euler, GLMULTI, aligned GLMULTI, direct Euler)")
+def _hist_inputs(name, x_seq, v_init, scale, weights, batch_size, per_batch):
+    """The reference's .float().contiguous() casts plus the shape checks the native kernels
+    need (the reference reads out of bounds on a mismatch; here it is a ValueError)."""
+    if not x_seq.is_cuda:
+        raise RuntimeError(f"{name} requires CUDA tensors")
+    x = x_seq.float().contiguous()
+    v = v_init.float().contiguous()
+    s = None if scale is None else scale.float().contiguous()
+    w = weights.float().contiguous()
+    T, N = x.shape
+    B = int(batch_size)
+    if B < 1 or N % B:
+        raise ValueError(f"Flattened neuron count {N} is not divisible by batch size {B}")
+    if v.shape != (N,):
+        raise ValueError(f"{name}: v_init must have shape ({N},), got {tuple(v.shape)}")
+    expected_w = (T, B, T) if per_batch else (T, T)
+    if tuple(w.shape) != expected_w:
+        raise ValueError(f"{name}: weights must have shape {expected_w}, got {tuple(w.shape)}")
+    if s is not None and tuple(s.shape) != ((T, B) if per_batch else (T,)):
+        raise ValueError(f"{name}: scale must have shape {(T, B) if per_batch else (T,)}, "
+                         f"got {tuple(s.shape)}")
+    return x, v, s, w, T, N, B
 
-    return type(name, (), {"apply": staticmethod(apply)})
+
+def _hist_save(ctx, x, tau, threshold, surrogate_grad_scale, original_dtype, B, per_batch,
+               full=False, h_beta=1.0, residual_mix=0.0):
+    ctx.input_shape = x.shape
+    ctx.tau = float(tau)
+    ctx.threshold = float(threshold)
+    ctx.surrogate_grad_scale = float(surrogate_grad_scale)
+    ctx.original_dtype = original_dtype
+    ctx.batch_size = B
+    ctx.per_batch = int(per_batch)
+    ctx.full_history_grad = bool(full)
+    ctx.h_beta = float(h_beta)
+    ctx.residual_mix = float(residual_mix)
 
 
-LIFFDEVOPREDICTORFunction = _not_native("LIFFDEVOPREDICTORFunction")
-LIFFDEFAGL1Function = _not_native("LIFFDEFAGL1Function")
-LIFFDEFAGL1TorchFunction = _not_native("LIFFDEFAGL1TorchFunction")
-LIFFDEVOGL1Function = _not_native("LIFFDEVOGL1Function")
+def _hist_workspace(ctx, device):
+    T, N = ctx.input_shape
+    nbytes = _capi.history_workspace_bytes(device, T, N, ctx.batch_size, ctx.per_batch)
+    return torch.empty(max(nbytes, 8), dtype=torch.uint8, device=device)
+
+
+class LIFFDEVOGL1Function(torch.autograd.Function):
+    """Variable-order GL1 with a shared or per-sample schedule (fde_cupy_kernels_all.py:
+    1751-1840).
+
+    apply(x_seq[T,N], v_init[N], scale[T] or [T,B], weights[T,T] or [T,B,T], tau, threshold,
+          surrogate_grad_scale, batch_size, full_history_grad=False) -> spikes[T,N]
+    p_t = s_t*(x_t - v)/tau - sum_{i<t} W[t,i] v_i.  Backward returns (grad_x, grad_v_init,
+    grad_scale, grad_weights, None x 5); grad_weights is the full matrix -grad_pre @ v_hist^T
+    per sample (per-sample tables) or over all neurons.
+    """
+
+    @staticmethod
+    def forward(ctx, x_seq, v_init, scale, weights, tau, threshold, surrogate_grad_scale,
+                batch_size, full_history_grad=False):
+        name = "LIFFDEVOGL1Function"
+        original_dtype = x_seq.dtype
+        per_batch = int(scale.dim() == 2)
+        x, v, s, w, T, N, B = _hist_inputs(name, x_seq, v_init, scale, weights, batch_size,
+                                           per_batch)
+        spike, v_pre, v_hist, drift = (torch.empty_like(x) for _ in range(4))
+        with torch.cuda.device(x.device), _prof.native_call(
+                "vo_gl1_forward", 1, _prof.history_forward_bytes(T, N, 4), x.device):
+            code = _capi.lib().dfsnn_vo_gl1_forward(
+                _capi.ptr(x), _capi.ptr(v), _capi.ptr(s), _capi.ptr(w), B, per_batch,
+                _capi.ptr(spike), _capi.ptr(v_pre), _capi.ptr(v_hist), _capi.ptr(drift), T, N,
+                float(tau), float(threshold), _capi.stream_of(x))
+        _capi.check(code, f"{name}.forward")
+        ctx.save_for_backward(s, w, v_pre, v_hist, drift)
+        _hist_save(ctx, x, tau, threshold, surrogate_grad_scale, original_dtype, B, per_batch,
+                   full_history_grad)
+        return spike.to(dtype=original_dtype)
+
+    @staticmethod
+    def backward(ctx, grad_spike_seq):
+        s, w, v_pre, v_hist, drift = ctx.saved_tensors
+        T, N = ctx.input_shape
+        dev = v_pre.device
+        g = grad_spike_seq.float().contiguous()
+        grad_x = torch.empty((T, N), device=dev, dtype=torch.float32)
+        grad_v = torch.empty(N, device=dev, dtype=torch.float32)
+        grad_scale = torch.empty_like(s) if ctx.needs_input_grad[2] else None
+        grad_weights = torch.empty_like(w) if ctx.needs_input_grad[3] else None
+        nparam = (2 if grad_weights is not None else 0) + (1 if grad_scale is not None else 0)
+        with torch.cuda.device(dev):
+            ws = _hist_workspace(ctx, dev)
+            with _prof.native_call("vo_gl1_backward", 4 if nparam else 1,
+                                   _prof.history_backward_bytes(T, N, min(nparam, 2)), dev):
+                code = _capi.lib().dfsnn_vo_gl1_backward(
+                    _capi.ptr(g), _capi.ptr(s), _capi.ptr(w), _capi.ptr(v_pre), _capi.ptr(v_hist),
+                    _capi.ptr(drift), ctx.batch_size, ctx.per_batch, _capi.ptr(grad_x),
+                    _capi.ptr(grad_v), _capi.ptr(grad_scale), _capi.ptr(grad_weights), T, N,
+                    ctx.tau, ctx.threshold, ctx.surrogate_grad_scale, int(ctx.full_history_grad),
+                    _capi.ptr(ws), ws.numel(), _capi.stream_of(v_pre))
+        _capi.check(code, "LIFFDEVOGL1Function.backward")
+        return (grad_x.to(dtype=ctx.original_dtype), grad_v, grad_scale, grad_weights,
+                None, None, None, None, None)
+
+
+def _fagl1_forward(ctx, name, x_seq, v_init, weights, tau, h_beta, threshold,
+                   surrogate_grad_scale, batch_size, full_history_grad, torch_variant=False):
+    original_dtype = x_seq.dtype
+    if not x_seq.is_cuda:
+        raise RuntimeError(f"{name} requires CUDA tensors")
+    T = x_seq.shape[0]
+    if T > 64 and not torch_variant:
+        raise ValueError("FAGL1 CuPy kernel currently supports at most 64 time steps")
+    per_batch = int(weights.dim() == 3)
+    x, v, _, w, T, N, B = _hist_inputs(name, x_seq, v_init, None, weights, batch_size, per_batch)
+    spike, v_pre, v_hist = (torch.empty_like(x) for _ in range(3))
+    L = _capi.lib()
+    with torch.cuda.device(x.device), _prof.native_call(
+            "fa_gl1_forward", 1, _prof.history_forward_bytes(T, N, 4 if torch_variant else 3),
+            x.device):
+        if torch_variant:
+            # same recurrence through the VO-GL1 entry point with s_t = h_beta (no T <= 64 cap)
+            s = torch.full((T, B) if per_batch else (T,), float(h_beta), device=x.device,
+                           dtype=torch.float32)
+            drift = torch.empty_like(x)
+            code = L.dfsnn_vo_gl1_forward(
+                _capi.ptr(x), _capi.ptr(v), _capi.ptr(s), _capi.ptr(w), B, per_batch,
+                _capi.ptr(spike), _capi.ptr(v_pre), _capi.ptr(v_hist), _capi.ptr(drift), T, N,
+                float(tau), float(threshold), _capi.stream_of(x))
+        else:
+            code = L.dfsnn_fa_gl1_forward(
+                _capi.ptr(x), _capi.ptr(v), _capi.ptr(w), B, per_batch, _capi.ptr(spike),
+                _capi.ptr(v_pre), _capi.ptr(v_hist), T, N, float(tau), float(h_beta),
+                float(threshold), _capi.stream_of(x))
+    _capi.check(code, f"{name}.forward")
+    ctx.save_for_backward(w, v_pre, v_hist)
+    _hist_save(ctx, x, tau, threshold, surrogate_grad_scale, original_dtype, B, per_batch,
+               full_history_grad, h_beta=h_beta)
+    return spike.to(dtype=original_dtype)
+
+
+class LIFFDEFAGL1Function(torch.autograd.Function):
+    """Fixed-order GL1 with per-sample causal attention rows (fde_cupy_kernels_all.py:
+    1379-1498).
+
+    apply(x_seq[T,N], v_init[N], weights[T,T] or [T,B,T], tau, h_beta, threshold,
+          surrogate_grad_scale, batch_size, full_history_grad=False) -> spikes[T,N]
+    T <= 64.  Backward returns (grad_x, grad_v_init, grad_weights, None x 6): per sample,
+    -grad_pre @ v_hist^T on the strict lower triangle (zeros elsewhere); shared, the full matrix
+    (the reference's TF32 matmul; here fp32 products summed in double).
+    """
+
+    @staticmethod
+    def forward(ctx, x_seq, v_init, weights, tau, h_beta, threshold, surrogate_grad_scale,
+                batch_size, full_history_grad=False):
+        return _fagl1_forward(ctx, "LIFFDEFAGL1Function", x_seq, v_init, weights, tau, h_beta,
+                              threshold, surrogate_grad_scale, batch_size, full_history_grad)
+
+    @staticmethod
+    def backward(ctx, grad_spike_seq):
+        w, v_pre, v_hist = ctx.saved_tensors
+        T, N = ctx.input_shape
+        dev = v_pre.device
+        g = grad_spike_seq.float().contiguous()
+        grad_x = torch.empty((T, N), device=dev, dtype=torch.float32)
+        grad_v = torch.empty(N, device=dev, dtype=torch.float32)
+        grad_weights = torch.empty_like(w) if ctx.needs_input_grad[2] else None
+        with torch.cuda.device(dev):
+            ws = _hist_workspace(ctx, dev)
+            with _prof.native_call("fa_gl1_backward", 4 if grad_weights is not None else 1,
+                                   _prof.history_backward_bytes(
+                                       T, N, 1 if grad_weights is not None else 0), dev):
+                code = _capi.lib().dfsnn_fa_gl1_backward(
+                    _capi.ptr(g), _capi.ptr(w), _capi.ptr(v_pre), _capi.ptr(v_hist),
+                    ctx.batch_size, ctx.per_batch, _capi.ptr(grad_x), _capi.ptr(grad_v),
+                    _capi.ptr(grad_weights), T, N, ctx.tau, ctx.h_beta, ctx.threshold,
+                    ctx.surrogate_grad_scale, int(ctx.full_history_grad), _capi.ptr(ws),
+                    ws.numel(), _capi.stream_of(v_pre))
+        _capi.check(code, "LIFFDEFAGL1Function.backward")
+        return (grad_x.to(dtype=ctx.original_dtype), grad_v, grad_weights,
+                None, None, None, None, None, None)
+
+
+class LIFFDEFAGL1TorchFunction(torch.autograd.Function):
+    """The reference's PyTorch formulation of FAGL1 (fde_cupy_kernels_all.py:1501-1587) with
+    its own gradient contract: the weight gradient is -grad_pre @ v_hist^T over every entry,
+    per sample or shared.  Computed by the native VO-GL1 kernels with s_t = h_beta (the same
+    recurrence), so it agrees with the PyTorch op sequence within fp32 rounding rather than bit
+    for bit; it needs CUDA tensors, T <= 256, and T <= 64 with full_history_grad.
+    """
+
+    @staticmethod
+    def forward(ctx, x_seq, v_init, weights, tau, h_beta, threshold, surrogate_grad_scale,
+                batch_size, full_history_grad=False):
+        return _fagl1_forward(ctx, "LIFFDEFAGL1TorchFunction", x_seq, v_init, weights, tau,
+                              h_beta, threshold, surrogate_grad_scale, batch_size,
+                              full_history_grad, torch_variant=True)
+
+    @staticmethod
+    def backward(ctx, grad_spike_seq):
+        w, v_pre, v_hist = ctx.saved_tensors
+        T, N = ctx.input_shape
+        dev = v_pre.device
+        g = grad_spike_seq.float().contiguous()
+        grad_x = torch.empty((T, N), device=dev, dtype=torch.float32)
+        grad_v = torch.empty(N, device=dev, dtype=torch.float32)
+        grad_weights = torch.empty_like(w) if ctx.needs_input_grad[2] else None
+        s = torch.full((T, ctx.batch_size) if ctx.per_batch else (T,), ctx.h_beta,
+                       device=dev, dtype=torch.float32)
+        with torch.cuda.device(dev):
+            ws = _hist_workspace(ctx, dev)
+            with _prof.native_call("fa_gl1_backward", 4 if grad_weights is not None else 1,
+                                   _prof.history_backward_bytes(
+                                       T, N, 1 if grad_weights is not None else 0), dev):
+                code = _capi.lib().dfsnn_vo_gl1_backward(
+                    _capi.ptr(g), _capi.ptr(s), _capi.ptr(w), _capi.ptr(v_pre), _capi.ptr(v_hist),
+                    None, ctx.batch_size, ctx.per_batch, _capi.ptr(grad_x), _capi.ptr(grad_v),
+                    None, _capi.ptr(grad_weights), T, N, ctx.tau, ctx.threshold,
+                    ctx.surrogate_grad_scale, int(ctx.full_history_grad), _capi.ptr(ws),
+                    ws.numel(), _capi.stream_of(v_pre))
+        _capi.check(code, "LIFFDEFAGL1TorchFunction.backward")
+        return (grad_x.to(dtype=ctx.original_dtype), grad_v, grad_weights,
+                None, None, None, None, None, None)
+
+
+class LIFFDEVOPREDICTORFunction(torch.autograd.Function):
+    """Variable-order predictor with a shared or per-sample schedule (fde_cupy_kernels_all.py:
+    1098-1191).
+
+    apply(x_seq[T,N], v_init[N], scale[T] or [T,B], weights[T,T] or [T,B,T], tau, threshold,
+          surrogate_grad_scale, residual_mix, batch_size) -> spikes[T,N]
+    p_t = v0 + s_t*(d_t + sum_{i<t} W[t,i] d_i) + residual_mix*(v - v0).  Backward returns
+    (grad_x, grad_v_init, grad_scale, grad_weights, None x 5) with grad_scale = sum
+    grad_pre*(drift + W @ drift) and grad_weights = (grad_pre*scale) @ drift^T.
+    """
+
+    @staticmethod
+    def forward(ctx, x_seq, v_init, scale, weights, tau, threshold, surrogate_grad_scale,
+                residual_mix, batch_size):
+        name = "LIFFDEVOPREDICTORFunction"
+        original_dtype = x_seq.dtype
+        per_batch = int(scale.dim() == 2)
+        x, v, s, w, T, N, B = _hist_inputs(name, x_seq, v_init, scale, weights, batch_size,
+                                           per_batch)
+        spike, v_pre, drift = (torch.empty_like(x) for _ in range(3))
+        with torch.cuda.device(x.device), _prof.native_call(
+                "vo_predictor_forward", 1, _prof.history_forward_bytes(T, N, 3), x.device):
+            code = _capi.lib().dfsnn_vo_predictor_forward(
+                _capi.ptr(x), _capi.ptr(v), _capi.ptr(s), _capi.ptr(w), B, per_batch,
+                _capi.ptr(spike), _capi.ptr(v_pre), _capi.ptr(drift), T, N, float(tau),
+                float(threshold), float(residual_mix), _capi.stream_of(x))
+        _capi.check(code, f"{name}.forward")
+        ctx.save_for_backward(s, w, v_pre, drift)
+        _hist_save(ctx, x, tau, threshold, surrogate_grad_scale, original_dtype, B, per_batch,
+                   residual_mix=residual_mix)
+        return spike.to(dtype=original_dtype)
+
+    @staticmethod
+    def backward(ctx, grad_spike_seq):
+        s, w, v_pre, drift = ctx.saved_tensors
+        T, N = ctx.input_shape
+        dev = v_pre.device
+        g = grad_spike_seq.float().contiguous()
+        grad_x = torch.empty((T, N), device=dev, dtype=torch.float32)
+        grad_v = torch.empty(N, device=dev, dtype=torch.float32)
+        grad_scale = torch.empty_like(s) if ctx.needs_input_grad[2] else None
+        grad_weights = torch.empty_like(w) if ctx.needs_input_grad[3] else None
+        params = grad_scale is not None or grad_weights is not None
+        with torch.cuda.device(dev):
+            ws = _hist_workspace(ctx, dev)
+            with _prof.native_call("vo_predictor_backward", 4 if params else 1,
+                                   _prof.history_backward_bytes(T, N, 1 if params else 0), dev):
+                code = _capi.lib().dfsnn_vo_predictor_backward(
+                    _capi.ptr(g), _capi.ptr(s), _capi.ptr(w), _capi.ptr(v_pre), _capi.ptr(drift),
+                    ctx.batch_size, ctx.per_batch, _capi.ptr(grad_x), _capi.ptr(grad_v),
+                    _capi.ptr(grad_scale), _capi.ptr(grad_weights), T, N, ctx.tau,
+                    ctx.threshold, ctx.surrogate_grad_scale, ctx.residual_mix, _capi.ptr(ws),
+                    ws.numel(), _capi.stream_of(v_pre))
+        _capi.check(code, "LIFFDEVOPREDICTORFunction.backward")
+        return (grad_x.to(dtype=ctx.original_dtype), grad_v, grad_scale, grad_weights,
+                None, None, None, None, None)

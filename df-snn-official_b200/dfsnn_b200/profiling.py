@@ -101,6 +101,16 @@ def single1_backward_bytes(T, N):
     return N * (16 * T + 8)                      # grad_s, grad_v, x in; grad_x out; v0 in, grad_v0 out
 
 
+def history_forward_bytes(T, N, seqs_out):
+    return N * (4 * T * (1 + seqs_out) + 4)      # x in; spike, v_pre, history (+ drift) out; v0 in
+
+
+def history_backward_bytes(T, N, param_seqs):
+    # grad_spike, v_pre in; grad_x, grad_pre out; grad_v0 out; the parameter reduction reads
+    # grad_pre and the saved sequences back (param_seqs of them, 0 when no parameter grads)
+    return N * (4 * T * (4 + (1 + param_seqs if param_seqs else 0)) + 4)
+
+
 def euler_forward_bytes(T, N):
     return N * (8 * T + 8)                       # x in, spikes out; z0 in, z_final out
 

@@ -154,3 +154,59 @@ def predictor_weights(beta_val, T, device=None, dtype=torch.float32):
 def predictor_constants(beta, h):
     """(h^beta, Gamma(beta+1)) as _multi_step_forward_cupy passes them (:2211-2215)."""
     return h ** beta, math.exp(math.lgamma(beta + 1.0))
+
+
+def build_vogl1_schedule(beta_schedule, step_size):
+    """VO-GL1 terms for a shared beta[T] or per-sample beta[T, B] schedule
+    (LIFNeuronFDE.build_vogl1_schedule, neuron.py:2010-2031): beta clamped to
+    [1e-6, 1-1e-6], scale = h**beta, weights[t, i] = c_{t-i}^(beta_t) for i < t with
+    c_0 = 1, c_m = (1 - (1+beta_t)/m) c_{m-1}.  The reference builds each row in a Python loop
+    over lags; here the recurrence runs once for all t at a time (the same elementwise fp32
+    operations, so the same values), and the rows are one gather.  Differentiable in beta."""
+    beta = beta_schedule.to(dtype=torch.float32).clamp(1e-6, 1.0 - 1e-6)
+    T = beta.shape[0]
+    h = torch.as_tensor(step_size, device=beta.device, dtype=torch.float32)
+    scale = torch.pow(h, beta)
+    cols = [torch.ones_like(beta)]
+    for lag in range(1, T):
+        cols.append((1.0 - (1.0 + beta) / float(lag)) * cols[-1])
+    C = torch.stack(cols, dim=-1)                          # [T, (B,) lag]
+    t_idx = torch.arange(T, device=beta.device)
+    lag = (t_idx[:, None] - t_idx[None, :]).clamp_min(0)   # [t, i]
+    causal = t_idx[None, :] < t_idx[:, None]
+    if beta.dim() == 1:
+        W = torch.gather(C, 1, lag) * causal
+    else:
+        B = beta.shape[1]
+        W = torch.gather(C, 2, lag[:, None, :].expand(T, B, T)) * causal[:, None, :]
+    return {"beta": beta, "scale": scale, "weights": W}
+
+
+def build_vopredictor_schedule(beta_schedule, step_size):
+    """VO-PREDICTOR terms (LIFNeuronFDE.build_vopredictor_schedule, neuron.py:2063-2089):
+    scale = h**beta / Gamma(beta+1); row t has weights (t-i)^(beta_t-1) - (t-i-1)^(beta_t-1)
+    for i <= t-2 and 1 at i = t-1.  Built row by row with the reference's tensor shapes, so
+    pow sees the same operands (its vectorised CPU path rounds by shape)."""
+    beta = beta_schedule.to(dtype=torch.float32).clamp(1e-6, 1.0 - 1e-6)
+    T = beta.shape[0]
+    dev = beta.device
+    h = torch.as_tensor(step_size, device=dev, dtype=torch.float32)
+    scale = torch.pow(h, beta) / torch.exp(torch.lgamma(beta + 1.0))
+    per_sample = beta.dim() == 2
+    tail = (beta.shape[1],) if per_sample else ()
+    rows = []
+    for t in range(T):
+        if t == 0:
+            active = torch.zeros((0,) + tail, device=dev, dtype=torch.float32)
+        elif t == 1:
+            active = torch.ones_like(beta[t]).unsqueeze(0)
+        else:
+            lags = torch.arange(t, 1, -1, device=dev, dtype=torch.float32)
+            e = beta[t] - 1.0
+            if per_sample:
+                lags, e = lags[:, None], e[None]
+            diff = torch.pow(lags, e) - torch.pow(lags - 1.0, e)
+            active = torch.cat((diff, torch.ones((1,) + tail, device=dev)), dim=0)
+        row = torch.cat((active, torch.zeros((T - t,) + tail, device=dev)), dim=0)
+        rows.append(row.transpose(0, 1) if per_sample else row)
+    return {"beta": beta_schedule, "scale": scale, "weights": torch.stack(rows)}

@@ -210,6 +210,77 @@ int dfsnn_direct_euler_backward(const float* grad_spike, const float* grad_z_fin
                                 float spike_update_dt, void* workspace, size_t workspace_bytes,
                                 void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * History-table Functions with shared or per-sample parameters: VO-GL1, FAGL1,
+ * VO-PREDICTOR (LIFFDEVOGL1Function, LIFFDEFAGL1Function, LIFFDEVOPREDICTORFunction)
+ *
+ * batch = B: neuron n belongs to sample n / (N/B); N % B must be 0.  per_batch = 0: scale is
+ * [T] and weights [T][T]; per_batch = 1: scale is [T][B] and weights [T][B][T].  T <= 256
+ * (DFSNN_MAX_T); FAGL1 and every full-history backward T <= 64 (the reference's limits).
+ * ------------------------------------------------------------------------------- */
+
+/* Replaces the lif_fde_vo_gl1_forward_kernel launch of LIFFDEVOGL1Function.forward
+ * (fde_cupy_kernels_all.py:1786-1809 launching :1594-1630): writes spike, v_pre, v_hist (v
+ * after reset) and drift, all [T, N]. */
+int dfsnn_vo_gl1_forward(const float* x, const float* v0, const float* scale,
+                         const float* weights, int batch, int per_batch, float* spike,
+                         float* v_pre, float* v_hist, float* drift, int T, long long N, float tau,
+                         float threshold, void* stream);
+
+/* Replaces the lif_fde_fa_gl1_forward_kernel launch of LIFFDEFAGL1Function.forward
+ * (:1413-1455 launching :1200-1232); the per-step scale is h_beta.  per_batch follows the
+ * weights' rank ([T][B][T] or [T][T]). */
+int dfsnn_fa_gl1_forward(const float* x, const float* v0, const float* weights, int batch,
+                         int per_batch, float* spike, float* v_pre, float* v_hist, int T,
+                         long long N, float tau, float h_beta, float threshold, void* stream);
+
+/* Replaces the lif_fde_vo_predictor_forward_kernel launch of LIFFDEVOPREDICTORFunction.forward
+ * (:1121-1156 launching :1017-1057): writes spike, v_pre and drift. */
+int dfsnn_vo_predictor_forward(const float* x, const float* v0, const float* scale,
+                               const float* weights, int batch, int per_batch, float* spike,
+                               float* v_pre, float* drift, int T, long long N, float tau,
+                               float threshold, float residual_mix, void* stream);
+
+/* Bytes of device workspace the three backward entry points need (8-byte aligned): grad_pre
+ * plus the partial sums of the parameter reduction.  0 for invalid arguments. */
+size_t dfsnn_history_backward_workspace_size(int T, long long N, int batch, int per_batch);
+
+/* Replaces LIFFDEVOGL1Function.backward (:1811-1840): the lif_fde_vo_gl1_backward_kernel
+ * (:1633-1668) or lif_fde_vo_gl1_full_backward_kernel (:1670-1709, full_history = 1) launch,
+ * then grad_scale = sum grad_pre*drift and grad_weights = -grad_pre @ v_hist^T over each
+ * sample (per_batch) or all neurons -- every entry, upper triangle included, as the
+ * reference's einsum / matmul.  Sums in double.  grad_scale / grad_weights may be NULL
+ * (v_hist / drift are then not read). */
+int dfsnn_vo_gl1_backward(const float* grad_spike, const float* scale, const float* weights,
+                          const float* v_pre, const float* v_hist, const float* drift, int batch,
+                          int per_batch, float* grad_x, float* grad_v0, float* grad_scale,
+                          float* grad_weights, int T, long long N, float tau, float threshold,
+                          float surrogate_scale, int full_history, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* Replaces LIFFDEFAGL1Function.backward (:1457-1497): the lif_fde_fa_gl1_backward_kernel
+ * (:1235-1272) or lif_fde_fa_gl1_full_backward_kernel (:1274-1312) launch, then
+ * grad_weights = -grad_pre @ v_hist^T: per sample with zeros on and above the diagonal
+ * (lif_fde_fa_gl1_weight_grad_kernel, :1314-1344), or over all neurons with every entry (the
+ * reference's matmul, which it runs in TF32; here fp32 products summed in double). */
+int dfsnn_fa_gl1_backward(const float* grad_spike, const float* weights, const float* v_pre,
+                          const float* v_hist, int batch, int per_batch, float* grad_x,
+                          float* grad_v0, float* grad_weights, int T, long long N, float tau,
+                          float h_beta, float threshold, float surrogate_scale, int full_history,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces LIFFDEVOPREDICTORFunction.backward (:1158-1191): the
+ * lif_fde_vo_predictor_backward_kernel launch (:1058-1096), then
+ * grad_scale = sum grad_pre*(drift + weights @ drift) and
+ * grad_weights = (grad_pre*scale) @ drift^T per sample or over all neurons (full matrices). */
+int dfsnn_vo_predictor_backward(const float* grad_spike, const float* scale,
+                                const float* weights, const float* v_pre, const float* drift,
+                                int batch, int per_batch, float* grad_x, float* grad_v0,
+                                float* grad_scale, float* grad_weights, int T, long long N,
+                                float tau, float threshold, float surrogate_scale,
+                                float residual_mix, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
 /* ---- self-check (no reference counterpart) ----------------------------------------
  * The backward kernels divide the arctan surrogate's numerator by its denominator with an
  * FMA-corrected reciprocal (Markstein) instead of the IEEE division sequence.  This entry

@@ -36,6 +36,9 @@ LIB_KERNELS = [
     "trap1_forward_kernel_code", "trap1_backward_kernel_code",
     "predictor1_forward_kernel_code", "predictor1_backward_kernel_code",
     "euler_forward_kernel_code", "euler_backward_kernel_code",
+    "vo_gl1_backward_kernel_code", "vo_gl1_full_backward_kernel_code",
+    "fa_gl1_forward_kernel_code", "fa_gl1_backward_kernel_code", "fa_gl1_full_backward_kernel_code",
+    "vo_predictor_forward_kernel_code", "vo_predictor_backward_kernel_code",
 ]
 
 # Statements whose fused multiply-add NVRTC forms but GCC does not (see collect_sources).
@@ -48,6 +51,12 @@ NVRTC_CONTRACTIONS = [
      "grad_v_mem = fmaf(-trap_weights[weight_idx], grad_v, grad_v_mem);"),
     ("hist_integral += predictor_weights[weight_idx] * hist_dv;",
      "hist_integral = fmaf(predictor_weights[weight_idx], hist_dv, hist_integral);"),
+    ("hist += weights[wi] * drift_seq[i * N + n];",
+     "hist = fmaf(weights[wi], drift_seq[i * N + n], hist);"),
+    ("hist += weights[wi] * v_hist_seq[i * N + n];",
+     "hist = fmaf(weights[wi], v_hist_seq[i * N + n], hist);"),
+    ("grad_hist[i] -= weights[wi] * grad_pre;",
+     "grad_hist[i] = fmaf(-weights[wi], grad_pre, grad_hist[i]);"),
 ]
 
 # Host launchers (this repository's code): one OpenMP loop over global thread indices.
@@ -126,6 +135,42 @@ void ref_lifeuler_forward(const float* x, const float* v0, float* s, float* v, i
 void ref_lifeuler_backward(const float* gs, const float* gv, const float* x, const float* v0,
                            float* gx, float* gv0, int T, int N, float tau, float th, float sg) {
     DFSNN_REF_LOOP(N, lif_euler_backward_kernel(gs, gv, x, v0, gx, gv0, T, N, tau, th, sg));
+}
+void ref_vogl1_forward(const float* x, const float* v0, const float* scale, const float* W,
+                       float* s, float* vpre, float* vhist, float* drift, int T, int N, int B,
+                       int per_batch, float tau, float th) {
+    DFSNN_REF_LOOP(N, lif_fde_vo_gl1_forward_kernel(x, v0, scale, W, s, vpre, vhist, drift, T, N, B, per_batch, tau, th));
+}
+void ref_vogl1_backward(int full, const float* gs, const float* scale, const float* W,
+                        const float* vpre, float* gx, float* gv0, float* gpre, int T, int N,
+                        int B, int per_batch, float tau, float th, float sg) {
+    if (full)
+        DFSNN_REF_LOOP(N, lif_fde_vo_gl1_full_backward_kernel(gs, scale, W, vpre, gx, gv0, gpre, T, N, B, per_batch, tau, th, sg));
+    else
+        DFSNN_REF_LOOP(N, lif_fde_vo_gl1_backward_kernel(gs, scale, W, vpre, gx, gv0, gpre, T, N, B, per_batch, tau, th, sg));
+}
+void ref_fagl1_forward(const float* x, const float* v0, const float* W, float* s, float* vpre,
+                       float* vhist, int T, int N, int B, int per_batch, float tau, float hb,
+                       float th) {
+    DFSNN_REF_LOOP(N, lif_fde_fa_gl1_forward_kernel(x, v0, W, s, vpre, vhist, T, N, B, per_batch, tau, hb, th));
+}
+void ref_fagl1_backward(int full, const float* gs, const float* W, const float* vpre, float* gx,
+                        float* gv0, float* gpre, int T, int N, int B, int per_batch, float tau,
+                        float hb, float th, float sg) {
+    if (full)
+        DFSNN_REF_LOOP(N, lif_fde_fa_gl1_full_backward_kernel(gs, W, vpre, gx, gv0, gpre, T, N, B, per_batch, tau, hb, th, sg));
+    else
+        DFSNN_REF_LOOP(N, lif_fde_fa_gl1_backward_kernel(gs, W, vpre, gx, gv0, gpre, T, N, B, per_batch, tau, hb, th, sg));
+}
+void ref_vopred_forward(const float* x, const float* v0, const float* scale, const float* W,
+                        float* s, float* vpre, float* drift, int T, int N, int B, int per_batch,
+                        float tau, float th, float rm) {
+    DFSNN_REF_LOOP(N, lif_fde_vo_predictor_forward_kernel(x, v0, scale, W, s, vpre, drift, T, N, B, per_batch, tau, th, rm));
+}
+void ref_vopred_backward(const float* gs, const float* scale, const float* W, const float* vpre,
+                         float* gx, float* gv0, float* gpre, int T, int N, int B, int per_batch,
+                         float tau, float th, float sg, float rm) {
+    DFSNN_REF_LOOP(N, lif_fde_vo_predictor_backward_kernel(gs, scale, W, vpre, gx, gv0, gpre, T, N, B, per_batch, tau, th, sg, rm));
 }
 void ref_glmulti_forward(const float* x, const float* v0, const float* scale, const float* W,
                          float* s, float* vpre, float* vhist, float* drift, int T, int N,

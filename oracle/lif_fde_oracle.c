@@ -199,6 +199,141 @@ void orc_single1_backward(int scheme, const float* gS, const float* gV, const fl
 }
 
 /* ------------------------------------------------------------------------------------
+ * History family with optional per-sample tables (neuron n belongs to sample n / (N/B);
+ * per_batch: scale [T][B], W [T][B][T]; else scale [T], W [T][T]):
+ *   mode 0 "GLX": VO-GL1 (fde_cupy_kernels_all.py:1594-1630) and FAGL1 (:1200-1233, scale
+ *          = h_beta everywhere, scale == NULL): v_pre = s*drift - sum_i W v_hist_i
+ *   mode 1 "VOPRED": VO-PREDICTOR (:1017-1056): history over the drift,
+ *          v_pre = v0 + s*(drift + hist) + rm*(v - v0)
+ * Outputs spike, v_pre and the history source (v_hist or drift); for VOPRED also the
+ * drift-plus-history the parameter gradient needs (the reference recomputes it with a
+ * torch.matmul; a reduction input, compared within tolerance).
+ * ---------------------------------------------------------------------------------- */
+static inline int64_t hf_w(int per_batch, int B, int T, int t, int b, int i) {
+    return per_batch ? ((int64_t)(t * B + b) * T + i) : ((int64_t)t * T + i);
+}
+static inline float hf_s(const float* scale, float hb, int per_batch, int B, int t, int b) {
+    return scale ? scale[per_batch ? (t * B + b) : t] : hb;
+}
+
+void orc_hfam_forward(int mode, const float* x, const float* v0, const float* scale, float hb,
+                      const float* W, int per_batch, int B, float* spike, float* vpre,
+                      float* hsrc, float* aux, int T, int64_t N, float tau, float th, float rm) {
+    const int64_t F = N / B;
+    #pragma omp parallel for schedule(static)
+    for (int64_t n = 0; n < N; ++n) {
+        const int b = (int)(n / F);
+        float v = v0[n];
+        for (int t = 0; t < T; ++t) {
+            const int64_t o = (int64_t)t * N + n;
+            const float drift = (x[o] - v) / tau;                        /* (-v + x)/tau */
+            float hist = 0.0f;
+            for (int i = 0; i < t; ++i)
+                hist = fmaf(W[hf_w(per_batch, B, T, t, b, i)], hsrc[(int64_t)i * N + n], hist);
+            const float sv = hf_s(scale, hb, per_batch, B, t, b);
+            float p;
+            if (mode == 0) {
+                p = fmaf(sv, drift, -hist);                               /* :1624 / :1226 */
+                if (aux) aux[o] = drift;
+            } else {
+                p = fmaf(rm, v - v0[n], fmaf(sv, drift + hist, v0[n]));  /* :1047 */
+                hsrc[o] = drift;
+                if (aux) aux[o] = drift + hist;
+            }
+            const float sp = (p >= th) ? 1.0f : 0.0f;
+            spike[o] = sp;
+            vpre[o] = p;
+            v = p - sp * th;
+            if (mode == 0) hsrc[o] = v;
+        }
+    }
+}
+
+/* hist_mode 0: VO-GL1 / FAGL1 truncated (:1632-1668, :1235-1272): grad_v_next =
+ *   -gp * (s/tau + sum_i W[t,i]); 1: full history (:1670-1709, :1274-1312); 2: VO-PREDICTOR
+ *   truncated (:1058-1096): grad_v_next = gp * (rm - s/tau). */
+void orc_hfam_backward(int hist_mode, const float* gS, const float* scale, float hb,
+                       const float* W, int per_batch, int B, const float* vpre, float* gx,
+                       float* gv0, float* gpre, int T, int64_t N, float tau, float th, float sg,
+                       float rm) {
+    const int64_t F = N / B;
+    #pragma omp parallel
+    {
+        float* A = (float*)malloc(sizeof(float) * (size_t)(T > 0 ? T : 1));
+        #pragma omp for schedule(static)
+        for (int64_t n = 0; n < N; ++n) {
+            const int b = (int)(n / F);
+            for (int t = 0; t < T; ++t) A[t] = 0.0f;
+            float gvn = 0.0f, ginit = 0.0f;
+            for (int t = T - 1; t >= 0; --t) {
+                const int64_t o = (int64_t)t * N + n;
+                const float sur = surr_fma(vpre[o] - th, sg);
+                const float sv = hf_s(scale, hb, per_batch, B, t, b);
+                const float gp = fmaf(gS[o], sur, hist_mode == 1 ? A[t] : gvn);
+                gpre[o] = gp;
+                gx[o] = (gp * sv) / tau;
+                if (hist_mode == 0) {
+                    float hsum = 0.0f;
+                    for (int i = 0; i < t; ++i) hsum = hsum + W[hf_w(per_batch, B, T, t, b, i)];
+                    gvn = (-gp) * (sv / tau + hsum);
+                } else if (hist_mode == 2) {
+                    gvn = gp * (rm - sv / tau);
+                } else {
+                    const float prev = ((-gp) * sv) / tau;
+                    if (t == 0) ginit = ginit + prev; else A[t - 1] = A[t - 1] + prev;
+                    for (int i = 0; i < t; ++i)
+                        A[i] = fmaf(-W[hf_w(per_batch, B, T, t, b, i)], gp, A[i]);
+                }
+            }
+            gv0[n] = hist_mode == 1 ? ginit : gvn;
+        }
+        free(A);
+    }
+}
+
+/* Per-sample parameter gradients in double: gs[t][b] = sum_{n in b} G[t,n] E[t,n] (gs may be
+ * NULL) and gW[t][b][i] = sign * sum_{n in b} G[t,n] * (scale ? scale[t][b] : 1) * V[i,n],
+ * zero for i >= t when lower_only (torch.sum / einsum / matmul of the reference Functions:
+ * :1829-1838, :1167-1181, :1478-1497). */
+void orc_hfam_param_grads(const float* G, const float* V, const float* E, const float* scale,
+                          int per_batch, int B, int T, int64_t N, double sign, int lower_only,
+                          double* gs, double* gW) {
+    const int64_t F = N / B;
+    #pragma omp parallel for schedule(static)
+    for (int64_t row = 0; row < (int64_t)T * B; ++row) {
+        const int t = (int)(row / B), b = (int)(row % B);
+        const int ob = per_batch ? b : 0;
+        const double sv = scale ? (double)scale[per_batch ? (t * B + b) : t] : 1.0;
+        double s = 0.0;
+        for (int64_t f = 0; f < F; ++f) {
+            const int64_t n = (int64_t)b * F + f;
+            if (E) s += (double)G[(int64_t)t * N + n] * (double)E[(int64_t)t * N + n];
+        }
+        if (gs) {
+            if (per_batch) gs[t * B + b] = s;
+            else {
+                #pragma omp atomic
+                gs[t] += s;
+            }
+        }
+        for (int i = 0; i < T; ++i) {
+            double acc = 0.0;
+            if (!(lower_only && i >= t))
+                for (int64_t f = 0; f < F; ++f) {
+                    const int64_t n = (int64_t)b * F + f;
+                    acc += (double)G[(int64_t)t * N + n] * sv * (double)V[(int64_t)i * N + n];
+                }
+            const int64_t o = per_batch ? ((int64_t)(t * B + ob) * T + i) : ((int64_t)t * T + i);
+            if (per_batch) gW[o] = sign * acc;
+            else {
+                #pragma omp atomic
+                gW[o] += sign * acc;
+            }
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------------------
  * Library glmulti: forward = lif_fde_vo_gl1_forward_kernel with per_batch=0
  * (fde_cupy_kernels_all.py:1594-1630); backward = lif_fde_glmulti_backward_kernel
  * (:1845-1875, truncated) or lif_fde_glmulti_full_backward_kernel (:1877-1913, full);

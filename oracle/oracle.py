@@ -45,6 +45,12 @@ def lib():
         L.orc_single_forward.argtypes = [_i, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f, _f, _f]
         L.orc_single_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f, _f, _f, _f]
         L.orc_single1_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f, _f]
+        L.orc_hfam_forward.argtypes = [_i, _p, _p, _p, _f, _p, _i, _i, _p, _p, _p, _p, _i, _i64,
+                                       _f, _f, _f]
+        L.orc_hfam_backward.argtypes = [_i, _p, _p, _f, _p, _i, _i, _p, _p, _p, _p, _i, _i64, _f,
+                                        _f, _f, _f]
+        L.orc_hfam_param_grads.argtypes = [_p, _p, _p, _p, _i, _i, _i, _i64, ctypes.c_double, _i,
+                                           _p, _p]
         L.orc_glmulti_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f]
         L.orc_glmulti_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f]
         L.orc_glmulti_param_grads.argtypes = [_p, _p, _p, _p, _p, _i, _i64]
@@ -83,6 +89,12 @@ def ref():
         R.ref_predictor1_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f, _f, _f, _f]
         R.ref_lifeuler_forward.argtypes = [_p, _p, _p, _p, _i, _i, _f, _f, _f]
         R.ref_lifeuler_backward.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f]
+        R.ref_vogl1_forward.argtypes = [_p] * 8 + [_i] * 4 + [_f, _f]
+        R.ref_vogl1_backward.argtypes = [_i] + [_p] * 7 + [_i] * 4 + [_f] * 3
+        R.ref_fagl1_forward.argtypes = [_p] * 6 + [_i] * 4 + [_f] * 3
+        R.ref_fagl1_backward.argtypes = [_i] + [_p] * 6 + [_i] * 4 + [_f] * 4
+        R.ref_vopred_forward.argtypes = [_p] * 7 + [_i] * 4 + [_f] * 3
+        R.ref_vopred_backward.argtypes = [_p] * 7 + [_i] * 4 + [_f] * 4
         R.ref_glmulti_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f]
         R.ref_glmulti_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f]
         R.ref_aligned_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f]
@@ -299,3 +311,102 @@ def euler_backward(gS, gzf, x, zpre, sin_, in_scale, gain, tau, step, sg, sdt, i
                                  T, N, in_scale, gain, tau, step, sg, sdt)
         g3 = g3f.astype(np.float64)
     return gx, gz0, g3
+
+
+# ---------------------------------------------------------------------------------------
+# history family with per-sample tables: VO-GL1, FAGL1, VO-PREDICTOR
+# (fde_cupy_kernels_all.py:1594-1843, :1200-1500, :1017-1198)
+# ---------------------------------------------------------------------------------------
+HFAM = {"vogl1": 0, "fagl1": 0, "vopred": 1}
+
+
+def hfam_forward(kind, x, v0, scale, W, B, tau, th, hb=1.0, rm=0.0, impl="oracle"):
+    """kind in vogl1 / fagl1 / vopred; scale None for fagl1 (uses hb); per-sample tables when
+    W has three dimensions.  Returns spike, vpre, hsrc (v_hist or drift) and aux (drift for
+    the GL kinds, drift + history for vopred; oracle only)."""
+    x, v0, W = _c(x), _c(v0), _c(W)
+    T, N = x.shape
+    per_batch = int(W.ndim == 3)
+    sc = None if scale is None else _c(scale)
+    s, vpre, hsrc, aux = (_empty(T, N) for _ in range(4))
+    if impl == "oracle":
+        lib().orc_hfam_forward(HFAM[kind], _ptr(x), _ptr(v0), None if sc is None else _ptr(sc),
+                               hb, _ptr(W), per_batch, B, _ptr(s), _ptr(vpre), _ptr(hsrc),
+                               _ptr(aux), T, N, tau, th, rm)
+        return {"spike": s, "vpre": vpre, "hsrc": hsrc, "aux": aux}
+    R = ref()
+    if kind == "vogl1":
+        R.ref_vogl1_forward(_ptr(x), _ptr(v0), _ptr(sc), _ptr(W), _ptr(s), _ptr(vpre), _ptr(hsrc),
+                            _ptr(aux), T, N, B, per_batch, tau, th)
+    elif kind == "fagl1":
+        R.ref_fagl1_forward(_ptr(x), _ptr(v0), _ptr(W), _ptr(s), _ptr(vpre), _ptr(hsrc), T, N, B,
+                            per_batch, tau, hb, th)
+    else:
+        R.ref_vopred_forward(_ptr(x), _ptr(v0), _ptr(sc), _ptr(W), _ptr(s), _ptr(vpre), _ptr(hsrc),
+                             T, N, B, per_batch, tau, th, rm)
+    return {"spike": s, "vpre": vpre, "hsrc": hsrc}
+
+
+def hfam_backward(kind, full, gS, vpre, scale, W, B, tau, th, sg, hb=1.0, rm=0.0, impl="oracle"):
+    gS, vpre, W = _c(gS), _c(vpre), _c(W)
+    T, N = gS.shape
+    per_batch = int(W.ndim == 3)
+    sc = None if scale is None else _c(scale)
+    gx, gpre = _empty(T, N), _empty(T, N)
+    gv0 = np.empty(N, dtype=np.float32)
+    if impl == "oracle":
+        mode = 2 if kind == "vopred" else (1 if full else 0)
+        lib().orc_hfam_backward(mode, _ptr(gS), None if sc is None else _ptr(sc), hb, _ptr(W),
+                                per_batch, B, _ptr(vpre), _ptr(gx), _ptr(gv0), _ptr(gpre), T, N,
+                                tau, th, sg, rm)
+    else:
+        R = ref()
+        if kind == "vogl1":
+            R.ref_vogl1_backward(int(full), _ptr(gS), _ptr(sc), _ptr(W), _ptr(vpre), _ptr(gx),
+                                 _ptr(gv0), _ptr(gpre), T, N, B, per_batch, tau, th, sg)
+        elif kind == "fagl1":
+            R.ref_fagl1_backward(int(full), _ptr(gS), _ptr(W), _ptr(vpre), _ptr(gx), _ptr(gv0),
+                                 _ptr(gpre), T, N, B, per_batch, tau, hb, th, sg)
+        else:
+            R.ref_vopred_backward(_ptr(gS), _ptr(sc), _ptr(W), _ptr(vpre), _ptr(gx), _ptr(gv0),
+                                  _ptr(gpre), T, N, B, per_batch, tau, th, sg, rm)
+    return gx, gv0, gpre
+
+
+def hfam_param_grads(G, V, E, scale, per_batch, B, sign, lower_only):
+    """(gs, gW) as float64 arrays: gs[t,b] = sum G*E over sample b (None if E is None),
+    gW[t,b,i] = sign * sum G*scale*V (per-sample layout [T,B,T] / [T,T])."""
+    G, V = _c(G), _c(V)
+    T, N = G.shape
+    Ec = None if E is None else _c(E)
+    sc = None if scale is None else _c(scale)
+    gs = np.zeros((T, B) if per_batch else T, dtype=np.float64)
+    gW = np.zeros((T, B, T) if per_batch else (T, T), dtype=np.float64)
+    lib().orc_hfam_param_grads(_ptr(G), _ptr(V), None if Ec is None else _ptr(Ec),
+                               None if sc is None else _ptr(sc), int(per_batch), B, T, N,
+                               float(sign), int(lower_only), _ptr(gs), _ptr(gW))
+    return (None if E is None else gs), gW
+
+
+def hfam_params(kind, gpre, hsrc, drift, scale, W, B, lower_only_batch=True):
+    """(grad_scale, grad_weights) in double as the reference Functions form them:
+    VO-GL1 sum G*drift and -G@v_hist^T (:1829-1838); FAGL1 -G@v_hist^T, lower triangle only
+    per sample (:1478-1497; the PyTorch Function keeps every entry: lower_only_batch=False);
+    VO-PREDICTOR sum G*(drift + W@drift) and (G*scale)@drift^T (:1167-1181) -- hsrc is the
+    drift for VO-PREDICTOR."""
+    W = np.asarray(W)
+    per_batch = W.ndim == 3
+    if kind == "vogl1":
+        return hfam_param_grads(gpre, hsrc, drift, None, per_batch, B, -1.0, 0)
+    if kind == "fagl1":
+        return None, hfam_param_grads(gpre, hsrc, None, None, per_batch, B, -1.0,
+                                      int(per_batch and lower_only_batch))[1]
+    _, gW = hfam_param_grads(gpre, hsrc, None, scale, per_batch, B, 1.0, 0)
+    T, N = gpre.shape
+    F = N // B
+    G = np.asarray(gpre, np.float64).reshape(T, B, F)
+    D = np.asarray(hsrc, np.float64).reshape(T, B, F)
+    Wd = W.astype(np.float64)
+    hist = np.einsum("tbi,ibf->tbf", Wd, D) if per_batch else np.einsum("ti,ibf->tbf", Wd, D)
+    gsb = np.sum(G * (D + hist), axis=2)
+    return (gsb if per_batch else gsb.sum(axis=1)), gW

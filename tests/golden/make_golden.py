@@ -185,6 +185,113 @@ def kernel_fixtures(T, N, seed):
           pred=fw["pred"], hist=fw["hist"], gx=gx, gv0=gv, ga=ga)
 
 
+def history_tables(T, B, seed):
+    """VO-GL1 / VO-PREDICTOR schedules from the reference's builders
+    (LIFNeuronFDE.build_vogl1_schedule / build_vopredictor_schedule, neuron.py:2010-2090) for
+    a shared beta[T] and a per-sample beta[T, B]; FAGL1 rows = GL coefficients x a random
+    positive causal attention, shared [T, T] and per-sample [T, B, T] (the shape of
+    _build_fagl1_weights, neuron.py:1790-1888)."""
+    import torch
+    from spikeDE_dis.neuron import LIFNeuronFDE
+    g = torch.Generator().manual_seed(seed)
+    out = {}
+    for tag, beta in (("shared", 0.2 + 0.6 * torch.rand(T, generator=g)),
+                      ("batch", 0.2 + 0.6 * torch.rand(T, B, generator=g))):
+        vo = LIFNeuronFDE.build_vogl1_schedule(beta, H)
+        vp = LIFNeuronFDE.build_vopredictor_schedule(beta, H)
+        out[f"vogl1_{tag}"] = (vo["scale"].numpy().copy(), vo["weights"].numpy().copy())
+        out[f"vopred_{tag}"] = (vp["scale"].numpy().copy(), vp["weights"].numpy().copy())
+        out[f"beta_{tag}"] = beta.numpy().copy()
+    beta = 0.6
+    c = [1.0]
+    for k in range(1, T + 1):
+        c.append(c[-1] * (1.0 - (1.0 + beta) / k))
+    lag = np.subtract.outer(np.arange(T), np.arange(T))
+    gl = np.where(lag > 0, np.asarray(c, np.float64)[np.clip(lag, 0, T)], 0.0)
+    rnd = np.random.default_rng(seed)
+    att_s = rnd.uniform(0.5, 1.5, size=(T, T))
+    att_b = rnd.uniform(0.5, 1.5, size=(T, B, T))
+    out["fagl1_shared"] = (None, (gl * att_s).astype(np.float32))
+    out["fagl1_batch"] = (None, (gl[:, None, :] * att_b).astype(np.float32))
+    return out
+
+
+def history_fixtures(T, B, F, seed):
+    """kern_hist_<kind>_T<T>.npz: the reference's VO-GL1 / FAGL1 / VO-PREDICTOR kernel
+    sources compiled for the host (fde_cupy_kernels_all.py:1017-1096, :1200-1312,
+    :1594-1709), shared and per-sample tables, truncated and full history; and
+    torch_fagl1_<tables>_T<T>.npz from the reference's LIFFDEFAGL1TorchFunction
+    (:1501-1587) with autograd."""
+    import torch
+    sys.path.insert(0, REPO)
+    from oracle import build_ref, oracle
+    if not oracle.ref_available():
+        build_ref.build(build_ref_reference)
+    from spikeDE_dis.fde_cupy_kernels_all import LIFFDEFAGL1TorchFunction
+    N = B * F
+    g = np.random.default_rng(seed)
+    x = (g.standard_normal((T, N)) * 5.0).astype(np.float32)
+    v0 = (g.standard_normal(N) * 0.1).astype(np.float32)
+    gS = g.standard_normal((T, N)).astype(np.float32)
+    tables = history_tables(T, B, seed)
+    hb = np.float32(H ** 0.6)
+    rm = 0.25
+    for kind in ("vogl1", "fagl1", "vopred"):
+        arrays = dict(x=x, v0=v0, gS=gS, B=np.int32(B), h_beta=hb, residual_mix=np.float32(rm))
+        for tag in ("shared", "batch"):
+            scale, W = tables[f"{kind}_{tag}"]
+            if scale is not None:
+                arrays[f"{tag}_scale"] = scale
+                arrays[f"{tag}_beta"] = tables[f"beta_{tag}"]
+            arrays[f"{tag}_W"] = W
+            fw = oracle.hfam_forward(kind, x, v0, scale, W, B, TAU, TH, hb, rm, impl="ref")
+            for k in ("spike", "vpre", "hsrc"):
+                arrays[f"{tag}_{k}"] = fw[k]
+            for full in ((0, 1) if kind != "vopred" else (0,)):
+                gx, gv0, gpre = oracle.hfam_backward(kind, full, gS, fw["vpre"], scale, W, B, TAU,
+                                                     TH, SG, hb, rm, impl="ref")
+                arrays[f"{tag}_f{full}_gx"] = gx
+                arrays[f"{tag}_f{full}_gv0"] = gv0
+                arrays[f"{tag}_f{full}_gpre"] = gpre
+        _save(f"kern_hist_{kind}_T{T}.npz", **arrays)
+    for tag in ("shared", "batch"):
+        _, W = tables[f"fagl1_{tag}"]
+        for full in (False, True):
+            xt = torch.from_numpy(x).requires_grad_(True)
+            vt = torch.from_numpy(v0).requires_grad_(True)
+            Wt = torch.from_numpy(W).requires_grad_(True)
+            s = LIFFDEFAGL1TorchFunction.apply(xt, vt, Wt, TAU, float(hb), TH, SG, B, full)
+            s.backward(torch.from_numpy(gS))
+            _save(f"torch_fagl1_{tag}_{'full' if full else 'trunc'}_T{T}.npz", x=x, v0=v0, W=W,
+                  gS=gS, B=np.int32(B), h_beta=hb, spike=s.detach().numpy(),
+                  gx=xt.grad.numpy(), gv0=vt.grad.numpy(), gW=Wt.grad.numpy())
+
+
+def fagl1_neuron_fixture():
+    """torch_fagl1_neuron.npz: LIFNeuronFDE(method='fagl1') attention projections after
+    __init__ (seeded per layer name) and _build_fagl1_weights on a fixed input
+    (neuron.py:1205-1221, :1790-1866) for both attn_init and attn_mode values; plus the
+    GL1 full-history rows _build_gl1_causal_weights (:1880-1896)."""
+    import torch
+    from spikeDE_dis.neuron import LIFNeuronFDE
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn((8, 4, 3, 5), generator=g) * 2.0 + 0.5
+    out = {"x": x.numpy()}
+    for init in ("zero_q", "orthogonal_zero_score"):
+        for mode in ("per_sample", "batch_shared"):
+            n = LIFNeuronFDE(tau=TAU, threshold=TH, surrogate_grad_scale=SG, method="fagl1",
+                             beta=0.6, T=8, step_size=H, name="lif3", step_mode="m",
+                             backend="torch", attn_init=init, attn_mode=mode)
+            tag = f"{init}_{mode}"
+            out[f"{tag}_q"] = n.fagl_q_proj.weight.detach().numpy().copy()
+            out[f"{tag}_k"] = n.fagl_k_proj.weight.detach().numpy().copy()
+            out[f"{tag}_W"] = n._build_fagl1_weights(x).detach().numpy().copy()
+            out[f"{tag}_entropy"] = np.float32(n.get_attention_stats()["entropy"])
+    n = LIFNeuronFDE(method="gl1", beta=0.6, T=8, step_size=H, step_mode="m", backend="torch")
+    out["gl1_rows"] = n._build_gl1_causal_weights(8, torch.device("cpu")).numpy()
+    _save("torch_fagl1_neuron.npz", **out)
+
+
 def weight_tables():
     """GL / trapezoid / predictor tables and the glmulti schedule, as the reference builds
     them (neuron.py:1446-1459, :1516-1570, :1494-1514), plus LIFNeuronFDE state_dict keys."""
@@ -223,6 +330,8 @@ def main():
     global build_ref_reference
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", choices=["history"], default=None,
+                    help="write only this group of fixtures")
     args = ap.parse_args()
     build_ref_reference = args.reference
     _stub_h5py()
@@ -230,6 +339,10 @@ def main():
     sys.path.insert(0, os.path.join(args.reference, "examples", "cnn128"))
     import torch
     torch.set_num_threads(4)
+    if args.only == "history":
+        history_fixtures(16, 4, 32, 11)
+        fagl1_neuron_fixture()
+        return
     for method in ("gl", "trap", "predictor"):
         torch_single(None, method, 0.7, 20, 4, 128, "spiking", 42)
         torch_single(None, method, 0.5, 16, 4, 128, "config1", 0)
@@ -240,6 +353,8 @@ def main():
     torch_aligned(None, 16, 4, 128, "spiking", 4)
     torch_aligned(None, 8, 4, 64, "steady", 5)
     kernel_fixtures(16, 256, 7)
+    history_fixtures(16, 4, 32, 11)
+    fagl1_neuron_fixture()
     weight_tables()
 
 

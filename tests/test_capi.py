@@ -125,3 +125,45 @@ def test_schedule_validation_before_launch():
     assert f(F, F, F, 3, 16, 2, F, F, F, None) == _capi.DFSNN_ERR_PARAM
     assert b(F, F, F, F, None, None, 3, 16, 1, None, None) == _capi.DFSNN_ERR_NULL
     assert b(F, F, F, F, None, None, 3, 0, 1, F, None) == _capi.DFSNN_ERR_SHAPE
+
+
+def test_history_validation(L):
+    """VO-GL1 / FAGL1 / VO-PREDICTOR entry points reject bad arguments before any launch."""
+    ws = L.dfsnn_history_backward_workspace_size
+    assert ws(16, 1000, 4, 0) > 0 and ws(16, 1000, 4, 1) > 0
+    assert ws(0, 1000, 4, 0) == 0 and ws(257, 1000, 4, 0) == 0
+    assert ws(16, 1000, 3, 0) == 0 and ws(16, 1000, 0, 0) == 0 and ws(16, 1000, 4, 2) == 0
+    F = FAKE
+    vf = L.dfsnn_vo_gl1_forward
+    assert vf(F, F, F, F, 3, 0, F, F, F, F, 16, 1000, 2.0, 1.0, None) == _capi.DFSNN_ERR_SHAPE
+    assert vf(F, F, F, F, 0, 0, F, F, F, F, 16, 1000, 2.0, 1.0, None) == _capi.DFSNN_ERR_SHAPE
+    assert vf(F, F, F, F, 4, 0, F, F, F, F, 257, 1000, 2.0, 1.0, None) == _capi.DFSNN_ERR_T_LIMIT
+    assert vf(F, F, None, F, 4, 0, F, F, F, F, 16, 1000, 2.0, 1.0, None) == _capi.DFSNN_ERR_NULL
+    assert vf(F, F, F, F, 4, 0, F, F, F, None, 16, 1000, 2.0, 1.0, None) == _capi.DFSNN_ERR_NULL
+    assert vf(F, F, F, F, 4, 2, F, F, F, F, 16, 1000, 2.0, 1.0, None) == _capi.DFSNN_ERR_PARAM
+    assert vf(F, F, F, F, 4, 0, F, F, F, F, 16, 1000, 0.0, 1.0, None) == _capi.DFSNN_ERR_PARAM
+    ff = L.dfsnn_fa_gl1_forward
+    assert ff(F, F, F, 1, 0, F, F, F, 65, 100, 2.0, 0.25, 1.0, None) == _capi.DFSNN_ERR_T_LIMIT
+    assert ff(F, F, None, 1, 0, F, F, F, 16, 100, 2.0, 0.25, 1.0, None) == _capi.DFSNN_ERR_NULL
+    assert ff(F, F, F, 1, 0, F, F, F, 16, 100, 2.0, float("nan"), 1.0, None) == _capi.DFSNN_ERR_PARAM
+    pf = L.dfsnn_vo_predictor_forward
+    assert pf(F, F, F, F, 1, 0, F, F, F, 16, 100, 2.0, 1.0, float("inf"), None) == _capi.DFSNN_ERR_PARAM
+    assert pf(F, F, F, F, 1, 0, F, F, None, 16, 100, 2.0, 1.0, 0.2, None) == _capi.DFSNN_ERR_NULL
+    vb = L.dfsnn_vo_gl1_backward
+    big = ws(16, 100, 1, 0)
+    assert vb(F, F, F, F, F, F, 1, 0, F, F, F, F, 65, 100, 2.0, 1.0, 5.0, 1, F, big, None) == \
+        _capi.DFSNN_ERR_T_LIMIT
+    assert vb(F, F, F, F, F, F, 1, 0, F, F, F, F, 16, 100, 2.0, 1.0, 5.0, 2, F, big, None) == \
+        _capi.DFSNN_ERR_PARAM
+    assert vb(F, F, F, F, F, F, 1, 0, F, F, F, F, 16, 100, 2.0, 1.0, 5.0, 0, F, big - 8, None) == \
+        _capi.DFSNN_ERR_WORKSPACE
+    assert vb(F, F, F, F, None, F, 1, 0, F, F, F, F, 16, 100, 2.0, 1.0, 5.0, 0, F, big, None) == \
+        _capi.DFSNN_ERR_NULL                                       # grad_weights needs v_hist
+    assert vb(F, F, F, F, F, None, 1, 0, F, F, F, None, 16, 100, 2.0, 1.0, 5.0, 0, F, big, None) == \
+        _capi.DFSNN_ERR_NULL                                       # grad_scale needs drift
+    fb = L.dfsnn_fa_gl1_backward
+    assert fb(F, F, F, F, 1, 0, F, F, F, 65, 100, 2.0, 0.25, 1.0, 5.0, 0, F, big, None) == \
+        _capi.DFSNN_ERR_T_LIMIT
+    pb = L.dfsnn_vo_predictor_backward
+    assert pb(F, F, F, F, F, 3, 0, F, F, F, F, 16, 100, 2.0, 1.0, 5.0, 0.2, F, big, None) == \
+        _capi.DFSNN_ERR_SHAPE

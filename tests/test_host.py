@@ -100,8 +100,18 @@ def test_no_cpu_fallback():
         make_glmulti(8)(torch.zeros(8, 2, 3))
     with pytest.raises(NotImplementedError):
         neuron.LIFNeuronFDE(method="gl", step_mode="s")(torch.zeros(2, 3))
-    with pytest.raises(NotImplementedError):
-        fde_kernels.LIFFDEVOGL1Function.apply(x)
+    with pytest.raises(RuntimeError):
+        fde_kernels.LIFFDEVOGL1Function.apply(x, torch.zeros(4), torch.ones(8), torch.zeros(8, 8),
+                                              2.0, 1.0, 5.0, 1)
+    with pytest.raises(RuntimeError):
+        fde_kernels.LIFFDEFAGL1Function.apply(x, torch.zeros(4), torch.zeros(8, 8), 2.0, 0.25,
+                                              1.0, 5.0, 1)
+    with pytest.raises(RuntimeError):
+        fde_kernels.LIFFDEFAGL1TorchFunction.apply(x, torch.zeros(4), torch.zeros(8, 8), 2.0,
+                                                   0.25, 1.0, 5.0, 1)
+    with pytest.raises(RuntimeError):
+        fde_kernels.LIFFDEVOPREDICTORFunction.apply(x, torch.zeros(4), torch.ones(8),
+                                                    torch.zeros(8, 8), 2.0, 1.0, 5.0, 0.2, 1)
 
 
 def test_reference_limits_raise_value_error():
@@ -132,3 +142,38 @@ def test_integrate_registers_reference_module_names():
                 sys.modules.pop(k, None)
             else:
                 sys.modules[k] = v
+
+
+@pytest.mark.parametrize("init", ["zero_q", "orthogonal_zero_score"])
+@pytest.mark.parametrize("mode", ["per_sample", "batch_shared"])
+def test_fagl1_neuron_attention_rows_vs_reference(init, mode):
+    """method='fagl1': the seeded projection init and _build_fagl1_weights against the
+    reference's LIFNeuronFDE (neuron.py:1205-1221, :1790-1866), bit for bit on the host."""
+    d = np.load(os.path.join(GOLDEN, "torch_fagl1_neuron.npz"))
+    n = neuron.LIFNeuronFDE(tau=2.0, threshold=1.0, surrogate_grad_scale=5.0, method="fagl1",
+                            beta=0.6, T=8, step_size=0.1, name="lif3", step_mode="m",
+                            backend="torch", attn_init=init, attn_mode=mode)
+    tag = f"{init}_{mode}"
+    assert np.array_equal(n.fagl_q_proj.weight.detach().numpy(), d[f"{tag}_q"])
+    assert np.array_equal(n.fagl_k_proj.weight.detach().numpy(), d[f"{tag}_k"])
+    W = n._build_fagl1_weights(torch.from_numpy(d["x"]))
+    assert np.array_equal(W.detach().numpy(), d[f"{tag}_W"])
+    assert np.float32(n.get_attention_stats()["entropy"]) == d[f"{tag}_entropy"]
+
+
+def test_gl1_full_history_rows_vs_reference():
+    d = np.load(os.path.join(GOLDEN, "torch_fagl1_neuron.npz"))
+    n = neuron.LIFNeuronFDE(method="gl1", beta=0.6, T=8, step_size=0.1, step_mode="m")
+    assert np.array_equal(n._build_gl1_causal_weights(8, torch.device("cpu")).numpy(),
+                          d["gl1_rows"])
+
+
+def test_history_method_validation():
+    with pytest.raises(ValueError):
+        neuron.LIFNeuronFDE(method="fagl1", beta_learnable=True, step_mode="m")
+    with pytest.raises(ValueError):
+        neuron.LIFNeuronFDE(method="vogl1", vo_solver="rk4", step_mode="m")
+    with pytest.raises(ValueError):
+        neuron.LIFNeuronFDE(method="gl1", history_grad_mode="exact", step_mode="m")
+    with pytest.raises(ValueError):
+        neuron.LIFNeuronFDE(method="fagl1", attn_dim=2, step_mode="m")

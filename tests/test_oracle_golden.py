@@ -119,6 +119,78 @@ def test_glmulti_vs_reference_kernels(kind):
     assert_close(gv0, d["gv0"], rtol=1e-5, mask=mask, what="gv0")
 
 
+@pytest.mark.parametrize("kind", ["vogl1", "fagl1", "vopred"])
+@pytest.mark.parametrize("tag", ["shared", "batch"])
+def test_history_vs_reference_kernels_bitwise(kind, tag):
+    d = load(f"kern_hist_{kind}_T16.npz")
+    B, hb, rm = int(d["B"]), float(d["h_beta"]), float(d["residual_mix"])
+    scale = d.get(f"{tag}_scale")
+    W = d[f"{tag}_W"]
+    fw = O.hfam_forward(kind, d["x"], d["v0"], scale, W, B, TAU, TH, hb, rm)
+    for k in ("spike", "vpre", "hsrc"):
+        assert_bitwise(fw[k], d[f"{tag}_{k}"], what=k)
+    for full in ((0, 1) if kind != "vopred" else (0,)):
+        gx, gv0, gpre = O.hfam_backward(kind, full, d["gS"], fw["vpre"], scale, W, B, TAU, TH, SG,
+                                        hb, rm)
+        assert_bitwise(gx, d[f"{tag}_f{full}_gx"], what="gx")
+        assert_bitwise(gv0, d[f"{tag}_f{full}_gv0"], what="gv0")
+        assert_bitwise(gpre, d[f"{tag}_f{full}_gpre"], what="gpre")
+
+
+@pytest.mark.parametrize("kind", ["vogl1", "vopred"])
+@pytest.mark.parametrize("tag", ["shared", "batch"])
+def test_history_schedule_builders_vs_reference(kind, tag):
+    """dfsnn_b200.schedule.build_vogl1_schedule / build_vopredictor_schedule against the
+    reference's LIFNeuronFDE builders (neuron.py:2010-2089), bit for bit."""
+    import torch
+    from dfsnn_b200 import schedule as S
+    d = load(f"kern_hist_{kind}_T16.npz")
+    fn = S.build_vogl1_schedule if kind == "vogl1" else S.build_vopredictor_schedule
+    terms = fn(torch.from_numpy(d[f"{tag}_beta"]), H)
+    assert_bitwise(terms["scale"].numpy(), d[f"{tag}_scale"], what="scale")
+    assert_bitwise(terms["weights"].numpy(), d[f"{tag}_W"], what="weights")
+
+
+@pytest.mark.parametrize("per_batch", [False, True])
+def test_history_param_grads_vs_einsum(per_batch):
+    rng = np.random.default_rng(5)
+    T, B, F = 7, 3, 41
+    G = rng.standard_normal((T, B * F)).astype(np.float32)
+    V = rng.standard_normal((T, B * F)).astype(np.float32)
+    E = rng.standard_normal((T, B * F)).astype(np.float32)
+    scale = rng.uniform(0.1, 0.3, size=(T, B) if per_batch else T).astype(np.float32)
+    Gd, Vd, Ed = (a.astype(np.float64).reshape(T, B, F) for a in (G, V, E))
+    gs, gW = O.hfam_param_grads(G, V, E, None, per_batch, B, -1.0, 0)
+    M = np.einsum("tbf,ibf->tbi", Gd, Vd)
+    D = np.sum(Gd * Ed, axis=2)
+    assert np.allclose(gs, D if per_batch else D.sum(1), rtol=1e-12, atol=1e-12)
+    assert np.allclose(gW, -M if per_batch else -M.sum(1), rtol=1e-12, atol=1e-12)
+    _, gWl = O.hfam_param_grads(G, V, None, scale, per_batch, B, 1.0, 1)
+    sc = scale.astype(np.float64)
+    want = M * (sc[:, :, None] if per_batch else sc[:, None, None])
+    want = want if per_batch else want.sum(1)
+    mask = np.tril(np.ones((T, T)), -1)
+    want = want * (mask[:, None, :] if per_batch else mask)
+    assert np.allclose(gWl, want, rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("tag", ["shared", "batch"])
+@pytest.mark.parametrize("full", ["trunc", "full"])
+def test_fagl1_vs_reference_torch(tag, full):
+    """The reference's PyTorch FAGL1 Function (fde_cupy_kernels_all.py:1501-1587) against the
+    oracle's kernel-order restatement: same recurrence, different fp32 rounding."""
+    d = load(f"torch_fagl1_{tag}_{full}_T16.npz")
+    B, hb = int(d["B"]), float(d["h_beta"])
+    fw = O.hfam_forward("fagl1", d["x"], d["v0"], None, d["W"], B, TAU, TH, hb)
+    mask = assert_spikes(fw["spike"], d["spike"], fw["vpre"], TH)
+    gx, gv0, gpre = O.hfam_backward("fagl1", int(full == "full"), d["gS"], fw["vpre"], None,
+                                    d["W"], B, TAU, TH, SG, hb)
+    assert_close(gx, d["gx"], rtol=TORCH_RTOL, mask=mask, what="gx")
+    assert_close(gv0, d["gv0"], rtol=TORCH_RTOL, mask=mask, what="gv0")
+    _, gW = O.hfam_params("fagl1", gpre, fw["hsrc"], None, None, d["W"], B, lower_only_batch=False)
+    assert_close(gW, d["gW"], rtol=TORCH_RTOL, what="gW")
+
+
 @pytest.mark.skipif(not O.ref_available(), reason="reference not compiled for the host here")
 def test_oracle_vs_live_reference_kernels():
     rng = np.random.default_rng(11)
