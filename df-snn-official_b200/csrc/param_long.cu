@@ -17,11 +17,13 @@
 //  * param_long: any T.  Grid (rows, tiles, tiles); block (s, bt, bi) computes the 64 x 64
 //    output tile (bt, bi), each of its 256 threads a 4 x 4 block, from chunks of 32 neurons
 //    staged through shared memory, multiplied in fp32 and folded into doubles per chunk.
-//  * param_small<T> (T = 8, 16): one block per row computes all T x T outputs.  Threads form
-//    groups of (T/4)^2, each thread a 4 x 4 block of M; the groups split every 256-neuron
-//    chunk by 4-neuron quads (LDS.128 of each G and V row), and the group results are summed
-//    in a fixed order at the end.  About one shared-memory wavefront per neuron, so the
-//    kernel runs at the speed of its global loads.
+//  * param_small<T> (T = 8, 16): one block per row computes all T x T outputs.  Chunks of
+//    2048/T neurons stream into padded shared-memory rows by 4-byte cp.async (any alignment,
+//    zero-filled past the segment) through a 4-stage pipeline, three chunks ahead of the
+//    products (one ahead left the kernel waiting on DRAM latency at ~2 TB/s).  Threads form groups of (T/4)^2, each thread a 4 x 4 block of M; the
+//    groups split a chunk by 4-neuron quads (LDS.128 of each G and V row), and the group
+//    results are summed in a fixed order at the end.  About one shared-memory wavefront per
+//    neuron, so the kernel runs at the speed of its global loads.
 #include "kernels.h"
 #include "lif_common.cuh"
 
@@ -117,17 +119,56 @@ __global__ void __launch_bounds__(256) param_long(const float* G, const float* V
 }
 
 // ---- small T -------------------------------------------------------------------------
-template <int T>
+template <int T, int DIAG>
 struct SmallCfg {
-    static constexpr int kK = 256;                  // neurons per chunk
+    static constexpr int kK = 2048 / T;             // neurons per chunk: 2048 words per array
     static constexpr int kRS = kK + 8;              // padded row: LDS.128 rows 8 banks apart
+    static constexpr int kNA = DIAG == kDiagNone ? 2 : 3;   // staged arrays: G, V (, E)
     static constexpr int kGS = (T / 4) * (T / 4);   // threads per group
     static constexpr int kNG = 256 / kGS;           // groups per block
     static constexpr int kQ = kK / 4;               // quads per chunk
-    static constexpr int kStage = 3 * T * kRS * 4;
+    static constexpr int kStages = 4;               // chunks in flight: kStages - 1 ahead
+    static constexpr int kStageFloats = kNA * T * kRS;
+    static constexpr int kStage = kStages * kStageFloats * 4;
     static constexpr int kReduce = kNG * (T * T + T) * 8;
     static constexpr int kBytes = kStage > kReduce ? kStage : kReduce;
+    static_assert(kQ % kNG == 0, "every group takes the same number of quads");
 };
+
+// 4-byte asynchronous copy global -> shared (LDGSTS); src_bytes 0 fills the word with zero
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(valid ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int PENDING>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(PENDING) : "memory");
+}
+
+// stage the chunk starting at neuron k0: word e = tid + 256 j of each array is row e / kK,
+// column e % kK (a warp covers 32 consecutive neurons of one row)
+template <int T, int DIAG>
+__device__ __forceinline__ void small_stage(float* st, const float* G, const float* V,
+                                            const float* E, long long N, long long k0,
+                                            long long ne) {
+    using C = SmallCfg<T, DIAG>;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int e = threadIdx.x + 256 * j;
+        const int row = e / C::kK, col = e % C::kK;
+        const long long n = k0 + col;
+        const bool ok = n < ne;
+        const long long off = (long long)row * N + (ok ? n : 0);   // a valid address always
+        cp_async4(st + row * C::kRS + col, G + off, ok);
+        cp_async4(st + (T + row) * C::kRS + col, V + off, ok);
+        if (DIAG != kDiagNone) cp_async4(st + (2 * T + row) * C::kRS + col, E + off, ok);
+    }
+}
 
 template <int T, int DIAG>
 __global__ void __launch_bounds__(256) param_small(const float* __restrict__ G,
@@ -135,52 +176,66 @@ __global__ void __launch_bounds__(256) param_small(const float* __restrict__ G,
                                                    const float* __restrict__ E, long long N,
                                                    long long F, int chunks, long long per,
                                                    double* part) {
-    using C = SmallCfg<T>;
+    using C = SmallCfg<T, DIAG>;
     extern __shared__ __align__(16) unsigned char smem[];
-    float* sG = reinterpret_cast<float*>(smem);
-    float* sV = sG + T * C::kRS;
-    float* sE = sV + T * C::kRS;
+    float* stages = reinterpret_cast<float*>(smem);
     const int tid = threadIdx.x;
     const int grp = tid / C::kGS, lt = tid % C::kGS;
     const int ty = lt / (T / 4), tx = lt % (T / 4);
-    // diagonal term: thread lt of a group owns rows lt, lt + kGS, ... (T / kGS of them)
-    constexpr int kDR = (T + C::kGS - 1) / C::kGS;
+    // Thread (ty, tx) owns M[ty + (T/4) r][tx + (T/4) c], r, c < 4: for a fixed r the group's
+    // G rows are consecutive, so with the padded row stride (8 banks per row) the 16-byte
+    // loads of one warp fall in distinct bank groups.  (Rows 4ty + r, 4 rows apart, hit the
+    // same banks: a 4-way conflict that held the kernel at ~2 TB/s.)  The diagonal d[t] of
+    // row t = ty + (T/4) r is taken by the thread with r = tx (mod T/4): kDR rows each.
+    constexpr int kSt = T / 4;
+    constexpr int kDR = 4 / kSt;
     const Segment sg = row_segment(F, chunks, per);
+    const long long nchunks = sg.ne > sg.nb ? (sg.ne - sg.nb + C::kK - 1) / C::kK : 0;
     double acc[4][4], dacc[kDR];
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[r][c] = 0.0;
 #pragma unroll
-    for (int r = 0; r < kDR; ++r) dacc[r] = 0.0;
-    for (long long k0 = sg.nb; k0 < sg.ne; k0 += C::kK) {
-        {
-            const long long n = k0 + tid;
-            const bool ok = n < sg.ne;
+    for (int k = 0; k < kDR; ++k) dacc[k] = 0.0;
+    // prologue: kStages - 1 chunks in flight (one commit group each, empty past the end)
 #pragma unroll
-            for (int t = 0; t < T; ++t) {
-                sG[t * C::kRS + tid] = ok ? ld_stream(G + (long long)t * N + n) : 0.0f;
-                sV[t * C::kRS + tid] = ok ? ld_stream(V + (long long)t * N + n) : 0.0f;
-                if (DIAG != kDiagNone)
-                    sE[t * C::kRS + tid] = ok ? ld_stream(E + (long long)t * N + n) : 0.0f;
-            }
+    for (int s = 0; s < C::kStages - 1; ++s) {
+        if (s < nchunks)
+            small_stage<T, DIAG>(stages + s * C::kStageFloats, G, V, E, N, sg.nb + s * C::kK,
+                                 sg.ne);
+        cp_async_commit();
+    }
+    for (long long it = 0; it < nchunks; ++it) {
+        cp_async_wait<C::kStages - 2>();      // chunk `it` has landed
+        __syncthreads();                      // ... for every thread; stage it-1 is free
+        {
+            const long long nx = it + C::kStages - 1;
+            if (nx < nchunks)
+                small_stage<T, DIAG>(stages + (int)(nx % C::kStages) * C::kStageFloats, G, V, E,
+                                     N, sg.nb + nx * C::kK, sg.ne);
+            cp_async_commit();
         }
-        __syncthreads();
+        const float* sG = stages + (int)(it % C::kStages) * C::kStageFloats;
+        const float* sV = sG + T * C::kRS;
+        const float* sE = sV + T * C::kRS;
         float pc[4][4], pd[kDR];
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
             for (int c = 0; c < 4; ++c) pc[r][c] = 0.0f;
 #pragma unroll
-        for (int r = 0; r < kDR; ++r) pd[r] = 0.0f;
-        for (int q = grp; q < C::kQ; q += C::kNG) {
+        for (int k = 0; k < kDR; ++k) pd[k] = 0.0f;
+#pragma unroll
+        for (int qi = 0; qi < C::kQ / C::kNG; ++qi) {
+            const int q = grp + qi * C::kNG;
             float4 g[4], v[4];
 #pragma unroll
             for (int r = 0; r < 4; ++r)
-                g[r] = *reinterpret_cast<const float4*>(sG + (4 * ty + r) * C::kRS + 4 * q);
+                g[r] = *reinterpret_cast<const float4*>(sG + (ty + kSt * r) * C::kRS + 4 * q);
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-                v[c] = *reinterpret_cast<const float4*>(sV + (4 * tx + c) * C::kRS + 4 * q);
+                v[c] = *reinterpret_cast<const float4*>(sV + (tx + kSt * c) * C::kRS + 4 * q);
 #pragma unroll
             for (int r = 0; r < 4; ++r)
 #pragma unroll
@@ -192,19 +247,21 @@ __global__ void __launch_bounds__(256) param_small(const float* __restrict__ G,
                 }
             if (DIAG != kDiagNone) {
 #pragma unroll
-                for (int r = 0; r < kDR; ++r) {
-                    const int t = lt + r * C::kGS;
-                    if (t < T) {
-                        const float4 e = *reinterpret_cast<const float4*>(sE + t * C::kRS + 4 * q);
-                        if (DIAG == kDiagProduct) {
-                            const float4 gg = *reinterpret_cast<const float4*>(sG + t * C::kRS + 4 * q);
-                            pd[r] = __fmaf_rn(gg.x, e.x, pd[r]);
-                            pd[r] = __fmaf_rn(gg.y, e.y, pd[r]);
-                            pd[r] = __fmaf_rn(gg.z, e.z, pd[r]);
-                            pd[r] = __fmaf_rn(gg.w, e.w, pd[r]);
-                        } else {
-                            pd[r] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(pd[r], e.x), e.y), e.z), e.w);
-                        }
+                for (int k = 0; k < kDR; ++k) {
+                    const int r = tx + kSt * k;                  // this thread's diagonal row
+                    const float4 e = *reinterpret_cast<const float4*>(
+                        sE + (ty + kSt * r) * C::kRS + 4 * q);
+                    if (DIAG == kDiagProduct) {
+                        float4 gg = g[0];                        // g[r] without a dynamic index
+#pragma unroll
+                        for (int rr = 1; rr < 4; ++rr)
+                            if (r == rr) gg = g[rr];
+                        pd[k] = __fmaf_rn(gg.x, e.x, pd[k]);
+                        pd[k] = __fmaf_rn(gg.y, e.y, pd[k]);
+                        pd[k] = __fmaf_rn(gg.z, e.z, pd[k]);
+                        pd[k] = __fmaf_rn(gg.w, e.w, pd[k]);
+                    } else {
+                        pd[k] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(pd[k], e.x), e.y), e.z), e.w);
                     }
                 }
             }
@@ -214,21 +271,20 @@ __global__ void __launch_bounds__(256) param_small(const float* __restrict__ G,
 #pragma unroll
             for (int c = 0; c < 4; ++c) acc[r][c] += (double)pc[r][c];
 #pragma unroll
-        for (int r = 0; r < kDR; ++r) dacc[r] += (double)pd[r];
-        __syncthreads();
+        for (int k = 0; k < kDR; ++k) dacc[k] += (double)pd[k];
     }
+    cp_async_wait<0>();
+    __syncthreads();          // all stages idle: the reduction area may overwrite them
     // fixed-order sum over the groups: red[g][0..T) = d, red[g][T..) = M
     double* red = reinterpret_cast<double*>(smem);
     constexpr int kRow = T * T + T;
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) red[grp * kRow + T + (4 * ty + r) * T + 4 * tx + c] = acc[r][c];
+        for (int c = 0; c < 4; ++c)
+            red[grp * kRow + T + (ty + kSt * r) * T + tx + kSt * c] = acc[r][c];
 #pragma unroll
-    for (int r = 0; r < kDR; ++r) {
-        const int t = lt + r * C::kGS;
-        if (t < T) red[grp * kRow + t] = dacc[r];
-    }
+    for (int k = 0; k < kDR; ++k) red[grp * kRow + ty + kSt * (tx + kSt * k)] = dacc[k];
     __syncthreads();
     double* out = part + (size_t)blockIdx.x * kRow;
     for (int e = tid; e < kRow; e += 256) {
@@ -259,7 +315,7 @@ int param_rows_chunks(int T, long long N, int B) {
     long long target, cap;
     if (T == 8 || T == 16) {
         target = 148 * 8;
-        cap = (F + SmallCfg<8>::kK - 1) / SmallCfg<8>::kK;
+        cap = (F + 127) / 128;
     } else {
         const int tiles = (T + kLT - 1) / kLT;
         target = 2368 / (tiles * tiles);
@@ -278,11 +334,11 @@ cudaError_t param_rows_launch(const float* G, const float* V, const float* E, in
     long long per = (F + chunks - 1) / chunks;
     const dim3 rows((unsigned)((long long)B * chunks));
     if (small_ok && (T == 8 || T == 16)) {
-        per = (per + 3) / 4 * 4;
+        per = (per + 3) / 4 * 4;                 // segments start on whole quads
 #define DFSNN_SMALL(TV, DV)                                                                   \
         if (T == TV && diag == DV) {                                                          \
             auto k = param_small<TV, DV>;                                                     \
-            const int bytes = SmallCfg<TV>::kBytes;                                           \
+            const int bytes = SmallCfg<TV, DV>::kBytes;                                       \
             cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); \
             if (e != cudaSuccess) return e;                                                   \
             k<<<rows, 256, bytes, st>>>(G, V, E, N, F, chunks, per, part);                    \

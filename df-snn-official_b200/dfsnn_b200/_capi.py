@@ -63,6 +63,10 @@ SIGNATURES = {
     "dfsnn_vo_predictor_forward": (_i, [_p, _p, _p, _p, _i, _i, _p, _p, _p, _i, _ll, _f, _f, _f,
                                         _p]),
     "dfsnn_history_backward_workspace_size": (_sz, [_i, _ll, _i, _i]),
+    "dfsnn_gl_history_step": (_i, [_i, _p, _p, _i, _i, _p, _i, _p, _i, _p, _p, _ll, _p, _i, _p]),
+    "dfsnn_gl_history_step_workspace_size": (_sz, [_i, _ll]),
+    "dfsnn_gl_history_step_backward": (_i, [_i, _p, _p, _p, _i, _i, _p, _i, _p, _p, _p, _p, _p,
+                                            _ll, _p, _sz, _p]),
     "dfsnn_vo_gl1_backward": (_i, [_p, _p, _p, _p, _p, _p, _i, _i, _p, _p, _p, _p, _i, _ll, _f,
                                    _f, _f, _i, _p, _sz, _p]),
     "dfsnn_fa_gl1_backward": (_i, [_p, _p, _p, _p, _i, _i, _p, _p, _p, _i, _ll, _f, _f, _f, _f,

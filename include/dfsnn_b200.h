@@ -281,6 +281,47 @@ int dfsnn_vo_predictor_backward(const float* grad_spike, const float* scale,
                                 float residual_mix, void* workspace, size_t workspace_bytes,
                                 void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * Multi-term GL integrator of the SNN wrapper path (spikeDE_dis/solver.py)
+ * ------------------------------------------------------------------------------- */
+
+#define DFSNN_F32 0
+#define DFSNN_F64 1
+
+/* One integrator step for one state component, replacing the per-step body of
+ * forward_glmulti_cupy (solver.py:3310-3362: torch.stack of the history, weighted_sum
+ * kernels :90-104 per 96-row chunk, the chunk sum, f - conv and the c~_0^-1 scale) and of
+ * backward_glmulti_cupy (:2959-2995: the coefficient dot product and the same update):
+ *   out = c0_inv[0] * (f - conv),  conv = sum_{row_begin <= j < row_end} c_tilde[coeff_base - j]
+ *                                         * rows[j][n]
+ * rows is a device table of row pointers (state_size elements each, dtype DFSNN_F32 or
+ * DFSNN_F64).  chunk > 0: fused multiply-add chains over chunks of `chunk` rows whose results
+ * are added in order (the forward's weighted_sum kernels); chunk == 0: one chain (the
+ * adjoint's dot product); chunk < 0: multiply, then add, term by term (the forward's PyTorch
+ * loop for history_chunk_size <= 0).  diff (optional) receives f - conv.  If table is not
+ * NULL, table[out_slot] = out is stored by the kernel (out_slot >= row_end), so later steps
+ * find this step's output; c_tilde and c0_inv are device arrays. */
+int dfsnn_gl_history_step(int dtype, const void* f, const void* const* rows, int row_begin,
+                          int row_end, const void* c_tilde, int coeff_base, const void* c0_inv,
+                          int chunk, void* out, void* diff, long long state_size, void** table,
+                          int out_slot, void* stream);
+
+/* Bytes of workspace dfsnn_gl_history_step_backward needs for `rows` history rows. */
+size_t dfsnn_gl_history_step_workspace_size(int rows, long long state_size);
+
+/* Gradients of one step given grad_out: grad_f = c0_inv*grad_out; if grad_rows is not NULL,
+ * grad_rows[j - row_begin][n] = c_tilde[coeff_base - j] * (-grad_f[n]) ([rows, state_size]);
+ * grad_coeff[j - row_begin] = sum_n rows[j][n] * (-grad_f[n]) and grad_c0_inv[0] =
+ * sum_n grad_out[n] * diff[n], both summed in double (either may be NULL).  The autograd of
+ * the reference's step with an attached history sum (_CupyWeightedHistorySum.backward,
+ * solver.py:136-146, and the PyTorch ops around it). */
+int dfsnn_gl_history_step_backward(int dtype, const void* grad_out, const void* c0_inv,
+                                   const void* const* rows, int row_begin, int row_end,
+                                   const void* c_tilde, int coeff_base, const void* diff,
+                                   void* grad_f, void* grad_rows, void* grad_coeff,
+                                   void* grad_c0_inv, long long state_size, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 /* ---- self-check (no reference counterpart) ----------------------------------------
  * The backward kernels divide the arctan surrogate's numerator by its denominator with an
  * FMA-corrected reciprocal (Markstein) instead of the IEEE division sequence.  This entry

@@ -172,6 +172,12 @@ void ref_vopred_backward(const float* gs, const float* scale, const float* W, co
                          float tau, float th, float sg, float rm) {
     DFSNN_REF_LOOP(N, lif_fde_vo_predictor_backward_kernel(gs, scale, W, vpre, gx, gv0, gpre, T, N, B, per_batch, tau, th, sg, rm));
 }
+void ref_weighted_sum_f32(const float* coeff, const float* history, float* out, int L, int S) {
+    DFSNN_REF_LOOP(S, weighted_sum_f32(coeff, history, out, L, S));
+}
+void ref_weighted_sum_f64(const double* coeff, const double* history, double* out, int L, int S) {
+    DFSNN_REF_LOOP(S, weighted_sum_f64(coeff, history, out, L, S));
+}
 void ref_glmulti_forward(const float* x, const float* v0, const float* scale, const float* W,
                          float* s, float* vpre, float* vhist, float* drift, int T, int N,
                          float tau, float th) {
@@ -250,6 +256,41 @@ def _function_local_string(path, func_name, var_name="code"):
     raise RuntimeError(f"{func_name}.{var_name} not found in {path}")
 
 
+def _weighted_sum_sources(path):
+    """The weighted_sum kernel of solver.py (_get_weighted_sum_kernel, :77-104) is an f-string
+    over the element type; rebuild it for float and double from the file's syntax tree
+    (nothing of solver.py is imported), with NVRTC's contraction of the accumulation."""
+    with open(path) as f:
+        tree = ast.parse(f.read())
+    template = None
+    for node in ast.walk(tree):
+        if isinstance(node, ast.FunctionDef) and node.name == "_get_weighted_sum_kernel":
+            for sub in ast.walk(node):
+                if (isinstance(sub, ast.Assign) and len(sub.targets) == 1
+                        and isinstance(sub.targets[0], ast.Name) and sub.targets[0].id == "code"
+                        and isinstance(sub.value, ast.JoinedStr)):
+                    template = sub.value
+    if template is None:
+        raise RuntimeError("_get_weighted_sum_kernel.code not found in " + path)
+    out = []
+    for type_name, suffix, fma in (("float", "f32", "fmaf"), ("double", "f64", "fma")):
+        text = ""
+        for part in template.values:
+            if isinstance(part, ast.Constant):
+                text += part.value
+            elif isinstance(part, ast.FormattedValue) and isinstance(part.value, ast.Name) \
+                    and part.value.id == "type_name":
+                text += type_name
+            else:
+                raise RuntimeError("unexpected field in the weighted_sum template")
+        stmt = "acc += coeff[j] * history[j * state_size + idx];"
+        if stmt not in text or "void weighted_sum(" not in text:
+            raise RuntimeError("weighted_sum kernel body not recognised")
+        text = text.replace(stmt, f"acc = {fma}(coeff[j], history[j * state_size + idx], acc);")
+        out.append(text.replace("void weighted_sum(", f"void weighted_sum_{suffix}("))
+    return "\n".join(out)
+
+
 def collect_sources(reference):
     _stub_h5py()
     sys.path.insert(0, reference)
@@ -267,6 +308,7 @@ def collect_sources(reference):
     euler_path = os.path.join(reference, "spikeDE_dis", "direct_euler_cupy.py")
     fma_parts.append(_function_local_string(euler_path, "_get_forward_kernel"))
     fma_parts.append(_function_local_string(euler_path, "_get_backward_kernel"))
+    fma_parts.append(_weighted_sum_sources(os.path.join(reference, "spikeDE_dis", "solver.py")))
     # The reference substitutes HISTORY_RHO into this statement as text before compiling
     # (aligned_glmulti.py:90); do the same with a run-time variable.
     target = "adj[j]-=w[t*T+j]*r;"

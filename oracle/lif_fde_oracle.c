@@ -632,3 +632,40 @@ int orc_num_threads(void) {
     return 1;
 #endif
 }
+
+/* ---------------------------------------------------------------------------------------
+ * Multi-term GL integrator step of the SNN wrapper path (spikeDE_dis/solver.py):
+ *   out[n] = c0_inv * (f[n] - conv[n]),  conv[n] = sum_{r < L} coef[r] * hist[r*S + n]
+ * chunk > 0: forward_glmulti_cupy (:3331-3358) -- per chunk of `chunk` rows the weighted_sum
+ *            kernel (:90-104, acc += coeff[j]*history[...], one fma per term under NVRTC
+ *            --fmad=true), chunk results summed left to right by PyTorch adds;
+ * chunk == 0: one fma chain over all rows (the adjoint's dot product, :2976-2987, whose
+ *            cuBLAS summation order is unspecified; this is the order the kernels use);
+ * chunk < 0: the forward's PyTorch loop for history_chunk_size <= 0 (:3323-3330),
+ *            conv = conv + coef*row with both operations rounded.
+ * ------------------------------------------------------------------------------------- */
+#define ORC_GL_STEP(NAME, F, FMA)                                                          \
+void NAME(const F* f, const F* hist, const F* coef, int L, int64_t S, F c0_inv, int chunk,  \
+          F* out) {                                                                        \
+    _Pragma("omp parallel for schedule(static)")                                           \
+    for (int64_t n = 0; n < S; ++n) {                                                      \
+        F conv = (F)0;                                                                     \
+        if (chunk < 0) {                                                                   \
+            for (int r = 0; r < L; ++r) {                                                  \
+                const F p = coef[r] * hist[(int64_t)r * S + n];                            \
+                conv = conv + p;                                                           \
+            }                                                                              \
+        } else {                                                                           \
+            const int step = chunk > 0 ? chunk : (L > 0 ? L : 1);                          \
+            for (int c0 = 0; c0 < L; c0 += step) {                                         \
+                const int c1 = c0 + step < L ? c0 + step : L;                              \
+                F acc = (F)0;                                                              \
+                for (int r = c0; r < c1; ++r) acc = FMA(coef[r], hist[(int64_t)r * S + n], acc); \
+                conv = c0 == 0 ? acc : conv + acc;                                         \
+            }                                                                              \
+        }                                                                                  \
+        out[n] = c0_inv * (f[n] - conv);                                                   \
+    }                                                                                      \
+}
+ORC_GL_STEP(orc_gl_step_f32, float, fmaf)
+ORC_GL_STEP(orc_gl_step_f64, double, fma)

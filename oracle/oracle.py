@@ -51,6 +51,8 @@ def lib():
                                         _f, _f, _f]
         L.orc_hfam_param_grads.argtypes = [_p, _p, _p, _p, _i, _i, _i, _i64, ctypes.c_double, _i,
                                            _p, _p]
+        L.orc_gl_step_f32.argtypes = [_p, _p, _p, _i, _i64, _f, _i, _p]
+        L.orc_gl_step_f64.argtypes = [_p, _p, _p, _i, _i64, ctypes.c_double, _i, _p]
         L.orc_glmulti_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f]
         L.orc_glmulti_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i64, _f, _f, _f]
         L.orc_glmulti_param_grads.argtypes = [_p, _p, _p, _p, _p, _i, _i64]
@@ -95,6 +97,8 @@ def ref():
         R.ref_fagl1_backward.argtypes = [_i] + [_p] * 6 + [_i] * 4 + [_f] * 4
         R.ref_vopred_forward.argtypes = [_p] * 7 + [_i] * 4 + [_f] * 3
         R.ref_vopred_backward.argtypes = [_p] * 7 + [_i] * 4 + [_f] * 4
+        R.ref_weighted_sum_f32.argtypes = [_p, _p, _p, _i, _i]
+        R.ref_weighted_sum_f64.argtypes = [_p, _p, _p, _i, _i]
         R.ref_glmulti_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f]
         R.ref_glmulti_backward.argtypes = [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _f]
         R.ref_aligned_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f]
@@ -410,3 +414,67 @@ def hfam_params(kind, gpre, hsrc, drift, scale, W, B, lower_only_batch=True):
     hist = np.einsum("tbi,ibf->tbf", Wd, D) if per_batch else np.einsum("ti,ibf->tbf", Wd, D)
     gsb = np.sum(G * (D + hist), axis=2)
     return (gsb if per_batch else gsb.sum(axis=1)), gW
+
+
+# ---------------------------------------------------------------------------------------
+# multi-term GL integrator of the SNN wrapper path (solver.py:2905-3002, :3270-3369)
+# ---------------------------------------------------------------------------------------
+def gl_step(f, hist, coef, c0_inv, chunk):
+    """One integrator step: c0_inv * (f - conv) over hist [L, S] with coefficients coef[L]
+    (see orc_gl_step_*; chunk > 0 weighted_sum chunks, 0 one chain, < 0 PyTorch loop)."""
+    dt = np.asarray(f).dtype
+    f = np.ascontiguousarray(f).reshape(-1)
+    S = f.size
+    hist = np.ascontiguousarray(hist, dtype=dt).reshape(-1, S)
+    coef = np.ascontiguousarray(coef, dtype=dt)
+    out = np.empty_like(f)
+    fn = lib().orc_gl_step_f32 if dt == np.float32 else lib().orc_gl_step_f64
+    fn(_ptr(f), _ptr(hist), _ptr(coef), hist.shape[0], S, float(c0_inv), int(chunk), _ptr(out))
+    return out
+
+
+def weighted_sum_ref(coeff, history):
+    """The reference's weighted_sum kernel source compiled for the host."""
+    dt = np.asarray(history).dtype
+    history = np.ascontiguousarray(history)
+    L, S = history.shape
+    coeff = np.ascontiguousarray(coeff, dtype=dt)
+    out = np.empty(S, dtype=dt)
+    fn = ref().ref_weighted_sum_f32 if dt == np.float32 else ref().ref_weighted_sum_f64
+    fn(_ptr(coeff), _ptr(history), _ptr(out), L, S)
+    return out
+
+
+def glmulti_integrate(f_of, y0, c_tilde, c0_inv, T, memory=None, chunk=96):
+    """forward_glmulti_cupy (solver.py:3314-3362) for one integrated component given the
+    coefficient table: f_of(k, y_current) -> f_k (numpy), y0 the initial state.  Returns the
+    list of states y_1..y_T.  chunk as the reference's history_chunk_size (<= 0: PyTorch
+    loop)."""
+    kchunk = chunk if chunk > 0 else -1
+    hist, y = [], y0
+    for k in range(T):
+        f = f_of(k, y)
+        mem = k + 1 if memory in (None, -1) else min(memory, k + 1)
+        start = max(0, k + 1 - mem)
+        rows = hist[start:k] if k > start else []
+        coef = np.array([c_tilde[k + 1 - j] for j in range(start, start + len(rows))], f.dtype)
+        H = np.stack(rows) if rows else np.zeros((0, f.size), f.dtype)
+        y = gl_step(f, H, coef, c0_inv, kchunk).reshape(f.shape)
+        hist.append(y)
+    return hist
+
+
+def glmulti_adjoint(vjp_of, adj0, c_tilde, c0_inv, steps, memory=None):
+    """backward_glmulti_cupy's update (solver.py:2958-2995) for one component: vjp_of(k,
+    adj) -> vjp_y; rows 0..k of the adjoint history with c~[k+1-j], one fma chain."""
+    hist = [adj0]
+    adj = adj0
+    for k in range(steps - 1):
+        f = vjp_of(k, adj)
+        mem = k + 1 if memory in (None, -1) else min(memory, k + 1)
+        start = max(0, k + 1 - mem)
+        rows = hist[start:k + 1]
+        coef = np.array([c_tilde[k + 1 - j] for j in range(start, k + 1)], f.dtype)
+        adj = gl_step(f, np.stack(rows), coef, c0_inv, 0).reshape(f.shape)
+        hist.append(adj)
+    return adj

@@ -276,3 +276,78 @@ def test_history_empty():
     out.sum().backward()
     assert out.shape == (T, 0)
     assert float(s.grad.abs().sum()) == 0.0 and float(W.grad.abs().sum()) == 0.0
+
+
+# -------------------------------------------------------------------------------------
+# LIFNeuronFDE methods on top of these Functions (neuron.py:1718-2061)
+# -------------------------------------------------------------------------------------
+def _neuron(method, **kw):
+    from dfsnn_b200 import neuron
+    return neuron.LIFNeuronFDE(tau=2.0, threshold=TH, surrogate_grad_scale=SG, method=method,
+                               beta=0.6, T=kw.pop("T", 8), step_size=0.1, name="lif1",
+                               step_mode="m", backend=kw.pop("backend", "cupy"), **kw).to(DEV)
+
+
+@pytest.mark.parametrize("method", ["vogl1", "vopredictor"])
+@pytest.mark.parametrize("per_sample", [False, True])
+def test_neuron_variable_order_vs_oracle(method, per_sample):
+    from dfsnn_b200 import schedule
+    T, B = 8, 4
+    g = torch.Generator(device=DEV).manual_seed(3)
+    x = torch.randn((T, B, 3, 17), device=DEV, generator=g) * 5.0
+    beta = 0.2 + 0.6 * torch.rand((T, B) if per_sample else (T,), device=DEV, generator=g)
+    n = _neuron(method, T=T, vo_residual_mix=RM, history_grad_mode="full")
+    s = n(x, beta_schedule=beta)
+    build = schedule.build_vogl1_schedule if method == "vogl1" else schedule.build_vopredictor_schedule
+    terms = build(beta, 0.1)
+    kind = "vogl1" if method == "vogl1" else "vopred"
+    N = x[0].numel()
+    fw = O.hfam_forward(kind, cpu(x).reshape(T, N), np.zeros(N, np.float32), cpu(terms["scale"]),
+                        cpu(terms["weights"]), B, 2.0, TH, HB, RM)
+    assert_bitwise(cpu(s).reshape(T, N), fw["spike"], what="spike")
+    assert float(n.v.abs().sum()) == 0.0 and n.k == T
+
+
+@pytest.mark.parametrize("mode", ["per_sample", "batch_shared"])
+@pytest.mark.parametrize("backend", ["cupy", "torch"])
+def test_neuron_fagl1_vs_oracle(mode, backend):
+    T, B = 8, 4
+    g = torch.Generator(device=DEV).manual_seed(4)
+    x = (torch.randn((T, B, 5, 13), device=DEV, generator=g) * 5.0).requires_grad_(True)
+    n = _neuron("fagl1", T=T, attn_mode=mode, backend=backend, history_grad_mode="full")
+    with torch.no_grad():
+        W = n._build_fagl1_weights(x)
+    n._fagl_stats_counter = 0
+    s = n(x)
+    N = x[0].numel()
+    fw = O.hfam_forward("fagl1", cpu(x).reshape(T, N), np.zeros(N, np.float32), None, cpu(W), B,
+                        2.0, TH, np.float32(0.1 ** 0.6))
+    assert_bitwise(cpu(s).reshape(T, N), fw["spike"], what="spike")
+    s.sum().backward()
+    assert n.fagl_q_proj.weight.grad is not None and n.fagl_k_proj.weight.grad is not None
+    assert torch.isfinite(x.grad).all()
+    assert n.get_attention_stats() is not None
+
+
+def test_neuron_gl1_full_history_vs_oracle():
+    T, B = 16, 2
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = torch.randn((T, B, 300), device=DEV, generator=g) * 5.0
+    n = _neuron("gl1", T=T, history_grad_mode="full")
+    s = n(x)
+    W = n._build_gl1_causal_weights(T, x.device)
+    N = x[0].numel()
+    fw = O.hfam_forward("fagl1", cpu(x).reshape(T, N), np.zeros(N, np.float32), None, cpu(W), B,
+                        2.0, TH, np.float32(0.1 ** 0.6))
+    assert_bitwise(cpu(s).reshape(T, N), fw["spike"], what="spike")
+
+
+def test_neuron_variable_order_requires_schedule():
+    n = _neuron("vogl1")
+    with pytest.raises(ValueError):
+        n(torch.zeros((8, 2, 3), device=DEV))
+    with pytest.raises(ValueError):
+        n(torch.zeros((8, 2, 3), device=DEV), beta_schedule=torch.full((7,), 0.5, device=DEV))
+    m = _neuron("vogl1", vo_solver="l1")
+    with pytest.raises(NotImplementedError):
+        m(torch.zeros((8, 2, 3), device=DEV), beta_schedule=torch.full((8,), 0.5, device=DEV))
