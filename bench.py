@@ -59,9 +59,11 @@ def parse():
                     help="profiling: comma list of scheme:T (e.g. glmulti:16) instead of all")
     ap.add_argument("--neurons", type=int, default=0,
                     help="profiling: neurons per GPU instead of 16*128*64*64")
-    ap.add_argument("--workload", choices=("layers", "cnn128", "history"), default="layers",
-                    help="layers: the LIFNeuronFDE layer step (default); cnn128: synthetic "
-                         "CNN128 training step, data-parallel, samples/s; history: the "
+    ap.add_argument("--workload", choices=("layers", "cnn128", "spikformer256", "history"),
+                    default="layers",
+                    help="layers: the LIFNeuronFDE layer step (default); cnn128 / "
+                         "spikformer256: synthetic network training step, data-parallel, "
+                         "samples/s; history: the "
                          "VO-GL1 / FAGL1 / VO-PREDICTOR Functions with per-sample tables")
     args = ap.parse_args()
     global SHAPE, COMBOS
@@ -469,6 +471,164 @@ def run_e2e(args, layers, x16, gS16, gV16, dev, world):
 CNN_T, CNN_B, CNN_CLASSES = 16, 16, 11
 
 
+def glmulti_neuron_factory(T, B):
+    """LIFNeuronFDE layers as the examples configure them: glmulti with aligned semantics
+    (installed as the examples do), full-history gradient, one Softplus mass parameter
+    shared by every layer (examples/cnn128/cnn128_aligned.py:14-19)."""
+    import torch
+    import torch.nn as nn
+    from dfsnn_b200 import aligned_glmulti
+    from dfsnn_b200.neuron import LIFNeuronFDE
+    aligned_glmulti.install("native")
+    raw = nn.Parameter(torch.log(torch.expm1(torch.tensor(MASSES))))
+
+    def neuron(name):
+        return LIFNeuronFDE(tau=2.0, threshold=1.0, surrogate_grad_scale=5.0,
+                            surrogate_function="arctan", beta=MULTI_BETA[0], T=T,
+                            method="glmulti", step_size=0.1, batchsize=B, name=name,
+                            backend="cupy", step_mode="m", multi_beta=MULTI_BETA,
+                            multi_coefficient=MASSES, learn_coefficient=True,
+                            coefficient_constraint="softplus", shared_multi_coefficient=raw,
+                            coefficient_update_interval=1, glmulti_history_grad="full")
+
+    return neuron
+
+
+SPK_T, SPK_B, SPK_CLASSES, SPK_DIM, SPK_DEPTH, SPK_HEADS = 8, 16, 300, 256, 2, 16
+
+
+def make_spikformer256(dev):
+    """The direct-FDE Spikformer of the reference examples (examples/spikformer_har_lip/
+    model.py:726-960, spikformer_e256_lif_fde: embed 256, depth 2, 16 heads, MLP ratio 4):
+    SPS patch embedding (four Conv3x3-BN-LIF-MaxPool(3,2,1) stages 2->32->64->128->256, then a
+    Conv3x3-BN-LIF relative position embedding added to its input: 8x8 = 64 tokens), two
+    blocks of spiking self-attention (1x1 Conv1d-BN-LIF for q, k, v; (q k^T) v * 0.25; LIF;
+    Conv1d-BN-LIF projection) and MLP (Conv1d 256->1024-BN-LIF, 1024->256-BN-LIF) with
+    residuals and drop path 0.1*i/(depth-1), and the head: mean over tokens, Linear per
+    time step, mean over time.  Every LIF is the glmulti neuron of the CNN128 configuration
+    at T=8.  Layers applied per frame run on all T*B frames at once (the reference's
+    _time_distributed, :421-427)."""
+    import torch
+    import torch.nn as nn
+    from dfsnn_b200.neuron import LIFNeuronFDE
+    neuron = glmulti_neuron_factory(SPK_T, SPK_B)
+
+    def td(module, x):
+        T, B = x.shape[:2]
+        y = module(x.flatten(0, 1))
+        return y.reshape((T, B) + tuple(y.shape[1:]))
+
+    class DropPath(nn.Module):
+        def __init__(self, p):
+            super().__init__()
+            self.p = p
+
+        def forward(self, x):
+            if self.p == 0.0 or not self.training:
+                return x
+            keep = 1.0 - self.p
+            mask = x.new_empty((x.shape[0],) + (1,) * (x.dim() - 1)).bernoulli_(keep)
+            return x * mask / keep
+
+    class SPS(nn.Module):
+        def __init__(self, dim):
+            super().__init__()
+            chans = [2, dim // 8, dim // 4, dim // 2, dim]
+            self.convs = nn.ModuleList(nn.Conv2d(chans[i], chans[i + 1], 3, padding=1, bias=False)
+                                       for i in range(4))
+            self.bns = nn.ModuleList(nn.BatchNorm2d(chans[i + 1]) for i in range(4))
+            self.lifs = nn.ModuleList(neuron(f"patch_lif{i + 1}") for i in range(4))
+            self.pool = nn.MaxPool2d(3, stride=2, padding=1)
+            self.rpe_conv = nn.Conv2d(dim, dim, 3, padding=1, bias=False)
+            self.rpe_bn = nn.BatchNorm2d(dim)
+            self.rpe_lif = neuron("rpe_lif")
+
+        def forward(self, x):
+            for conv, bn, lif in zip(self.convs, self.bns, self.lifs):
+                x = td(self.pool, lif(td(bn, td(conv, x))))
+            x = x + self.rpe_lif(td(self.rpe_bn, td(self.rpe_conv, x)))
+            T, B, C, H, W = x.shape
+            return x.reshape(T, B, C, H * W)
+
+    class SSA(nn.Module):
+        def __init__(self, dim, heads):
+            super().__init__()
+            self.dim, self.heads = dim, heads
+            self.qkv = nn.ModuleList(nn.Conv1d(dim, dim, 1, bias=False) for _ in range(3))
+            self.qkv_bn = nn.ModuleList(nn.BatchNorm1d(dim) for _ in range(3))
+            self.qkv_lif = nn.ModuleList(neuron(n) for n in ("q_lif", "k_lif", "v_lif"))
+            self.attn_lif = neuron("attn_lif")
+            self.proj = nn.Conv1d(dim, dim, 1)
+            self.proj_bn = nn.BatchNorm1d(dim)
+            self.proj_lif = neuron("proj_lif")
+
+        def forward(self, x):
+            heads = []
+            for conv, bn, lif in zip(self.qkv, self.qkv_bn, self.qkv_lif):
+                y = lif(td(bn, td(conv, x)))
+                T, B, C, N = y.shape
+                heads.append(y.transpose(-1, -2).reshape(T, B, N, self.heads, C // self.heads)
+                             .permute(0, 1, 3, 2, 4))
+            q, k, v = heads
+            x = ((q @ k.transpose(-2, -1)) @ v) * 0.25
+            T, B, _, N, _ = x.shape
+            x = self.attn_lif(x.permute(0, 1, 2, 4, 3).reshape(T, B, self.dim, N))
+            return self.proj_lif(td(self.proj_bn, td(self.proj, x)))
+
+    class MLP(nn.Module):
+        def __init__(self, dim, hidden):
+            super().__init__()
+            self.fc1, self.bn1, self.lif1 = nn.Conv1d(dim, hidden, 1), nn.BatchNorm1d(hidden), neuron("mlp_lif1")
+            self.fc2, self.bn2, self.lif2 = nn.Conv1d(hidden, dim, 1), nn.BatchNorm1d(dim), neuron("mlp_lif2")
+
+        def forward(self, x):
+            x = self.lif1(td(self.bn1, td(self.fc1, x)))
+            return self.lif2(td(self.bn2, td(self.fc2, x)))
+
+    class Block(nn.Module):
+        def __init__(self, dim, heads, drop):
+            super().__init__()
+            self.attn, self.mlp, self.drop = SSA(dim, heads), MLP(dim, 4 * dim), DropPath(drop)
+
+        def forward(self, x):
+            x = x + td(self.drop, self.attn(x))
+            return x + td(self.drop, self.mlp(x))
+
+    class Spikformer(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.patch_embed = SPS(SPK_DIM)
+            self.blocks = nn.ModuleList(Block(SPK_DIM, SPK_HEADS, 0.1 * i / max(1, SPK_DEPTH - 1))
+                                        for i in range(SPK_DEPTH))
+            self.head = nn.Linear(SPK_DIM, SPK_CLASSES)
+            self.apply(self._init_weights)
+
+        @staticmethod
+        def _init_weights(m):                  # as the reference model (model.py:899-910)
+            if isinstance(m, nn.Conv2d):
+                nn.init.kaiming_normal_(m.weight, mode="fan_out", nonlinearity="relu")
+            elif isinstance(m, (nn.BatchNorm1d, nn.BatchNorm2d)):
+                nn.init.constant_(m.weight, 1)
+                nn.init.constant_(m.bias, 0)
+            elif isinstance(m, nn.Linear):
+                nn.init.trunc_normal_(m.weight, std=0.02)
+                if m.bias is not None:
+                    nn.init.constant_(m.bias, 0)
+
+        def forward(self, x):
+            x = self.patch_embed(x)
+            for blk in self.blocks:
+                x = blk(x)
+            return self.head(x.mean(-1)).mean(0)
+
+        def reset(self):
+            for m in self.modules():
+                if isinstance(m, LIFNeuronFDE):
+                    m.reset()
+
+    return Spikformer().to(dev)
+
+
 def make_cnn128(dev):
     """The CNN128 topology of the reference examples (examples/cnn128/cnn128_aligned.py:8-40):
     five blocks Conv2d(3x3, 128, no bias) -> BatchNorm2d -> LIFNeuronFDE -> MaxPool2d(2), then
@@ -479,19 +639,8 @@ def make_cnn128(dev):
     norm per frame as in the reference; output = mean over time."""
     import torch
     import torch.nn as nn
-    from dfsnn_b200 import aligned_glmulti
     from dfsnn_b200.neuron import LIFNeuronFDE
-    aligned_glmulti.install("native")
-    raw = nn.Parameter(torch.log(torch.expm1(torch.tensor(MASSES))))
-
-    def neuron(name):
-        return LIFNeuronFDE(tau=2.0, threshold=1.0, surrogate_grad_scale=5.0,
-                            surrogate_function="arctan", beta=MULTI_BETA[0], T=CNN_T,
-                            method="glmulti", step_size=0.1, batchsize=CNN_B, name=name,
-                            backend="cupy", step_mode="m", multi_beta=MULTI_BETA,
-                            multi_coefficient=MASSES, learn_coefficient=True,
-                            coefficient_constraint="softplus", shared_multi_coefficient=raw,
-                            coefficient_update_interval=1, glmulti_history_grad="full")
+    neuron = glmulti_neuron_factory(CNN_T, CNN_B)
 
     class CNN128(nn.Module):
         def __init__(self):
@@ -528,7 +677,25 @@ def make_cnn128(dev):
     return CNN128().to(dev)
 
 
+NETWORKS = {
+    # name: (builder, T, B, classes, frame kind, description)
+    "cnn128": ("make_cnn128", CNN_T, CNN_B, CNN_CLASSES, "poisson",
+               "CNN128 (5x conv128-BN-LIF-pool, fc512-LIF, fc256-LIF, fc11) training step, SGD, "
+               "LIFNeuronFDE glmulti aligned full history, shared Softplus masses, T=16, B=16 per "
+               "GPU, frames [16,16,2,128,128] Bernoulli(0.05)*Poisson(1), 11 classes"),
+    "spikformer256": ("make_spikformer256", SPK_T, SPK_B, SPK_CLASSES, "bernoulli",
+                      "Spikformer256 (SPS 2->256, 64 tokens, depth 2, 16 heads, MLP 1024) "
+                      "training step, SGD, LIFNeuronFDE glmulti aligned full history, shared "
+                      "Softplus masses, T=8, B=16 per GPU, frames [8,16,2,128,128] "
+                      "Bernoulli(0.05), 300 classes"),
+}
+
+
 def run_cnn128(args):
+    return run_network(args, "cnn128")
+
+
+def run_network(args, name):
     import torch
     import torch.distributed as dist
     import torch.nn.functional as F
@@ -544,18 +711,20 @@ def run_cnn128(args):
         init_process_group("nccl", timeout_s=300, device=dev)
     K, W = args.steps, max(args.warmup, 3)
     torch.manual_seed(1234 + rank)
-    model = make_cnn128(dev)
+    builder, NT, NB, NCLS, frame_kind, desc = NETWORKS[name]
+    model = globals()[builder](dev)
     net = model
     if world > 1:
         net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local],
                                                         broadcast_buffers=False)
     opt = torch.optim.SGD(model.parameters(), lr=1e-3, momentum=0.9)
     g = torch.Generator(device=dev).manual_seed(99 + rank)
-    # synthetic event frames: Bernoulli(0.05) spike counts scaled by Poisson(1), 11 classes
-    shape = (CNN_T, CNN_B, 2, 128, 128)
-    frames = (torch.rand(shape, device=dev, generator=g) < 0.05).float() * \
-        torch.poisson(torch.ones(shape, device=dev), generator=g)
-    labels = torch.randint(0, CNN_CLASSES, (CNN_B,), device=dev, generator=g)
+    # synthetic event frames: Bernoulli(0.05) spikes (scaled by Poisson(1) counts for CNN128)
+    shape = (NT, NB, 2, 128, 128)
+    frames = (torch.rand(shape, device=dev, generator=g) < 0.05).float()
+    if frame_kind == "poisson":
+        frames = frames * torch.poisson(torch.ones(shape, device=dev), generator=g)
+    labels = torch.randint(0, NCLS, (NB,), device=dev, generator=g)
 
     def step():
         model.reset()
@@ -590,14 +759,12 @@ def run_cnn128(args):
     summary = timer.summary()
     if rank == 0:
         line = {
-            "metric": "CNN128 synthetic training samples/s", "value": world * CNN_B * K / (ms / 1e3),
+            "metric": f"{'CNN128' if name == 'cnn128' else 'Spikformer256'} synthetic training "
+                      "samples/s", "value": world * NB * K / (ms / 1e3),
             "unit": "samples/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "CNN128 (5x conv128-BN-LIF-pool, fc512-LIF, fc256-LIF, fc11) "
-                       "training step, SGD, LIFNeuronFDE glmulti aligned full history, shared "
-                       "Softplus masses, T=16, B=16 per GPU, frames [16,16,2,128,128] "
-                       "Bernoulli(0.05)*Poisson(1), 11 classes",
+            "config": {"workload": desc,
                        "parallelism": f"dp{world}" + (" (DDP, NCCL)" if world > 1 else "")},
             "lif_kernels": {k: {"calls_per_step": v["calls"] / K,
                                 "ms_per_call": round(v["ms_per_call"], 4)}
@@ -749,8 +916,8 @@ def run_history(args):
 
 def main():
     args = parse()
-    if args.workload == "cnn128":
-        return run_cnn128(args) if args.impl == "native" else 0
+    if args.workload in NETWORKS:
+        return run_network(args, args.workload) if args.impl == "native" else 0
     if args.workload == "history":
         return run_history(args) if args.impl == "native" else 0
     if args.impl == "reference":
