@@ -59,14 +59,26 @@ def parse():
                     help="profiling: comma list of scheme:T (e.g. glmulti:16) instead of all")
     ap.add_argument("--neurons", type=int, default=0,
                     help="profiling: neurons per GPU instead of 16*128*64*64")
-    ap.add_argument("--workload", choices=("layers", "cnn128", "spikformer256", "history"),
+    ap.add_argument("--workload", choices=("layers", "long", "cnn128", "spikformer256",
+                                           "history"),
                     default="layers",
-                    help="layers: the LIFNeuronFDE layer step (default); cnn128 / "
+                    help="layers: the LIFNeuronFDE layer step (default); long: the "
+                         "long-history layer step (T = 64, 256); cnn128 / "
                          "spikformer256: synthetic network training step, data-parallel, "
                          "samples/s; history: the "
                          "VO-GL1 / FAGL1 / VO-PREDICTOR Functions with per-sample tables")
     args = ap.parse_args()
-    global SHAPE, COMBOS
+    global SHAPE, COMBOS, WORKLOAD, X_MEAN, X_STD, TS
+    if args.workload == "long":
+        # the long-history configuration: GL and predictor at T = 64 and 256, 4,194,304
+        # neurons, input current N(0.2, 0.4^2)
+        SHAPE = (16, 4194304 // 16)
+        TS = (64, 256)
+        COMBOS = [(T, sch) for T in TS for sch in ("gl", "predictor")]
+        X_MEAN, X_STD = 0.2, 0.4
+        WORKLOAD = ("LIFNeuronFDE layer fwd+bwd, schemes gl/predictor (single order, beta 0.5) at "
+                    "T=64 and T=256, 4,194,304 neurons per GPU, x~N(0.2,0.4^2), upstream grads "
+                    "N(0,1) on spikes and membrane")
     if args.only:
         COMBOS = [(int(c.split(":")[1]), c.split(":")[0]) for c in args.only.split(",")]
     if args.neurons:
@@ -75,6 +87,7 @@ def parse():
 
 
 COMBOS = [(T, sch) for T in TS for sch in SCHEMES]
+X_MEAN, X_STD = 0.3, 0.5
 
 
 def units_per_step(neurons):
@@ -289,9 +302,10 @@ def run_native(args):
     K, W = args.steps, max(args.warmup, 3)
     neurons = math.prod(SHAPE)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    x16 = torch.randn((16,) + SHAPE, device=dev, generator=g).mul_(0.5).add_(0.3)
-    gS16 = torch.randn((16,) + SHAPE, device=dev, generator=g)
-    gV16 = torch.randn((16,) + SHAPE, device=dev, generator=g)
+    TMAX = max(T for T, _ in COMBOS)
+    x16 = torch.randn((TMAX,) + SHAPE, device=dev, generator=g).mul_(X_STD).add_(X_MEAN)
+    gS16 = torch.randn((TMAX,) + SHAPE, device=dev, generator=g)
+    gV16 = torch.randn((TMAX,) + SHAPE, device=dev, generator=g)
     layers = make_layers(dev)
 
     def step():
@@ -341,13 +355,33 @@ def run_native(args):
                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
                     "algorithmic_bytes_per_launch": d["bytes_per_call"],
                     "traffic": ncu_traffic(name, sorted({T for T, _ in COMBOS}))}
+    if args.workload == "long" and "single_forward" in summary:
+        # T >= 64: the forward's Kahan history chains are FP32-bound (no tensor cores apply:
+        # a fused multiply-add and three adds per term, in a fixed order); roofline against the
+        # FP32 lanes at the clock seen during the run
+        d = summary["single_forward"]
+        instr = 4 * sum(neurons * T * (T - 1) // 2 for T, _ in COMBOS)
+        sec = d["ms_total"] / K / 1e3
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        mhz = (clk or {}).get("sm_mhz") or 1965.0
+        peak_ops = sms * 128 * mhz * 1e6
+        roofline = {"bound": "fp32", "kernel": "single_forward",
+                    "achieved": instr / sec / 1e12, "peak": peak_ops / 1e12,
+                    "unit": "T FP32 instructions/s (per lane)",
+                    "frac": instr / sec / peak_ops,
+                    "peak_source": f"{sms} SMs x 128 FP32 lanes x {mhz:.0f} MHz (median under load)",
+                    "work": "4 FP32 instructions per history term (fma + 3 add/sub, Kahan), "
+                            "N*T(T-1)/2 terms per call",
+                    "hbm_frac_of_measured": d["gbs"] / peak if d["gbs"] else None,
+                    "traffic": None}
     kernels = {k: {"calls_per_step": v["calls"] / K, "ms_per_call": round(v["ms_per_call"], 4),
                    "gbs": round(v["gbs"], 1) if v["gbs"] else None,
                    "frac_of_hbm": round(v["gbs"] / peak, 4) if v["gbs"] else None}
                for k, v in summary.items()}
 
-    # end to end through the public API with host buffers (pinned), copies timed
-    e2e = run_e2e(args, layers, x16, gS16, gV16, dev, world)
+    # end to end through the public API with host buffers (pinned), copies timed (the
+    # headline layer workload; the long-history workload is measured on the device only)
+    e2e = run_e2e(args, layers, x16, gS16, gV16, dev, world) if args.workload == "layers" else None
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
@@ -363,7 +397,7 @@ def run_native(args):
         "clocks": clk,
         "e2e": e2e,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "layers":
         n = args.cpu_sample
         dt, kind, cores = cpu_workload_time(n)
         line["cpu_baseline"] = {"value": units_per_step(n) / dt, "unit": UNIT, "cores": cores,

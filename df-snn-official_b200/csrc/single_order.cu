@@ -168,17 +168,38 @@ __global__ void __launch_bounds__(256) single_fwd_x2(SingleArgs a) {
     *reinterpret_cast<uint2*>(a.bits + n) = make_uint2(b0, b1);
 }
 
-// ------------------------------------------------------------------------------------
-// forward, any T: history in shared memory [T][64]
-// ------------------------------------------------------------------------------------
 constexpr int kLongBlock = 64;
 
+// ------------------------------------------------------------------------------------
+// forward, T > 32: blocked pull form.  The history sum of step k is one Kahan chain over
+// i = 0..k-1 whose loop-carried path (fma, add, sub, sub) is ~16 cycles per term, and the
+// shared-memory history (T floats per neuron) leaves room for only ~200 neurons (6 warps)
+// per SM: one chain per thread left the FP32 pipes less than half busy (ncu: issue stalls on
+// fixed-latency dependencies).  The chains of the kBlk steps k0..k0+kBlk-1 are independent
+// over the terms i < k0, which are known before step k0 starts, so they advance together
+// there (kBlk chains per thread, four terms per iteration, one history load per term and a
+// sliding window of weights); inside the block, each new history value is folded into the
+// later chains of the block as soon as it exists.  Every chain still takes its terms in the
+// reference's order i = 0, 1, ..., k-1: the sums are bit-identical.
+// ------------------------------------------------------------------------------------
+#define DFSNN_KAHAN(S, C, W, H)                                                           \
+    do {                                                                                  \
+        const float y_ = __fmaf_rn((W), (H), -(C));                                       \
+        const float t_ = __fadd_rn((S), y_);                                              \
+        (C) = __fsub_rn(__fsub_rn(t_, (S)), y_);                                          \
+        (S) = t_;                                                                         \
+    } while (0)
+
+constexpr int kBlk = 8;           // chains advanced together
+constexpr int kBlkPad = 8;        // zeros in front of the weight table (window reads)
+
 template <int SCHEME, bool TP2>
-__global__ void __launch_bounds__(kLongBlock) single_fwd_smem(SingleArgs a) {
+__global__ void __launch_bounds__(kLongBlock) single_fwd_blk(SingleArgs a) {
     extern __shared__ float sh[];
     const int T = a.T;
-    float* sw = sh;                                  // [T+1]
-    float* hv = sh + ((T + 1 + 3) & ~3) + threadIdx.x;   // [T][kLongBlock]
+    float* sw = sh + kBlkPad;                        // [T+1] after kBlkPad zeros
+    float* hv = sh + ((kBlkPad + T + 1 + 3) & ~3) + threadIdx.x;   // [T][kLongBlock]
+    if (threadIdx.x < kBlkPad) sh[threadIdx.x] = 0.0f;
     for (int e = threadIdx.x; e <= T; e += blockDim.x) sw[e] = a.w[e];
     __syncthreads();
     const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -189,33 +210,87 @@ __global__ void __launch_bounds__(kLongBlock) single_fwd_smem(SingleArgs a) {
     const float w_cur = sw[T];
     float v = a.v0[n];
     uint32_t bits = 0;
-    float xn = ld_stream(a.x + n);
-    for (int k = 0; k < T; ++k) {
-        const float xk = xn;
-        if (k + 1 < T) xn = ld_stream(a.x + (k + 1) * N + n);
-        const float dv = div_tau<TP2>(__fsub_rn(xk, v), a.tau, a.inv_tau);
-        float sum = 0.0f, c = 0.0f;
-        const float* wk = sw + (T - k);
-        for (int i = 0; i < k; ++i) {
-            const float y = __fmaf_rn(wk[i], hv[i * kLongBlock], -c);
-            const float t = __fadd_rn(sum, y);
-            c = __fsub_rn(__fsub_rn(t, sum), y);
-            sum = t;
+    for (int k0 = 0; k0 < T; k0 += kBlk) {
+        float xk[kBlk];
+#pragma unroll
+        for (int j = 0; j < kBlk; ++j)
+            if (k0 + j < T) xk[j] = ld_stream(a.x + (long long)(k0 + j) * N + n);
+        float sm[kBlk], cm[kBlk];
+#pragma unroll
+        for (int j = 0; j < kBlk; ++j) sm[j] = cm[j] = 0.0f;
+        // chains k0 + j over the known terms i < k0 (k0 % 4 == 0): weight sw[T - k0 - j + i]
+        // = wb[i - j]; per iteration the window holds wb[i - kBlk + 1 .. i + 3]
+        const float* wb = sw + (T - k0);             // i - j >= -(kBlk - 1) stays in sh
+        float wm[kBlk];                              // wm[d] = wb[i - d], d = 1..kBlk-1
+#pragma unroll
+        for (int d = 1; d < kBlk; ++d) wm[d] = wb[-d];
+        // operands of iteration i are loaded during iteration i - 4 (shared-memory latency
+        // off the dependency chains: only ~6 warps per SM are resident to hide it)
+        float wa[4], h[4];
+        if (k0 > 0) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                wa[u] = wb[u];
+                h[u] = hv[u * kLongBlock];
+            }
         }
-        const float p = single_update<SCHEME>(v, dv, sum, trap_factor, pred_scale, w_cur, a.h_beta);
-        const bool fire = p >= a.th;
-        const float s = fire ? 1.0f : 0.0f;
-        v = __fsub_rn(p, s * a.th);
-        hv[k * kLongBlock] = (SCHEME == kPRED || SCHEME == kPRED1) ? div_tau<TP2>(-v, a.tau, a.inv_tau) : v;
-        bits |= (fire ? 1u : 0u) << (k & 31);
-        st_stream(a.spike + k * N + n, s);
-        st_stream(a.v + k * N + n, v);
-        if ((k & 31) == 31 || k == T - 1) {
-            a.bits[(long long)(k >> 5) * N + n] = bits;
-            bits = 0;
+#pragma unroll 2
+        for (int i = 0; i < k0; i += 4) {           // k0 % 8 == 0: an even trip count
+            float wn[4], hn[4];
+            if (i + 4 < k0) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    wn[u] = wb[i + 4 + u];
+                    hn[u] = hv[(i + 4 + u) * kLongBlock];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int j = 0; j < kBlk; ++j) {
+                    // weight of term i + u for chain j: wb[i + u - j]
+                    const int d = j - u;                 // > 0: from the carried window
+                    const float w = d > 0 ? wm[d > 0 ? d : 1] : wa[d > 0 ? 0 : -d];
+                    DFSNN_KAHAN(sm[j], cm[j], w, h[u]);
+                }
+#pragma unroll
+            for (int d = kBlk - 1; d >= 1; --d)         // slide by four terms
+                wm[d] = d > 4 ? wm[d - 4] : wa[4 - d];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                wa[u] = wn[u];
+                h[u] = hn[u];
+            }
+        }
+        // the block's own steps, in order; each new history value goes into the later chains
+#pragma unroll
+        for (int j = 0; j < kBlk; ++j) {
+            const int k = k0 + j;
+            if (k < T) {
+                const float dv = div_tau<TP2>(__fsub_rn(xk[j], v), a.tau, a.inv_tau);
+                const float p = single_update<SCHEME>(v, dv, sm[j], trap_factor, pred_scale,
+                                                      w_cur, a.h_beta);
+                const bool fire = p >= a.th;
+                const float s = fire ? 1.0f : 0.0f;
+                v = __fsub_rn(p, s * a.th);
+                const float hk = (SCHEME == kPRED || SCHEME == kPRED1)
+                                     ? div_tau<TP2>(-v, a.tau, a.inv_tau) : v;
+                hv[k * kLongBlock] = hk;
+#pragma unroll
+                for (int jj = j + 1; jj < kBlk; ++jj)    // term k of chain k0 + jj: sw[T - jj + j]
+                    DFSNN_KAHAN(sm[jj], cm[jj], sw[T - jj + j], hk);
+                bits |= (fire ? 1u : 0u) << (k & 31);
+                st_stream(a.spike + (long long)k * N + n, s);
+                st_stream(a.v + (long long)k * N + n, v);
+                if ((k & 31) == 31 || k == T - 1) {
+                    a.bits[(long long)(k >> 5) * N + n] = bits;
+                    bits = 0;
+                }
+            }
         }
     }
 }
+#undef DFSNN_KAHAN
 
 // ------------------------------------------------------------------------------------
 // backward: truncated reverse sweep from the saved membrane and spike bits (any T)
@@ -462,8 +537,8 @@ cudaError_t fwd_dispatch(const SingleArgs& a, cudaStream_t st) {
         return cudaGetLastError();
     }
     const unsigned grid = (unsigned)((a.N + kLongBlock - 1) / kLongBlock);
-    const size_t smem = sizeof(float) * (((T + 1 + 3) & ~3) + (size_t)T * kLongBlock);
-    auto k = single_fwd_smem<SCHEME, TP2>;
+    const size_t smem = sizeof(float) * (((kBlkPad + T + 1 + 3) & ~3) + (size_t)T * kLongBlock);
+    auto k = single_fwd_blk<SCHEME, TP2>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     k<<<grid, kLongBlock, smem, st>>>(a);
