@@ -59,16 +59,23 @@ def parse():
                     help="profiling: comma list of scheme:T (e.g. glmulti:16) instead of all")
     ap.add_argument("--neurons", type=int, default=0,
                     help="profiling: neurons per GPU instead of 16*128*64*64")
-    ap.add_argument("--workload", choices=("layers", "long", "cnn128", "spikformer256",
-                                           "history"),
+    ap.add_argument("--workload", choices=("layers", "long", "aligned", "cnn128",
+                                           "spikformer256", "history"),
                     default="layers",
                     help="layers: the LIFNeuronFDE layer step (default); long: the "
-                         "long-history layer step (T = 64, 256); cnn128 / "
+                         "long-history layer step (T = 64, 256); aligned: the layer step with "
+                         "the examples' aligned glmulti kernels; cnn128 / "
                          "spikformer256: synthetic network training step, data-parallel, "
                          "samples/s; history: the "
                          "VO-GL1 / FAGL1 / VO-PREDICTOR Functions with per-sample tables")
     args = ap.parse_args()
     global SHAPE, COMBOS, WORKLOAD, X_MEAN, X_STD, TS
+    if args.workload == "aligned":
+        COMBOS = [(T, "aligned") for T in TS]
+        WORKLOAD = ("LIFNeuronFDE layer fwd+bwd with the examples' aligned glmulti kernels "
+                    "(AlignedGLMulti, full history, softplus masses) at T=8 and T=16, input "
+                    "[T,16,128,64,64] = 8,388,608 neurons per GPU, x~N(0.3,0.5^2), upstream "
+                    "grads N(0,1)")
     if args.workload == "long":
         # the long-history configuration: GL and predictor at T = 64 and 256, 4,194,304
         # neurons, input current N(0.2, 0.4^2)
@@ -254,12 +261,18 @@ class ClockSampler:
 
 def make_layers(device):
     from dfsnn_b200.neuron import LIFNeuronFDE
+    if any(sch == "aligned" for _, sch in COMBOS):
+        # the examples' aligned semantics replace the library glmulti Function for the whole
+        # process, as their install() does (so "aligned" and "glmulti" never share a run)
+        from dfsnn_b200 import aligned_glmulti
+        aligned_glmulti.install("native")
     layers = {}
     for T, sch in COMBOS:
+        method = "glmulti" if sch == "aligned" else sch
         kw = dict(tau=TAU, threshold=TH, surrogate_grad_scale=SG, surrogate_function="arctan",
-                  T=T, method=sch, step_size=H, batchsize=SHAPE[0], step_mode="m",
+                  T=T, method=method, step_size=H, batchsize=SHAPE[0], step_mode="m",
                   backend="cupy")
-        if sch == "glmulti":
+        if method == "glmulti":
             kw.update(beta=MULTI_BETA[0], multi_beta=MULTI_BETA, multi_coefficient=MASSES,
                       learn_coefficient=True, coefficient_constraint="softplus",
                       glmulti_history_grad="full")
@@ -311,7 +324,8 @@ def run_native(args):
     def step():
         mass_grads = []
         for T, sch in COMBOS:
-            _, _, pg = layer_step(layers[(T, sch)], x16[:T], gS16[:T], gV16[:T], sch != "glmulti")
+            _, _, pg = layer_step(layers[(T, sch)], x16[:T], gS16[:T], gV16[:T],
+                                  sch not in ("glmulti", "aligned"))
             mass_grads += pg
         if world > 1:
             allreduce_flat(mass_grads)       # the one gradient exchange per step
@@ -749,8 +763,11 @@ def run_network(args, name):
     model = globals()[builder](dev)
     net = model
     if world > 1:
-        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local],
-                                                        broadcast_buffers=False)
+        # the graph is the same every step: static_graph lets DDP skip its per-step search
+        # for unused parameters, and bucket views avoid a copy of every gradient
+        net = torch.nn.parallel.DistributedDataParallel(
+            model, device_ids=[local], broadcast_buffers=False,
+            gradient_as_bucket_view=True, static_graph=True)
     opt = torch.optim.SGD(model.parameters(), lr=1e-3, momentum=0.9)
     g = torch.Generator(device=dev).manual_seed(99 + rank)
     # synthetic event frames: Bernoulli(0.05) spikes (scaled by Poisson(1) counts for CNN128)
