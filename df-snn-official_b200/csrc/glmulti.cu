@@ -154,32 +154,88 @@ __global__ void __launch_bounds__(256) glm_fwd_x2(GlmArgs a) {
     }
 }
 
+
 // ------------------------------------------------------------------------------------
-// forward, any T: history in shared memory [T][blockDim]
+// forward, T > 32: blocked pull form.  The history sum of step k is one fused multiply-add
+// chain over i = 0..k-1 (4 cycles per term).  The chains of the eight steps k0..k0+7 are
+// independent over the terms i < k0, which are known before step k0, so they advance
+// together (one history load per term, the weights of the eight rows from shared memory four
+// terms at a time); inside the block each new v_k is folded into the later chains as soon as
+// it exists.  Every chain keeps the reference's term order: the sums are bit-identical.
+// The block's threads share the staged weight rows, so they run the step blocks in lockstep
+// (threads past N only help stage).
 // ------------------------------------------------------------------------------------
+constexpr int kGLB = 64;          // threads per block
+constexpr int kGLC = 8;           // chains advanced together
+
+__host__ __device__ __forceinline__ int pad4(int t) { return (t + 3) & ~3; }
+
+// rows k0..k0+kGLC-1 of W (zeros past T) -> sWr[kGLC][pad4(T)]; block-wide
+__device__ __forceinline__ void stage_w_rows(float* sWr, const float* W, int T, int k0) {
+    const int TP = pad4(T);
+    for (int e = threadIdx.x; e < kGLC * TP; e += blockDim.x) {
+        const int j = e / TP, i = e % TP;
+        const int t = k0 + j;
+        sWr[e] = (t < T && i < T) ? __ldg(W + (size_t)t * T + i) : 0.0f;
+    }
+}
+
+// chains h[j] (steps k0 + j) over the terms i < k0 (k0 % 4 == 0)
+__device__ __forceinline__ void glm_hist_block(float (&h)[kGLC], const float* sWr,
+                                               const float* vh, int TP, int k0) {
+#pragma unroll
+    for (int j = 0; j < kGLC; ++j) h[j] = 0.0f;
+#pragma unroll 2
+    for (int i = 0; i < k0; i += 4) {
+        const float v0 = vh[i * kGLB], v1 = vh[(i + 1) * kGLB];
+        const float v2 = vh[(i + 2) * kGLB], v3 = vh[(i + 3) * kGLB];
+#pragma unroll
+        for (int j = 0; j < kGLC; ++j) {
+            const float4 w = *reinterpret_cast<const float4*>(sWr + j * TP + i);
+            h[j] = __fmaf_rn(w.x, v0, h[j]);
+            h[j] = __fmaf_rn(w.y, v1, h[j]);
+            h[j] = __fmaf_rn(w.z, v2, h[j]);
+            h[j] = __fmaf_rn(w.w, v3, h[j]);
+        }
+    }
+}
+
 template <bool TP2>
-__global__ void __launch_bounds__(128) glm_fwd_smem(GlmArgs a) {
-    extern __shared__ float sh[];
-    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (n >= a.N) return;
+__global__ void __launch_bounds__(kGLB) glm_fwd_blk(GlmArgs a) {
+    extern __shared__ __align__(16) float shb[];
+    const int T = a.T, TP = pad4(T);
+    float* sWr = shb;                                 // [kGLC][TP]
+    float* vh = shb + kGLC * TP + threadIdx.x;        // [T][kGLB]
+    const long long n = (long long)blockIdx.x * kGLB + threadIdx.x;
+    const bool live = n < a.N;
     const long long N = a.N;
-    const int T = a.T;
-    float* vh = sh + threadIdx.x;
-    const int st = blockDim.x;
-    float v = a.v0[n];
-    float xn = ld_stream(a.x + n);
-    for (int t = 0; t < T; ++t) {
-        const float xt = xn;
-        if (t + 1 < T) xn = ld_stream(a.x + (t + 1) * N + n);
-        const float d = div_tau<TP2>(__fsub_rn(xt, v), a.tau, a.inv_tau);
-        const float* wrow = a.W + (size_t)t * T;
-        float hist = 0.0f;
-        for (int i = 0; i < t; ++i) hist = __fmaf_rn(__ldg(wrow + i), vh[i * st], hist);
-        const float p = __fmaf_rn(__ldg(a.scale + t), d, -hist);
-        const float s = (p >= a.th) ? 1.0f : 0.0f;
-        v = __fsub_rn(p, s * a.th);
-        vh[t * st] = v;
-        st_stream(a.spike + t * N + n, s);
+    float v = live ? a.v0[n] : 0.0f;
+    for (int k0 = 0; k0 < T; k0 += kGLC) {
+        __syncthreads();                              // the previous rows are no longer read
+        stage_w_rows(sWr, a.W, T, k0);
+        __syncthreads();
+        if (!live) continue;
+        float xk[kGLC];
+#pragma unroll
+        for (int j = 0; j < kGLC; ++j)
+            if (k0 + j < T) xk[j] = ld_stream(a.x + (long long)(k0 + j) * N + n);
+        float h[kGLC];
+        glm_hist_block(h, sWr, vh, TP, k0);
+#pragma unroll
+        for (int j = 0; j < kGLC; ++j) {
+            const int k = k0 + j;
+            if (k < T) {
+                const float d = div_tau<TP2>(__fsub_rn(xk[j], v), a.tau, a.inv_tau);
+                const float p = __fmaf_rn(__ldg(a.scale + k), d, -h[j]);
+                const float s = (p >= a.th) ? 1.0f : 0.0f;
+                v = __fsub_rn(p, s * a.th);
+                vh[k * kGLB] = v;
+#pragma unroll
+                for (int jj = j + 1; jj < kGLC; ++jj)  // term k of chain k0 + jj
+                    h[jj] = __fmaf_rn(sWr[jj * TP + k], v, h[jj]);
+                st_stream(a.spike + (long long)k * N + n, s);
+            }
+        }
     }
 }
 
@@ -546,7 +602,7 @@ __global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
 // ------------------------------------------------------------------------------------
 // backward, 32 < T <= 256 (full history T <= 64): one thread per neuron, history in shared
 // memory ([T][64] floats per block; the full-history adjoint sums another [T][64]).  The
-// recompute is the forward's pull-form sum (glm_fwd_smem), the reverse sweep is the
+// recompute is the forward's pull-form sum (as glm_fwd_blk), the reverse sweep is the
 // reference's loop; v_t, the drift and grad_pre go to [T, N] scratch for param_long.
 // ------------------------------------------------------------------------------------
 constexpr int kLongThreads = 64;
@@ -554,44 +610,112 @@ constexpr int kLongThreads = 64;
 template <bool FULL, bool TP2>
 __global__ void __launch_bounds__(kLongThreads) glm_bwd_long(GlmArgs a, float* Vs, float* Ds,
                                                              float* Gs) {
-    extern __shared__ float sh[];
+    extern __shared__ __align__(16) float sh[];
+    static_assert(kLongThreads == kGLB, "the blocked recompute shares glm_fwd_blk's layout");
     const long long n = (long long)blockIdx.x * kLongThreads + threadIdx.x;
-    if (n >= a.N) return;
+    const bool live = n < a.N;
     const long long N = a.N;
-    const int T = a.T;
-    float* vh = sh + threadIdx.x;
-    float* A = sh + (size_t)T * kLongThreads + threadIdx.x;
-    float v = a.v0[n];
-    for (int t = 0; t < T; ++t) {
-        const float d = div_tau<TP2>(__fsub_rn(ld_stream(a.x + t * N + n), v), a.tau, a.inv_tau);
-        const float* wrow = a.W + (size_t)t * T;
-        float hist = 0.0f;
-        for (int i = 0; i < t; ++i) hist = __fmaf_rn(__ldg(wrow + i), vh[i * kLongThreads], hist);
-        const float p = __fmaf_rn(__ldg(a.scale + t), d, -hist);
-        const float z = __fsub_rn(p, a.th);
-        v = (p >= a.th) ? z : p;                     // p - spike*th, spike*th exactly th or 0
-        vh[t * kLongThreads] = v;
-        Vs[t * N + n] = v;
-        Ds[t * N + n] = d;
-        Gs[t * N + n] = surrogate_fma(z, a.sg);
+    const int T = a.T, TP = pad4(T);
+    float* sWr = sh;                                              // [kGLC][TP]
+    float* vh = sh + kGLC * TP + threadIdx.x;                     // [T][64]
+    float* A = vh + (size_t)T * kLongThreads;                     // [T][64] (full history)
+    // recompute, blocked as glm_fwd_blk (same sums, same order)
+    float v = live ? a.v0[n] : 0.0f;
+    for (int k0 = 0; k0 < T; k0 += kGLC) {
+        __syncthreads();
+        stage_w_rows(sWr, a.W, T, k0);
+        __syncthreads();
+        if (!live) continue;
+        float xk[kGLC];
+#pragma unroll
+        for (int j = 0; j < kGLC; ++j)
+            if (k0 + j < T) xk[j] = ld_stream(a.x + (long long)(k0 + j) * N + n);
+        float h[kGLC];
+        glm_hist_block(h, sWr, vh, TP, k0);
+#pragma unroll
+        for (int j = 0; j < kGLC; ++j) {
+            const int t = k0 + j;
+            if (t < T) {
+                const float d = div_tau<TP2>(__fsub_rn(xk[j], v), a.tau, a.inv_tau);
+                const float p = __fmaf_rn(__ldg(a.scale + t), d, -h[j]);
+                const float z = __fsub_rn(p, a.th);
+                v = (p >= a.th) ? z : p;             // p - spike*th, spike*th exactly th or 0
+                vh[t * kLongThreads] = v;
+#pragma unroll
+                for (int jj = j + 1; jj < kGLC; ++jj)
+                    h[jj] = __fmaf_rn(sWr[jj * TP + t], v, h[jj]);
+                Vs[(long long)t * N + n] = v;
+                Ds[(long long)t * N + n] = d;
+                Gs[(long long)t * N + n] = surrogate_fma(z, a.sg);
+            }
+        }
     }
     if constexpr (FULL) {
-        for (int t = 0; t < T; ++t) A[t * kLongThreads] = 0.0f;
+        // reverse sweep, blocked: the adjoints of the block's steps are in registers; every
+        // earlier adjoint A[i] then takes the block's updates in one pass, in the reference's
+        // order (steps descending; the lowest step's -gx on A[lo-1] just before its fma)
+        if (live)
+            for (int t = 0; t < T; ++t) A[t * kLongThreads] = 0.0f;
         float ginit = 0.0f;
-        for (int t = T - 1; t >= 0; --t) {
-            const float gp = __fmaf_rn(ld_stream(a.gS + t * N + n), Gs[t * N + n], A[t * kLongThreads]);
-            Gs[t * N + n] = gp;
-            const float gd = __fmul_rn(gp, __ldg(a.scale + t));
-            const float gx = div_tau<TP2>(gd, a.tau, a.inv_tau);
-            st_stream(a.gx + t * N + n, gx);
-            if (t == 0) ginit = __fsub_rn(ginit, gx);            // + (-gd)/tau == -gx exactly
-            else A[(t - 1) * kLongThreads] = __fsub_rn(A[(t - 1) * kLongThreads], gx);
-            const float* wrow = a.W + (size_t)t * T;
-            for (int i = 0; i < t; ++i)
-                A[i * kLongThreads] = __fmaf_rn(-__ldg(wrow + i), gp, A[i * kLongThreads]);
+        for (int lo = ((T - 1) / kGLC) * kGLC; lo >= 0; lo -= kGLC) {
+            const int nb = (T - lo) < kGLC ? (T - lo) : kGLC;   // steps lo .. lo + nb - 1
+            __syncthreads();
+            stage_w_rows(sWr, a.W, T, lo);
+            __syncthreads();
+            if (!live) continue;
+            float ab[kGLC], gpb[kGLC], gsb[kGLC], sub[kGLC];
+            // the block's inputs are read before its sequential steps (the steps store grad_pre
+            // over the surrogates, so the loads would otherwise wait behind those stores)
+#pragma unroll
+            for (int j = 0; j < kGLC; ++j) {
+                const long long o = (long long)(lo + j) * N + n;
+                ab[j] = j < nb ? A[(lo + j) * kLongThreads] : 0.0f;
+                gsb[j] = j < nb ? ld_stream(a.gS + o) : 0.0f;
+                sub[j] = j < nb ? Gs[o] : 0.0f;
+            }
+            float gxl = 0.0f;
+#pragma unroll
+            for (int j = kGLC - 1; j >= 0; --j) {
+                gpb[j] = 0.0f;
+                if (j < nb) {
+                    const int t = lo + j;
+                    const long long o = (long long)t * N + n;
+                    const float gp = __fmaf_rn(gsb[j], sub[j], ab[j]);
+                    Gs[o] = gp;
+                    gpb[j] = gp;
+                    const float gd = __fmul_rn(gp, __ldg(a.scale + t));
+                    const float gx = div_tau<TP2>(gd, a.tau, a.inv_tau);
+                    st_stream(a.gx + o, gx);
+                    if (j > 0) ab[j - 1] = __fsub_rn(ab[j - 1], gx);   // + (-gd)/tau == -gx
+                    else if (t == 0) ginit = __fsub_rn(ginit, gx);
+                    else gxl = gx;
+#pragma unroll
+                    for (int jj = 0; jj < j; ++jj)
+                        ab[jj] = __fmaf_rn(-sWr[j * TP + lo + jj], gp, ab[jj]);
+                }
+            }
+            for (int i = 0; i < lo; i += 4) {        // lo % 8 == 0
+                float av[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) av[u] = A[(i + u) * kLongThreads];
+#pragma unroll
+                for (int j = kGLC - 1; j >= 0; --j) {
+                    if (j < nb) {
+                        const float4 w = *reinterpret_cast<const float4*>(sWr + j * TP + i);
+                        if (j == 0 && i + 4 == lo) av[3] = __fsub_rn(av[3], gxl);
+                        av[0] = __fmaf_rn(-w.x, gpb[j], av[0]);
+                        av[1] = __fmaf_rn(-w.y, gpb[j], av[1]);
+                        av[2] = __fmaf_rn(-w.z, gpb[j], av[2]);
+                        av[3] = __fmaf_rn(-w.w, gpb[j], av[3]);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) A[(i + u) * kLongThreads] = av[u];
+            }
         }
-        a.gv0[n] = ginit;
+        if (live) a.gv0[n] = ginit;
     } else {
+        if (!live) return;
         float gvn = 0.0f;
         for (int t = T - 1; t >= 0; --t) {
             const float gp = __fmaf_rn(ld_stream(a.gS + t * N + n), Gs[t * N + n], gvn);
@@ -746,7 +870,8 @@ cudaError_t glmulti_backward_long_launch(const float* gS, const float* x, const 
     float* Ds = scratch + (size_t)T * N;
     float* Gs = scratch + 2 * (size_t)T * N;
     if (N > 0) {
-        const size_t smem = sizeof(float) * (size_t)(full ? 2 : 1) * T * kLongThreads;
+        const size_t smem = sizeof(float) * ((size_t)kGLC * pad4(T) +
+                                             (size_t)(full ? 2 : 1) * T * kLongThreads);
         const unsigned grid = (unsigned)((N + kLongThreads - 1) / kLongThreads);
         auto k = full ? (tau_pow2 ? glm_bwd_long<true, true> : glm_bwd_long<true, false>)
                       : (tau_pow2 ? glm_bwd_long<false, true> : glm_bwd_long<false, false>);
@@ -794,17 +919,17 @@ cudaError_t glmulti_forward_launch(const float* x, const float* v0, const float*
 #undef DFSNN_FWD
         return cudaGetLastError();
     }
-    const unsigned grid = (unsigned)((N + 127) / 128);
-    const size_t smem = sizeof(float) * (size_t)T * 128;
+    const unsigned grid = (unsigned)((N + kGLB - 1) / kGLB);
+    const size_t smem = sizeof(float) * ((size_t)kGLC * pad4(T) + (size_t)T * kGLB);
     cudaError_t e;
     if (tau_pow2) {
-        e = cudaFuncSetAttribute(glm_fwd_smem<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        e = cudaFuncSetAttribute(glm_fwd_blk<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        glm_fwd_smem<true><<<grid, 128, smem, st>>>(a);
+        glm_fwd_blk<true><<<grid, kGLB, smem, st>>>(a);
     } else {
-        e = cudaFuncSetAttribute(glm_fwd_smem<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        e = cudaFuncSetAttribute(glm_fwd_blk<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        glm_fwd_smem<false><<<grid, 128, smem, st>>>(a);
+        glm_fwd_blk<false><<<grid, kGLB, smem, st>>>(a);
     }
     return cudaGetLastError();
 }

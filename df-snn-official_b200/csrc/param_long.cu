@@ -17,7 +17,8 @@
 //  * param_long: any T.  Grid (rows, tiles, tiles); block (s, bt, bi) computes the 64 x 64
 //    output tile (bt, bi), each of its 256 threads a 4 x 4 block, from chunks of 32 neurons
 //    staged through shared memory, multiplied in fp32 and folded into doubles per chunk.
-//  * param_small<T> (T = 8, 16): one block per row computes all T x T outputs.  Chunks of
+//  * param_small<TB> (T <= TB, TB = 8, 16, 32, 64): one block per row computes all T x T
+//    outputs.  Chunks of
 //    2048/T neurons stream into padded shared-memory rows by 4-byte cp.async (any alignment,
 //    zero-filled past the segment) through a 4-stage pipeline, three chunks ahead of the
 //    products (one ahead left the kernel waiting on DRAM latency at ~2 TB/s).  Threads form groups of (T/4)^2, each thread a 4 x 4 block of M; the
@@ -118,19 +119,24 @@ __global__ void __launch_bounds__(256) param_long(const float* G, const float* V
         row[t0 + 4 * ty + tx] = diag ? accs : 0.0;
 }
 
-// ---- small T -------------------------------------------------------------------------
-template <int T, int DIAG>
+// ---- T <= 64 -------------------------------------------------------------------------
+// Template bucket TB in {8, 16, 32, 64}, runtime T <= TB (rows T..TB-1 are staged as zeros).
+template <int TB, int DIAG>
 struct SmallCfg {
-    static constexpr int kK = 2048 / T;             // neurons per chunk: 2048 words per array
-    static constexpr int kRS = kK + 8;              // padded row: LDS.128 rows 8 banks apart
+    static constexpr int kK = 2048 / TB;            // neurons per chunk: 2048 words per array
+    // padded row: with thread (ty, tx) reading rows ty + kSt*r / tx + kSt*c, the rows of one
+    // 16-byte load are consecutive; 8 banks per row (TB <= 16, two quads per warp) or 4 banks
+    // per row (TB >= 32, up to 8 rows per warp) put them in distinct bank groups
+    static constexpr int kRS = kK + (TB >= 32 ? 4 : 8);
     static constexpr int kNA = DIAG == kDiagNone ? 2 : 3;   // staged arrays: G, V (, E)
-    static constexpr int kGS = (T / 4) * (T / 4);   // threads per group
+    static constexpr int kSt = TB / 4;
+    static constexpr int kGS = kSt * kSt;           // threads per group
     static constexpr int kNG = 256 / kGS;           // groups per block
     static constexpr int kQ = kK / 4;               // quads per chunk
     static constexpr int kStages = 4;               // chunks in flight: kStages - 1 ahead
-    static constexpr int kStageFloats = kNA * T * kRS;
+    static constexpr int kStageFloats = kNA * TB * kRS;
     static constexpr int kStage = kStages * kStageFloats * 4;
-    static constexpr int kReduce = kNG * (T * T + T) * 8;
+    static constexpr int kReduce = kNG * (TB * TB + TB) * 8;
     static constexpr int kBytes = kStage > kReduce ? kStage : kReduce;
     static_assert(kQ % kNG == 0, "every group takes the same number of quads");
 };
@@ -151,44 +157,43 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // stage the chunk starting at neuron k0: word e = tid + 256 j of each array is row e / kK,
-// column e % kK (a warp covers 32 consecutive neurons of one row)
-template <int T, int DIAG>
+// column e % kK (a warp covers consecutive neurons of one row); rows >= T read as zeros
+template <int TB, int DIAG>
 __device__ __forceinline__ void small_stage(float* st, const float* G, const float* V,
-                                            const float* E, long long N, long long k0,
+                                            const float* E, int T, long long N, long long k0,
                                             long long ne) {
-    using C = SmallCfg<T, DIAG>;
+    using C = SmallCfg<TB, DIAG>;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int e = threadIdx.x + 256 * j;
         const int row = e / C::kK, col = e % C::kK;
         const long long n = k0 + col;
-        const bool ok = n < ne;
-        const long long off = (long long)row * N + (ok ? n : 0);   // a valid address always
+        const bool ok = n < ne && row < T;
+        const long long off = ok ? (long long)row * N + n : 0;   // a valid address always
         cp_async4(st + row * C::kRS + col, G + off, ok);
-        cp_async4(st + (T + row) * C::kRS + col, V + off, ok);
-        if (DIAG != kDiagNone) cp_async4(st + (2 * T + row) * C::kRS + col, E + off, ok);
+        cp_async4(st + (TB + row) * C::kRS + col, V + off, ok);
+        if (DIAG != kDiagNone) cp_async4(st + (2 * TB + row) * C::kRS + col, E + off, ok);
     }
 }
 
-template <int T, int DIAG>
+template <int TB, int DIAG>
 __global__ void __launch_bounds__(256) param_small(const float* __restrict__ G,
                                                    const float* __restrict__ V,
-                                                   const float* __restrict__ E, long long N,
-                                                   long long F, int chunks, long long per,
-                                                   double* part) {
-    using C = SmallCfg<T, DIAG>;
+                                                   const float* __restrict__ E, int T,
+                                                   long long N, long long F, int chunks,
+                                                   long long per, double* part) {
+    using C = SmallCfg<TB, DIAG>;
+    constexpr int kSt = C::kSt;
     extern __shared__ __align__(16) unsigned char smem[];
     float* stages = reinterpret_cast<float*>(smem);
     const int tid = threadIdx.x;
     const int grp = tid / C::kGS, lt = tid % C::kGS;
-    const int ty = lt / (T / 4), tx = lt % (T / 4);
-    // Thread (ty, tx) owns M[ty + (T/4) r][tx + (T/4) c], r, c < 4: for a fixed r the group's
-    // G rows are consecutive, so with the padded row stride (8 banks per row) the 16-byte
-    // loads of one warp fall in distinct bank groups.  (Rows 4ty + r, 4 rows apart, hit the
-    // same banks: a 4-way conflict that held the kernel at ~2 TB/s.)  The diagonal d[t] of
-    // row t = ty + (T/4) r is taken by the thread with r = tx (mod T/4): kDR rows each.
-    constexpr int kSt = T / 4;
-    constexpr int kDR = 4 / kSt;
+    const int ty = lt / kSt, tx = lt % kSt;
+    // Thread (ty, tx) owns M[ty + kSt r][tx + kSt c], r, c < 4.  Diagonal d[t]: for kSt <= 4
+    // row t = ty + kSt r is taken by the thread with tx = r mod kSt (kDR rows each); for
+    // kSt > 4 by the thread with tx == ty (all four of its rows).
+    constexpr int kDR = kSt <= 4 ? 4 / kSt : 4;
+    const bool dthread = kSt <= 4 || tx == ty;
     const Segment sg = row_segment(F, chunks, per);
     const long long nchunks = sg.ne > sg.nb ? (sg.ne - sg.nb + C::kK - 1) / C::kK : 0;
     double acc[4][4], dacc[kDR];
@@ -202,8 +207,8 @@ __global__ void __launch_bounds__(256) param_small(const float* __restrict__ G,
 #pragma unroll
     for (int s = 0; s < C::kStages - 1; ++s) {
         if (s < nchunks)
-            small_stage<T, DIAG>(stages + s * C::kStageFloats, G, V, E, N, sg.nb + s * C::kK,
-                                 sg.ne);
+            small_stage<TB, DIAG>(stages + s * C::kStageFloats, G, V, E, T, N,
+                                  sg.nb + s * C::kK, sg.ne);
         cp_async_commit();
     }
     for (long long it = 0; it < nchunks; ++it) {
@@ -212,13 +217,13 @@ __global__ void __launch_bounds__(256) param_small(const float* __restrict__ G,
         {
             const long long nx = it + C::kStages - 1;
             if (nx < nchunks)
-                small_stage<T, DIAG>(stages + (int)(nx % C::kStages) * C::kStageFloats, G, V, E,
-                                     N, sg.nb + nx * C::kK, sg.ne);
+                small_stage<TB, DIAG>(stages + (int)(nx % C::kStages) * C::kStageFloats, G, V,
+                                      E, T, N, sg.nb + nx * C::kK, sg.ne);
             cp_async_commit();
         }
         const float* sG = stages + (int)(it % C::kStages) * C::kStageFloats;
-        const float* sV = sG + T * C::kRS;
-        const float* sE = sV + T * C::kRS;
+        const float* sV = sG + TB * C::kRS;
+        const float* sE = sV + TB * C::kRS;
         float pc[4][4], pd[kDR];
 #pragma unroll
         for (int r = 0; r < 4; ++r)
@@ -245,10 +250,10 @@ __global__ void __launch_bounds__(256) param_small(const float* __restrict__ G,
                     pc[r][c] = __fmaf_rn(g[r].z, v[c].z, pc[r][c]);
                     pc[r][c] = __fmaf_rn(g[r].w, v[c].w, pc[r][c]);
                 }
-            if (DIAG != kDiagNone) {
+            if (DIAG != kDiagNone && dthread) {
 #pragma unroll
                 for (int k = 0; k < kDR; ++k) {
-                    const int r = tx + kSt * k;                  // this thread's diagonal row
+                    const int r = kSt <= 4 ? tx + kSt * k : k;   // this thread's diagonal row
                     const float4 e = *reinterpret_cast<const float4*>(
                         sE + (ty + kSt * r) * C::kRS + 4 * q);
                     if (DIAG == kDiagProduct) {
@@ -275,21 +280,28 @@ __global__ void __launch_bounds__(256) param_small(const float* __restrict__ G,
     }
     cp_async_wait<0>();
     __syncthreads();          // all stages idle: the reduction area may overwrite them
-    // fixed-order sum over the groups: red[g][0..T) = d, red[g][T..) = M
+    // fixed-order sum over the groups: red[g][0..TB) = d, red[g][TB..) = M (TB-strided)
     double* red = reinterpret_cast<double*>(smem);
-    constexpr int kRow = T * T + T;
+    constexpr int kRow = TB * TB + TB;
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-            red[grp * kRow + T + (ty + kSt * r) * T + tx + kSt * c] = acc[r][c];
+            red[grp * kRow + TB + (ty + kSt * r) * TB + tx + kSt * c] = acc[r][c];
+    if (dthread) {            // covers every diagonal row (zeros without DIAG)
 #pragma unroll
-    for (int k = 0; k < kDR; ++k) red[grp * kRow + ty + kSt * (tx + kSt * k)] = dacc[k];
+        for (int k = 0; k < kDR; ++k) {
+            const int r = kSt <= 4 ? tx + kSt * k : k;
+            red[grp * kRow + ty + kSt * r] = dacc[k];
+        }
+    }
     __syncthreads();
-    double* out = part + (size_t)blockIdx.x * kRow;
-    for (int e = tid; e < kRow; e += 256) {
+    const int R = T + T * T;                  // output row [T + T*T] of the runtime T
+    double* out = part + (size_t)blockIdx.x * R;
+    for (int e = tid; e < R; e += 256) {
+        const int src = e < T ? e : TB + ((e - T) / T) * TB + (e - T) % T;
         double s = 0.0;
-        for (int g = 0; g < C::kNG; ++g) s += red[g * kRow + e];
+        for (int g = 0; g < C::kNG; ++g) s += red[g * kRow + src];
         out[e] = s;
     }
 }
@@ -307,13 +319,13 @@ int param_long_slices(int T, long long N) {
 cudaError_t param_long_launch(const float* G, const float* V, const float* E, int T, long long N,
                               bool diag_product, double* part, int slices, cudaStream_t st) {
     return param_rows_launch(G, V, E, T, N, 1, diag_product ? kDiagProduct : kDiagSum, part,
-                             slices, false, st);
+                             slices, true, st);
 }
 
 int param_rows_chunks(int T, long long N, int B) {
     const long long F = N / (B < 1 ? 1 : B);
     long long target, cap;
-    if (T == 8 || T == 16) {
+    if (T <= 64) {
         target = 148 * 8;
         cap = (F + 127) / 128;
     } else {
@@ -333,19 +345,22 @@ cudaError_t param_rows_launch(const float* G, const float* V, const float* E, in
     const long long F = N / B;
     long long per = (F + chunks - 1) / chunks;
     const dim3 rows((unsigned)((long long)B * chunks));
-    if (small_ok && (T == 8 || T == 16)) {
+    if (small_ok && T <= 64) {
         per = (per + 3) / 4 * 4;                 // segments start on whole quads
+        const int TB = T <= 8 ? 8 : T <= 16 ? 16 : T <= 32 ? 32 : 64;
 #define DFSNN_SMALL(TV, DV)                                                                   \
-        if (T == TV && diag == DV) {                                                          \
+        if (TB == TV && diag == DV) {                                                         \
             auto k = param_small<TV, DV>;                                                     \
             const int bytes = SmallCfg<TV, DV>::kBytes;                                       \
             cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); \
             if (e != cudaSuccess) return e;                                                   \
-            k<<<rows, 256, bytes, st>>>(G, V, E, N, F, chunks, per, part);                    \
+            k<<<rows, 256, bytes, st>>>(G, V, E, T, N, F, chunks, per, part);                 \
             return cudaGetLastError();                                                        \
         }
         DFSNN_SMALL(8, kDiagNone) DFSNN_SMALL(8, kDiagSum) DFSNN_SMALL(8, kDiagProduct)
         DFSNN_SMALL(16, kDiagNone) DFSNN_SMALL(16, kDiagSum) DFSNN_SMALL(16, kDiagProduct)
+        DFSNN_SMALL(32, kDiagNone) DFSNN_SMALL(32, kDiagSum) DFSNN_SMALL(32, kDiagProduct)
+        DFSNN_SMALL(64, kDiagNone) DFSNN_SMALL(64, kDiagSum) DFSNN_SMALL(64, kDiagProduct)
 #undef DFSNN_SMALL
     }
     per = (per + kLK - 1) / kLK * kLK;
