@@ -60,13 +60,14 @@ def parse():
     ap.add_argument("--neurons", type=int, default=0,
                     help="profiling: neurons per GPU instead of 16*128*64*64")
     ap.add_argument("--workload", choices=("layers", "long", "aligned", "cnn128",
-                                           "spikformer256", "history"),
+                                           "spikformer256", "history", "integrator"),
                     default="layers",
                     help="layers: the LIFNeuronFDE layer step (default); long: the "
                          "long-history layer step (T = 64, 256); aligned: the layer step with "
                          "the examples' aligned glmulti kernels; cnn128 / "
                          "spikformer256: synthetic network training step, data-parallel, "
-                         "samples/s; history: the "
+                         "samples/s; integrator: the SNN wrapper's multi-term GL "
+                         "integrator and adjoint; history: the "
                          "VO-GL1 / FAGL1 / VO-PREDICTOR Functions with per-sample tables")
     args = ap.parse_args()
     global SHAPE, COMBOS, WORKLOAD, X_MEAN, X_STD, TS
@@ -965,8 +966,98 @@ def run_history(args):
     return 0
 
 
+def run_integrator(args):
+    """One step: the SNN wrapper's multi-term GL integration (forward_glmulti_cupy, as
+    FDEAdjointMethod runs it, without autograd) over T = 64 steps of a [16, 64, 64, 64] =
+    4,194,304-element state and its adjoint (backward_glmulti_cupy) over the same grid.  The
+    right-hand side is elementwise (-v + I_k for the state, a pass-through spike sum), so the
+    time is the history steps': each step reads its f and every earlier state row (O(T^2)
+    rows in total) and writes the new row."""
+    import torch
+    from dfsnn_b200 import fde_solver, profiling
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    K, W = args.steps, max(args.warmup, 3)
+    T = 64
+    shape = (16, 64, 64, 64)
+    g = torch.Generator(device=dev).manual_seed(7)
+    current = torch.randn((T,) + shape, device=dev, generator=g).mul_(0.4).add_(0.2)
+    adj_src = torch.randn(shape, device=dev, generator=g)
+    t_grid = torch.linspace(0.0, 0.1 * T, T + 1, device=dev)
+    beta = torch.tensor(MULTI_BETA)
+    coef = torch.tensor(MASSES)
+
+    calls = {"k": 0}
+
+    def rhs(t, y):                       # step index from a call counter: no host sync on t
+        k = calls["k"]
+        calls["k"] += 1
+        return (current[min(k, T - 1)] - y[0], y[1] + y[0])
+
+    def adjoint_rhs(t, aug):
+        _, adj, params = aug
+        return None, [adj[0] * -0.5 + adj_src], []
+
+    def step():
+        calls["k"] = 0
+        with torch.no_grad():
+            hist = fde_solver.forward_glmulti_cupy(rhs, (torch.zeros(shape, device=dev),
+                                                         torch.zeros(shape, device=dev)),
+                                                   beta, t_grid, multi_coefficient=coef)
+            adj, _ = fde_solver.backward_glmulti_cupy(
+                adjoint_rhs, (None, [torch.ones(shape, device=dev)], []), beta, t_grid,
+                hist, multi_coefficient=coef)
+        return adj
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev.index)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with profiling.NativeCallTimer() as timer:
+        start.record()
+        for _ in range(K):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end)
+    summary = timer.summary()
+    peak, peak_src = measured_hbm_peak()
+    d = summary.get("gl_history_step")
+    roofline = None
+    if d:
+        roofline = {"bound": "hbm", "kernel": "gl_history_step", "achieved": d["gbs"],
+                    "peak": peak, "unit": "GB/s", "frac": d["gbs"] / peak if d["gbs"] else None,
+                    "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
+                    "algorithmic_bytes_per_launch": d["bytes_per_call"], "traffic": None}
+    S = math.prod(shape)
+    line = {
+        "metric": "multi-term GL integrator state-element-steps/s (forward + adjoint)",
+        "value": K * 2 * T * S / (ms / 1e3), "unit": "element-steps/s", "n_gpus": 1,
+        "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "forward_glmulti_cupy (no autograd) + backward_glmulti_cupy, T=64 "
+                   "steps, state [16,64,64,64] = 4,194,304 elements, glmulti orders "
+                   "[0.3,0.4,0.5] masses [0.5,0.5,0.7], elementwise right-hand side",
+                   "T": T, "state_elements": S, "l2": "history rows larger than L2"},
+        "gpu_launches": timer.total_launches(),
+        "roofline": roofline,
+        "kernels": {k: {"calls_per_step": v["calls"] / K, "ms_per_call": round(v["ms_per_call"], 4),
+                        "gbs": round(v["gbs"], 1) if v["gbs"] else None}
+                    for k, v in summary.items()},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "integrator":
+        return run_integrator(args) if args.impl == "native" else 0
     if args.workload in NETWORKS:
         return run_network(args, args.workload) if args.impl == "native" else 0
     if args.workload == "history":

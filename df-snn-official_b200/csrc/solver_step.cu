@@ -91,6 +91,79 @@ __global__ void __launch_bounds__(256) gl_step(StepArgs<F> a) {
     if (a.diff) a.diff[n] = d;
 }
 
+// Four consecutive elements per thread (S % 4 == 0, f / out / diff 16-byte aligned): every
+// history row is read with 16-byte loads when its pointer is aligned (a uniform test: all
+// threads see the same row), else with four scalar loads; the arithmetic per element is the
+// scalar kernel's.
+template <typename F>
+struct Vec4;
+template <>
+struct Vec4<float> {
+    using T = float4;
+};
+template <>
+struct Vec4<double> {
+    using T = double4;
+};
+
+template <typename F>
+__device__ __forceinline__ void load4(const F* p, long long n, F (&v)[4]) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0 && (sizeof(F) == 4 ||
+                                                       (reinterpret_cast<uintptr_t>(p) & 31) == 0)) {
+        const typename Vec4<F>::T q = *reinterpret_cast<const typename Vec4<F>::T*>(p + n);
+        v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+    } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = p[n + u];
+    }
+}
+
+template <typename F>
+__global__ void __launch_bounds__(256) gl_step4(StepArgs<F> a) {
+    const long long n = 4 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
+    if (a.table_out && n == 0) a.table_out[a.out_slot] = a.out;
+    if (n >= a.S) return;
+    F conv[4] = {F(0), F(0), F(0), F(0)};
+    if (a.chunk < 0) {
+        for (int j = a.row_begin; j < a.row_end; ++j) {
+            const F c = a.c_tilde[a.coeff_base - j];
+            F r[4];
+            load4(a.rows[j], n, r);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) conv[u] = add_t(conv[u], mul_t(c, r[u]));
+        }
+    } else {
+        const int step = a.chunk > 0 ? a.chunk : (a.row_end - a.row_begin);
+        bool first = true;
+        for (int c0 = a.row_begin; c0 < a.row_end; c0 += step) {
+            const int c1 = (c0 + step) < a.row_end ? (c0 + step) : a.row_end;
+            F acc[4] = {F(0), F(0), F(0), F(0)};
+#pragma unroll 4
+            for (int j = c0; j < c1; ++j) {
+                const F c = a.c_tilde[a.coeff_base - j];
+                F r[4];
+                load4(a.rows[j], n, r);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) acc[u] = fma_t(c, r[u], acc[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) conv[u] = first ? acc[u] : add_t(conv[u], acc[u]);
+            first = false;
+        }
+    }
+    const F c0 = *a.c0_inv;
+    F fv[4];
+    load4(a.f, n, fv);
+    F y[4], d[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        d[u] = sub_t(fv[u], conv[u]);
+        y[u] = mul_t(c0, d[u]);
+    }
+    *reinterpret_cast<typename Vec4<F>::T*>(a.out + n) = {y[0], y[1], y[2], y[3]};
+    if (a.diff) *reinterpret_cast<typename Vec4<F>::T*>(a.diff + n) = {d[0], d[1], d[2], d[3]};
+}
+
 template <typename F>
 struct StepBwdArgs {
     const F* g;
@@ -180,8 +253,16 @@ cudaError_t step_launch(const void* f, const void* const* rows, int row_begin, i
     a.out = static_cast<F*>(out);
     a.diff = static_cast<F*>(diff);
     a.S = S;
-    const long long blocks = S > 0 ? (S + 255) / 256 : 1;
-    gl_step<F><<<(unsigned)blocks, 256, 0, st>>>(a);
+    constexpr uintptr_t kAlign = sizeof(F) == 4 ? 15 : 31;
+    const bool vec = S % 4 == 0 && ((reinterpret_cast<uintptr_t>(f) | reinterpret_cast<uintptr_t>(out) |
+                                     reinterpret_cast<uintptr_t>(diff)) & kAlign) == 0;
+    if (vec) {
+        const long long blocks = S > 0 ? (S / 4 + 255) / 256 : 1;
+        gl_step4<F><<<(unsigned)blocks, 256, 0, st>>>(a);
+    } else {
+        const long long blocks = S > 0 ? (S + 255) / 256 : 1;
+        gl_step<F><<<(unsigned)blocks, 256, 0, st>>>(a);
+    }
     return cudaGetLastError();
 }
 

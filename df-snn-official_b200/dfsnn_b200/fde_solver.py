@@ -21,6 +21,7 @@ dot) raises TypeError.
 import torch
 
 from . import _capi
+from . import profiling as _prof
 
 _DTYPE = {torch.float32: 0, torch.float64: 1}
 
@@ -54,11 +55,14 @@ def _as_tensor(v, dtype, device):
 def _launch_step(f, table, row_begin, row_end, c_tilde, coeff_base, c0_inv, chunk, out, diff,
                  slot):
     L = _capi.lib()
-    code = L.dfsnn_gl_history_step(
-        _DTYPE[f.dtype], _capi.ptr(f), _capi.ptr(table), row_begin, row_end,
-        _capi.ptr(c_tilde), coeff_base, _capi.ptr(c0_inv), chunk, _capi.ptr(out),
-        _capi.ptr(diff), f.numel(), _capi.ptr(table) if slot is not None else None,
-        -1 if slot is None else slot, _capi.stream_of(f))
+    # algorithmic bytes: f and the history rows in, y (and f - conv) out
+    nbytes = f.numel() * f.element_size() * (row_end - row_begin + 2 + (diff is not None))
+    with _prof.native_call("gl_history_step", 1, nbytes, f.device):
+        code = L.dfsnn_gl_history_step(
+            _DTYPE[f.dtype], _capi.ptr(f), _capi.ptr(table), row_begin, row_end,
+            _capi.ptr(c_tilde), coeff_base, _capi.ptr(c0_inv), chunk, _capi.ptr(out),
+            _capi.ptr(diff), f.numel(), _capi.ptr(table) if slot is not None else None,
+            -1 if slot is None else slot, _capi.stream_of(f))
     _capi.check(code, "dfsnn_gl_history_step")
 
 
