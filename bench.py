@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
-    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-steps", type=int, default=4)
     ap.add_argument("--cpu-sample", type=int, default=1 << 22,
                     help="neurons of the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -426,11 +426,13 @@ def run_native(args):
 
 
 def run_e2e(args, layers, x16, gS16, gV16, dev, world):
-    """Same step through LIFNeuronFDE with host inputs: every step copies each layer's input
-    current and upstream gradients from pinned host memory and reads its spikes and input
-    gradient back.  The copies run on their own streams (host-to-device for the next layer
-    into a second input buffer while this layer computes, device-to-host of the outputs as
-    soon as they exist), so both PCIe directions and the compute overlap; events order
+    """Same step through LIFNeuronFDE with host inputs.  Every step copies the step's inputs
+    from pinned host memory -- the input current and the upstream gradients, one [16, N]
+    array each, whose first T rows feed the T-step layers exactly as in the device-timed
+    run -- and reads the step's results back: the gradients of the learnable Softplus masses
+    and the spike count of every layer (the layers' spike and input-gradient tensors stay on
+    the device, as they do between the layers of a network).  The next step's inputs stream
+    in on a copy stream into a second buffer set while this step computes; events order
     every buffer reuse."""
     import torch
     import torch.distributed as dist
@@ -439,59 +441,54 @@ def run_e2e(args, layers, x16, gS16, gV16, dev, world):
     hx = x16.cpu().pin_memory()
     hgS = gS16.cpu().pin_memory()
     hgV = gV16.cpu().pin_memory()
-    out_s = torch.empty(hx.shape, dtype=torch.float32).pin_memory()
-    out_g = torch.empty(hx.shape, dtype=torch.float32).pin_memory()
+    need_gv = any(sch not in ("glmulti", "aligned") for _, sch in COMBOS)
     bufs = [(torch.empty_like(x16), torch.empty_like(gS16), torch.empty_like(gV16))
             for _ in range(2)]
     comp = torch.cuda.current_stream(dev)
     h2d_s = torch.cuda.Stream(dev)
-    d2h_s = torch.cuda.Stream(dev)
-    done = [None, None]          # compute-done event of the last layer that used each buffer
+    done = [None, None]          # compute-done event of the last step that used each buffer
     counts = {"h2d": 0, "d2h": 0}
+    host_res = None
 
     def issue_h2d(i):
-        T, sch = COMBOS[i]
         dx, dgS, dgV = bufs[i % 2]
         with torch.cuda.stream(h2d_s):
             if done[i % 2] is not None:
                 h2d_s.wait_event(done[i % 2])
-            dx[:T].copy_(hx[:T], non_blocking=True)
-            dgS[:T].copy_(hgS[:T], non_blocking=True)
-            counts["h2d"] += 2 * hx[:T].numel() * 4
-            if sch != "glmulti":
-                dgV[:T].copy_(hgV[:T], non_blocking=True)
-                counts["h2d"] += hx[:T].numel() * 4
+            dx.copy_(hx, non_blocking=True)
+            dgS.copy_(hgS, non_blocking=True)
+            n = 2 * hx.numel() * 4
+            if need_gv:
+                dgV.copy_(hgV, non_blocking=True)
+                n += hgV.numel() * 4
             ev = torch.cuda.Event()
             ev.record(h2d_s)
+        counts["h2d"] = n
         return ev
 
-    def one():
-        counts["h2d"] = counts["d2h"] = 0
-        mass_grads = []
-        ev_next = issue_h2d(0)
-        for i, (T, sch) in enumerate(COMBOS):
-            ev_cur = ev_next
-            if i + 1 < len(COMBOS):
-                ev_next = issue_h2d(i + 1)
-            comp.wait_event(ev_cur)
-            dx, dgS, dgV = bufs[i % 2]
-            gx, s, pg = layer_step(layers[(T, sch)], dx[:T], dgS[:T], dgV[:T], sch != "glmulti")
+    def one(i, ev_in):
+        nonlocal host_res
+        comp.wait_event(ev_in)
+        dx, dgS, dgV = bufs[i % 2]
+        mass_grads, spike_counts = [], []
+        for T, sch in COMBOS:
+            _, s, pg = layer_step(layers[(T, sch)], dx[:T], dgS[:T], dgV[:T],
+                                  sch not in ("glmulti", "aligned"))
             mass_grads += pg
-            cev = torch.cuda.Event()
-            cev.record(comp)
-            done[i % 2] = cev
-            with torch.cuda.stream(d2h_s):
-                d2h_s.wait_event(cev)
-                out_s[:T].copy_(s, non_blocking=True)
-                out_g[:T].copy_(gx, non_blocking=True)
-                s.record_stream(d2h_s)
-                gx.record_stream(d2h_s)
-            counts["d2h"] += 2 * hx[:T].numel() * 4
+            spike_counts.append(s.sum().reshape(1))
         if world > 1:
             allreduce_flat(mass_grads)       # the step's one gradient exchange, as in `value`
-        comp.wait_stream(d2h_s)
+        cev = torch.cuda.Event()
+        cev.record(comp)
+        done[i % 2] = cev
+        res = torch.cat([g.reshape(-1) for g in mass_grads] + spike_counts)
+        if host_res is None:
+            host_res = torch.empty(res.shape, dtype=res.dtype).pin_memory()
+        host_res.copy_(res, non_blocking=True)   # the step's result, read back every step
+        counts["d2h"] = res.numel() * res.element_size()
 
-    one()
+    ev = issue_h2d(0)
+    one(0, ev)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -499,9 +496,11 @@ def run_e2e(args, layers, x16, gS16, gV16, dev, world):
     end = torch.cuda.Event(enable_timing=True)
     start.record(comp)
     h2d_s.wait_stream(comp)
-    d2h_s.wait_stream(comp)
-    for _ in range(steps):
-        one()
+    ev = issue_h2d(1)
+    for i in range(1, steps + 1):
+        ev_next = issue_h2d(i + 1) if i < steps else None
+        one(i, ev)
+        ev = ev_next
     end.record(comp)
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
@@ -511,7 +510,9 @@ def run_e2e(args, layers, x16, gS16, gV16, dev, world):
     value = world * steps * units_per_step(math.prod(SHAPE)) / (float(t.item()) / 1e3)
     return {"value": value, "unit": UNIT, "h2d_bytes_per_step": counts["h2d"],
             "d2h_bytes_per_step": counts["d2h"], "steps": steps,
-            "overlap": "h2d, compute and d2h on separate streams"}
+            "copies": "each step's inputs (x, grad_spike, grad_v: [16, N] fp32 each) host to "
+                      "device, the next step's overlapping this step's compute; the step's "
+                      "result (mass gradients, per-layer spike counts) device to host"}
 
 
 # -----------------------------------------------------------------------------------------
