@@ -177,3 +177,68 @@ def test_history_method_validation():
         neuron.LIFNeuronFDE(method="gl1", history_grad_mode="exact", step_mode="m")
     with pytest.raises(ValueError):
         neuron.LIFNeuronFDE(method="fagl1", attn_dim=2, step_mode="m")
+
+
+def test_fde_solver_install_rebinds_reference_names():
+    """fde_solver.install() points spikeDE_dis.solver's glmulti entries (module names and the
+    CuPy / torch dispatch tables, solver.py:4752-4806) and snn.py's imported name at the
+    B200 integrator."""
+    import types
+    from dfsnn_b200 import fde_solver
+    solver = types.ModuleType("spikeDE_dis.solver")
+    solver.CUPY_SOLVERS_FORWARD = {"glmulti": None, "gl-f": "keep"}
+    solver.CUPY_SOLVERS_BACKWARD = {"glmulti": None}
+    solver.TORCH_SOLVERS_BACKWARD = {"glmulti": None}
+    solver.forward_glmulti_cupy = solver.backward_glmulti_cupy = None
+    snn = types.ModuleType("spikeDE_dis.snn")
+    snn.forward_glmulti_cupy = None
+    saved = {k: sys.modules.get(k) for k in ("spikeDE_dis.solver", "spikeDE_dis.snn")}
+    try:
+        sys.modules["spikeDE_dis.solver"], sys.modules["spikeDE_dis.snn"] = solver, snn
+        fde_solver.install()
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                sys.modules.pop(k, None)
+            else:
+                sys.modules[k] = v
+    assert solver.CUPY_SOLVERS_FORWARD["glmulti"] is fde_solver.forward_glmulti_cupy
+    assert solver.CUPY_SOLVERS_FORWARD["gl-f"] == "keep"
+    assert solver.CUPY_SOLVERS_BACKWARD["glmulti"] is fde_solver.backward_glmulti_cupy
+    assert solver.TORCH_SOLVERS_BACKWARD["glmulti"] is fde_solver.backward_glmulti_cupy
+    assert solver.forward_glmulti_cupy is fde_solver.forward_glmulti_cupy
+    assert snn.forward_glmulti_cupy is fde_solver.forward_glmulti_cupy
+
+
+def test_fde_solver_rejects_cpu_and_half():
+    from dfsnn_b200 import fde_solver
+    y = torch.zeros(3)
+    with pytest.raises(RuntimeError):
+        fde_solver.forward_glmulti_cupy(lambda t, s: s, (y, y), [0.5], torch.tensor([0.0, 0.1]),
+                                        multi_coefficient=[1.0])
+    with pytest.raises(ValueError):
+        fde_solver.forward_glmulti_cupy(lambda t, s: s, (y, y), [0.5], torch.tensor([0.0]),
+                                        multi_coefficient=[1.0])
+
+
+@pytest.mark.parametrize("workload,combos", [
+    ("layers", {(8, "glmulti"), (8, "gl"), (8, "trap"), (8, "predictor"), (16, "glmulti"),
+                (16, "gl"), (16, "trap"), (16, "predictor")}),
+    ("long", {(64, "gl"), (64, "predictor"), (256, "gl"), (256, "predictor")}),
+    ("aligned", {(8, "aligned"), (16, "aligned")}),
+])
+def test_bench_workload_configuration(workload, combos, monkeypatch):
+    """bench.py's workloads: the schemes and step counts each one runs (no GPU needed)."""
+    import importlib
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    monkeypatch.syspath_prepend(repo)
+    bench = importlib.import_module("bench")
+    bench = importlib.reload(bench)
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--workload", workload])
+    args = bench.parse()
+    assert args.workload == workload
+    assert set(bench.COMBOS) == combos
+    neurons = 4194304 if workload == "long" else 16 * 128 * 64 * 64
+    assert bench.SHAPE[0] * bench.SHAPE[1] == neurons or \
+        bench.SHAPE[0] * bench.SHAPE[1] * bench.SHAPE[2] * bench.SHAPE[3] == neurons
+    importlib.reload(bench)          # leave module globals at their defaults for other tests
