@@ -23,6 +23,7 @@
 namespace dfsnn {
 
 struct AlnArgs {
+    float negz;          // -0.0f, set by the host (pmz2: products a packed sum may consume)
     const float* x;
     const float* v0;
     const float* a;      // [T] per-step gain (the schedule's scale)
@@ -107,9 +108,9 @@ __global__ void __launch_bounds__(256) aln_fwd_reg(AlnArgs a) {
 }
 
 // Forward, T <= TB <= 16, two neurons per thread (Toeplitz schedule; a general W runs the
-// scalar body per neuron).  Products are packed; every sum that consumes a product is a
-// per-half scalar add (pack2.cuh).  The history sum h is accumulated negated,
-// h' = h' + round(-w*v), so v = round(a*f) - h is an add.
+// scalar body per neuron).  Every product is formed by pmz2 and every sum is packed
+// (pack2.cuh).  The history sum h is accumulated negated, h' = h' + round(-w*v), so
+// v = round(a*f) - h is an add.
 template <int TB, bool TP2>
 __global__ void __launch_bounds__(256) aln_fwd_x2(AlnArgs a) {
     __shared__ float sW[TB * TB];
@@ -141,19 +142,25 @@ __global__ void __launch_bounds__(256) aln_fwd_x2(AlnArgs a) {
         if (t < T) xr[t] = ld2_stream(a.x + t * N + n);
     float2 v = *reinterpret_cast<const float2*>(a.v0 + n);
     float2 hn[TB];                                                   // -h, push form
+    const float2 nz2 = f2(a.negz);
 #pragma unroll
     for (int t = 0; t < TB; ++t) hn[t] = f2(-0.0f);
 #pragma unroll
     for (int t = 0; t < TB; ++t) {
         if (t < T) {
-            // sums that consume a product are per-half scalar ops (pack2.cuh)
-            const float2 d = div_tau2<TP2>(ssub2(xr[t], v), a.tau, inv2);
-            const float2 pred = sadd2(v, d);
+            // every product is a pmz2 product, so the sums that consume them may be packed
+            const float2 xm = psub2(xr[t], v);
+            const float2 d = TP2 ? pmz2(xm, inv2, nz2)
+                                 : make_float2(__fdiv_rn(xm.x, a.tau), __fdiv_rn(xm.y, a.tau));
+            const float2 pred = padd2(v, d);
             const float2 s = fire2(pred, a.th);
-            const float2 f = sadd2(d, div_tau2<TP2>(smul2(s, mth), a.tau, inv2));   // d - s*th/tau
-            v = sadd2(pmul2(a2, f), hn[t]);                          // a*f - h
+            const float2 sm = pmz2(s, mth, nz2);
+            const float2 smt = TP2 ? pmz2(sm, inv2, nz2)
+                                   : make_float2(__fdiv_rn(sm.x, a.tau), __fdiv_rn(sm.y, a.tau));
+            const float2 f = padd2(d, smt);                          // d - s*th/tau
+            v = padd2(pmz2(a2, f, nz2), hn[t]);                      // a*f - h
 #pragma unroll
-            for (int u = t + 1; u < TB; ++u) hn[u] = sadd2(hn[u], pmul2(nw[u - t], v));
+            for (int u = t + 1; u < TB; ++u) hn[u] = padd2(hn[u], pmz2(nw[u - t], v, nz2));
             st2_stream(a.spike + t * N + n, s);
         }
     }
@@ -335,6 +342,7 @@ __device__ __forceinline__ void aln_bwd_warp_reverse(const AlnArgs& a, const flo
     const int c2 = 2 * (threadIdx.x & 31);
     const float2 inv2 = f2(a.inv_tau), sg2 = f2(a.sg);
     const float2 one_m2 = f2(__fsub_rn(1.0f, __fdiv_rn(1.0f, a.tau)));
+    const float2 nz2 = f2(a.negz);
     float2 A[T];
 #pragma unroll
     for (int t = 0; t < T; ++t) A[t] = f2(0.0f);
@@ -344,26 +352,26 @@ __device__ __forceinline__ void aln_bwd_warp_reverse(const AlnArgs& a, const flo
         const float2 gnum = pmul2(*reinterpret_cast<const float2*>(G + t * TN + c2), sg2);
         const float2 q = quot2<SLOW>(gnum, den[t]);                     // (g*sg)/den, exact
         const float2 r = A[t];
-        const float2 ra = pmul2(r, a2);
-        const float2 qa = sadd2(q, ra);
+        const float2 ra = pmz2(r, a2, nz2);
+        const float2 qa = padd2(q, ra);
         const float2 gx = TP2 ? pmul2(qa, inv2)
                               : make_float2(__fdiv_rn(qa.x, a.tau), __fdiv_rn(qa.y, a.tau));
         *reinterpret_cast<float2*>(G + t * TN + c2) = gx;
-        const float2 rat = TP2 ? pmul2(ra, inv2)
+        const float2 rat = TP2 ? pmz2(ra, inv2, nz2)
                                : make_float2(__fdiv_rn(ra.x, a.tau), __fdiv_rn(ra.y, a.tau));
-        const float2 prev = ssub2(pmul2(q, one_m2), rat);
-        if (t) A[t - 1] = sadd2(A[t - 1], prev);
+        const float2 prev = psub2(pmz2(q, one_m2, nz2), rat);
+        if (t) A[t - 1] = padd2(A[t - 1], prev);
         else *reinterpret_cast<float2*>(V0 + c2) = prev;
 #pragma unroll
         for (int j = 0; j < t; ++j) {
             const float2 rwj = FAST ? rw[t - j] : f2(__fmul_rn(a.rho, sW[t * T + j]));
-            A[j] = ssub2(A[j], pmul2(rwj, r));
+            A[j] = psub2(A[j], pmz2(rwj, r, nz2));
         }
         *reinterpret_cast<float2*>(GP + t * RS + c2) = r;
         // e_t = r_t (v_t + h_t) / a_t feeds only the grad_a reduction: product with the
         // correctly rounded reciprocal of a_t (within an ulp of the quotient per term)
-        const float2 rx = pmul2(r, *reinterpret_cast<const float2*>(X + t * TN + c2));
-        gsa[t] = sadd2(gsa[t], pmul2(rx, f2(FAST ? sInvA[0] : sInvA[t])));
+        const float2 rx = pmz2(r, *reinterpret_cast<const float2*>(X + t * TN + c2), nz2);
+        gsa[t] = padd2(gsa[t], pmz2(rx, f2(FAST ? sInvA[0] : sInvA[t]), nz2));
     }
 }
 
@@ -384,6 +392,7 @@ __device__ __forceinline__ void aln_bwd_warp_tile(const AlnArgs& a, const float*
     const float2 thr_tau = f2(div_tau<TP2>(th, a.tau, a.inv_tau));   // spike*th/tau for spike = 1
     float2 v = *reinterpret_cast<const float2*>(V0 + c2);
     float2 hs[T], den[T];
+    const float2 nz2 = f2(a.negz);
     bool bad = false;
 #pragma unroll
     for (int t = 0; t < T; ++t) hs[t] = f2(0.0f);
@@ -391,28 +400,28 @@ __device__ __forceinline__ void aln_bwd_warp_tile(const AlnArgs& a, const float*
     for (int t = 0; t < T; ++t) {
         const float2 a2 = f2(FAST ? sA[0] : sA[t]);
         const float2 xs = *reinterpret_cast<const float2*>(X + t * TN + c2);
-        const float2 xm = ssub2(xs, v);
-        const float2 d = TP2 ? pmul2(xm, inv2)
+        const float2 xm = psub2(xs, v);
+        const float2 d = TP2 ? pmz2(xm, inv2, nz2)
                              : make_float2(__fdiv_rn(xm.x, a.tau), __fdiv_rn(xm.y, a.tau));
-        const float2 pred = sadd2(v, d);
+        const float2 pred = padd2(v, d);
         // f = d - spike*th/tau; spike*th/tau is exactly thr_tau or 0 (and d - 0 == d)
-        const float2 dm = ssub2(d, thr_tau);
+        const float2 dm = psub2(d, thr_tau);
         const float2 f = make_float2(pred.x >= th ? dm.x : d.x, pred.y >= th ? dm.y : d.y);
         const float2 h = hs[t];
-        v = ssub2(pmul2(a2, f), h);
+        v = psub2(pmz2(a2, f, nz2), h);
 #pragma unroll
         for (int u = t + 1; u < T; ++u) {
             const float2 w = FAST ? wr[u - t] : f2(sW[u * T + t]);
-            hs[u] = sadd2(hs[u], pmul2(w, v));
+            hs[u] = padd2(hs[u], pmz2(w, v, nz2));
         }
-        const float2 z = pmul2(zc2, ssub2(pred, th2));
-        const float2 dn = pmul2(f2(2.0f), sadd2(f2(1.0f), pmul2(z, z)));
+        const float2 z = pmz2(zc2, psub2(pred, th2), nz2);
+        const float2 dn = pmul2(f2(2.0f), padd2(f2(1.0f), pmz2(z, z, nz2)));
         den[t] = dn;
         const float2 g = *reinterpret_cast<const float2*>(G + t * TN + c2);
         bad |= !(dn.x <= 0x1p64f) || !(dn.y <= 0x1p64f) ||
                !quot_num_ok(__fmul_rn(g.x, sg)) || !quot_num_ok(__fmul_rn(g.y, sg));
         *reinterpret_cast<float2*>(Vs + t * RS + c2) = v;
-        *reinterpret_cast<float2*>(X + t * TN + c2) = sadd2(v, h);     // v_t + h_t
+        *reinterpret_cast<float2*>(X + t * TN + c2) = padd2(v, h);     // v_t + h_t
     }
     if (__any_sync(0xffffffffu, bad))
         aln_bwd_warp_reverse<T, TP2, FAST, true>(a, sW, sA, sInvA, rw, X, G, V0, GP, den, gsa);
@@ -639,6 +648,7 @@ cudaError_t aligned_backward_long_launch(const float* g, const float* x, const f
                                          double* part, int slices, float* scratch,
                                          unsigned int* err, cudaStream_t st) {
     AlnArgs a{};
+    a.negz = -0.0f;
     a.x = x; a.v0 = v0; a.a = a_; a.W = W; a.g = g; a.gx = gx; a.gv0 = gv0;
     a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau; a.th = th; a.sg = sg; a.rho = rho;
     cudaError_t e = cudaMemsetAsync(err, 0, sizeof(unsigned int), st);
@@ -667,6 +677,7 @@ cudaError_t aligned_forward_launch(const float* x, const float* v0, const float*
                                    float th, bool tau_pow2, cudaStream_t st) {
     if (N == 0) return cudaSuccess;
     AlnArgs a{};
+    a.negz = -0.0f;
     a.x = x; a.v0 = v0; a.a = a_; a.W = W; a.spike = spike; a.T = T; a.N = N; a.tau = tau;
     a.inv_tau = 1.0f / tau; a.th = th;
     const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(v0) |
@@ -709,6 +720,7 @@ cudaError_t aligned_backward_launch(const float* g, const float* x, const float*
                                     float sg, float rho, bool tau_pow2, double* part,
                                     unsigned int* err, int nblocks, cudaStream_t st) {
     AlnArgs a{};
+    a.negz = -0.0f;
     a.x = x; a.v0 = v0; a.a = a_; a.W = W; a.g = g; a.gx = gx; a.gv0 = gv0; a.part = part;
     a.err = err; a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau; a.th = th; a.sg = sg;
     a.rho = rho;

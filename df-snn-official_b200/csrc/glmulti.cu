@@ -30,6 +30,7 @@
 namespace dfsnn {
 
 struct GlmArgs {
+    float negz;           // -0.0f, set by the host (pmz2: products a packed sum may consume)
     const float* x;       // [T, N]
     const float* v0;      // [N]
     const float* scale;   // [T]
@@ -449,18 +450,19 @@ __device__ __forceinline__ void glm_bwd_warp_reverse(const GlmArgs& a, const flo
 #pragma unroll
         for (int t = 0; t < T; ++t) A[t] = f2(0.0f);
         float2 ginit = f2(0.0f);
+        const float2 nz2 = f2(a.negz);
 #pragma unroll
         for (int t = T - 1; t >= 0; --t) {
             const float2 sur = quot2<SLOW>(sg2, bden[t]);
             const float2 gs = *reinterpret_cast<const float2*>(G + t * TN + c2);
             const float2 gp = pfma2(gs, sur, A[t]);
             const float2 gd = pmul2(gp, f2(FAST ? sc : sScale[t]));
-            const float2 gx = TP2 ? pmul2(gd, inv2)
+            const float2 gx = TP2 ? pmz2(gd, inv2, nz2)
                                   : make_float2(__fdiv_rn(gd.x, a.tau), __fdiv_rn(gd.y, a.tau));
             *reinterpret_cast<float2*>(G + t * TN + c2) = gx;
             // the reference's (-gd)/tau is -gx exactly (round-to-nearest is symmetric)
-            if (t == 0) ginit = ssub2(ginit, gx);                 // gx is a product: scalar
-            else A[t - 1] = ssub2(A[t - 1], gx);
+            if (t == 0) ginit = psub2(ginit, gx);                 // gx is a pmz2 product
+            else A[t - 1] = psub2(A[t - 1], gx);
 #pragma unroll
             for (int i = 0; i < t; ++i) A[i] = pfma2(nwgt2<T, FAST>(sW, nw, t, i), gp, A[i]);
             *reinterpret_cast<float2*>(GP + t * RS + c2) = gp;
@@ -862,6 +864,7 @@ cudaError_t glmulti_backward_long_launch(const float* gS, const float* x, const 
                                          double* part, int slices, float* scratch,
                                          unsigned int* err, cudaStream_t st) {
     GlmArgs a{};
+    a.negz = -0.0f;
     a.x = x; a.v0 = v0; a.scale = scale; a.W = W; a.gS = gS; a.gx = gx; a.gv0 = gv0;
     a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau; a.th = th; a.sg = sg;
     cudaError_t e = cudaMemsetAsync(err, 0, sizeof(unsigned int), st);
@@ -891,6 +894,7 @@ cudaError_t glmulti_forward_launch(const float* x, const float* v0, const float*
                                    const float* W, float* spike, int T, long long N, float tau,
                                    float th, bool tau_pow2, cudaStream_t st) {
     GlmArgs a{};
+    a.negz = -0.0f;
     a.x = x; a.v0 = v0; a.scale = scale; a.W = W; a.spike = spike;
     a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau; a.th = th;
     if (N == 0) return cudaSuccess;
@@ -945,6 +949,7 @@ cudaError_t glmulti_backward_launch(const float* gS, const float* x, const float
                                     float th, float sg, bool full, bool tau_pow2, double* part,
                                     unsigned int* err, int nblocks, cudaStream_t st) {
     GlmArgs a{};
+    a.negz = -0.0f;
     a.x = x; a.v0 = v0; a.scale = scale; a.W = W; a.gS = gS; a.gx = gx; a.gv0 = gv0;
     a.part = part; a.err = err; a.T = T; a.N = N; a.tau = tau; a.inv_tau = 1.0f / tau;
     a.th = th; a.sg = sg;
