@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(256) single_fwd_x2(SingleArgs a) {
 }
 
 constexpr int kLongBlock = 64;
+constexpr int kBlk16MinT = 33;    // sixteen chains per thread from this T on
 
 // ------------------------------------------------------------------------------------
 // forward, T > 32: blocked pull form.  The history sum of step k is one Kahan chain over
@@ -190,11 +191,15 @@ constexpr int kLongBlock = 64;
         (S) = t_;                                                                         \
     } while (0)
 
-constexpr int kBlk = 8;           // chains advanced together
-constexpr int kBlkPad = 8;        // zeros in front of the weight table (window reads)
+constexpr int kBlkPad = 16;       // zeros in front of the weight table (window reads, KB <= 16)
 
-template <int SCHEME, bool TP2>
+// KB chains advance together (8 or 16; a multiple of 8, so every k0 gives an even trip count
+// of the unrolled term loop).  The 6 warps per SM that fit leave the FP32 pipes idle between
+// dependent operations unless each thread carries enough independent chains.
+template <int SCHEME, bool TP2, int KB>
 __global__ void __launch_bounds__(kLongBlock) single_fwd_blk(SingleArgs a) {
+    static_assert(KB % 8 == 0 && KB <= kBlkPad, "KB: 8 or 16");
+    constexpr int kBlk = KB;
     extern __shared__ float sh[];
     const int T = a.T;
     float* sw = sh + kBlkPad;                        // [T+1] after kBlkPad zeros
@@ -538,7 +543,7 @@ cudaError_t fwd_dispatch(const SingleArgs& a, cudaStream_t st) {
     }
     const unsigned grid = (unsigned)((a.N + kLongBlock - 1) / kLongBlock);
     const size_t smem = sizeof(float) * (((kBlkPad + T + 1 + 3) & ~3) + (size_t)T * kLongBlock);
-    auto k = single_fwd_blk<SCHEME, TP2>;
+    auto k = T >= kBlk16MinT ? single_fwd_blk<SCHEME, TP2, 16> : single_fwd_blk<SCHEME, TP2, 8>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     k<<<grid, kLongBlock, smem, st>>>(a);
