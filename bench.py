@@ -220,29 +220,48 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index):
+        """Start sampling; returns once nvidia-smi has printed its first sample (at most 10 s),
+        so that a short timed region that follows is still sampled.  Only samples printed
+        after that first one are reported."""
+        import threading
         import torch
         self.proc = None
+        self.lines = []
+        self.first = threading.Event()
         try:
             uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", uuid], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                 "-lms", "100", "-i", uuid], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                 text=True)
         except Exception:
             self.proc = None
+            return
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+        self.first.wait(10.0)
+
+    def _read(self):
+        for i, line in enumerate(self.proc.stdout):
+            if i == 0:
+                self.first.set()
+            else:
+                self.lines.append(line)
+        self.first.set()
 
     def stop(self):
         if self.proc is None:
             return None
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=10)
+            self.proc.wait(timeout=10)
+            self.reader.join(timeout=10)
         except Exception:
             self.proc.kill()
             return None
         sms, maxes, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        for line in list(self.lines):
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
