@@ -169,7 +169,6 @@ __global__ void __launch_bounds__(256) single_fwd_x2(SingleArgs a) {
 }
 
 constexpr int kLongBlock = 64;
-constexpr int kBlk16MinT = 33;    // sixteen chains per thread from this T on
 
 // ------------------------------------------------------------------------------------
 // forward, T > 32: blocked pull form.  The history sum of step k is one Kahan chain over
@@ -287,6 +286,116 @@ __global__ void __launch_bounds__(kLongBlock) single_fwd_blk(SingleArgs a) {
                 bits |= (fire ? 1u : 0u) << (k & 31);
                 st_stream(a.spike + (long long)k * N + n, s);
                 st_stream(a.v + (long long)k * N + n, v);
+                if ((k & 31) == 31 || k == T - 1) {
+                    a.bits[(long long)(k >> 5) * N + n] = bits;
+                    bits = 0;
+                }
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// forward, T >= 128, history read back from the membrane output.  Same blocked pull form and
+// term order as single_fwd_blk, but the history value of step i is re-read from row i of v,
+// which this thread wrote when it finished step i (the PREDICTOR schemes convert it with the
+// same -v/tau that produced it), instead of being kept in shared memory.  With no T floats of
+// shared memory per neuron, residency is set by registers instead of shared memory, and the
+// rows of the resident neurons (T floats each) stay in L2: the history loads are cache hits,
+// issued two iterations (eight terms) before their use.
+// ------------------------------------------------------------------------------------
+constexpr int kL2Block = 128;
+constexpr int kL2MinT = 128;      // history read back from v from this T on (T = 64: 7 % slower,
+                                  // T = 256: 9 % faster than shared memory)
+constexpr int kL2Chains = 16;
+
+template <int SCHEME, bool TP2, int KB>
+__global__ void __launch_bounds__(kL2Block) single_fwd_l2(SingleArgs a) {
+    static_assert(KB % 8 == 0 && KB <= kBlkPad, "KB: 8 or 16");
+    constexpr int kBlk = KB;
+    constexpr bool PRED = SCHEME == kPRED || SCHEME == kPRED1;
+    extern __shared__ __align__(16) float sh[];
+    const int T = a.T;
+    // weight table sw[0..T] placed so that sw + T is 16-byte aligned, with at least 16 zeros
+    // in front of it: the window wb[i-16 .. i+3] of every term iteration is five float4 loads
+    const int off = kBlkPad + ((4 - (T & 3)) & 3);
+    float* sw = sh + off;
+    if (threadIdx.x < off) sh[threadIdx.x] = 0.0f;
+    for (int e = threadIdx.x; e <= T; e += blockDim.x) sw[e] = a.w[e];
+    __syncthreads();
+    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= a.N) return;
+    const long long N = a.N;
+    const float* hrow = a.v + n;                     // v of step i at hrow[i * N]
+    auto hist = [&](float vv) { return PRED ? div_tau<TP2>(-vv, a.tau, a.inv_tau) : vv; };
+    const float trap_factor = __fmaf_rn(1.5f, a.beta, 0.5f);
+    const float pred_scale = __fdiv_rn(a.h_beta, a.gamma1);
+    const float w_cur = sw[T];
+    float v = a.v0[n];
+    uint32_t bits = 0;
+    for (int k0 = 0; k0 < T; k0 += kBlk) {
+        float xk[kBlk];
+#pragma unroll
+        for (int j = 0; j < kBlk; ++j)
+            if (k0 + j < T) xk[j] = ld_stream(a.x + (long long)(k0 + j) * N + n);
+        float sm[kBlk], cm[kBlk];
+#pragma unroll
+        for (int j = 0; j < kBlk; ++j) sm[j] = cm[j] = 0.0f;
+        const float* wb = sw + (T - k0);             // weight of term i, chain j: wb[i - j]
+        // four terms i..i+3 against all chains; hb holds their raw v and is refilled with
+        // terms i+8..i+11 once used (two buffers, so the loads are two iterations ahead)
+        auto terms = [&](int i, float (&hb)[4]) {
+            const float4* w4 = reinterpret_cast<const float4*>(wb + i - 16);
+            float wl[20];                            // wl[16 + d] = wb[i + d]
+#pragma unroll
+            for (int q = 0; q < 5; ++q) {
+                const float4 t4 = w4[q];
+                wl[4 * q] = t4.x;
+                wl[4 * q + 1] = t4.y;
+                wl[4 * q + 2] = t4.z;
+                wl[4 * q + 3] = t4.w;
+            }
+            float hu[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) hu[u] = hist(hb[u]);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int j = 0; j < kBlk; ++j) DFSNN_KAHAN(sm[j], cm[j], wl[16 + u - j], hu[u]);
+            if (i + 8 < k0) {                        // k0 % 4 == 0: i + 11 < k0 as well
+#pragma unroll
+                for (int u = 0; u < 4; ++u) hb[u] = hrow[(long long)(i + 8 + u) * N];
+            }
+        };
+        if (k0 > 0) {                                // k0 >= kBlk >= 8 terms are known
+            float ha[4], hc[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                ha[u] = hrow[(long long)u * N];
+                hc[u] = hrow[(long long)(4 + u) * N];
+            }
+            for (int i = 0; i < k0; i += 8) {       // k0 % 8 == 0
+                terms(i, ha);
+                terms(i + 4, hc);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kBlk; ++j) {
+            const int k = k0 + j;
+            if (k < T) {
+                const float dv = div_tau<TP2>(__fsub_rn(xk[j], v), a.tau, a.inv_tau);
+                const float p = single_update<SCHEME>(v, dv, sm[j], trap_factor, pred_scale,
+                                                      w_cur, a.h_beta);
+                const bool fire = p >= a.th;
+                const float s = fire ? 1.0f : 0.0f;
+                v = __fsub_rn(p, s * a.th);
+                const float hk = hist(v);
+#pragma unroll
+                for (int jj = j + 1; jj < kBlk; ++jj)
+                    DFSNN_KAHAN(sm[jj], cm[jj], sw[T - jj + j], hk);
+                bits |= (fire ? 1u : 0u) << (k & 31);
+                st_stream(a.spike + (long long)k * N + n, s);
+                a.v[(long long)k * N + n] = v;          // re-read as history: keep it cached
                 if ((k & 31) == 31 || k == T - 1) {
                     a.bits[(long long)(k >> 5) * N + n] = bits;
                     bits = 0;
@@ -541,9 +650,15 @@ cudaError_t fwd_dispatch(const SingleArgs& a, cudaStream_t st) {
         else single_fwd_reg<SCHEME, 32, TP2><<<grid, 256, 0, st>>>(a);
         return cudaGetLastError();
     }
+    if (T >= kL2MinT) {
+        const unsigned grid = (unsigned)((a.N + kL2Block - 1) / kL2Block);
+        const size_t smem = sizeof(float) * (size_t)(kBlkPad + 3 + T + 1);
+        single_fwd_l2<SCHEME, TP2, kL2Chains><<<grid, kL2Block, smem, st>>>(a);
+        return cudaGetLastError();
+    }
     const unsigned grid = (unsigned)((a.N + kLongBlock - 1) / kLongBlock);
     const size_t smem = sizeof(float) * (((kBlkPad + T + 1 + 3) & ~3) + (size_t)T * kLongBlock);
-    auto k = T >= kBlk16MinT ? single_fwd_blk<SCHEME, TP2, 16> : single_fwd_blk<SCHEME, TP2, 8>;
+    auto k = single_fwd_blk<SCHEME, TP2, 16>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     k<<<grid, kLongBlock, smem, st>>>(a);
