@@ -284,7 +284,11 @@ def run_single(method, x, v0, w, tau, beta, gS, gV, h=0.1):
                                     "euler"])
 @pytest.mark.parametrize("T,N", [(1, 50), (5, 999), (8, 1000), (16, 4099), (20, 512), (32, 300),
                                  (33, 300), (64, 1000), (100, 257), (256, 130), (8, 2), (16, 2),
-                                 (16, 4100), (8, 70002), (16, 70000)])
+                                 (16, 4100), (8, 70002), (16, 70000),
+                                 # around the switch to the L2-history kernel (T >= 128), with
+                                 # T % 4 != 0 (weight-table alignment) and ragged 16-step blocks
+                                 (127, 40), (128, 40), (131, 77), (150, 300), (203, 65),
+                                 (256, 1)])
 @pytest.mark.parametrize("tau", [2.0, 0.7])
 def test_single_vs_oracle(method, T, N, tau):
     beta = 0.7 if T != 64 else 0.5
