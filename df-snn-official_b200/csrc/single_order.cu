@@ -503,15 +503,43 @@ __global__ void __launch_bounds__(256) single_bwd_loop(SingleArgs a) {
     const float w_cur = (SCHEME == kPRED) ? __ldg(a.w + T) : 0.0f;
     float gv = 0.0f;
     uint32_t bits = 0;
-    for (int t = T - 1; t >= 0; --t) {
-        if (t == T - 1 || (t & 31) == 31) bits = a.bits_in[(long long)(t >> 5) * N + n];
-        const float vt = ld_stream(a.vs + t * N + n);
-        const float gst = ld_stream(a.gS + t * N + n);
-        const float gvt = ld_stream(a.gV + t * N + n);
-        float gxt;
-        single_bwd_step<SCHEME, TP2>(a, t, vt, (bits >> (t & 31)) & 1u, gst, gvt, gv, trap_factor,
-                                     pred_scale, w_cur, &gxt, [&](int L) { return sw[T - L]; });
-        st_stream(a.gx + t * N + n, gxt);
+    // rows are consumed from t = T-1 down; the loads of the next kPf rows are issued before
+    // the current kPf rows are processed, so each thread keeps two groups of loads in flight
+    constexpr int kPf = 4;
+    float vb[kPf], gsb[kPf], gvb[kPf];
+    auto load_rows = [&](int t0, float (&vr)[kPf], float (&sr)[kPf], float (&gr)[kPf]) {
+#pragma unroll
+        for (int u = 0; u < kPf; ++u) {
+            const long long t = t0 - u;
+            if (t >= 0) {
+                vr[u] = ld_stream(a.vs + t * N + n);
+                sr[u] = ld_stream(a.gS + t * N + n);
+                gr[u] = ld_stream(a.gV + t * N + n);
+            }
+        }
+    };
+    load_rows(T - 1, vb, gsb, gvb);
+    for (int t0 = T - 1; t0 >= 0; t0 -= kPf) {
+        float vn[kPf], gsn[kPf], gvn[kPf];
+        if (t0 >= kPf) load_rows(t0 - kPf, vn, gsn, gvn);
+#pragma unroll
+        for (int u = 0; u < kPf; ++u) {
+            const int t = t0 - u;
+            if (t >= 0) {
+                if (t == T - 1 || (t & 31) == 31) bits = a.bits_in[(long long)(t >> 5) * N + n];
+                float gxt;
+                single_bwd_step<SCHEME, TP2>(a, t, vb[u], (bits >> (t & 31)) & 1u, gsb[u],
+                                             gvb[u], gv, trap_factor, pred_scale, w_cur, &gxt,
+                                             [&](int L) { return sw[T - L]; });
+                st_stream(a.gx + (long long)t * N + n, gxt);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kPf; ++u) {
+            vb[u] = vn[u];
+            gsb[u] = gsn[u];
+            gvb[u] = gvn[u];
+        }
     }
     a.gv0[n] = gv;
 }
