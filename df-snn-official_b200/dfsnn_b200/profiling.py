@@ -89,6 +89,16 @@ def glmulti_backward_bytes(T, N):
     return N * (12 * T + 8)                      # x, grad_spike in; grad_x out; v0 in, grad_v0 out
 
 
+def schedule_forward_bytes(J, T):
+    # masses, basis [J, T+1] and step powers in; scale [T], W [T, T] and c~ [T+1] out
+    return 4 * (J + J * (T + 1) + J + T + T * T + T + 1)
+
+
+def schedule_backward_bytes(J, T):
+    # the forward's inputs and c~ in, grad_scale [T] and grad_W [T, T] in; grad masses [J] out
+    return 4 * (J + J * (T + 1) + J + (T + 1) + T + T * T + J)
+
+
 def single_forward_bytes(T, N):
     return N * (12 * T + 4 + 4 * ((T + 31) // 32))   # x in; spike, v, bits out; v0 in
 

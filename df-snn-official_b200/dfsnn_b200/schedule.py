@@ -80,6 +80,7 @@ class GLMultiScheduleFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, src, basis, h_pow, constraint):
         from . import _capi
+        from . import profiling as _prof
         src_f = src.detach().float().contiguous()
         basis_f = basis.float().contiguous()
         hp = h_pow.float().contiguous()
@@ -89,7 +90,8 @@ class GLMultiScheduleFunction(torch.autograd.Function):
         scale = torch.empty(T, device=dev, dtype=torch.float32)
         W = torch.empty((T, T), device=dev, dtype=torch.float32)
         ct = torch.empty(T + 1, device=dev, dtype=torch.float32)
-        with torch.cuda.device(dev):
+        with torch.cuda.device(dev), _prof.native_call(
+                "glmulti_schedule_forward", 1, _prof.schedule_forward_bytes(J, T), dev):
             code = _capi.lib().dfsnn_glmulti_schedule_forward(
                 _capi.ptr(src_f), _capi.ptr(basis_f), _capi.ptr(hp), J, T, int(constraint),
                 _capi.ptr(scale), _capi.ptr(W), _capi.ptr(ct), _capi.stream_of(src_f))
@@ -102,12 +104,15 @@ class GLMultiScheduleFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_scale, grad_W):
         from . import _capi
+        from . import profiling as _prof
         src_f, basis_f, hp, ct = ctx.saved_tensors
         J, T1 = basis_f.shape
         gs = None if grad_scale is None else grad_scale.float().contiguous()
         gw = None if grad_W is None else grad_W.float().contiguous()
         grad = torch.empty(J, device=src_f.device, dtype=torch.float32)
-        with torch.cuda.device(src_f.device):
+        with torch.cuda.device(src_f.device), _prof.native_call(
+                "glmulti_schedule_backward", 1, _prof.schedule_backward_bytes(J, T1 - 1),
+                src_f.device):
             code = _capi.lib().dfsnn_glmulti_schedule_backward(
                 _capi.ptr(src_f), _capi.ptr(basis_f), _capi.ptr(hp), _capi.ptr(ct),
                 _capi.ptr(gs), _capi.ptr(gw), J, T1 - 1, ctx.constraint, _capi.ptr(grad),
