@@ -116,13 +116,22 @@ __global__ void __launch_bounds__(256) aln_fwd_x2(AlnArgs a) {
     __shared__ float sW[TB * TB];
     __shared__ float sA[TB];
     const int T = a.T;
+    // this thread's x rows and v0 are requested before the block stages W and checks it, so
+    // their memory latency overlaps the staging and the block barrier
+    const long long n = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
+    float2 xr[TB], v = f2(0.0f);
+    if (n < a.N) {
+#pragma unroll
+        for (int t = 0; t < TB; ++t)
+            if (t < T) xr[t] = ld2_stream(a.x + t * a.N + n);
+        v = *reinterpret_cast<const float2*>(a.v0 + n);
+    }
     for (int e = threadIdx.x; e < TB * TB; e += blockDim.x) {
         const int t = e / TB, i = e % TB;
         sW[e] = (t < T && i < T) ? a.W[t * T + i] : 0.0f;
     }
     for (int e = threadIdx.x; e < TB; e += blockDim.x) sA[e] = e < T ? a.a[e] : 0.0f;
     const bool fast = block_toeplitz(a.W, a.a, T);
-    const long long n = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
     if (n >= a.N) return;
     if (!fast) {
         aln_fwd_body<TB, TP2, false>(a, sW, sA, n);
@@ -136,11 +145,6 @@ __global__ void __launch_bounds__(256) aln_fwd_x2(AlnArgs a) {
     const float2 a2 = f2(sA[0]);
     const float2 inv2 = f2(a.inv_tau);
     const float2 mth = f2(-a.th);
-    float2 xr[TB];
-#pragma unroll
-    for (int t = 0; t < TB; ++t)
-        if (t < T) xr[t] = ld2_stream(a.x + t * N + n);
-    float2 v = *reinterpret_cast<const float2*>(a.v0 + n);
     float2 hn[TB];                                                   // -h, push form
     const float2 nz2 = f2(a.negz);
 #pragma unroll
@@ -683,13 +687,13 @@ cudaError_t aligned_forward_launch(const float* x, const float* v0, const float*
     const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(v0) |
                          reinterpret_cast<uintptr_t>(spike);
     if (T <= 16 && (N % 2) == 0 && (al & 7u) == 0) {
-        const unsigned g2 = (unsigned)((N / 2 + 255) / 256);
+        const unsigned g2 = (unsigned)((N / 2 + 127) / 128);        // 128-thread blocks
         if (T <= 8) {
-            if (tau_pow2) aln_fwd_x2<8, true><<<g2, 256, 0, st>>>(a);
-            else aln_fwd_x2<8, false><<<g2, 256, 0, st>>>(a);
+            if (tau_pow2) aln_fwd_x2<8, true><<<g2, 128, 0, st>>>(a);
+            else aln_fwd_x2<8, false><<<g2, 128, 0, st>>>(a);
         } else {
-            if (tau_pow2) aln_fwd_x2<16, true><<<g2, 256, 0, st>>>(a);
-            else aln_fwd_x2<16, false><<<g2, 256, 0, st>>>(a);
+            if (tau_pow2) aln_fwd_x2<16, true><<<g2, 128, 0, st>>>(a);
+            else aln_fwd_x2<16, false><<<g2, 128, 0, st>>>(a);
         }
         return cudaGetLastError();
     }

@@ -113,13 +113,22 @@ __global__ void __launch_bounds__(256) glm_fwd_x2(GlmArgs a) {
     __shared__ float sW[TB * TB];
     __shared__ float sScale[TB];
     const int T = a.T;
+    // this thread's x rows and v0 are requested before the block stages W and checks it, so
+    // their memory latency overlaps the staging and the block barrier
+    const long long n = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
+    float2 xr[TB], v = f2(0.0f);
+    if (n < a.N) {
+#pragma unroll
+        for (int t = 0; t < TB; ++t)
+            if (t < T) xr[t] = ld2_stream(a.x + t * a.N + n);
+        v = *reinterpret_cast<const float2*>(a.v0 + n);
+    }
     for (int e = threadIdx.x; e < TB * TB; e += blockDim.x) {
         const int t = e / TB, i = e % TB;
         sW[e] = (t < T && i < T) ? a.W[t * T + i] : 0.0f;
     }
     for (int e = threadIdx.x; e < TB; e += blockDim.x) sScale[e] = e < T ? a.scale[e] : 0.0f;
     const bool fast = block_toeplitz(a.W, a.scale, T);
-    const long long n = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
     if (n >= a.N) return;
     if (!fast) {
         glm_fwd_body<TB, TP2, false>(a, sW, sScale, n);
@@ -133,11 +142,6 @@ __global__ void __launch_bounds__(256) glm_fwd_x2(GlmArgs a) {
     const float2 sc2 = f2(sScale[0]);
     const float2 inv2 = f2(a.inv_tau);
     const float2 mth = f2(-a.th);
-    float2 xr[TB];
-#pragma unroll
-    for (int t = 0; t < TB; ++t)
-        if (t < T) xr[t] = ld2_stream(a.x + t * N + n);
-    float2 v = *reinterpret_cast<const float2*>(a.v0 + n);
     float2 hn[TB];                                                  // -history, push form
 #pragma unroll
     for (int t = 0; t < TB; ++t) hn[t] = f2(-0.0f);
@@ -901,13 +905,15 @@ cudaError_t glmulti_forward_launch(const float* x, const float* v0, const float*
     const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(v0) |
                          reinterpret_cast<uintptr_t>(spike);
     if (T <= 16 && (N % 2) == 0 && (al & 7u) == 0) {
-        const unsigned grid = (unsigned)((N / 2 + 255) / 256);
+        // 128-thread blocks: at two blocks of 256 per SM (the registers' limit) the blocks'
+        // load and compute phases overlapped less than at four of 128
+        const unsigned grid = (unsigned)((N / 2 + 127) / 128);
         if (T <= 8) {
-            if (tau_pow2) glm_fwd_x2<8, true><<<grid, 256, 0, st>>>(a);
-            else glm_fwd_x2<8, false><<<grid, 256, 0, st>>>(a);
+            if (tau_pow2) glm_fwd_x2<8, true><<<grid, 128, 0, st>>>(a);
+            else glm_fwd_x2<8, false><<<grid, 128, 0, st>>>(a);
         } else {
-            if (tau_pow2) glm_fwd_x2<16, true><<<grid, 256, 0, st>>>(a);
-            else glm_fwd_x2<16, false><<<grid, 256, 0, st>>>(a);
+            if (tau_pow2) glm_fwd_x2<16, true><<<grid, 128, 0, st>>>(a);
+            else glm_fwd_x2<16, false><<<grid, 128, 0, st>>>(a);
         }
         return cudaGetLastError();
     }
