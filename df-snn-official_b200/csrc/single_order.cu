@@ -379,6 +379,20 @@ __global__ void __launch_bounds__(kL2Block) single_fwd_l2(SingleArgs a) {
                 terms(i + 4, hc);
             }
         }
+        // weights of lags 1..15 for the block's own terms: wlag[16 - L] = sw[T - L] (16-byte
+        // aligned, T >= 16)
+        float wlag[16];
+        {
+            const float4* l4 = reinterpret_cast<const float4*>(sw + T - 16);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 t4 = l4[q];
+                wlag[4 * q] = t4.x;
+                wlag[4 * q + 1] = t4.y;
+                wlag[4 * q + 2] = t4.z;
+                wlag[4 * q + 3] = t4.w;
+            }
+        }
 #pragma unroll
         for (int j = 0; j < kBlk; ++j) {
             const int k = k0 + j;
@@ -392,7 +406,7 @@ __global__ void __launch_bounds__(kL2Block) single_fwd_l2(SingleArgs a) {
                 const float hk = hist(v);
 #pragma unroll
                 for (int jj = j + 1; jj < kBlk; ++jj)
-                    DFSNN_KAHAN(sm[jj], cm[jj], sw[T - jj + j], hk);
+                    DFSNN_KAHAN(sm[jj], cm[jj], wlag[16 - (jj - j)], hk);
                 bits |= (fire ? 1u : 0u) << (k & 31);
                 st_stream(a.spike + (long long)k * N + n, s);
                 a.v[(long long)k * N + n] = v;          // re-read as history: keep it cached
