@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(256) aln_fwd_reg(AlnArgs a) {
 // (pack2.cuh).  The history sum h is accumulated negated, h' = h' + round(-w*v), so
 // v = round(a*f) - h is an add.
 template <int TB, bool TP2>
-__global__ void __launch_bounds__(256) aln_fwd_x2(AlnArgs a) {
+__global__ void __launch_bounds__(128, 5) aln_fwd_x2(AlnArgs a) {
     __shared__ float sW[TB * TB];
     __shared__ float sA[TB];
     const int T = a.T;

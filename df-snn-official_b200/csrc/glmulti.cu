@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(256) glm_fwd_reg(GlmArgs a) {
 // Used when N is even and x / v0 / spike are 8-byte aligned.
 // ------------------------------------------------------------------------------------
 template <int TB, bool TP2>
-__global__ void __launch_bounds__(256) glm_fwd_x2(GlmArgs a) {
+__global__ void __launch_bounds__(128, 5) glm_fwd_x2(GlmArgs a) {
     __shared__ float sW[TB * TB];
     __shared__ float sScale[TB];
     const int T = a.T;
@@ -905,8 +905,8 @@ cudaError_t glmulti_forward_launch(const float* x, const float* v0, const float*
     const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(v0) |
                          reinterpret_cast<uintptr_t>(spike);
     if (T <= 16 && (N % 2) == 0 && (al & 7u) == 0) {
-        // 128-thread blocks: at two blocks of 256 per SM (the registers' limit) the blocks'
-        // load and compute phases overlapped less than at four of 128
+        // 128-thread blocks, five per SM (the kernel's launch bounds cap it at 102 registers):
+        // at two blocks of 256 per SM the blocks' load and compute phases overlapped less
         const unsigned grid = (unsigned)((N / 2 + 127) / 128);
         if (T <= 8) {
             if (tau_pow2) glm_fwd_x2<8, true><<<grid, 128, 0, st>>>(a);
