@@ -242,3 +242,33 @@ def test_bench_workload_configuration(workload, combos, monkeypatch):
     assert bench.SHAPE[0] * bench.SHAPE[1] == neurons or \
         bench.SHAPE[0] * bench.SHAPE[1] * bench.SHAPE[2] * bench.SHAPE[3] == neurons
     importlib.reload(bench)          # leave module globals at their defaults for other tests
+
+
+def test_bench_clock_sampler_parses_nvidia_smi(tmp_path, monkeypatch):
+    """bench.py's clock record: median SM clock, max clock and the throttle reasons reported
+    Active, from a stand-in nvidia-smi on PATH; the sampler waits for its first sample and
+    reports only the samples after it (no GPU needed)."""
+    import importlib
+    import types
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    monkeypatch.syspath_prepend(repo)
+    bench = importlib.import_module("bench")
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text(
+        "#!/bin/bash\n"
+        "echo '0, 1000, 1965, 300, 0x0, Not Active, Not Active, Not Active, Not Active'\n"
+        "for c in 1900 1800 1700; do\n"
+        "  echo \"0, $c, 1965, 700, 0x4, Not Active, Not Active, Not Active, Active\"\n"
+        "  sleep 0.05\n"
+        "done\n"
+        "exec sleep 10\n")                     # the sampler's terminate() ends it, as nvidia-smi
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", str(tmp_path) + os.pathsep + os.environ.get("PATH", ""))
+    monkeypatch.setattr(torch.cuda, "get_device_properties",
+                        lambda i: types.SimpleNamespace(uuid="00000000-0000-0000-0000-000000000000"))
+    sampler = bench.ClockSampler(0)
+    import time
+    time.sleep(0.5)
+    rec = sampler.stop()
+    assert rec == {"sm_mhz": 1800.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"],
+                   "samples": 3}
