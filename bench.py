@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=1 << 22,
                     help="neurons of the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpu-reference", action="store_true",
+                    help="skip the reference's own GPU path timed on the same GPU")
     ap.add_argument("--only", default="",
                     help="profiling: comma list of scheme:T (e.g. glmulti:16) instead of all")
     ap.add_argument("--neurons", type=int, default=0,
@@ -215,68 +217,98 @@ def ncu_traffic(kernel, Ts):
 
 
 class ClockSampler:
+    """SM clock, its maximum and the active clock-event reasons, sampled during the timed
+    region: NVML read from a thread every 10 ms (read-only queries), else nvidia-smi.
+    stop() returns {"sm_mhz": median, "sm_max_mhz", "reasons": [...], "samples", "source"}
+    or None."""
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
 
-    def __init__(self, device_index):
-        """Start sampling; returns once nvidia-smi has printed its first sample (at most 10 s),
-        so that a short timed region that follows is still sampled.  Only samples printed
-        after that first one are reported."""
+    def __init__(self, device_index, period_s=0.01):
         import threading
         import torch
-        self.proc = None
-        self.lines = []
-        self.first = threading.Event()
+        self.samples, self.proc, self.thread = [], None, None
+        self.source = None
+        self.halt = threading.Event()
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
         try:
-            uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self._read_nvml(pynvml, h, smax)          # fails here, not in the thread
+            self.source = "nvml"
+
+            def loop():
+                while not self.halt.is_set():
+                    try:
+                        self._read_nvml(pynvml, h, smax)
+                    except Exception:
+                        return
+                    self.halt.wait(period_s)
+            self.samples.clear()
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.samples.clear()
+        try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", uuid], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                 "-lms", "50", "-i", uuid], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                 text=True)
+            self.source = "nvidia-smi"
+            self.first = threading.Event()
+            self.reader = threading.Thread(target=self._read_smi, daemon=True)
+            self.reader.start()
+            self.first.wait(10.0)
         except Exception:
             self.proc = None
-            return
-        self.reader = threading.Thread(target=self._read, daemon=True)
-        self.reader.start()
-        self.first.wait(10.0)
 
-    def _read(self):
+    def _read_nvml(self, pynvml, h, smax):
+        sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+        bits = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+        self.samples.append((sm, smax, {n for n, b in self.REASONS if bits & b}))
+
+    def _read_smi(self):
+        # the first line is printed before __init__ returns, i.e. before the timed region
         for i, line in enumerate(self.proc.stdout):
-            if i == 0:
-                self.first.set()
-            else:
-                self.lines.append(line)
+            parts = [p.strip() for p in line.split(",")]
+            self.first.set()
+            if i == 0 or len(parts) < 9:
+                continue
+            try:
+                sm, smax = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            names = [n for n, _ in self.REASONS]
+            self.samples.append((sm, smax, {n for n, v in zip(names, parts[5:9])
+                                            if v.lower().startswith("active")}))
         self.first.set()
 
     def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=10)
-            self.reader.join(timeout=10)
-        except Exception:
-            self.proc.kill()
-            return None
-        sms, maxes, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in list(self.lines):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
+        if self.thread is not None:
+            self.halt.set()
+            self.thread.join(timeout=5)
+        elif self.proc is not None:
+            self.proc.terminate()
             try:
-                sms.append(float(parts[1]))
-                maxes.append(float(parts[2]))
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(nm)
-        if not sms:
+                self.proc.wait(timeout=10)
+                self.reader.join(timeout=10)
+            except Exception:
+                self.proc.kill()
+        else:
             return None
-        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
-                "reasons": sorted(reasons), "samples": len(sms)}
+        samples = list(self.samples)
+        if not samples:
+            return None
+        return {"sm_mhz": statistics.median(s[0] for s in samples),
+                "sm_max_mhz": max(s[1] for s in samples),
+                "reasons": sorted(set().union(*(s[2] for s in samples))),
+                "samples": len(samples), "source": self.source}
 
 
 def make_layers(device):
@@ -300,6 +332,61 @@ def make_layers(device):
             kw.update(beta=BETA, store_v_seq=True)
         layers[(T, sch)] = LIFNeuronFDE(**kw).to(device)
     return layers
+
+
+def run_gpu_reference(args, x16, gS16, gV16, dev):
+    """The reference's own GPU path on this GPU, same workload: the unmodified reference
+    LIFNeuronFDE(backend='cupy') (the staged package in baseline/_ref) whose CuPy launches
+    run the reference's own kernel source texts, compiled for sm_100 with its options
+    (oracle/build_ref.py, launched by oracle/cupy_standin), and its own PyTorch glue
+    (torch.sum / torch.matmul for the glmulti parameter gradients).  Same layers, inputs and
+    step as the native arm; CUDA events on the same stream."""
+    import torch
+    from oracle import reference_gpu
+    why = reference_gpu.missing()
+    if why:
+        return {"unavailable": why}
+    ref = reference_gpu.Reference()
+    try:
+        ref.use_reference()
+        layers = {}
+        for T, sch in COMBOS:
+            if sch == "aligned":
+                return {"unavailable": "the aligned workload has no library-path reference"}
+            kw = dict(tau=TAU, threshold=TH, surrogate_grad_scale=SG, surrogate_function="arctan",
+                      T=T, method=sch, step_size=H, batchsize=SHAPE[0], step_mode="m",
+                      backend="cupy")
+            if sch == "glmulti":
+                kw.update(beta=MULTI_BETA[0], multi_beta=MULTI_BETA, multi_coefficient=MASSES,
+                          learn_coefficient=True, coefficient_constraint="softplus",
+                          glmulti_history_grad="full")
+            else:
+                kw.update(beta=BETA, store_v_seq=True)
+            layers[(T, sch)] = ref.neuron.LIFNeuronFDE(**kw).to(dev)
+
+        def step():
+            for T, sch in COMBOS:
+                layer_step(layers[(T, sch)], x16[:T], gS16[:T], gV16[:T], sch != "glmulti")
+
+        K, W = min(args.steps, 50), max(args.warmup, 3)
+        for _ in range(W):
+            step()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(K):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / K
+        return {"value": units_per_step(math.prod(SHAPE)) / (ms / 1e3), "unit": UNIT,
+                "ms_per_step": ms, "steps": K, "warmup": W,
+                "impl": "unmodified reference LIFNeuronFDE(backend='cupy') and autograd "
+                        "Functions; their kernel source texts compiled for sm_100 with the "
+                        "reference's options, launched through a CuPy stand-in (driver API)"}
+    finally:
+        ref.close()
 
 
 def layer_step(layer, x, gS, gV, single):
@@ -431,6 +518,11 @@ def run_native(args):
         "clocks": clk,
         "e2e": e2e,
     }
+    if rank == 0 and world == 1 and args.workload == "layers" and not args.no_gpu_reference:
+        gref = run_gpu_reference(args, x16, gS16, gV16, dev)
+        if gref.get("value"):
+            gref["native_over_reference"] = value / gref["value"]
+        line["gpu_reference"] = gref
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "layers":
         n = args.cpu_sample
         dt, kind, cores = cpu_workload_time(n)

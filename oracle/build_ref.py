@@ -12,7 +12,17 @@ Floating-point contraction follows the reference's compile flags: the library ke
 built by NVRTC with its default --fmad=true (here: -ffp-contract=fast with FMA hardware),
 the aligned kernels with --fmad=false (here: -ffp-contract=off).
 
-Usage: python oracle/build_ref.py [--reference /root/reference]
+The same kernel source texts are also compiled for the GPU (build_cuda): every text the
+reference hands to cupy.RawKernel, with the options it passes (none for
+spikeDE_dis/fde_cupy_kernels_all.py and direct_euler_cupy.py; --fmad=false for the
+examples' aligned kernels, with HISTORY_RHO substituted into the text as the reference
+does), one nvcc cubin per text for sm_100 (the target CuPy's NVRTC build uses on a B200),
+into oracle/_ref/cuda/ with a manifest keyed by source and options.  oracle/cupy_standin
+launches them, so that the reference's own Python code runs its own kernels on the GPU.
+
+The reference checkout is found at $DFSNN_REFERENCE, else at DEFAULT_REFERENCE.
+
+Usage: python oracle/build_ref.py [--reference PATH] [--no-cuda]
 Exits 0 without building when the reference checkout is absent.
 """
 import argparse
@@ -24,6 +34,17 @@ import types
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
+CUDA_OUT = os.path.join(OUT, "cuda")
+DEFAULT_REFERENCE = "/root/reference"
+# The examples' HISTORY_RHO values prebuilt for the GPU: 1.0 is the value every shipped
+# policy uses (examples/cnn128/train_ablation.py:21); 0.5 lets tests exercise the rho path.
+ALIGNED_RHOS = (1.0, 0.5)
+CUDA_ARCH = ["-gencode", "arch=compute_100,code=sm_100"]
+
+
+def reference_path(explicit=None):
+    return explicit or os.environ.get("DFSNN_REFERENCE") or DEFAULT_REFERENCE
+
 
 # The reference's kernels that run one thread per neuron with no inter-thread traffic.
 LIB_KERNELS = [
@@ -344,9 +365,74 @@ def build(reference, cxx="g++"):
     return lib
 
 
+def _source_key():
+    import importlib.util
+    path = os.path.join(HERE, "cupy_standin", "cupy", "_source_key.py")
+    spec = importlib.util.spec_from_file_location("dfsnn_ref_source_key", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.source_key
+
+
+def cuda_sources(reference):
+    """(code, options) pairs exactly as the reference passes them to cupy.RawKernel."""
+    _stub_h5py()
+    for p in (reference, os.path.join(reference, "examples", "cnn128")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import spikeDE_dis.fde_cupy_kernels_all as lib  # noqa: E402
+    import aligned_glmulti as alg  # noqa: E402
+    out = [(getattr(lib, name), ()) for name in sorted(dir(lib)) if name.endswith("_kernel_code")]
+    euler_path = os.path.join(reference, "spikeDE_dis", "direct_euler_cupy.py")
+    out.append((_function_local_string(euler_path, "_get_forward_kernel"), ()))
+    out.append((_function_local_string(euler_path, "_get_backward_kernel"), ()))
+    target = "adj[j]-=w[t*T+j]*r;"
+    if target not in alg.BACKWARD:
+        raise RuntimeError("aligned_backward history statement not found")
+    for rho in ALIGNED_RHOS:
+        # the text substitution of examples/cnn128/aligned_glmulti.py:90
+        code = alg.BACKWARD.replace(target, f"adj[j]-={rho:.8f}f*w[t*T+j]*r;")
+        out.append((alg.FORWARD + code, ("--fmad=false",)))
+    return out
+
+
+def build_cuda(reference, nvcc=None):
+    import json
+    import re
+    if not os.path.isdir(os.path.join(reference, "spikeDE_dis")):
+        print(f"build_ref: no reference checkout at {reference}; CUDA build skipped")
+        return None
+    nvcc = nvcc or os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
+    key_of = _source_key()
+    os.makedirs(CUDA_OUT, exist_ok=True)
+    manifest, procs = {}, []
+    for code, options in cuda_sources(reference):
+        key = key_of(code, options)
+        if key in manifest:
+            continue
+        names = re.findall(r"__global__\s+void\s+(\w+)", code)
+        src = os.path.join(CUDA_OUT, key + ".cu")
+        cubin = os.path.join(CUDA_OUT, key + ".cubin")
+        with open(src, "w") as f:
+            f.write(code)
+        manifest[key] = {"cubin": key + ".cubin", "names": names, "options": list(options)}
+        procs.append(subprocess.Popen([nvcc, "-cubin", *CUDA_ARCH, *options, "-w", src,
+                                       "-o", cubin]))
+    if any(p.wait() != 0 for p in procs):
+        raise RuntimeError("build_ref: nvcc failed on a reference kernel source")
+    with open(os.path.join(CUDA_OUT, "manifest.json"), "w") as f:
+        json.dump(manifest, f, indent=1)
+    print(f"build_ref: built {len(manifest)} reference kernel modules for sm_100 in {CUDA_OUT}")
+    return CUDA_OUT
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None)
     ap.add_argument("--cxx", default="g++")
+    ap.add_argument("--no-cuda", action="store_true")
     args = ap.parse_args()
-    build(args.reference, args.cxx)
+    ref = reference_path(args.reference)
+    build(ref, args.cxx)
+    if not args.no_cuda:
+        build_cuda(ref)

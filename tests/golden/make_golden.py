@@ -1,7 +1,8 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Run in a container that holds the reference checkout (default /root/reference):
-    python tests/golden/make_golden.py [--reference /root/reference]
+Run in a container that holds the reference checkout ($DFSNN_REFERENCE, else the default
+of oracle/build_ref.py):
+    python tests/golden/make_golden.py [--reference PATH]
 
 Two kinds of fixture are written, each an .npz holding its inputs and outputs:
   * torch_*.npz  -- the reference's own PyTorch code:
@@ -323,16 +324,19 @@ def weight_tables():
     _save("torch_tables.npz", **out)
 
 
-build_ref_reference = "/root/reference"
+build_ref_reference = None
 
 
 def main():
     global build_ref_reference
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    from build_ref import reference_path
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None)
     ap.add_argument("--only", choices=["history"], default=None,
                     help="write only this group of fixtures")
     args = ap.parse_args()
+    args.reference = reference_path(args.reference)
     build_ref_reference = args.reference
     _stub_h5py()
     sys.path.insert(0, args.reference)

@@ -1,0 +1,375 @@
+"""This library against the reference's own kernels, both on the GPU.
+
+The reference side is the unmodified reference package (staged in baseline/_ref by
+oracle/stage_ref.py): its autograd Functions, its LIFNeuronFDE and the CNN128 example run
+their own code, and their CuPy launches run the reference's own kernel source texts,
+compiled for sm_100 with the reference's options by oracle/build_ref.py and launched by
+oracle/cupy_standin.  The native side is this library, either called directly or
+registered under the reference's module names by dfsnn_b200.integrate.install().
+
+Bar: per-neuron outputs (spikes, membranes, grad_x, grad_v0, and every network gradient
+that depends on them only) are bit-identical; the reductions over neurons (grad_scale,
+grad_weights and the mass gradients) are compared with a float64 evaluation of the same
+sums on the GPU at 1e-5 relative to each tensor's scale (|err| <= 1e-5 (|ref| + rms)),
+for this library and for the reference alike; the largest per-element relative error of
+both is printed next to it.
+"""
+import math
+
+import pytest
+import torch
+
+import refenv
+from dfsnn_b200 import fde_kernels, schedule
+from dfsnn_b200 import aligned_glmulti as native_aligned
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(refenv.missing() is not None,
+                                 reason=str(refenv.missing()))]
+
+DEV = "cuda:0"
+TAU, TH, SG, H, BETA = 2.0, 1.0, 5.0, 0.1, 0.5
+RTOL = 1e-5
+CONFIG2_N = 16 * 128 * 64 * 64          # [T, 16, 128, 64, 64]
+CONFIG3_N = 4194304
+
+
+@pytest.fixture(scope="module")
+def ref():
+    r = refenv.Reference("cnn128")
+    yield r
+    r.close()
+
+
+def gen(T, N, seed, kind):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    x = torch.randn((T, N), device=DEV, generator=g)
+    if kind == "config2":
+        x.mul_(0.5).add_(0.3)
+    elif kind == "config3":
+        x.mul_(0.4).add_(0.2)
+    else:                                   # spiking regime (the reference's test_method)
+        x.mul_(5.0)
+    gS = torch.randn((T, N), device=DEV, generator=g)
+    gV = torch.randn((T, N), device=DEV, generator=g)
+    v0 = torch.randn(N, device=DEV, generator=g).mul_(0.1)
+    return x, gS, gV, v0
+
+
+def differing(a, b):
+    """Number of elements whose float32 bits differ (+0 and -0 count as equal)."""
+    a = a.detach().float().contiguous()
+    b = b.detach().float().contiguous()
+    eq = (a.view(torch.int32) == b.view(torch.int32)) | ((a == 0) & (b == 0))
+    return int((~eq).sum())
+
+
+def assert_bitwise(got, want, what):
+    n = differing(got, want)
+    assert n == 0, f"{what}: {n} of {got.numel()} values differ from the reference kernels"
+
+
+def reduction_check(got, refv, truth, what):
+    """got (this library) and refv (the reference's torch glue) against the float64 sums."""
+    truth = truth.double()
+    rms = float(truth.pow(2).mean().sqrt()) + 1e-30
+    out = {}
+    for name, v in (("native", got), ("reference", refv)):
+        err = (v.double() - truth).abs()
+        bound = float((err / (RTOL * (truth.abs() + rms))).max())
+        nz = truth.abs() > 0
+        rel = float((err[nz] / truth.abs()[nz]).max()) if bool(nz.any()) else 0.0
+        out[name] = (bound, rel)
+    print(f"\n{what}: err/limit native {out['native'][0]:.3g} reference {out['reference'][0]:.3g}; "
+          f"max per-element rel err native {out['native'][1]:.3g} reference "
+          f"{out['reference'][1]:.3g}")
+    assert out["native"][0] <= 1.0, f"{what}: err/limit {out['native'][0]:.3g}"
+    return out
+
+
+# -------------------------------------------------------------------------------------
+# single-order Functions (gl, gl1, trap, trap1, predictor, predictor1, LIF Euler)
+# -------------------------------------------------------------------------------------
+def single_args(scheme, T):
+    hb = H ** BETA
+    g1 = math.gamma(BETA + 1.0)
+    w = {"gl": schedule.gl_weights, "gl1": schedule.gl_weights, "trap": schedule.trap_weights,
+         "trap1": schedule.trap_weights, "predictor": schedule.predictor_weights,
+         "predictor1": schedule.predictor_weights}
+    if scheme == "euler":
+        return "LIFEulerFunction", (TAU, TH, 0.0, SG)
+    table = w[scheme](BETA, T).to(DEV)
+    name = {"gl": "LIFFDEGLFunction", "gl1": "LIFFDEGL1Function", "trap": "LIFFDETRAPFunction",
+            "trap1": "LIFFDETRAP1Function", "predictor": "LIFFDEPREDICTORFunction",
+            "predictor1": "LIFFDEPREDICTOR1Function"}[scheme]
+    if scheme == "gl1":
+        return name, (table, TAU, BETA, H, TH, 0.0, SG)
+    if scheme.startswith("predictor"):
+        return name, (table, TAU, BETA, TH, 0.0, SG, hb, g1)
+    return name, (table, TAU, BETA, TH, 0.0, SG)
+
+
+def run_single(fn, x, v0, args, gS, gV):
+    xr = x.clone().requires_grad_(True)
+    vr = v0.clone().requires_grad_(True)
+    s, v = fn.apply(xr, vr, *args)
+    torch.autograd.backward([s, v], [gS, gV])
+    return s.detach(), v.detach(), xr.grad, vr.grad
+
+
+SINGLE_CASES = ([(sch, T, "config2", CONFIG2_N) for sch in ("gl", "trap", "predictor")
+                 for T in (8, 16)]
+                + [(sch, 16, "spiking", 1 << 20) for sch in
+                   ("gl", "gl1", "trap", "trap1", "predictor", "predictor1", "euler")]
+                + [(sch, T, "config3", CONFIG3_N) for sch in ("gl", "predictor")
+                   for T in (64, 256)])
+
+
+@pytest.mark.parametrize("scheme,T,kind,N", SINGLE_CASES)
+def test_single_order_bitwise(ref, scheme, T, kind, N):
+    name, args = single_args(scheme, T)
+    x, gS, gV, v0 = gen(T, N, 11 + T, kind)
+    want = run_single(getattr(ref.kernels, name), x, v0, args, gS, gV)
+    got = run_single(getattr(fde_kernels, name), x, v0, args, gS, gV)
+    torch.cuda.synchronize()
+    for what, a, b in zip(("spikes", "membrane", "grad_x", "grad_v0"), got, want):
+        assert_bitwise(a, b, f"{scheme} T={T} {kind} {what}")
+
+
+# -------------------------------------------------------------------------------------
+# library glmulti
+# -------------------------------------------------------------------------------------
+def glmulti_schedule(T):
+    basis = schedule.glmulti_basis([0.3, 0.4, 0.5], T)
+    terms = schedule.build_glmulti_schedule(torch.tensor([0.5, 0.5, 0.7]),
+                                            torch.tensor([0.3, 0.4, 0.5]), basis, H, T)
+    return terms["scale"].contiguous().to(DEV), terms["weights"].contiguous().to(DEV)
+
+
+def glmulti_truth(ref, x, v0, scale, W, gS, full):
+    """grad_scale and grad_weights summed in float64 from the reference kernels' own
+    per-neuron sequences (drift, v_hist, grad_pre; fde_cupy_kernels_all.py:1999-2009)."""
+    import cupy
+    T, N = x.shape
+    fwd, bwd, fbwd = ref.kernels.LIFFDEGLMultiFunction.get_kernels()
+    s, vpre, vhist, drift = [torch.empty_like(x) for _ in range(4)]
+    grid = ((N + 255) // 256,)
+    fwd(grid, (256,), tuple(cupy.from_dlpack(t) for t in (x, v0, scale, W, s, vpre, vhist, drift))
+        + (cupy.int32(T), cupy.int32(N), cupy.int32(1), cupy.int32(0), cupy.float32(TAU),
+           cupy.float32(TH)))
+    gx, gpre = torch.empty_like(x), torch.empty_like(x)
+    gv = torch.empty_like(v0)
+    if full:
+        arrays = (gS, scale, W, vpre, gx, gv, gpre)
+        kern = fbwd
+    else:
+        arrays = (gS, scale, vpre, gx, gv, gpre)
+        kern = bwd
+    kern(grid, (256,), tuple(cupy.from_dlpack(t) for t in arrays)
+         + (cupy.int32(T), cupy.int32(N), cupy.float32(TAU), cupy.float32(TH), cupy.float32(SG)))
+    gp = gpre.double()
+    return (gp * drift.double()).sum(1), -(gp @ vhist.double().t())
+
+
+def run_glmulti(fn, x, v0, scale, W, gS, full):
+    xr, vr = x.clone().requires_grad_(True), v0.clone().requires_grad_(True)
+    sr, Wr = scale.clone().requires_grad_(True), W.clone().requires_grad_(True)
+    s = fn.apply(xr, vr, sr, Wr, TAU, TH, SG, 16, full)
+    s.backward(gS)
+    return s.detach(), xr.grad, vr.grad, sr.grad, Wr.grad
+
+
+GLM_CASES = ([(T, full, "config2", CONFIG2_N) for T in (8, 16) for full in (True, False)]
+             + [(16, True, "spiking", 1 << 20), (64, True, "config3", CONFIG3_N),
+                (256, False, "config3", CONFIG3_N)])
+
+
+@pytest.mark.parametrize("T,full,kind,N", GLM_CASES)
+def test_glmulti_vs_reference_kernels(ref, T, full, kind, N):
+    x, gS, _, v0 = gen(T, N, 101 + T, kind)
+    scale, W = glmulti_schedule(T)
+    want = run_glmulti(ref.kernels.LIFFDEGLMultiFunction, x, v0, scale, W, gS, full)
+    got = run_glmulti(fde_kernels.LIFFDEGLMultiFunction, x, v0, scale, W, gS, full)
+    tag = f"glmulti T={T} full={full} {kind}"
+    for what, a, b in zip(("spikes", "grad_x", "grad_v0"), got[:3], want[:3]):
+        assert_bitwise(a, b, f"{tag} {what}")
+    ts, tw = glmulti_truth(ref, x, v0, scale, W, gS, full)
+    reduction_check(got[3], want[3], ts, f"{tag} grad_scale")
+    reduction_check(got[4], want[4], tw, f"{tag} grad_weights")
+
+
+# -------------------------------------------------------------------------------------
+# the examples' aligned glmulti (examples/cnn128/aligned_glmulti.py)
+# -------------------------------------------------------------------------------------
+def aligned_truth(alg, x, v0, a, W, g):
+    """grad a and grad W in float64 from the reference kernels' own adjoint and history
+    (aligned_glmulti.py:33-41, 144)."""
+    T, N = x.shape
+    s, p, h = [torch.empty_like(x) for _ in range(3)]
+    grid = ((N + 255) // 256,)
+    import cupy
+    alg.cupy_launch("aligned_forward", [x, v0, a, W, s, p, h],
+                    [cupy.int32(T), cupy.int32(N), cupy.float32(TAU), cupy.float32(TH)], grid)
+    gx, ga = torch.empty_like(x), torch.empty_like(x)
+    gv = torch.empty_like(v0)
+    alg.cupy_launch("aligned_backward", [g, a, W, p, gx, gv, ga],
+                    [cupy.int32(T), cupy.int32(N), cupy.float32(TAU), cupy.float32(TH),
+                     cupy.float32(SG)], grid)
+    ga64, h64, W64, a64 = ga.double(), h.double(), W.double(), a.double()
+    gs = (ga64 * (h64 + W64 @ h64)).sum(1) / a64
+    gw = -(ga64 @ h64.t()) * torch.tril(torch.ones_like(W64), diagonal=-1)
+    return gs, gw
+
+
+@pytest.mark.parametrize("T,kind,N,rho", [(8, "config2", CONFIG2_N, 1.0),
+                                          (16, "config2", CONFIG2_N, 1.0),
+                                          (16, "spiking", 1 << 20, 1.0),
+                                          (16, "spiking", 1 << 18, 0.5),
+                                          (64, "config3", CONFIG3_N, 1.0)])
+def test_aligned_vs_reference_kernels(ref, T, kind, N, rho):
+    import aligned_glmulti as alg
+    old_backend, old_rho, old_native_rho = alg.BACKEND, alg.HISTORY_RHO, native_aligned.HISTORY_RHO
+    alg.BACKEND = "cupy"
+    alg.HISTORY_RHO = rho
+    native_aligned.HISTORY_RHO = rho
+    try:
+        x, gS, _, v0 = gen(T, N, 303 + T, kind)
+        v0.zero_()                               # the examples start from v_reset = 0
+        a, W = glmulti_schedule(T)
+        want = run_glmulti(alg.AlignedGLMulti, x, v0, a, W, gS, True)
+        got = run_glmulti(native_aligned.AlignedGLMulti, x, v0, a, W, gS, True)
+        tag = f"aligned T={T} {kind} rho={rho}"
+        for what, p, q in zip(("spikes", "grad_x", "grad_v0"), got[:3], want[:3]):
+            assert_bitwise(p, q, f"{tag} {what}")
+        ts, tw = aligned_truth(alg, x, v0, a, W, gS)
+        reduction_check(got[3], want[3], ts, f"{tag} grad_a")
+        reduction_check(got[4], want[4], tw, f"{tag} grad_w")
+    finally:
+        alg.BACKEND, alg.HISTORY_RHO = old_backend, old_rho
+        native_aligned.HISTORY_RHO = old_native_rho
+
+
+# -------------------------------------------------------------------------------------
+# the reference's LIFNeuronFDE, with its own kernels and with this library installed
+# -------------------------------------------------------------------------------------
+def reference_neuron(ref, method, T, B):
+    kw = dict(tau=TAU, threshold=TH, surrogate_grad_scale=SG, surrogate_function="arctan",
+              T=T, method=method, step_size=H, batchsize=B, step_mode="m", backend="cupy")
+    if method == "glmulti":
+        kw.update(beta=0.3, multi_beta=[0.3, 0.4, 0.5], multi_coefficient=[0.5, 0.5, 0.7],
+                  learn_coefficient=True, coefficient_constraint="softplus",
+                  glmulti_history_grad="full")
+    else:
+        kw.update(beta=BETA, store_v_seq=True)
+    return ref.neuron.LIFNeuronFDE(**kw).to(DEV)
+
+
+def neuron_step(layer, x, gS, gV, single):
+    layer.reset()
+    xr = x.clone().requires_grad_(True)
+    s = layer(xr)
+    outs, grads = [s], [gS]
+    if single:
+        outs.append(layer.v_seq)
+        grads.append(gV)
+    params = list(layer.parameters())
+    res = torch.autograd.grad(outs, [xr] + params, grads)
+    v = layer.v_seq.detach().clone() if single else None
+    return s.detach(), v, res[0], list(res[1:])
+
+
+@pytest.mark.parametrize("method", ["glmulti", "gl", "trap", "predictor"])
+@pytest.mark.parametrize("T", [8, 16])
+def test_reference_neuron_drop_in(ref, method, T):
+    """spikeDE_dis.neuron.LIFNeuronFDE(backend='cupy') itself: with its own module its lazy
+    imports (neuron.py:1994, 2105-2123) reach the reference kernels; after
+    integrate.install() the same unedited code reaches this library."""
+    shape = (T, 16, 128, 64, 64)
+    x, gS, gV, _ = gen(T, CONFIG2_N, 505 + T, "config2")
+    x, gS, gV = (t.reshape(shape) for t in (x, gS, gV))
+    single = method != "glmulti"
+    try:
+        ref.use_reference()
+        layer = reference_neuron(ref, method, T, 16)
+        want = neuron_step(layer, x, gS, gV, single)
+        ref.use_native()
+        from dfsnn_b200 import profiling
+        with profiling.NativeCallTimer() as timer:
+            got = neuron_step(layer, x, gS, gV, single)
+            torch.cuda.synchronize()
+        assert timer.total_launches() > 0, "the native kernels did not run"
+    finally:
+        ref.use_reference()
+    tag = f"LIFNeuronFDE {method} T={T}"
+    assert_bitwise(got[0], want[0], f"{tag} spikes")
+    assert_bitwise(got[2], want[2], f"{tag} grad_x")
+    if single:
+        assert_bitwise(got[1], want[1], f"{tag} v_seq")
+    for pg, pw in zip(got[3], want[3]):
+        scale = float(pw.abs().max()) + 1e-30
+        assert float((pg - pw).abs().max()) <= RTOL * scale * 10, f"{tag} mass gradient"
+
+
+# -------------------------------------------------------------------------------------
+# the CNN128 example itself (examples/cnn128/cnn128_aligned.py), unmodified
+# -------------------------------------------------------------------------------------
+def test_cnn128_example_drop_in(ref):
+    """make_model() from the example binds the example's AlignedGLMulti (its install('cupy'),
+    aligned_glmulti.py:157-162); one training step runs with the reference kernels, then
+    integrate.rebind_aligned() swaps in this library and the same step runs again.  Spikes
+    are bit-identical, so the logits, the loss and every convolution / batch-norm / linear
+    gradient are too; the shared mass gradient is a reduction (tolerance)."""
+    import aligned_glmulti as alg
+    import cnn128_aligned
+    from dfsnn_b200 import integrate
+    ref.use_reference()
+    library_ref, library_native = ref.kernels.LIFFDEGLMultiFunction, fde_kernels.LIFFDEGLMultiFunction
+    example_install, example_function = alg.install, alg.AlignedGLMulti
+    det, bench = torch.backends.cudnn.deterministic, torch.backends.cudnn.benchmark
+    torch.backends.cudnn.deterministic, torch.backends.cudnn.benchmark = True, False
+    try:
+        torch.manual_seed(0)
+        model = cnn128_aligned.make_model("cupy", [0.3, 0.4, 0.5], True, [0.5, 0.5, 0.7],
+                                          batch=16, T=16, num_classes=11).to(DEV)
+        g = torch.Generator(device=DEV).manual_seed(7)
+        shape = (16, 16, 2, 128, 128)
+        frames = (torch.rand(shape, device=DEV, generator=g) < 0.05).float()
+        frames = frames * torch.poisson(torch.ones(shape, device=DEV), generator=g)
+        labels = torch.randint(0, 11, (16,), device=DEV, generator=g)
+
+        def train_step():
+            for m in model.modules():
+                if isinstance(m, ref.neuron.LIFNeuronFDE):
+                    m.reset()
+            model.zero_grad(set_to_none=True)
+            torch.manual_seed(1)                 # the same dropout masks in both runs
+            out = model(frames)
+            loss = torch.nn.functional.cross_entropy(out, labels)
+            loss.backward()
+            torch.cuda.synchronize()
+            return out.detach(), {n: p.grad.detach().clone()
+                                  for n, p in model.named_parameters()}
+
+        calls = dict(alg.CALLS)
+        want_out, want_grads = train_step()
+        assert alg.CALLS["forward"] - calls["forward"] == 7
+        integrate.rebind_aligned(alg)
+        calls, native_calls = dict(alg.CALLS), dict(native_aligned.CALLS)
+        got_out, got_grads = train_step()
+        assert alg.CALLS == calls, "a reference kernel ran after the rebind"
+        assert native_aligned.CALLS["forward"] - native_calls["forward"] == 7
+        assert native_aligned.CALLS["backward"] - native_calls["backward"] == 7
+    finally:
+        torch.backends.cudnn.deterministic, torch.backends.cudnn.benchmark = det, bench
+        ref.kernels.LIFFDEGLMultiFunction = library_ref
+        fde_kernels.LIFFDEGLMultiFunction = library_native
+        alg.install, alg.AlignedGLMulti = example_install, example_function
+    assert_bitwise(got_out, want_out, "CNN128 logits")
+    shared = [n for n in want_grads if "multi_coefficient" in n]
+    assert shared, "no shared mass parameter found"
+    for n in want_grads:
+        if n in shared:
+            w, gg = want_grads[n], got_grads[n]
+            assert float((gg - w).abs().max()) <= RTOL * (float(w.abs().max()) + 1e-30) * 10, n
+        else:
+            assert_bitwise(got_grads[n], want_grads[n], f"CNN128 grad {n}")

@@ -266,9 +266,43 @@ def test_bench_clock_sampler_parses_nvidia_smi(tmp_path, monkeypatch):
     monkeypatch.setenv("PATH", str(tmp_path) + os.pathsep + os.environ.get("PATH", ""))
     monkeypatch.setattr(torch.cuda, "get_device_properties",
                         lambda i: types.SimpleNamespace(uuid="00000000-0000-0000-0000-000000000000"))
+    broken = types.ModuleType("pynvml")          # NVML unusable: the sampler falls back
+
+    def fail(*a):
+        raise RuntimeError("no NVML here")
+    broken.nvmlInit = fail
+    monkeypatch.setitem(sys.modules, "pynvml", broken)
     sampler = bench.ClockSampler(0)
     import time
     time.sleep(0.5)
     rec = sampler.stop()
     assert rec == {"sm_mhz": 1800.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"],
-                   "samples": 3}
+                   "samples": 3, "source": "nvidia-smi"}
+
+
+def test_bench_clock_sampler_nvml(monkeypatch):
+    """The NVML path: SM clock, maximum and clock-event reason bits read from a thread
+    (a stand-in pynvml; no GPU needed)."""
+    import importlib
+    import time
+    import types
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    monkeypatch.syspath_prepend(repo)
+    bench = importlib.import_module("bench")
+    clocks = iter([1500.0] + [1900.0, 1800.0, 1700.0] * 1000)
+    fake = types.ModuleType("pynvml")
+    fake.NVML_CLOCK_SM = 1
+    fake.nvmlInit = lambda: None
+    fake.nvmlDeviceGetHandleByUUID = lambda u: ("h", u)
+    fake.nvmlDeviceGetMaxClockInfo = lambda h, c: 1965
+    fake.nvmlDeviceGetClockInfo = lambda h, c: next(clocks)
+    fake.nvmlDeviceGetCurrentClocksEventReasons = lambda h: 0x4 | 0x1
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    monkeypatch.setattr(torch.cuda, "get_device_properties",
+                        lambda i: types.SimpleNamespace(uuid="00000000-0000-0000-0000-000000000000"))
+    sampler = bench.ClockSampler(0, period_s=0.005)
+    time.sleep(0.2)
+    rec = sampler.stop()
+    assert rec["source"] == "nvml" and rec["sm_max_mhz"] == 1965.0
+    assert rec["reasons"] == ["sw_power_cap"] and rec["samples"] >= 3
+    assert 1700.0 <= rec["sm_mhz"] <= 1900.0
