@@ -55,6 +55,13 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=1 << 22,
                     help="neurons of the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--network-source", choices=("example", "restatement"), default="example",
+                    help="network workloads: the reference example's own module (staged) or "
+                         "this repository's restatement of it")
+    ap.add_argument("--network-steps", type=int, default=10,
+                    help="timed CNN128 training steps of the default line's network record")
+    ap.add_argument("--no-network", action="store_true",
+                    help="skip the default line's CNN128 network record")
     ap.add_argument("--no-gpu-reference", action="store_true",
                     help="skip the reference's own GPU path timed on the same GPU")
     ap.add_argument("--only", default="",
@@ -528,6 +535,13 @@ def run_native(args):
         dt, kind, cores = cpu_workload_time(n)
         line["cpu_baseline"] = {"value": units_per_step(n) / dt, "unit": UNIT, "cores": cores,
                                 "kind": kind, "sample": cpu_sample_desc(n, kind)}
+    if args.workload == "layers" and not args.no_network:
+        # the network configuration at every N: CNN128 synthetic training, data-parallel
+        Kn = max(1, args.network_steps)
+        net = measure_network(args, "cnn128", dev, world, local, False, Kn, 3, args.network_source)
+        net["amp"] = measure_network(args, "cnn128", dev, world, local, True, Kn, 3,
+                                     args.network_source)
+        line["network"] = net
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -856,11 +870,155 @@ def run_cnn128(args):
     return run_network(args, "cnn128")
 
 
-def run_network(args, name):
+EXAMPLE_DIRS = {"cnn128": "cnn128", "spikformer256": "spikformer_har_lip"}
+
+
+def example_network(name, dev):
+    """The reference example itself, unmodified (staged in baseline/_ref), with this library
+    installed the documented way: integrate.install() before the model is built, the
+    example's own make_model() (which calls its install('cupy')), then
+    integrate.rebind_aligned().  The reference is imported without any CuPy, so none of its
+    own kernels can run.  Returns (model, reset, close) or None when it is not staged."""
+    from oracle import reference_gpu
+    if not reference_gpu.staged():
+        return None
+    from dfsnn_b200 import integrate
+    ref = reference_gpu.Reference(EXAMPLE_DIRS[name], standin=False)
+    ref.use_native()
+    if name == "cnn128":
+        import aligned_glmulti as alg
+        import cnn128_aligned
+        model = cnn128_aligned.make_model("cupy", MULTI_BETA, True, MASSES, batch=CNN_B, T=CNN_T,
+                                          num_classes=CNN_CLASSES)
+    else:
+        import aligned_glmulti as alg
+        model = alg.make_model("cupy", MULTI_BETA, True, MASSES, batch=SPK_B, T=SPK_T,
+                               num_classes=SPK_CLASSES)
+    from dfsnn_b200 import fde_kernels
+    library = fde_kernels.LIFFDEGLMultiFunction
+    integrate.rebind_aligned(alg)
+    model = model.to(dev)
+    lifs = [m for m in model.modules() if isinstance(m, ref.neuron.LIFNeuronFDE)]
+
+    def reset():
+        for m in lifs:
+            m.reset()
+
+    def close():
+        fde_kernels.LIFFDEGLMultiFunction = library
+        ref.close()
+    return model, reset, close
+
+
+def measure_network(args, name, dev, world, local, amp, K, W, source="example"):
+    """Synthetic training steps of CNN128 / Spikformer256, data-parallel (DDP over NCCL for
+    world > 1, B per GPU), AdamW as the reference trainer (train_transformer.py:131), fp32
+    or under autocast fp16 with a gradient scaler as the reference trainer runs by default
+    (train_transformer.py:111, 469-488).  Returns the record (every rank takes the same
+    collective steps)."""
     import torch
     import torch.distributed as dist
     import torch.nn.functional as F
     from dfsnn_b200 import profiling
+    torch.manual_seed(1234)                    # the same initial weights on every rank
+    _, NT, NB, NCLS, frame_kind, desc = NETWORKS[name]
+    built = example_network(name, dev) if source == "example" else None
+    if built is None:
+        source = "restatement"
+        model = globals()[NETWORKS[name][0]](dev)
+        reset, close = model.reset, (lambda: None)
+    else:
+        model, reset, close = built
+    try:
+        net = model
+        if world > 1:
+            net = torch.nn.parallel.DistributedDataParallel(
+                model, device_ids=[local], broadcast_buffers=False,
+                gradient_as_bucket_view=True, static_graph=True)
+        opt = torch.optim.AdamW(model.parameters(), lr=1e-4)
+        scaler = torch.amp.GradScaler("cuda", enabled=amp)
+        g = torch.Generator(device=dev).manual_seed(99 + int(os.environ.get("RANK", "0")))
+        shape = (NT, NB, 2, 128, 128)
+        frames = (torch.rand(shape, device=dev, generator=g) < 0.05).float()
+        if frame_kind == "poisson":
+            frames = frames * torch.poisson(torch.ones(shape, device=dev), generator=g)
+        labels = torch.randint(0, NCLS, (NB,), device=dev, generator=g)
+
+        def step():
+            reset()
+            with torch.autocast("cuda", dtype=torch.float16, enabled=amp):
+                loss = F.cross_entropy(net(frames), labels)
+            opt.zero_grad(set_to_none=True)
+            scaler.scale(loss).backward()
+            scaler.step(opt)
+            scaler.update()
+            return loss
+
+        for _ in range(W):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        with profiling.NativeCallTimer() as timer:
+            start.record()
+            for _ in range(K):
+                loss = step()
+            end.record()
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms_rank = start.elapsed_time(end)
+        t = torch.tensor([ms_rank], device=dev, dtype=torch.float64)
+        per_rank = [ms_rank]
+        allreduce = None
+        nparams = sum(p.numel() for p in model.parameters())
+        if world > 1:
+            gathered = [torch.zeros_like(t) for _ in range(world)]
+            dist.all_gather(gathered, t)
+            per_rank = [float(x.item()) for x in gathered]
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            # the gradient exchange alone: one all-reduce of all parameters (fp32)
+            buf = torch.zeros(nparams, device=dev)
+            for _ in range(3):
+                dist.all_reduce(buf)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(10):
+                dist.all_reduce(buf)
+            e1.record()
+            torch.cuda.synchronize()
+            allreduce = e0.elapsed_time(e1) / 10
+        ms = float(t.item())
+        summary = timer.summary()
+        rec = {
+            "metric": f"{'CNN128' if name == 'cnn128' else 'Spikformer256'} synthetic training "
+                      "samples/s", "value": world * NB * K / (ms / 1e3), "unit": "samples/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K,
+            "precision": "amp fp16 (autocast + GradScaler)" if amp else "fp32",
+            "model_source": ("the reference example's own module, unmodified, with this "
+                             "library installed (integrate.install, rebind_aligned)"
+                             if source == "example" else "this repository's restatement"),
+            "workload": desc, "parallelism": f"dp{world}" + (" (DDP, NCCL)" if world > 1 else ""),
+            "params": nparams,
+            "lif_ms_per_step": round(sum(v["ms_total"] for v in summary.values()) / K, 3),
+            "lif_launches_per_step": timer.total_launches() / K,
+            "allreduce_ms": allreduce,
+            "per_rank_ms_per_step": [round(x / K, 3) for x in per_rank],
+            "loss": float(loss.item()),
+        }
+        if world > 1:
+            net = None
+        return rec
+    finally:
+        close()
+
+
+def run_network(args, name):
+    import torch
+    import torch.distributed as dist
     from dfsnn_b200.distributed import init_process_group
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -871,74 +1029,20 @@ def run_network(args, name):
     if world > 1:
         init_process_group("nccl", timeout_s=300, device=dev)
     K, W = args.steps, max(args.warmup, 3)
-    torch.manual_seed(1234 + rank)
-    builder, NT, NB, NCLS, frame_kind, desc = NETWORKS[name]
-    model = globals()[builder](dev)
-    net = model
-    if world > 1:
-        # the graph is the same every step: static_graph lets DDP skip its per-step search
-        # for unused parameters, and bucket views avoid a copy of every gradient
-        net = torch.nn.parallel.DistributedDataParallel(
-            model, device_ids=[local], broadcast_buffers=False,
-            gradient_as_bucket_view=True, static_graph=True)
-    opt = torch.optim.SGD(model.parameters(), lr=1e-3, momentum=0.9)
-    g = torch.Generator(device=dev).manual_seed(99 + rank)
-    # synthetic event frames: Bernoulli(0.05) spikes (scaled by Poisson(1) counts for CNN128)
-    shape = (NT, NB, 2, 128, 128)
-    frames = (torch.rand(shape, device=dev, generator=g) < 0.05).float()
-    if frame_kind == "poisson":
-        frames = frames * torch.poisson(torch.ones(shape, device=dev), generator=g)
-    labels = torch.randint(0, NCLS, (NB,), device=dev, generator=g)
-
-    def step():
-        model.reset()
-        out = net(frames)
-        loss = F.cross_entropy(out, labels)
-        opt.zero_grad(set_to_none=True)
-        loss.backward()
-        opt.step()
-        return loss
-
-    for _ in range(W):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     clocks = ClockSampler(local)
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    with profiling.NativeCallTimer() as timer:
-        start.record()
-        for _ in range(K):
-            loss = step()
-        end.record()
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    recs = [measure_network(args, name, dev, world, local, amp, K, W, args.network_source)
+            for amp in (False, True)]
     clk = clocks.stop()
-    t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    summary = timer.summary()
     if rank == 0:
-        line = {
-            "metric": f"{'CNN128' if name == 'cnn128' else 'Spikformer256'} synthetic training "
-                      "samples/s", "value": world * NB * K / (ms / 1e3),
-            "unit": "samples/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": desc,
-                       "parallelism": f"dp{world}" + (" (DDP, NCCL)" if world > 1 else "")},
-            "lif_kernels": {k: {"calls_per_step": v["calls"] / K,
-                                "ms_per_call": round(v["ms_per_call"], 4)}
-                            for k, v in summary.items()},
-            "lif_ms_per_step": round(sum(v["ms_total"] for v in summary.values()) / K, 3),
-            "loss": float(loss.item()),
-            "clocks": clk,
-        }
+        line = dict(recs[0])
+        line.update({"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                     "dtype": "f32", "data": "synthetic",
+                     "config": {"workload": recs[0]["workload"],
+                                "parallelism": recs[0]["parallelism"]},
+                     "amp": recs[1], "clocks": clk})
         print(json.dumps(line), flush=True)
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     return 0
 

@@ -25,6 +25,11 @@ _OWNED = ("spikeDE_dis", "cupy", "h5py", "aligned_glmulti", "cnn128_aligned", "m
           "einops")
 
 
+def staged():
+    """True when the reference package and the example modules are staged."""
+    return os.path.isdir(os.path.join(STAGED, "spikeDE_dis")) and os.path.isdir(EXAMPLES)
+
+
 def missing():
     """Why the reference arm cannot run here, or None."""
     if not os.path.isdir(os.path.join(STAGED, "spikeDE_dis")):
@@ -82,10 +87,15 @@ def _stub_timm():
 
 
 class Reference:
-    def __init__(self, example=None):
+    """standin=False imports the reference without the CuPy stand-in: its own kernels then
+    cannot run at all (CUPY_AVAILABLE is false and every CuPy launch fails), which is how
+    the native benchmark uses the reference's network code."""
+
+    def __init__(self, example=None, standin=True):
         self._path = list(sys.path)
         self._before = set(sys.modules)
-        paths = [STANDIN, STAGED] + ([os.path.join(EXAMPLES, example)] if example else [])
+        paths = ([STANDIN] if standin else []) + [STAGED] + \
+            ([os.path.join(EXAMPLES, example)] if example else [])
         for p in reversed(paths):
             sys.path.insert(0, p)
         _stub_h5py()
@@ -94,8 +104,10 @@ class Reference:
         import spikeDE_dis.direct_euler_cupy as euler
         import spikeDE_dis.fde_cupy_kernels_all as kernels
         import spikeDE_dis.neuron as neuron
-        if not kernels.CUPY_AVAILABLE:
+        if standin and not kernels.CUPY_AVAILABLE:
             raise RuntimeError("the CuPy stand-in was not picked up")
+        if not standin and "cupy" in sys.modules:
+            raise RuntimeError("a cupy module is importable; the native benchmark expects none")
         self.kernels, self.euler, self.neuron = kernels, euler, neuron
         self.pkg = sys.modules["spikeDE_dis"]
 

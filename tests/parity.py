@@ -48,3 +48,18 @@ def assert_bitwise(got, ref, mask=None, what=""):
     bad &= ~((got == 0) & (ref == 0))
     assert not bad.any(), f"{what}: {int(bad.sum())} of {bad.size} values differ bitwise " \
                           f"(max abs diff {np.abs(got.astype(np.float64) - ref).max():.3g})"
+
+
+def differing_gpu(a, b):
+    """Number of elements of two same-shape tensors whose float32 bits differ (+0 and -0
+    count as equal), computed where the tensors live."""
+    import torch
+    a = a.detach().float().contiguous()
+    b = b.detach().float().contiguous()
+    eq = (a.view(torch.int32) == b.view(torch.int32)) | ((a == 0) & (b == 0))
+    return int((~eq).sum())
+
+
+def assert_bitwise_gpu(got, want, what=""):
+    n = differing_gpu(got, want)
+    assert n == 0, f"{what}: {n} of {got.numel()} values differ"
