@@ -55,11 +55,17 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=1 << 22,
                     help="neurons of the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--torch-sample", type=int, default=1 << 19,
+                    help="neurons of the reference PyTorch-path CPU sample")
     ap.add_argument("--network-source", choices=("example", "restatement"), default="example",
                     help="network workloads: the reference example's own module (staged) or "
                          "this repository's restatement of it")
     ap.add_argument("--network-steps", type=int, default=10,
                     help="timed CNN128 training steps of the default line's network record")
+    ap.add_argument("--no-sub-workloads", action="store_true",
+                    help="skip the default line's long-history and aligned-layer records")
+    ap.add_argument("--sub-steps", type=int, default=10,
+                    help="timed steps of the long-history record (about 52 ms each)")
     ap.add_argument("--no-network", action="store_true",
                     help="skip the default line's CNN128 network record")
     ap.add_argument("--no-gpu-reference", action="store_true",
@@ -156,6 +162,59 @@ def cpu_workload_time(n_sample, seed=0):
                                   spike=s, vseq=v)
     dt = time.perf_counter() - t0
     return dt, kind, O.num_threads()
+
+
+def cpu_torch_path_time(n_sample, seed=0):
+    """The reference's own PyTorch solver path on the host cores: the unmodified reference
+    LIFNeuronFDE(backend='torch') (staged in baseline/_ref; spikeDE_dis/neuron.py:1765-1788
+    and the single-step schemes :2292-2637) for the same layers -- glmulti, gl, trap,
+    predictor at T = 8 and 16 -- forward and backward on a sample of n_sample neurons, all
+    host threads.  Returns (seconds, threads) or None when the reference is not staged."""
+    import torch
+    from oracle import reference_gpu
+    if not reference_gpu.staged():
+        return None
+    threads = len(os.sched_getaffinity(0))
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    ref = reference_gpu.Reference(standin=False)
+    try:
+        g = torch.Generator().manual_seed(seed)
+        B = 16
+        shape = (16, B, n_sample // B)
+        x16 = torch.randn(shape, generator=g).mul_(0.5).add_(0.3)
+        gS16 = torch.randn(shape, generator=g)
+        gV16 = torch.randn(shape, generator=g)
+        def make():
+            out = []
+            for T in TS:
+                for sch in SCHEMES:
+                    kw = dict(tau=TAU, threshold=TH, surrogate_grad_scale=SG,
+                              surrogate_function="arctan", T=T, method=sch, step_size=H,
+                              batchsize=B, step_mode="m", backend="torch")
+                    if sch == "glmulti":
+                        kw.update(beta=MULTI_BETA[0], multi_beta=MULTI_BETA,
+                                  multi_coefficient=MASSES, learn_coefficient=True,
+                                  coefficient_constraint="softplus", glmulti_history_grad="full")
+                    else:
+                        kw.update(beta=BETA, store_v_seq=True)
+                    out.append((T, sch, ref.neuron.LIFNeuronFDE(**kw)))
+            return out
+
+        def run(layers, xs, gs, gv):
+            for T, sch, layer in layers:
+                layer_step(layer, xs[:T], gs[:T], gv[:T], sch != "glmulti")
+
+        # first-call overhead on separate layers (the history buffers keep their first shape)
+        small = slice(0, 1)
+        run(make(), x16[:, :, small], gS16[:, :, small], gV16[:, :, small])
+        layers = make()
+        t0 = time.perf_counter()
+        run(layers, x16, gS16, gV16)
+        return time.perf_counter() - t0, threads
+    finally:
+        ref.close()
+        torch.set_num_threads(prev)
 
 
 def cpu_sample_desc(n, kind):
@@ -318,18 +377,20 @@ class ClockSampler:
                 "samples": len(samples), "source": self.source}
 
 
-def make_layers(device):
+def make_layers(device, combos=None, batch=None):
     from dfsnn_b200.neuron import LIFNeuronFDE
-    if any(sch == "aligned" for _, sch in COMBOS):
+    combos = COMBOS if combos is None else combos
+    batch = SHAPE[0] if batch is None else batch
+    if any(sch == "aligned" for _, sch in combos):
         # the examples' aligned semantics replace the library glmulti Function for the whole
         # process, as their install() does (so "aligned" and "glmulti" never share a run)
         from dfsnn_b200 import aligned_glmulti
         aligned_glmulti.install("native")
     layers = {}
-    for T, sch in COMBOS:
+    for T, sch in combos:
         method = "glmulti" if sch == "aligned" else sch
         kw = dict(tau=TAU, threshold=TH, surrogate_grad_scale=SG, surrogate_function="arctan",
-                  T=T, method=method, step_size=H, batchsize=SHAPE[0], step_mode="m",
+                  T=T, method=method, step_size=H, batchsize=batch, step_mode="m",
                   backend="cupy")
         if method == "glmulti":
             kw.update(beta=MULTI_BETA[0], multi_beta=MULTI_BETA, multi_coefficient=MASSES,
@@ -411,6 +472,109 @@ def layer_step(layer, x, gS, gV, single):
     return res[0], s, list(res[1:])
 
 
+SUB_WORKLOADS = {
+    "long": dict(shape=(16, 4194304 // 16), mean=0.2, std=0.4,
+                 combos=[(T, sch) for T in (64, 256) for sch in ("gl", "predictor")],
+                 desc="LIFNeuronFDE gl/predictor (beta 0.5) fwd+bwd at T=64 and T=256, 4,194,304 "
+                      "neurons per GPU, x~N(0.2,0.4^2), upstream grads N(0,1) on spikes and "
+                      "membrane"),
+    "aligned": dict(shape=(16, 128, 64, 64), mean=0.3, std=0.5,
+                    combos=[(8, "aligned"), (16, "aligned")],
+                    desc="LIFNeuronFDE glmulti with the examples' aligned kernels (AlignedGLMulti, "
+                         "full history, learnable Softplus masses) fwd+bwd at T=8 and T=16, "
+                         "8,388,608 neurons per GPU, x~N(0.3,0.5^2), upstream grads N(0,1)"),
+}
+
+
+def fp32_roofline(d, combos, neurons, K, mhz, sms):
+    """Roofline of the single-order forward at T >= 64: its Kahan history chains (a fused
+    multiply-add and three adds per term, in a fixed order) bound it on the FP32 lanes at
+    the clock seen during the run."""
+    instr = 4 * sum(neurons * T * (T - 1) // 2 for T, _ in combos)
+    sec = d["ms_total"] / K / 1e3
+    peak_ops = sms * 128 * mhz * 1e6
+    return {"bound": "fp32", "kernel": "single_forward", "achieved": instr / sec / 1e12,
+            "peak": peak_ops / 1e12, "unit": "T FP32 instructions/s (per lane)",
+            "frac": instr / sec / peak_ops,
+            "peak_source": f"{sms} SMs x 128 FP32 lanes x {mhz:.0f} MHz (median under load)",
+            "work": "4 FP32 instructions per history term (fma + 3 add/sub, Kahan), "
+                    "N*T(T-1)/2 terms per call", "traffic": None}
+
+
+def measure_sub_workload(kind, K, W, dev, world, rank):
+    """Device-timed record of one more layer configuration at this N (same step, timing
+    and max-over-ranks rule as the headline): the long-history configuration or the
+    examples' aligned glmulti layer."""
+    import torch
+    import torch.distributed as dist
+    from dfsnn_b200 import fde_kernels, profiling
+    from dfsnn_b200.distributed import allreduce_flat
+    cfg = SUB_WORKLOADS[kind]
+    combos, shape = cfg["combos"], cfg["shape"]
+    neurons = math.prod(shape)
+    tmax = max(T for T, _ in combos)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    x = torch.randn((tmax,) + shape, device=dev, generator=g).mul_(cfg["std"]).add_(cfg["mean"])
+    gS = torch.randn((tmax,) + shape, device=dev, generator=g)
+    gV = torch.randn((tmax,) + shape, device=dev, generator=g)
+    library = fde_kernels.LIFFDEGLMultiFunction
+    try:
+        layers = make_layers(dev, combos, shape[0])
+
+        def step():
+            grads = []
+            for T, sch in combos:
+                _, _, pg = layer_step(layers[(T, sch)], x[:T], gS[:T], gV[:T],
+                                      sch not in ("glmulti", "aligned"))
+                grads += pg
+            if world > 1 and grads:
+                allreduce_flat(grads)
+
+        for _ in range(W):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        clocks = ClockSampler(dev.index)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        with profiling.NativeCallTimer() as timer:
+            start.record()
+            for _ in range(K):
+                step()
+            end.record()
+            torch.cuda.synchronize()
+        clk = clocks.stop()
+        t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    finally:
+        fde_kernels.LIFFDEGLMultiFunction = library
+    summary = timer.summary()
+    peak, peak_src = measured_hbm_peak()
+    kernels = {k: {"calls_per_step": v["calls"] / K, "ms_per_call": round(v["ms_per_call"], 4),
+                   "gbs": round(v["gbs"], 1) if v["gbs"] else None,
+                   "frac_of_hbm": round(v["gbs"] / peak, 4) if v["gbs"] else None}
+               for k, v in summary.items()}
+    if kind == "long" and "single_forward" in summary:
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        roofline = fp32_roofline(summary["single_forward"], combos, neurons, K,
+                                 (clk or {}).get("sm_mhz") or 1965.0, sms)
+        roofline["hbm_frac_of_measured"] = kernels["single_forward"]["frac_of_hbm"]
+    else:
+        name, d = max(summary.items(), key=lambda kv: kv[1]["ms_total"])
+        roofline = {"bound": "hbm", "kernel": name, "achieved": d["gbs"], "peak": peak,
+                    "unit": "GB/s", "frac": d["gbs"] / peak if d["gbs"] else None,
+                    "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
+                    "algorithmic_bytes_per_launch": d["bytes_per_call"], "traffic": None}
+    units = sum(T * neurons for T, _ in combos)
+    return {"workload": cfg["desc"], "value": world * K * units / (ms / 1e3), "unit": UNIT,
+            "ms_per_step": ms / K, "steps": K, "warmup": W, "n_gpus": world,
+            "gpu_launches": timer.total_launches(), "roofline": roofline, "kernels": kernels,
+            "clocks": clk}
+
+
 def run_native(args):
     import torch
     import torch.distributed as dist
@@ -484,24 +648,11 @@ def run_native(args):
                     "algorithmic_bytes_per_launch": d["bytes_per_call"],
                     "traffic": ncu_traffic(name, sorted({T for T, _ in COMBOS}))}
     if args.workload == "long" and "single_forward" in summary:
-        # T >= 64: the forward's Kahan history chains are FP32-bound (no tensor cores apply:
-        # a fused multiply-add and three adds per term, in a fixed order); roofline against the
-        # FP32 lanes at the clock seen during the run
+        # T >= 64: the forward's Kahan history chains are FP32-bound (no tensor cores apply)
         d = summary["single_forward"]
-        instr = 4 * sum(neurons * T * (T - 1) // 2 for T, _ in COMBOS)
-        sec = d["ms_total"] / K / 1e3
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        mhz = (clk or {}).get("sm_mhz") or 1965.0
-        peak_ops = sms * 128 * mhz * 1e6
-        roofline = {"bound": "fp32", "kernel": "single_forward",
-                    "achieved": instr / sec / 1e12, "peak": peak_ops / 1e12,
-                    "unit": "T FP32 instructions/s (per lane)",
-                    "frac": instr / sec / peak_ops,
-                    "peak_source": f"{sms} SMs x 128 FP32 lanes x {mhz:.0f} MHz (median under load)",
-                    "work": "4 FP32 instructions per history term (fma + 3 add/sub, Kahan), "
-                            "N*T(T-1)/2 terms per call",
-                    "hbm_frac_of_measured": d["gbs"] / peak if d["gbs"] else None,
-                    "traffic": None}
+        roofline = fp32_roofline(d, COMBOS, neurons, K, (clk or {}).get("sm_mhz") or 1965.0, sms)
+        roofline["hbm_frac_of_measured"] = d["gbs"] / peak if d["gbs"] else None
     kernels = {k: {"calls_per_step": v["calls"] / K, "ms_per_call": round(v["ms_per_call"], 4),
                    "gbs": round(v["gbs"], 1) if v["gbs"] else None,
                    "frac_of_hbm": round(v["gbs"] / peak, 4) if v["gbs"] else None}
@@ -535,6 +686,23 @@ def run_native(args):
         dt, kind, cores = cpu_workload_time(n)
         line["cpu_baseline"] = {"value": units_per_step(n) / dt, "unit": UNIT, "cores": cores,
                                 "kind": kind, "sample": cpu_sample_desc(n, kind)}
+        nt = max(16, args.torch_sample // 16 * 16)
+        tp = cpu_torch_path_time(nt)
+        if tp is not None:
+            line["cpu_baseline"]["torch_path"] = {
+                "value": units_per_step(nt) / tp[0], "unit": UNIT, "cores": tp[1],
+                "kind": "reference",
+                "sample": f"{nt} neurons (of 8,388,608) of the same workload through the "
+                          "unmodified reference LIFNeuronFDE(backend='torch') (its PyTorch "
+                          "solver path, truncated-history autograd), forward+backward, "
+                          "torch.set_num_threads(all host threads)"}
+    if args.workload == "layers" and not args.no_sub_workloads:
+        # the long-history configuration and the examples' aligned layer, at this N too
+        del x16, gS16, gV16
+        layers.clear()
+        torch.cuda.empty_cache()
+        for kind, Ks in (("long", max(1, min(K, args.sub_steps))), ("aligned", K)):
+            line[kind] = measure_sub_workload(kind, Ks, W, dev, world, rank)
     if args.workload == "layers" and not args.no_network:
         # the network configuration at every N: CNN128 synthetic training, data-parallel
         Kn = max(1, args.network_steps)
