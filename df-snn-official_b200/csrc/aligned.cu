@@ -469,12 +469,10 @@ __global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
         wr[d] = f2(w);
         rw[d] = f2(__fmul_rn(a.rho, w));                // (rho * w) as the reference rounds it
     }
-    float2 pw[4][4];
+    float acc[C::NACC];
     float2 gsa[T];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) pw[r][c] = f2(0.0f);
+    for (int e = 0; e < C::NACC; ++e) acc[e] = 0.0f;
 #pragma unroll
     for (int t = 0; t < T; ++t) gsa[t] = f2(0.0f);
     const long long ntiles = (N + TN - 1) / TN;
@@ -496,7 +494,7 @@ __global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
         if (fast) aln_bwd_warp_tile<T, TP2, true>(a, sW, sA, sInvA, wr, rw, X, G, V0, GP, Vs, gsa);
         else aln_bwd_warp_tile<T, TP2, false>(a, sW, sA, sInvA, wr, rw, X, G, V0, GP, Vs, gsa);
         __syncwarp();
-        warp_product<T>(GP, Vs, lane, pw);
+        warp_product<T>(GP, Vs, lane, acc);
         warp_store<T>(X, m, tile * TN, lane);
     }
     if (lane == 0) {
@@ -506,7 +504,7 @@ __global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
         }
         bulk_wait_all();
     }
-    warp_tiles_finish<T>(pw, gsa, aligned_smem, a.part, tid);
+    warp_tiles_finish<T>(acc, gsa, aligned_smem, a.part, tid);
 }
 
 namespace {

@@ -426,9 +426,8 @@ __global__ void __launch_bounds__(256) glm_bwd(GlmArgs a) {
 // constant the steps carry no bounds tests.  The drift overwrites x in the stage, grad_x
 // overwrites grad_spike and grad_v0 overwrites v0 (written back by TMA stores that clip
 // at N); grad_pre and v go to the warp's GP and V rows.  grad_scale is accumulated per
-// lane; grad_W per lane as a 4x4 block of the T x T product over one slice of the tile's
-// neurons.  GP and V rows are padded to 72 floats, which makes the product's float4 reads
-// free of bank conflicts.
+// lane; grad_W's T x T product of the GP and V rows runs on the tensor pipe (3xTF32
+// mma.sync, warp_tile.cuh), one zero-started accumulator per tile added to running sums.
 // ------------------------------------------------------------------------------------
 // Negated history weight of term (t, i) for both halves: registers (Toeplitz) or shared.
 template <int T, bool FAST>
@@ -564,12 +563,10 @@ __global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
     const float sc = sScale[0];
 #pragma unroll
     for (int d = 0; d < T; ++d) nw[d] = f2((fast && d > 0) ? -sW[d * T] : 0.0f);
-    float2 pw[4][4];
+    float acc[C::NACC];
     float2 gsa[T];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) pw[r][c] = f2(0.0f);
+    for (int e = 0; e < C::NACC; ++e) acc[e] = 0.0f;
 #pragma unroll
     for (int t = 0; t < T; ++t) gsa[t] = f2(0.0f);
     const long long ntiles = (N + TN - 1) / TN;
@@ -591,7 +588,7 @@ __global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
         if (fast) glm_bwd_warp_tile<T, FULL, TP2, true>(a, sW, sScale, nw, sc, X, G, V0, GP, Vs, gsa);
         else glm_bwd_warp_tile<T, FULL, TP2, false>(a, sW, sScale, nw, sc, X, G, V0, GP, Vs, gsa);
         __syncwarp();
-        warp_product<T>(GP, Vs, lane, pw);
+        warp_product<T>(GP, Vs, lane, acc);
         warp_store<T>(X, m, tile * TN, lane);
     }
     if (lane == 0) {
@@ -602,7 +599,7 @@ __global__ void __launch_bounds__(256, WarpBwdCfg<T>::kMinBlocks)
         }
         bulk_wait_all();   // stores complete before the stages are reused below
     }
-    warp_tiles_finish<T>(pw, gsa, aligned_smem, a.part, tid);
+    warp_tiles_finish<T>(acc, gsa, aligned_smem, a.part, tid);
 }
 
 // ------------------------------------------------------------------------------------

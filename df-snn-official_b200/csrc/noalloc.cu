@@ -14,7 +14,11 @@
 //   * the array exists once per device for the life of the process, and every call uses it:
 //     calls whose work overlaps on the GPU (two streams, or two host threads) race on it;
 //   * the first call on a device looks up the array's device address (once per device, with
-//     that device current); make that first call before any stream capture.
+//     that device current); make that first call before any stream capture, and no call on a
+//     device after cudaDeviceReset of it (the address is kept for the life of the process);
+//   * at most kNoAllocRows blocks write partial rows: below that the reduced outputs equal
+//     dfsnn_glmulti_backward's bit for bit (a 148-SM B200 uses 148 or 296 blocks);
+//   * a bounded wait that times out is reported only as NaN in grad_scale / grad_weights.
 #include <cmath>
 #include <cstdint>
 #include <mutex>
@@ -26,7 +30,7 @@ namespace {
 
 constexpr int kNoAllocMaxT = 16;
 constexpr int kNoAllocStride = kNoAllocMaxT + kNoAllocMaxT * kNoAllocMaxT;   // doubles per row
-constexpr int kNoAllocRows = 512;                                          // >= 148 SMs x 2 blocks
+constexpr int kNoAllocRows = 512;                                          // partial rows
 constexpr size_t kHeaderDoubles = 2;                                       // 16-byte error word
 
 // [16-byte error header][kNoAllocRows rows of partial sums]: 1.1 MB per device.

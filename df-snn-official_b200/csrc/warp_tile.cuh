@@ -4,10 +4,21 @@
 // [1 x 64] box; neurons past N read as zeros) into its own two shared-memory stages with one
 // mbarrier each, and writes grad_x / grad_v0 back with TMA stores that clip at N -- no block
 // barrier in the tile loop.  Lane l carries neurons 2l and 2l+1 as the halves of float2
-// values.  The shared-parameter product sum_n G[t,n] V[i,n] is accumulated per lane as a 4x4
-// block over one slice of each tile's neurons, from padded GP / V rows (the product's float4
-// reads are then free of bank conflicts), and reduced per block in double in a fixed order
-// at the end.
+// values.
+//
+// The shared-parameter product P[t][i] = sum_n GP[t,n] V[i,n] runs on the tensor pipe:
+// mma.sync m16n8k8 (tf32 inputs, fp32 accumulation) with every fp32 operand split into a
+// tf32 head and a tail (x = hi + lo, hi = x with its 13 low mantissa bits cleared, lo =
+// x - hi exactly) and three products per pair (lo*hi + hi*lo + hi*hi; the dropped lo*lo
+// and the tail's own truncation are ~2^-21 of each product).  Each tile's products start
+// from a zero accumulator and are added to the lane's running fp32 sums with
+// round-to-nearest adds; blocks then reduce in double in a fixed order (deterministic).
+// Fragment mapping (PTX m16n8k8 .tf32, groupID g = lane / 4, thread-in-group c = lane % 4):
+// A[m][k] = GP[t = m][neuron], B[k][n] = V[i = n][neuron], with the reduction index k
+// permuted -- k = c holds neuron 2c and k = c + 4 holds neuron 2c + 1 of each 8-neuron
+// step -- so that each lane's (a0, a2), (a1, a3) and (b0, b1) pairs are adjacent floats,
+// one 64-bit shared load each; rows RS = 72 floats apart (8 mod 32 banks) make the loads
+// of a warp free of bank conflicts.
 #pragma once
 #include <cstdint>
 
@@ -30,22 +41,19 @@ template <int T>
 struct WarpBwdCfg {
     static constexpr int kWarps = 8;
     static constexpr int TN = 64;                        // neurons per warp tile
-    // padded GP / V row stride (floats): rows start 32 B (T = 16) or 64 B (T = 8) apart
-    // modulo 128 B, so the product's float4 reads hit distinct banks
-    static constexpr int RS = T <= 8 ? 80 : 72;
+    static constexpr int RS = 72;                        // padded GP / V row stride (floats)
     static constexpr int STAGE = 2 * T * TN + TN;        // dense X rows, G rows, v0 row
     static constexpr int PER_WARP = 2 * STAGE + 2 * T * RS;   // two stages + GP + V rows
     static constexpr size_t kBytes = sizeof(float) * kWarps * PER_WARP + 128;  // + alignment
     static constexpr uint32_t kTxBytes = sizeof(float) * STAGE;
     static constexpr int kMinBlocks = T <= 8 ? 2 : 1;    // blocks per SM the registers allow
-    static constexpr int NRED = 16 + T;                  // doubles per thread in the reduction
-    static constexpr int TBLK = T / 4;                   // 4-row blocks along t (and along i)
-    static constexpr int LANES_PER_SLICE = TBLK * TBLK;
-    static constexpr int NSLICES = 32 / LANES_PER_SLICE;
-    static constexpr int GROUPS = TN / (4 * NSLICES);    // float4 neuron groups per lane
+    static constexpr int NT = T / 8;                     // mma n-tiles of 8 output columns
+    static constexpr int NACC = 4 * NT;                  // product accumulators per lane
+    static constexpr int NRED = NACC + T;                // doubles per thread in the reduction
     static_assert(T == 8 || T == 16, "warp-tiled backward covers T = 8 and T = 16");
     static_assert((sizeof(float) * STAGE) % 128 == 0 && (sizeof(float) * PER_WARP) % 128 == 0,
                   "TMA destinations must stay 128-byte aligned");
+    static_assert(RS % 32 == 8, "fragment loads are conflict-free for rows 8 banks apart");
     static_assert(sizeof(double) * 32 * kWarps * NRED <= kBytes - 128, "reduction scratch");
 };
 
@@ -77,34 +85,64 @@ __device__ __forceinline__ void warp_store(float* X, const TileMaps& m, long lon
     }
 }
 
-// pw[r][c] += sum over this lane's neurons of GP[t] * V[i], t = tr + TBLK*r,
-// i = tc + TBLK*c; each float4 group of neurons enters as two packed halves.
+// tf32 head of x (13 low mantissa bits cleared) and the exact tail x - head
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+    const uint32_t h = __float_as_uint(x) & 0xffffe000u;
+    hi = h;
+    lo = __float_as_uint(__fsub_rn(x, __uint_as_float(h)));
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// acc[4*nt + e] += this tile's sum over its 64 neurons of GP[t] * V[i] for the lane's
+// fragment entries e of n-tile nt: t = g + 8*(e >= 2), i = 8*nt + 2c + (e & 1).  For
+// T = 8 the A rows 8..15 are zero and their entries are never read.
 template <int T>
 __device__ __forceinline__ void warp_product(const float* GP, const float* Vs, int lane,
-                                             float2 (&pw)[4][4]) {
+                                             float (&acc)[WarpBwdCfg<T>::NACC]) {
     using C = WarpBwdCfg<T>;
     constexpr int RS = C::RS;
-    const int tr = lane % C::TBLK, tc = (lane / C::TBLK) % C::TBLK, sl = lane / C::LANES_PER_SLICE;
+    const int g = lane >> 2, c = lane & 3;
+    float d[C::NT][4];
 #pragma unroll
-    for (int jj = 0; jj < C::GROUPS; ++jj) {
-        const int kb = 4 * (sl * C::GROUPS + jj);
-        float4 g[4], v[4];
+    for (int nt = 0; nt < C::NT; ++nt)
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
-            g[r] = *reinterpret_cast<const float4*>(GP + (tr + C::TBLK * r) * RS + kb);
+        for (int e = 0; e < 4; ++e) d[nt][e] = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-            v[c] = *reinterpret_cast<const float4*>(Vs + (tc + C::TBLK * c) * RS + kb);
+    for (int k0 = 0; k0 < C::TN; k0 += 8) {
+        const float2 ar0 = *reinterpret_cast<const float2*>(GP + g * RS + k0 + 2 * c);
+        uint32_t ah[4], al[4];
+        split_tf32(ar0.x, ah[0], al[0]);
+        split_tf32(ar0.y, ah[2], al[2]);
+        if constexpr (T == 16) {
+            const float2 ar1 = *reinterpret_cast<const float2*>(GP + (g + 8) * RS + k0 + 2 * c);
+            split_tf32(ar1.x, ah[1], al[1]);
+            split_tf32(ar1.y, ah[3], al[3]);
+        } else {
+            ah[1] = al[1] = ah[3] = al[3] = 0u;
+        }
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const float2 g01 = make_float2(g[r].x, g[r].y), g23 = make_float2(g[r].z, g[r].w);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                pw[r][c] = fma2(g01, make_float2(v[c].x, v[c].y), pw[r][c]);
-                pw[r][c] = fma2(g23, make_float2(v[c].z, v[c].w), pw[r][c]);
-            }
+        for (int nt = 0; nt < C::NT; ++nt) {
+            const float2 br = *reinterpret_cast<const float2*>(Vs + (8 * nt + g) * RS + k0 + 2 * c);
+            uint32_t bh0, bl0, bh1, bl1;
+            split_tf32(br.x, bh0, bl0);
+            split_tf32(br.y, bh1, bl1);
+            mma_tf32(d[nt], al[0], al[1], al[2], al[3], bh0, bh1);
+            mma_tf32(d[nt], ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+            mma_tf32(d[nt], ah[0], ah[1], ah[2], ah[3], bh0, bh1);
         }
     }
+#pragma unroll
+    for (int nt = 0; nt < C::NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[4 * nt + e] = __fadd_rn(acc[4 * nt + e], d[nt][e]);
 }
 
 // num / b per half: div_markstein in packed form, or the IEEE division (SLOW).  The fast form
@@ -129,11 +167,13 @@ __device__ __forceinline__ bool quot_num_ok(float v) {
     return m <= 0x1p60f && (m >= 0x1p-60f || m == 0.0f);
 }
 
-// Block reduction in double, fixed order, into this block's partial row [T + T*T]:
-// gs (per-lane sums gsa over all lanes) then the T x T product (pw).  Uses the stages as
-// scratch: every warp must have finished its tiles and its stores.
+// Block reduction in double, fixed order, into this block's partial row [T + T*T]: the
+// per-lane sums gsa over all threads, then P[t][i] from the one lane of each warp that
+// holds it.  Uses the stages as scratch: every warp must have finished its tiles and its
+// stores.
 template <int T>
-__device__ __forceinline__ void warp_tiles_finish(const float2 (&pw)[4][4], const float2 (&gsa)[T],
+__device__ __forceinline__ void warp_tiles_finish(const float (&acc)[WarpBwdCfg<T>::NACC],
+                                                  const float2 (&gsa)[T],
                                                   unsigned char* aligned_smem, double* part_base,
                                                   int tid) {
     using C = WarpBwdCfg<T>;
@@ -141,24 +181,20 @@ __device__ __forceinline__ void warp_tiles_finish(const float2 (&pw)[4][4], cons
     double* red = reinterpret_cast<double*>(aligned_smem);
     double* mine = red + (size_t)tid * C::NRED;
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int e = 0; e < C::NACC; ++e) mine[e] = (double)acc[e];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) mine[r * 4 + c] = (double)pw[r][c].x + (double)pw[r][c].y;
-#pragma unroll
-    for (int t = 0; t < T; ++t) mine[16 + t] = (double)gsa[t].x + (double)gsa[t].y;
+    for (int t = 0; t < T; ++t) mine[C::NACC + t] = (double)gsa[t].x + (double)gsa[t].y;
     __syncthreads();
     double* part = part_base + (size_t)blockIdx.x * (T + T * T);
     for (int o = tid; o < T + T * T; o += blockDim.x) {
         double sum = 0.0;
         if (o < T) {
-            for (int q = 0; q < C::kWarps * 32; ++q) sum += red[(size_t)q * C::NRED + 16 + o];
+            for (int q = 0; q < C::kWarps * 32; ++q) sum += red[(size_t)q * C::NRED + C::NACC + o];
         } else {
             const int t = (o - T) / T, i = (o - T) % T;
-            const int r = t / C::TBLK, c = i / C::TBLK;
-            const int l0 = (t % C::TBLK) + C::TBLK * (i % C::TBLK);
-            for (int w = 0; w < C::kWarps; ++w)
-                for (int sl = 0; sl < C::NSLICES; ++sl)
-                    sum += red[(size_t)(w * 32 + sl * C::LANES_PER_SLICE + l0) * C::NRED + r * 4 + c];
+            const int lane = 4 * (t & 7) + ((i & 7) >> 1);
+            const int slot = 4 * (i >> 3) + ((t >= 8) ? 2 : 0) + (i & 1);
+            for (int w = 0; w < C::kWarps; ++w) sum += red[(size_t)(w * 32 + lane) * C::NRED + slot];
         }
         part[o] = sum;
     }

@@ -112,7 +112,14 @@ int dfsnn_glmulti_backward(const float* grad_spike, const float* x, const float*
  * file-scope device array that every device loading the library keeps until exit.
  * Limit: T <= 16 (DFSNN_ERR_T_LIMIT above).  All calls share that array: calls whose work
  * overlaps on the GPU (other streams or host threads) race.  The first call on a device
- * looks up the array's address; make it before any stream capture.  Allocates nothing. */
+ * looks up the array's address; make it before any stream capture, and make no call on a
+ * device after cudaDeviceReset of that device (the looked-up address is kept for the life
+ * of the process).  The array holds 512 rows of partial sums: while the regular entry point
+ * would use at most 512 (a 148-SM B200 uses 148 or 296), grad_scale / grad_weights equal its
+ * results bit for bit; beyond that the blocks are capped at 512 and the sums agree within
+ * the reduction tolerance.  A bounded device wait that times out shows only as NaN in
+ * grad_scale / grad_weights (there is no workspace to read the error word from), so a
+ * caller that passes both as NULL gets no timeout report.  Allocates nothing. */
 int dfsnn_glmulti_backward_noalloc(const float* grad_spike, const float* x, const float* v0,
                                    const float* scale, const float* weights, float* grad_x,
                                    float* grad_v0, float* grad_scale, float* grad_weights, int T,
