@@ -709,6 +709,14 @@ def run_native(args):
         net = measure_network(args, "cnn128", dev, world, local, False, Kn, 3, args.network_source)
         net["amp"] = measure_network(args, "cnn128", dev, world, local, True, Kn, 3,
                                      args.network_source)
+        if args.network_source == "example" and not args.no_gpu_reference:
+            # the same example network with the reference's own GPU kernels, same N
+            refnet = measure_network(args, "cnn128", dev, world, local, False, Kn, 3,
+                                     "example-reference")
+            if "value" in refnet:
+                refnet["amp"] = measure_network(args, "cnn128", dev, world, local, True, Kn, 3,
+                                                "example-reference")
+            net["reference_kernels"] = refnet
         line["network"] = net
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -1041,18 +1049,24 @@ def run_cnn128(args):
 EXAMPLE_DIRS = {"cnn128": "cnn128", "spikformer256": "spikformer_har_lip"}
 
 
-def example_network(name, dev):
+def example_network(name, dev, reference_kernels=False):
     """The reference example itself, unmodified (staged in baseline/_ref), with this library
     installed the documented way: integrate.install() before the model is built, the
     example's own make_model() (which calls its install('cupy')), then
     integrate.rebind_aligned().  The reference is imported without any CuPy, so none of its
-    own kernels can run.  Returns (model, reset, close) or None when it is not staged."""
+    own kernels can run.  With reference_kernels the same example runs its own aligned
+    kernels instead (the reference's GPU path, through the CuPy stand-in of oracle/, the
+    reference arm's infrastructure).  Returns (model, reset, close) or None when the example
+    (or, for reference_kernels, the prebuilt reference kernels) is missing."""
     from oracle import reference_gpu
-    if not reference_gpu.staged():
+    if not reference_gpu.staged() or (reference_kernels and reference_gpu.missing()):
         return None
     from dfsnn_b200 import integrate
-    ref = reference_gpu.Reference(EXAMPLE_DIRS[name], standin=False)
-    ref.use_native()
+    ref = reference_gpu.Reference(EXAMPLE_DIRS[name], standin=reference_kernels)
+    if reference_kernels:
+        ref.use_reference()
+    else:
+        ref.use_native()
     if name == "cnn128":
         import aligned_glmulti as alg
         import cnn128_aligned
@@ -1064,7 +1078,8 @@ def example_network(name, dev):
                                num_classes=SPK_CLASSES)
     from dfsnn_b200 import fde_kernels
     library = fde_kernels.LIFFDEGLMultiFunction
-    integrate.rebind_aligned(alg)
+    if not reference_kernels:
+        integrate.rebind_aligned(alg)
     model = model.to(dev)
     lifs = [m for m in model.modules() if isinstance(m, ref.neuron.LIFNeuronFDE)]
 
@@ -1090,7 +1105,12 @@ def measure_network(args, name, dev, world, local, amp, K, W, source="example"):
     from dfsnn_b200 import profiling
     torch.manual_seed(1234)                    # the same initial weights on every rank
     _, NT, NB, NCLS, frame_kind, desc = NETWORKS[name]
-    built = example_network(name, dev) if source == "example" else None
+    if source == "example-reference":
+        built = example_network(name, dev, reference_kernels=True)
+        if built is None:
+            return {"unavailable": "the staged reference example or its prebuilt kernels are missing"}
+    else:
+        built = example_network(name, dev) if source == "example" else None
     if built is None:
         source = "restatement"
         model = globals()[NETWORKS[name][0]](dev)
@@ -1166,9 +1186,13 @@ def measure_network(args, name, dev, world, local, amp, K, W, source="example"):
                       "samples/s", "value": world * NB * K / (ms / 1e3), "unit": "samples/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K,
             "precision": "amp fp16 (autocast + GradScaler)" if amp else "fp32",
-            "model_source": ("the reference example's own module, unmodified, with this "
-                             "library installed (integrate.install, rebind_aligned)"
-                             if source == "example" else "this repository's restatement"),
+            "model_source": {"example": "the reference example's own module, unmodified, with "
+                                        "this library installed (integrate.install, "
+                                        "rebind_aligned)",
+                             "example-reference": "the reference example's own module, unmodified, "
+                                                  "with the reference's own aligned kernels (its "
+                                                  "CuPy path through the stand-in)",
+                             }.get(source, "this repository's restatement"),
             "workload": desc, "parallelism": f"dp{world}" + (" (DDP, NCCL)" if world > 1 else ""),
             "params": nparams,
             "lif_ms_per_step": round(sum(v["ms_total"] for v in summary.values()) / K, 3),

@@ -14,6 +14,9 @@
 // backward (glmulti.cu), reducing grad a / grad W in-kernel.
 #include <atomic>
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
 #include "bulk_pipe.cuh"
 #include "kernels.h"
 #include "pack2.cuh"
@@ -30,6 +33,8 @@ struct AlnArgs {
     const float* W;      // [T, T]
     const float* g;      // [T, N] upstream grad of the spikes
     float* spike;
+    const void* xio;     // forward input x in the element type E of the forward kernels
+    void* sio;           // forward spikes in the element type E
     float* gx;
     float* gv0;
     double* part;
@@ -37,6 +42,61 @@ struct AlnArgs {
     int T;
     long long N;
     float tau, inv_tau, th, sg, rho;
+};
+
+// Element I/O of the forward kernels: fp32, or the fp16 / bf16 activations that reach the
+// layer under autocast.  The reference casts x with .float() and returns the spikes with
+// .to(x.dtype) (aligned_glmulti.py:112-121); a half-precision value converts to fp32
+// exactly and 0 / 1 spikes are exact in either type, so reading and writing the element
+// type directly gives the same values with a quarter of the cast traffic.
+template <typename E>
+struct Io;
+template <>
+struct Io<float> {
+    static __device__ __forceinline__ float ld(const void* p, long long i) {
+        return __ldcs(static_cast<const float*>(p) + i);
+    }
+    static __device__ __forceinline__ float2 ld2(const void* p, long long i) {
+        return __ldcs(reinterpret_cast<const float2*>(static_cast<const float*>(p) + i));
+    }
+    static __device__ __forceinline__ void st(void* p, long long i, float v) {
+        __stcs(static_cast<float*>(p) + i, v);
+    }
+    static __device__ __forceinline__ void st2(void* p, long long i, float2 v) {
+        __stcs(reinterpret_cast<float2*>(static_cast<float*>(p) + i), v);
+    }
+};
+template <>
+struct Io<__half> {
+    static __device__ __forceinline__ float ld(const void* p, long long i) {
+        return __half2float(__ldcs(static_cast<const __half*>(p) + i));
+    }
+    static __device__ __forceinline__ float2 ld2(const void* p, long long i) {
+        return __half22float2(__ldcs(reinterpret_cast<const __half2*>(static_cast<const __half*>(p) + i)));
+    }
+    static __device__ __forceinline__ void st(void* p, long long i, float v) {
+        __stcs(static_cast<__half*>(p) + i, __float2half_rn(v));
+    }
+    static __device__ __forceinline__ void st2(void* p, long long i, float2 v) {
+        __stcs(reinterpret_cast<__half2*>(static_cast<__half*>(p) + i), __float22half2_rn(v));
+    }
+};
+template <>
+struct Io<__nv_bfloat16> {
+    static __device__ __forceinline__ float ld(const void* p, long long i) {
+        return __bfloat162float(__ldcs(static_cast<const __nv_bfloat16*>(p) + i));
+    }
+    static __device__ __forceinline__ float2 ld2(const void* p, long long i) {
+        return __bfloat1622float2(
+            __ldcs(reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(p) + i)));
+    }
+    static __device__ __forceinline__ void st(void* p, long long i, float v) {
+        __stcs(static_cast<__nv_bfloat16*>(p) + i, __float2bfloat16_rn(v));
+    }
+    static __device__ __forceinline__ void st2(void* p, long long i, float2 v) {
+        __stcs(reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p) + i),
+               __float22bfloat162_rn(v));
+    }
 };
 
 // One forward step of aligned_forward (:11-14) given the step's history sum h (accumulated
@@ -61,7 +121,7 @@ __device__ __forceinline__ void aligned_push(float (&hs)[TB], const float* sW, c
     for (int u = t + 1; u < TB; ++u) hs[u] = __fadd_rn(hs[u], __fmul_rn(wgt<TB, FAST>(sW, wr, u, t), v));
 }
 
-template <int TB, bool TP2, bool FAST>
+template <int TB, bool TP2, bool FAST, typename E>
 __device__ __forceinline__ void aln_fwd_body(const AlnArgs& a, const float* sW, const float* sA,
                                              long long n) {
     const int T = a.T;
@@ -72,7 +132,7 @@ __device__ __forceinline__ void aln_fwd_body(const AlnArgs& a, const float* sW, 
     float xr[TB];
 #pragma unroll
     for (int t = 0; t < TB; ++t)
-        if (t < T) xr[t] = ld_stream(a.x + t * N + n);
+        if (t < T) xr[t] = Io<E>::ld(a.xio, t * N + n);
     float v = a.v0[n];
     float hs[TB];
 #pragma unroll
@@ -85,12 +145,12 @@ __device__ __forceinline__ void aln_fwd_body(const AlnArgs& a, const float* sW, 
             v = aligned_step<TP2>(xr[t], v, FAST ? sA[0] : sA[t], hs[t], a.tau, a.inv_tau, a.th,
                                   pred, fire);
             aligned_push<TB, FAST>(hs, sW, wr, t, v);
-            st_stream(a.spike + t * N + n, fire ? 1.0f : 0.0f);
+            Io<E>::st(a.sio, t * N + n, fire ? 1.0f : 0.0f);
         }
     }
 }
 
-template <int TB, bool TP2>
+template <int TB, bool TP2, typename E>
 __global__ void __launch_bounds__(256) aln_fwd_reg(AlnArgs a) {
     __shared__ float sW[TB * TB];
     __shared__ float sA[TB];
@@ -103,15 +163,15 @@ __global__ void __launch_bounds__(256) aln_fwd_reg(AlnArgs a) {
     const bool fast = block_toeplitz(a.W, a.a, T);
     const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (n >= a.N) return;
-    if (fast) aln_fwd_body<TB, TP2, true>(a, sW, sA, n);
-    else aln_fwd_body<TB, TP2, false>(a, sW, sA, n);
+    if (fast) aln_fwd_body<TB, TP2, true, E>(a, sW, sA, n);
+    else aln_fwd_body<TB, TP2, false, E>(a, sW, sA, n);
 }
 
 // Forward, T <= TB <= 16, two neurons per thread (Toeplitz schedule; a general W runs the
 // scalar body per neuron).  Every product is formed by pmz2 and every sum is packed
 // (pack2.cuh).  The history sum h is accumulated negated, h' = h' + round(-w*v), so
 // v = round(a*f) - h is an add.
-template <int TB, bool TP2>
+template <int TB, bool TP2, typename E>
 __global__ void __launch_bounds__(128, 5) aln_fwd_x2(AlnArgs a) {
     __shared__ float sW[TB * TB];
     __shared__ float sA[TB];
@@ -123,7 +183,7 @@ __global__ void __launch_bounds__(128, 5) aln_fwd_x2(AlnArgs a) {
     if (n < a.N) {
 #pragma unroll
         for (int t = 0; t < TB; ++t)
-            if (t < T) xr[t] = ld2_stream(a.x + t * a.N + n);
+            if (t < T) xr[t] = Io<E>::ld2(a.xio, t * a.N + n);
         v = *reinterpret_cast<const float2*>(a.v0 + n);
     }
     for (int e = threadIdx.x; e < TB * TB; e += blockDim.x) {
@@ -134,8 +194,8 @@ __global__ void __launch_bounds__(128, 5) aln_fwd_x2(AlnArgs a) {
     const bool fast = block_toeplitz(a.W, a.a, T);
     if (n >= a.N) return;
     if (!fast) {
-        aln_fwd_body<TB, TP2, false>(a, sW, sA, n);
-        aln_fwd_body<TB, TP2, false>(a, sW, sA, n + 1);
+        aln_fwd_body<TB, TP2, false, E>(a, sW, sA, n);
+        aln_fwd_body<TB, TP2, false, E>(a, sW, sA, n + 1);
         return;
     }
     const long long N = a.N;
@@ -165,7 +225,7 @@ __global__ void __launch_bounds__(128, 5) aln_fwd_x2(AlnArgs a) {
             v = padd2(pmz2(a2, f, nz2), hn[t]);                      // a*f - h
 #pragma unroll
             for (int u = t + 1; u < TB; ++u) hn[u] = padd2(hn[u], pmz2(nw[u - t], v, nz2));
-            st2_stream(a.spike + t * N + n, s);
+            Io<E>::st2(a.sio, t * N + n, s);
         }
     }
 }
@@ -549,7 +609,7 @@ int aln_grid_t(long long N) {
 // ------------------------------------------------------------------------------------
 constexpr int kAlnLongThreads = 64;
 
-template <bool TP2>
+template <bool TP2, typename E>
 __global__ void __launch_bounds__(kAlnLongThreads) aln_fwd_long(AlnArgs a) {
     extern __shared__ float sh[];
     const long long n = (long long)blockIdx.x * kAlnLongThreads + threadIdx.x;
@@ -564,10 +624,10 @@ __global__ void __launch_bounds__(kAlnLongThreads) aln_fwd_long(AlnArgs a) {
         for (int j = 0; j < t; ++j) h = __fadd_rn(h, __fmul_rn(__ldg(wrow + j), vh[j * kAlnLongThreads]));
         float pred;
         bool fire;
-        v = aligned_step<TP2>(ld_stream(a.x + t * N + n), v, __ldg(a.a + t), h, a.tau, a.inv_tau,
+        v = aligned_step<TP2>(Io<E>::ld(a.xio, t * N + n), v, __ldg(a.a + t), h, a.tau, a.inv_tau,
                               a.th, pred, fire);
         vh[t * kAlnLongThreads] = v;
-        st_stream(a.spike + t * N + n, fire ? 1.0f : 0.0f);
+        Io<E>::st(a.sio, t * N + n, fire ? 1.0f : 0.0f);
     }
 }
 
@@ -674,31 +734,29 @@ cudaError_t aligned_backward_long_launch(const float* g, const float* x, const f
     return launch_param_finalize(part, slices, T, T, ga, gW, 1, err, st);
 }
 
-cudaError_t aligned_forward_launch(const float* x, const float* v0, const float* a_,
-                                   const float* W, float* spike, int T, long long N, float tau,
-                                   float th, bool tau_pow2, cudaStream_t st) {
-    if (N == 0) return cudaSuccess;
-    AlnArgs a{};
-    a.negz = -0.0f;
-    a.x = x; a.v0 = v0; a.a = a_; a.W = W; a.spike = spike; a.T = T; a.N = N; a.tau = tau;
-    a.inv_tau = 1.0f / tau; a.th = th;
-    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(v0) |
+namespace {
+
+template <typename E>
+cudaError_t aligned_forward_t(AlnArgs& a, const void* x, const void* spike, int T, long long N,
+                              bool tau_pow2, cudaStream_t st) {
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(a.v0) |
                          reinterpret_cast<uintptr_t>(spike);
-    if (T <= 16 && (N % 2) == 0 && (al & 7u) == 0) {
+    if (T <= 16 && (N % 2) == 0 && (al & (2 * sizeof(E) - 1)) == 0 &&
+        (reinterpret_cast<uintptr_t>(a.v0) & 7u) == 0) {
         const unsigned g2 = (unsigned)((N / 2 + 127) / 128);        // 128-thread blocks
         if (T <= 8) {
-            if (tau_pow2) aln_fwd_x2<8, true><<<g2, 128, 0, st>>>(a);
-            else aln_fwd_x2<8, false><<<g2, 128, 0, st>>>(a);
+            if (tau_pow2) aln_fwd_x2<8, true, E><<<g2, 128, 0, st>>>(a);
+            else aln_fwd_x2<8, false, E><<<g2, 128, 0, st>>>(a);
         } else {
-            if (tau_pow2) aln_fwd_x2<16, true><<<g2, 128, 0, st>>>(a);
-            else aln_fwd_x2<16, false><<<g2, 128, 0, st>>>(a);
+            if (tau_pow2) aln_fwd_x2<16, true, E><<<g2, 128, 0, st>>>(a);
+            else aln_fwd_x2<16, false, E><<<g2, 128, 0, st>>>(a);
         }
         return cudaGetLastError();
     }
     if (T > 32) {
         const unsigned gl = (unsigned)((N + kAlnLongThreads - 1) / kAlnLongThreads);
         const size_t smem = sizeof(float) * (size_t)T * kAlnLongThreads;
-        auto k = tau_pow2 ? aln_fwd_long<true> : aln_fwd_long<false>;
+        auto k = tau_pow2 ? aln_fwd_long<true, E> : aln_fwd_long<false, E>;
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         k<<<gl, kAlnLongThreads, smem, st>>>(a);
@@ -706,14 +764,35 @@ cudaError_t aligned_forward_launch(const float* x, const float* v0, const float*
     }
     const unsigned grid = (unsigned)((N + 255) / 256);
     const int TB = tb_of(T);
-#define DFSNN_AF(TBV)                                                    \
-    if (TB == TBV) {                                                     \
-        if (tau_pow2) aln_fwd_reg<TBV, true><<<grid, 256, 0, st>>>(a);   \
-        else aln_fwd_reg<TBV, false><<<grid, 256, 0, st>>>(a);           \
+#define DFSNN_AF(TBV)                                                       \
+    if (TB == TBV) {                                                        \
+        if (tau_pow2) aln_fwd_reg<TBV, true, E><<<grid, 256, 0, st>>>(a);   \
+        else aln_fwd_reg<TBV, false, E><<<grid, 256, 0, st>>>(a);           \
     }
     DFSNN_AF(8) DFSNN_AF(16) DFSNN_AF(32)
 #undef DFSNN_AF
     return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t aligned_forward_launch_io(const void* x, int dtype, const float* v0, const float* a_,
+                                      const float* W, void* spike, int T, long long N, float tau,
+                                      float th, bool tau_pow2, cudaStream_t st) {
+    if (N == 0) return cudaSuccess;
+    AlnArgs a{};
+    a.negz = -0.0f;
+    a.v0 = v0; a.a = a_; a.W = W; a.xio = x; a.sio = spike; a.T = T; a.N = N; a.tau = tau;
+    a.inv_tau = 1.0f / tau; a.th = th;
+    if (dtype == kIoF16) return aligned_forward_t<__half>(a, x, spike, T, N, tau_pow2, st);
+    if (dtype == kIoBF16) return aligned_forward_t<__nv_bfloat16>(a, x, spike, T, N, tau_pow2, st);
+    return aligned_forward_t<float>(a, x, spike, T, N, tau_pow2, st);
+}
+
+cudaError_t aligned_forward_launch(const float* x, const float* v0, const float* a_,
+                                   const float* W, float* spike, int T, long long N, float tau,
+                                   float th, bool tau_pow2, cudaStream_t st) {
+    return aligned_forward_launch_io(x, kIoF32, v0, a_, W, spike, T, N, tau, th, tau_pow2, st);
 }
 
 cudaError_t aligned_backward_launch(const float* g, const float* x, const float* v0,

@@ -165,6 +165,21 @@ int dfsnn_aligned_forward(const float* x, const float* v0, const float* a,
                                                      (cudaStream_t)stream));
 }
 
+int dfsnn_aligned_forward_typed(const void* x, const float* v0, const float* a,
+                                const float* weights, void* spike, int dtype, int T, long long N,
+                                float tau, float threshold, void* stream) {
+    if (int s = check_seq(T, N, DFSNN_MAX_T_FULL)) return s;
+    if (dtype != DFSNN_DTYPE_F32 && dtype != DFSNN_DTYPE_F16 && dtype != DFSNN_DTYPE_BF16)
+        return DFSNN_ERR_PARAM;
+    if (N > 0 && (!x || !v0 || !a || !weights || !spike)) return DFSNN_ERR_NULL;
+    if (!valid_tau(tau) || !finite(threshold)) return DFSNN_ERR_PARAM;
+    const int io = dtype == DFSNN_DTYPE_F16 ? dfsnn::kIoF16
+                                            : (dtype == DFSNN_DTYPE_BF16 ? dfsnn::kIoBF16 : dfsnn::kIoF32);
+    return cuda_status(dfsnn::aligned_forward_launch_io(x, io, v0, a, weights, spike, T, N, tau,
+                                                        threshold, tau_is_pow2(tau),
+                                                        (cudaStream_t)stream));
+}
+
 size_t dfsnn_aligned_backward_workspace_size(int T, long long N) {
     if (T < 1 || T > DFSNN_MAX_T_FULL || N < 0) return 0;
     if (T > 32) return long_workspace_bytes(T, N);

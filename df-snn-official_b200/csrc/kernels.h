@@ -72,6 +72,11 @@ bool bulk_eligible(const void* p, const void* q, const void* r, long long N);
 cudaError_t aligned_forward_launch(const float* x, const float* v0, const float* a,
                                    const float* W, float* spike, int T, long long N, float tau,
                                    float th, bool tau_pow2, cudaStream_t st);
+// element types of x / spike for the typed forward
+constexpr int kIoF32 = 0, kIoF16 = 1, kIoBF16 = 2;
+cudaError_t aligned_forward_launch_io(const void* x, int dtype, const float* v0, const float* a,
+                                      const float* W, void* spike, int T, long long N, float tau,
+                                      float th, bool tau_pow2, cudaStream_t st);
 int aligned_bwd_blocks(int T, long long N, bool tau_pow2);
 int aligned_part_stride(int T);
 cudaError_t aligned_backward_launch(const float* g, const float* x, const float* v0,

@@ -23,6 +23,8 @@ MAX_T_FULL = 64
 
 GL, TRAP, PREDICTOR, GL1, TRAP1, PREDICTOR1, EULER_LIF = 0, 1, 2, 3, 4, 5, 6
 
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+
 _p = ctypes.c_void_p
 _i = ctypes.c_int
 _ll = ctypes.c_longlong
@@ -41,6 +43,7 @@ SIGNATURES = {
     "dfsnn_glmulti_backward_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _ll, _f, _f,
                                             _f, _i, _p]),
     "dfsnn_aligned_forward": (_i, [_p, _p, _p, _p, _p, _i, _ll, _f, _f, _p]),
+    "dfsnn_aligned_forward_typed": (_i, [_p, _p, _p, _p, _p, _i, _i, _ll, _f, _f, _p]),
     "dfsnn_aligned_backward_workspace_size": (_sz, [_i, _ll]),
     "dfsnn_aligned_backward": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _ll, _f, _f, _f, _f,
                                     _p, _sz, _p]),

@@ -11,6 +11,7 @@ from . import _capi
 from . import profiling as _prof
 
 BACKEND = "native"
+_HALF = {torch.float16: _capi.DTYPE_F16, torch.bfloat16: _capi.DTYPE_BF16}
 CALLS = {"forward": 0, "backward": 0}
 HISTORY_RHO = 1.0
 
@@ -35,22 +36,32 @@ class AlignedGLMulti(torch.autograd.Function):
         CALLS["forward"] += 1
         ctx.dtype = x.dtype
         ctx.constants = (float(tau), float(th), float(sg))
-        x, v, a, w = [z.float().contiguous() for z in (x, v, a, w)]
+        v, a, w = [z.float().contiguous() for z in (v, a, w)]
+        io = _HALF.get(x.dtype)
+        if io is not None:
+            # half-precision activations (autocast): read and written in their own type by
+            # the kernel -- the reference's .float() / .to(dtype) casts give the same values
+            x = x.contiguous()
+            elem = 2
+        else:
+            x = x.float().contiguous()
+            io, elem = _capi.DTYPE_F32, 4
         T, N = x.shape
         s = torch.empty_like(x)
         with torch.cuda.device(x.device), _prof.native_call(
-                "aligned_forward", 1, _prof.glmulti_forward_bytes(T, N), x.device):
-            code = _capi.lib().dfsnn_aligned_forward(
-                _capi.ptr(x), _capi.ptr(v), _capi.ptr(a), _capi.ptr(w), _capi.ptr(s), T, N,
+                "aligned_forward", 1, _prof.glmulti_forward_bytes(T, N, elem), x.device):
+            code = _capi.lib().dfsnn_aligned_forward_typed(
+                _capi.ptr(x), _capi.ptr(v), _capi.ptr(a), _capi.ptr(w), _capi.ptr(s), io, T, N,
                 float(tau), float(th), _capi.stream_of(x))
         _capi.check(code, "AlignedGLMulti.forward")
         ctx.save_for_backward(x, v, a, w)
-        return s.to(ctx.dtype)
+        return s
 
     @staticmethod
     def backward(ctx, g):
         CALLS["backward"] += 1
         x, v, a, w = ctx.saved_tensors
+        x = x.float().contiguous()
         g = g.float().contiguous()
         T, N = g.shape
         tau, th, sg = ctx.constants

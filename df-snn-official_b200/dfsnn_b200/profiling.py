@@ -81,8 +81,8 @@ def native_call(name, launches, nbytes, device):
 
 
 # Algorithmic bytes per call (fp32 I/O): compulsory HBM reads + writes of one call.
-def glmulti_forward_bytes(T, N):
-    return N * (8 * T + 4)                       # x in, spikes out; v0 in
+def glmulti_forward_bytes(T, N, elem=4):
+    return N * (2 * elem * T + 4)                # x in, spikes out (elem bytes each); v0 in
 
 
 def glmulti_backward_bytes(T, N):

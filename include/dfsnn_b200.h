@@ -135,6 +135,20 @@ int dfsnn_aligned_forward(const float* x, const float* v0, const float* a,
                           const float* weights, float* spike, int T, long long N, float tau,
                           float threshold, void* stream);
 
+/* Element types of dfsnn_aligned_forward_typed's x and spike arrays. */
+#define DFSNN_DTYPE_F32 0
+#define DFSNN_DTYPE_F16 1
+#define DFSNN_DTYPE_BF16 2
+
+/* Replaces AlignedGLMulti.forward for the half-precision activations it receives under
+ * autocast (aligned_glmulti.py:112-121: x.float(), the aligned_forward launch, s.to(x.dtype)):
+ * x and spike are float16 (DFSNN_DTYPE_F16) or bfloat16 (DFSNN_DTYPE_BF16) [T, N] arrays read
+ * and written in that type, the arithmetic is dfsnn_aligned_forward's fp32, so the spikes are
+ * the reference's.  DFSNN_DTYPE_F32 is dfsnn_aligned_forward. */
+int dfsnn_aligned_forward_typed(const void* x, const float* v0, const float* a,
+                                const float* weights, void* spike, int dtype, int T, long long N,
+                                float tau, float threshold, void* stream);
+
 size_t dfsnn_aligned_backward_workspace_size(int T, long long N);
 
 /* Replaces AlignedGLMulti.backward (aligned_glmulti.py:123-145): aligned_backward (:20-32)

@@ -88,6 +88,12 @@ def test_aligned_and_euler_validation(L):
     f = L.dfsnn_aligned_forward
     assert f(FAKE, FAKE, FAKE, FAKE, FAKE, 65, 10, 2.0, 1.0, None) == _capi.DFSNN_ERR_T_LIMIT
     assert L.dfsnn_aligned_backward_workspace_size(65, 10) == 0
+    t = L.dfsnn_aligned_forward_typed
+    assert t(FAKE, FAKE, FAKE, FAKE, FAKE, 3, 16, 10, 2.0, 1.0, None) == _capi.DFSNN_ERR_PARAM
+    assert t(FAKE, FAKE, FAKE, FAKE, FAKE, _capi.DTYPE_F16, 65, 10, 2.0, 1.0, None) \
+        == _capi.DFSNN_ERR_T_LIMIT
+    assert t(None, FAKE, FAKE, FAKE, FAKE, _capi.DTYPE_BF16, 16, 10, 2.0, 1.0, None) \
+        == _capi.DFSNN_ERR_NULL
     e = L.dfsnn_direct_euler_backward
     args = [FAKE] * 10 + [16, 100, 2.0, 1.0, 1.0, 1.0, 5.0, 1.0]
     assert e(*args, FAKE, 8, None) == _capi.DFSNN_ERR_WORKSPACE

@@ -219,6 +219,34 @@ def test_aligned_vs_oracle(T, N, tau, kind):
     assert_close(cpu(Wt.grad), r["gW"], what="grad_w")
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("T,N", [(8, 70001), (16, 4099), (16, 262144), (40, 1000)])
+def test_aligned_half_precision_io(dtype, T, N):
+    """Half-precision activations (autocast) are read and written in their own type by the
+    forward kernel; spikes and gradients equal the fp32 path on x.float() bit for bit, which is
+    what the reference's .float() / .to(dtype) casts compute (aligned_glmulti.py:112-145)."""
+    x, gS, _, v0 = rng_inputs(41 + T, T, N, "steady")
+    a, W = glmulti_tables(T)
+    xh = cuda(x).to(dtype)
+    gh = cuda(gS).to(dtype)
+    outs = []
+    for inp in (xh, xh.float()):
+        xr = inp.clone().requires_grad_(True)
+        vr = cuda(v0).requires_grad_(True)
+        ar, Wr = cuda(a).requires_grad_(True), cuda(W).requires_grad_(True)
+        s = alg.AlignedGLMulti.apply(xr, vr, ar, Wr, 2.0, TH, SG, 1, True)
+        assert s.dtype == inp.dtype
+        s.backward(gh.to(inp.dtype))
+        outs.append((s.detach().float(), xr.grad.float(), vr.grad, ar.grad, Wr.grad))
+    torch.cuda.synchronize()
+    (s1, gx1, gv1, ga1, gw1), (s2, gx2, gv2, ga2, gw2) = outs
+    assert_bitwise(cpu(s1), cpu(s2), what="spikes")
+    assert_bitwise(cpu(gx1.to(dtype).float()), cpu(gx2.to(dtype).float()), what="grad_x (as dtype)")
+    assert_bitwise(cpu(gv1), cpu(gv2), what="grad_v0")
+    assert_bitwise(cpu(ga1), cpu(ga2), what="grad_a")
+    assert_bitwise(cpu(gw1), cpu(gw2), what="grad_w")
+
+
 def test_aligned_history_rho():
     T, N = 16, 1000
     x, gS, _, v0 = rng_inputs(77, T, N)

@@ -241,6 +241,40 @@ def test_aligned_vs_reference_kernels(ref, T, kind, N, rho):
         native_aligned.HISTORY_RHO = old_native_rho
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_aligned_half_precision_vs_reference_kernels(ref, dtype):
+    """Under autocast the layer receives half-precision activations: the reference's
+    AlignedGLMulti casts them (.float(), .to(dtype)); this library reads and writes them in
+    their own type.  Spikes and every gradient are bit-identical."""
+    import aligned_glmulti as alg
+    old_backend = alg.BACKEND
+    alg.BACKEND = "cupy"
+    try:
+        T, N = 16, CONFIG2_N
+        x, gS, _, v0 = gen(T, N, 707, "config2")
+        v0.zero_()
+        a, W = glmulti_schedule(T)
+        xh, gh = x.to(dtype), gS.to(dtype)
+        res = []
+        for fn in (alg.AlignedGLMulti, native_aligned.AlignedGLMulti):
+            xr = xh.clone().requires_grad_(True)
+            vr, ar, Wr = (t.clone().requires_grad_(True) for t in (v0, a, W))
+            s = fn.apply(xr, vr, ar, Wr, TAU, TH, SG, 16, True)
+            s.backward(gh)
+            res.append((s.detach(), xr.grad, vr.grad, ar.grad, Wr.grad))
+        want, got = res
+        assert got[0].dtype == want[0].dtype == dtype and got[1].dtype == dtype
+        for what, p, q in zip(("spikes", "grad_x", "grad_v0"), got[:3], want[:3]):
+            assert torch.equal(p.view(torch.int16) if p.dtype != torch.float32 else p.view(torch.int32),
+                               q.view(torch.int16) if q.dtype != torch.float32 else q.view(torch.int32)), \
+                f"{dtype} {what}"
+        for what, p, q in zip(("grad_a", "grad_w"), got[3:], want[3:]):
+            scale = float(q.abs().max()) + 1e-30
+            assert float((p - q).abs().max()) <= 1e-4 * scale, f"{dtype} {what}"
+    finally:
+        alg.BACKEND = old_backend
+
+
 # -------------------------------------------------------------------------------------
 # the reference's LIFNeuronFDE, with its own kernels and with this library installed
 # -------------------------------------------------------------------------------------
