@@ -53,6 +53,9 @@ template <typename E>
 struct Io;
 template <>
 struct Io<float> {
+    using Raw2 = float2;                                  // two elements as loaded
+    static __device__ __forceinline__ Raw2 ld2raw(const void* p, long long i) { return ld2(p, i); }
+    static __device__ __forceinline__ float2 cvt2(Raw2 r) { return r; }
     static __device__ __forceinline__ float ld(const void* p, long long i) {
         return __ldcs(static_cast<const float*>(p) + i);
     }
@@ -66,36 +69,74 @@ struct Io<float> {
         __stcs(reinterpret_cast<float2*>(static_cast<float*>(p) + i), v);
     }
 };
+// two adjacent 16-bit elements as one 32-bit streaming access
+__device__ __forceinline__ uint32_t ld_cs_b32(const void* p) {
+    uint32_t v;
+    asm("ld.global.cs.b32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void st_cs_b32(void* p, uint32_t v) {
+    asm volatile("st.global.cs.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned short ld_cs_b16(const void* p) {
+    unsigned short v;
+    asm("ld.global.cs.b16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void st_cs_b16(void* p, unsigned short v) {
+    asm volatile("st.global.cs.b16 [%0], %1;" ::"l"(p), "h"(v) : "memory");
+}
+
 template <>
 struct Io<__half> {
+    using Raw2 = uint32_t;
+    static __device__ __forceinline__ Raw2 ld2raw(const void* p, long long i) {
+        return ld_cs_b32(static_cast<const __half*>(p) + i);
+    }
+    static __device__ __forceinline__ float2 cvt2(Raw2 u) {
+        return make_float2(__half2float(__ushort_as_half((unsigned short)(u & 0xffffu))),
+                           __half2float(__ushort_as_half((unsigned short)(u >> 16))));
+    }
     static __device__ __forceinline__ float ld(const void* p, long long i) {
-        return __half2float(__ldcs(static_cast<const __half*>(p) + i));
+        return __half2float(__ushort_as_half(ld_cs_b16(static_cast<const __half*>(p) + i)));
     }
     static __device__ __forceinline__ float2 ld2(const void* p, long long i) {
-        return __half22float2(__ldcs(reinterpret_cast<const __half2*>(static_cast<const __half*>(p) + i)));
+        const uint32_t u = ld_cs_b32(static_cast<const __half*>(p) + i);
+        return make_float2(__half2float(__ushort_as_half((unsigned short)(u & 0xffffu))),
+                           __half2float(__ushort_as_half((unsigned short)(u >> 16))));
     }
     static __device__ __forceinline__ void st(void* p, long long i, float v) {
-        __stcs(static_cast<__half*>(p) + i, __float2half_rn(v));
+        st_cs_b16(static_cast<__half*>(p) + i, __half_as_ushort(__float2half_rn(v)));
     }
     static __device__ __forceinline__ void st2(void* p, long long i, float2 v) {
-        __stcs(reinterpret_cast<__half2*>(static_cast<__half*>(p) + i), __float22half2_rn(v));
+        st_cs_b32(static_cast<__half*>(p) + i,
+                  (uint32_t)__half_as_ushort(__float2half_rn(v.x)) |
+                      ((uint32_t)__half_as_ushort(__float2half_rn(v.y)) << 16));
     }
 };
 template <>
 struct Io<__nv_bfloat16> {
+    using Raw2 = uint32_t;
+    static __device__ __forceinline__ Raw2 ld2raw(const void* p, long long i) {
+        return ld_cs_b32(static_cast<const __nv_bfloat16*>(p) + i);
+    }
+    static __device__ __forceinline__ float2 cvt2(Raw2 u) {
+        return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+    }
     static __device__ __forceinline__ float ld(const void* p, long long i) {
-        return __bfloat162float(__ldcs(static_cast<const __nv_bfloat16*>(p) + i));
+        return __uint_as_float((uint32_t)ld_cs_b16(static_cast<const __nv_bfloat16*>(p) + i) << 16);
     }
     static __device__ __forceinline__ float2 ld2(const void* p, long long i) {
-        return __bfloat1622float2(
-            __ldcs(reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(p) + i)));
+        const uint32_t u = ld_cs_b32(static_cast<const __nv_bfloat16*>(p) + i);
+        return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
     }
     static __device__ __forceinline__ void st(void* p, long long i, float v) {
-        __stcs(static_cast<__nv_bfloat16*>(p) + i, __float2bfloat16_rn(v));
+        st_cs_b16(static_cast<__nv_bfloat16*>(p) + i, __bfloat16_as_ushort(__float2bfloat16_rn(v)));
     }
     static __device__ __forceinline__ void st2(void* p, long long i, float2 v) {
-        __stcs(reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p) + i),
-               __float22bfloat162_rn(v));
+        st_cs_b32(static_cast<__nv_bfloat16*>(p) + i,
+                  (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v.x)) |
+                      ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v.y)) << 16));
     }
 };
 
@@ -179,11 +220,14 @@ __global__ void __launch_bounds__(128, 5) aln_fwd_x2(AlnArgs a) {
     // this thread's x rows and v0 are requested before the block stages W and checks it, so
     // their memory latency overlaps the staging and the block barrier
     const long long n = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
-    float2 xr[TB], v = f2(0.0f);
+    // the rows as loaded (half-precision pairs stay packed until their step uses them, so the
+    // loads are all in flight before any conversion waits on one)
+    typename Io<E>::Raw2 xr[TB];
+    float2 v = f2(0.0f);
     if (n < a.N) {
 #pragma unroll
         for (int t = 0; t < TB; ++t)
-            if (t < T) xr[t] = Io<E>::ld2(a.xio, t * a.N + n);
+            if (t < T) xr[t] = Io<E>::ld2raw(a.xio, t * a.N + n);
         v = *reinterpret_cast<const float2*>(a.v0 + n);
     }
     for (int e = threadIdx.x; e < TB * TB; e += blockDim.x) {
@@ -213,7 +257,7 @@ __global__ void __launch_bounds__(128, 5) aln_fwd_x2(AlnArgs a) {
     for (int t = 0; t < TB; ++t) {
         if (t < T) {
             // every product is a pmz2 product, so the sums that consume them may be packed
-            const float2 xm = psub2(xr[t], v);
+            const float2 xm = psub2(Io<E>::cvt2(xr[t]), v);
             const float2 d = TP2 ? pmz2(xm, inv2, nz2)
                                  : make_float2(__fdiv_rn(xm.x, a.tau), __fdiv_rn(xm.y, a.tau));
             const float2 pred = padd2(v, d);
