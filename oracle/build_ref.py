@@ -396,6 +396,33 @@ def cuda_sources(reference):
     return out
 
 
+_C_SIZES = {"int": 4, "unsigned": 4, "unsigned int": 4, "float": 4, "double": 8,
+            "long long": 8, "unsigned long long": 8, "size_t": 8, "bool": 1, "char": 1}
+
+
+def kernel_params(code, name):
+    """Byte size of every parameter of kernel `name` in `code` (8 for pointers), read from
+    its declaration, so that a launch can be checked against it before it reaches the GPU."""
+    import re
+    m = re.search(r"__global__\s+void\s+" + re.escape(name) + r"\s*\(([^)]*)\)", code)
+    if not m:
+        raise RuntimeError(f"kernel {name}: declaration not found")
+    sizes = []
+    for decl in m.group(1).split(","):
+        decl = decl.strip()
+        if not decl:
+            continue
+        if "*" in decl:
+            sizes.append(8)
+            continue
+        words = [w for w in re.sub(r"\b(const|__restrict__|volatile)\b", " ", decl).split()]
+        ctype = " ".join(words[:-1])
+        if ctype not in _C_SIZES:
+            raise RuntimeError(f"kernel {name}: unknown parameter type '{ctype}'")
+        sizes.append(_C_SIZES[ctype])
+    return sizes
+
+
 def build_cuda(reference, nvcc=None):
     import json
     import re
@@ -415,7 +442,8 @@ def build_cuda(reference, nvcc=None):
         cubin = os.path.join(CUDA_OUT, key + ".cubin")
         with open(src, "w") as f:
             f.write(code)
-        manifest[key] = {"cubin": key + ".cubin", "names": names, "options": list(options)}
+        manifest[key] = {"cubin": key + ".cubin", "names": names, "options": list(options),
+                         "params": {n: kernel_params(code, n) for n in names}}
         procs.append(subprocess.Popen([nvcc, "-cubin", *CUDA_ARCH, *options, "-w", src,
                                        "-o", cubin]))
     if any(p.wait() != 0 for p in procs):

@@ -6,7 +6,9 @@ tests put oracle/cupy_standin on sys.path; nothing of the library imports it).
 Covered: RawKernel(code, name, options) and its launch (grid, block, args, shared_mem,
 stream), from_dlpack of torch tensors, the scalar types (int32, float32, ...), and
 cuda.Device / cuda.ExternalStream / cuda.get_current_stream.  Everything else the real
-CuPy offers (asarray, empty, array arithmetic) raises NotImplementedError.
+CuPy offers (asarray, empty, array arithmetic) raises NotImplementedError.  Unlike CuPy, a
+launch whose arguments do not match the kernel's declared parameters (count and byte sizes,
+recorded in the manifest) is refused with TypeError before it reaches the GPU.
 
 CuPy compiles a RawKernel's source with NVRTC when it is first launched.  Here the same
 source texts, with the same options, are compiled ahead of time by oracle/build_ref.py
@@ -151,6 +153,7 @@ class RawKernel:
         if name not in entry["names"]:
             raise RuntimeError(f"RawKernel {name}: not a kernel of this source")
         self._cubin = os.path.join(KERNEL_DIR, entry["cubin"])
+        self._params = entry["params"][name]     # byte size of every declared parameter
 
     def _function(self, device):
         with _lock:
@@ -177,6 +180,12 @@ class RawKernel:
             held.append(c)
             if device is None and dev is not None:
                 device = dev
+        # the driver reads every declared parameter from the argument list: a launch with a
+        # different count or size would read past it, so it is refused here instead
+        sizes = [ctypes.sizeof(c) for c in held]
+        if sizes != self._params:
+            raise TypeError(f"RawKernel {self.name}: arguments of {sizes} bytes for parameters "
+                            f"of {self._params} bytes; not launched")
         if device is None:
             device = torch.cuda.current_device()
         fn = self._function(device)

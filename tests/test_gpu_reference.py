@@ -404,3 +404,86 @@ def test_cnn128_example_drop_in(ref):
             assert float((gg - w).abs().max()) <= 1e-4 * (float(w.abs().max()) + 1e-30), n
         else:
             assert_bitwise(got_grads[n], want_grads[n], f"CNN128 grad {n}")
+
+
+# -------------------------------------------------------------------------------------
+# history-table Functions (VO-GL1, FAGL1, VO-PREDICTOR) and direct Euler
+# -------------------------------------------------------------------------------------
+HB, RM = 0.25, 0.2
+HIST_FN = {"vogl1": "LIFFDEVOGL1Function", "fagl1": "LIFFDEFAGL1Function",
+           "vopred": "LIFFDEVOPREDICTORFunction"}
+# VO-PREDICTOR is not here: the reference's LIFFDEVOPREDICTORFunction.backward launches its
+# seven-pointer kernel with six arrays (fde_cupy_kernels_all.py:1160-1170 against :1047-1062),
+# so its GPU path reads past its argument list; VO-PREDICTOR is pinned against the host build
+# of the same kernel text (whose launcher passes all seven) and the oracle instead.
+HIST_CASES = [(kind, pb, full, T) for kind in ("vogl1", "fagl1") for pb in (False, True)
+              for full in (False, True) for T in (8, 16)]
+
+
+def hist_tables(kind, T, B, per_batch, seed):
+    """Causal tables of the shapes the reference's builders produce, random magnitudes."""
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    shape = (T, B, T) if per_batch else (T, T)
+    mask = torch.tril(torch.ones(T, T, device=DEV), -1)
+    W = (torch.rand(shape, device=DEV, generator=g) * 0.6 - 0.3) * (mask[:, None, :] if per_batch else mask)
+    scale = None if kind == "fagl1" else \
+        torch.rand((T, B) if per_batch else (T,), device=DEV, generator=g) * 0.3 + 0.1
+    return scale, W.contiguous()
+
+
+def run_hist(fn, kind, x, v0, scale, W, B, gS, full):
+    xr, vr, Wr = (t.clone().requires_grad_(True) for t in (x, v0, W))
+    sr = None if scale is None else scale.clone().requires_grad_(True)
+    if kind == "fagl1":
+        s = fn.apply(xr, vr, Wr, TAU, HB, TH, SG, B, full)
+    elif kind == "vogl1":
+        s = fn.apply(xr, vr, sr, Wr, TAU, TH, SG, B, full)
+    else:
+        s = fn.apply(xr, vr, sr, Wr, TAU, TH, SG, RM, B)
+    s.backward(gS)
+    return s.detach(), xr.grad, vr.grad, Wr.grad, None if sr is None else sr.grad
+
+
+@pytest.mark.parametrize("kind,per_batch,full,T", HIST_CASES)
+def test_history_functions_vs_reference_kernels(ref, kind, per_batch, full, T):
+    """Spikes, grad_x and grad_v0 bit-identical to the reference's own kernels; the table
+    gradients within 5e-3 of their scale -- the reference's FAGL1 weight gradient with a
+    shared table is a TF32 matmul (fde_cupy_kernels_all.py:1489-1496), so it is the looser
+    side here (the 1e-5 check of these reductions is against the float64 oracle)."""
+    B, N = 16, 1 << 20
+    x, gS, _, v0 = gen(T, N, 909 + T, "spiking")
+    scale, W = hist_tables(kind, T, B, per_batch, 31 + T)
+    name = HIST_FN[kind]
+    want = run_hist(getattr(ref.kernels, name), kind, x, v0, scale, W, B, gS, full)
+    got = run_hist(getattr(fde_kernels, name), kind, x, v0, scale, W, B, gS, full)
+    tag = f"{kind} per_batch={per_batch} full={full} T={T}"
+    for what, p, q in zip(("spikes", "grad_x", "grad_v0"), got[:3], want[:3]):
+        assert_bitwise(p, q, f"{tag} {what}")
+    for what, p, q in zip(("grad_W", "grad_scale"), got[3:], want[3:]):
+        if q is None:
+            continue
+        scale_q = float(q.abs().max()) + 1e-30
+        assert float((p - q).abs().max()) <= 5e-3 * scale_q, f"{tag} {what}"
+
+
+def test_direct_euler_vs_reference_kernels(ref):
+    """direct_euler_cupy.lif_like_euler_cupy against this library's: spikes, final state,
+    grad_x and grad_z0 bit-identical; the three scalar gradients, which the reference sums
+    with per-thread float atomics in no fixed order, within 1e-4 of their scale."""
+    from dfsnn_b200 import direct_euler as deu
+    T, N = 16, 1 << 20
+    x, gS, _, z0 = gen(T, N, 4242, "spiking")
+    gzf = torch.randn(N, device=DEV, generator=torch.Generator(device=DEV).manual_seed(5))
+    res = []
+    for fn in (ref.euler.lif_like_euler_cupy, deu.lif_like_euler_cupy):
+        xr, zr = x.clone().requires_grad_(True), z0.clone().requires_grad_(True)
+        pt = [torch.tensor(v, device=DEV, requires_grad=True) for v in (1.2, 0.9, 0.1)]
+        s, zf = fn(xr, zr, pt[0], pt[1], pt[2], 2.0, 1.0, 1.0, 1.0, SG, 0.5)
+        torch.autograd.backward([s, zf], [gS, gzf])
+        torch.cuda.synchronize()
+        res.append((s.detach(), zf.detach(), xr.grad, zr.grad, torch.stack([p.grad for p in pt])))
+    want, got = res
+    for what, p, q in zip(("spikes", "z_final", "grad_x", "grad_z0"), got[:4], want[:4]):
+        assert_bitwise(p, q, f"direct Euler {what}")
+    scale_q = float(want[4].abs().max()) + 1e-30
+    assert float((got[4] - want[4]).abs().max()) <= 1e-4 * scale_q, "direct Euler scalar grads"

@@ -46,3 +46,19 @@ def test_standin_rejects_unbuilt_source(ref):
         cupy.RawKernel(alg.FORWARD, "aligned_forward")
     with pytest.raises(NotImplementedError):
         cupy.asarray([1.0])
+
+
+def test_standin_refuses_mismatched_arguments(ref):
+    """A launch whose arguments do not match the kernel's declared parameters is refused on
+    the host (the driver would read past the argument list).  The reference's own
+    LIFFDEVOPREDICTORFunction.backward is such a launch: six arrays for the seven pointers of
+    lif_fde_vo_predictor_backward_kernel (fde_cupy_kernels_all.py:1160-1170, :1047-1062)."""
+    import cupy
+    import numpy as np
+    k = cupy.RawKernel(ref.kernels.vo_predictor_backward_kernel_code,
+                       "lif_fde_vo_predictor_backward_kernel")
+    assert len(k._params) == 15 and k._params[:7] == [8] * 7
+    with pytest.raises(TypeError, match="not launched"):
+        k((1,), (256,), (np.int32(1), np.float32(2.0)))
+    with pytest.raises(TypeError, match="not launched"):       # sizes, not just the count
+        k((1,), (256,), tuple([1] * 7 + [1] * 4 + [np.float32(1.0)] * 4))   # int64, not int32
