@@ -402,29 +402,36 @@ def make_layers(device, combos=None, batch=None):
     return layers
 
 
-def run_gpu_reference(args, x16, gS16, gV16, dev):
+def run_gpu_reference(args, x16, gS16, gV16, dev, combos=None, batch=None, max_steps=50,
+                      warmup=None):
     """The reference's own GPU path on this GPU, same workload: the unmodified reference
     LIFNeuronFDE(backend='cupy') (the staged package in baseline/_ref) whose CuPy launches
     run the reference's own kernel source texts, compiled for sm_100 with its options
     (oracle/build_ref.py, launched by oracle/cupy_standin), and its own PyTorch glue
-    (torch.sum / torch.matmul for the glmulti parameter gradients).  Same layers, inputs and
-    step as the native arm; CUDA events on the same stream."""
+    (torch.sum / torch.matmul for the glmulti parameter gradients).  For the aligned layers
+    the examples' own install('cupy') binds their AlignedGLMulti first, as make_model does.
+    Same layers, inputs and step as the native arm; CUDA events on the same stream."""
     import torch
     from oracle import reference_gpu
+    combos = COMBOS if combos is None else combos
+    batch = SHAPE[0] if batch is None else batch
     why = reference_gpu.missing()
     if why:
         return {"unavailable": why}
-    ref = reference_gpu.Reference()
+    aligned = any(sch == "aligned" for _, sch in combos)
+    ref = reference_gpu.Reference("cnn128" if aligned else None)
     try:
         ref.use_reference()
+        if aligned:
+            import aligned_glmulti as example_alg
+            example_alg.install("cupy")
         layers = {}
-        for T, sch in COMBOS:
-            if sch == "aligned":
-                return {"unavailable": "the aligned workload has no library-path reference"}
+        for T, sch in combos:
+            method = "glmulti" if sch == "aligned" else sch
             kw = dict(tau=TAU, threshold=TH, surrogate_grad_scale=SG, surrogate_function="arctan",
-                      T=T, method=sch, step_size=H, batchsize=SHAPE[0], step_mode="m",
+                      T=T, method=method, step_size=H, batchsize=batch, step_mode="m",
                       backend="cupy")
-            if sch == "glmulti":
+            if method == "glmulti":
                 kw.update(beta=MULTI_BETA[0], multi_beta=MULTI_BETA, multi_coefficient=MASSES,
                           learn_coefficient=True, coefficient_constraint="softplus",
                           glmulti_history_grad="full")
@@ -433,10 +440,12 @@ def run_gpu_reference(args, x16, gS16, gV16, dev):
             layers[(T, sch)] = ref.neuron.LIFNeuronFDE(**kw).to(dev)
 
         def step():
-            for T, sch in COMBOS:
-                layer_step(layers[(T, sch)], x16[:T], gS16[:T], gV16[:T], sch != "glmulti")
+            for T, sch in combos:
+                layer_step(layers[(T, sch)], x16[:T], gS16[:T], gV16[:T],
+                           sch not in ("glmulti", "aligned"))
 
-        K, W = min(args.steps, 50), max(args.warmup, 3)
+        K = min(args.steps, max_steps)
+        W = max(args.warmup, 3) if warmup is None else warmup
         for _ in range(W):
             step()
         torch.cuda.synchronize()
@@ -448,11 +457,13 @@ def run_gpu_reference(args, x16, gS16, gV16, dev):
         end.record()
         torch.cuda.synchronize()
         ms = start.elapsed_time(end) / K
-        return {"value": units_per_step(math.prod(SHAPE)) / (ms / 1e3), "unit": UNIT,
+        neurons = x16[0].numel()
+        return {"value": sum(T * neurons for T, _ in combos) / (ms / 1e3), "unit": UNIT,
                 "ms_per_step": ms, "steps": K, "warmup": W,
                 "impl": "unmodified reference LIFNeuronFDE(backend='cupy') and autograd "
-                        "Functions; their kernel source texts compiled for sm_100 with the "
-                        "reference's options, launched through a CuPy stand-in (driver API)"}
+                        "Functions" + (" with the examples' AlignedGLMulti" if aligned else "") +
+                        "; their kernel source texts compiled for sm_100 with the reference's "
+                        "options, launched through a CuPy stand-in (driver API)"}
     finally:
         ref.close()
 
@@ -501,7 +512,7 @@ def fp32_roofline(d, combos, neurons, K, mhz, sms):
                     "N*T(T-1)/2 terms per call", "traffic": None}
 
 
-def measure_sub_workload(kind, K, W, dev, world, rank):
+def measure_sub_workload(args, kind, K, W, dev, world, rank, gpu_reference=False):
     """Device-timed record of one more layer configuration at this N (same step, timing
     and max-over-ranks rule as the headline): the long-history configuration or the
     examples' aligned glmulti layer."""
@@ -569,10 +580,19 @@ def measure_sub_workload(kind, K, W, dev, world, rank):
                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
                     "algorithmic_bytes_per_launch": d["bytes_per_call"], "traffic": None}
     units = sum(T * neurons for T, _ in combos)
-    return {"workload": cfg["desc"], "value": world * K * units / (ms / 1e3), "unit": UNIT,
-            "ms_per_step": ms / K, "steps": K, "warmup": W, "n_gpus": world,
-            "gpu_launches": timer.total_launches(), "roofline": roofline, "kernels": kernels,
-            "clocks": clk}
+    rec = {"workload": cfg["desc"], "value": world * K * units / (ms / 1e3), "unit": UNIT,
+           "ms_per_step": ms / K, "steps": K, "warmup": W, "n_gpus": world,
+           "gpu_launches": timer.total_launches(), "roofline": roofline, "kernels": kernels,
+           "clocks": clk}
+    if world == 1 and gpu_reference:
+        # the reference's own GPU path on the same layers and inputs (bounded steps)
+        long_t = kind == "long"      # about a second per reference step: bounded sample
+        gref = run_gpu_reference(args, x, gS, gV, dev, combos, shape[0],
+                                 max_steps=3 if long_t else K, warmup=1 if long_t else None)
+        if gref.get("value"):
+            gref["native_over_reference"] = rec["value"] / gref["value"]
+        rec["gpu_reference"] = gref
+    return rec
 
 
 def run_native(args):
@@ -702,7 +722,8 @@ def run_native(args):
         layers.clear()
         torch.cuda.empty_cache()
         for kind, Ks in (("long", max(1, min(K, args.sub_steps))), ("aligned", K)):
-            line[kind] = measure_sub_workload(kind, Ks, W, dev, world, rank)
+            line[kind] = measure_sub_workload(args, kind, Ks, W, dev, world, rank,
+                                              gpu_reference=not args.no_gpu_reference)
     if args.workload == "layers" and not args.no_network:
         # the network configuration at every N: CNN128 synthetic training, data-parallel
         Kn = max(1, args.network_steps)
