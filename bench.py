@@ -578,7 +578,8 @@ def measure_sub_workload(args, kind, K, W, dev, world, rank, gpu_reference=False
         roofline = {"bound": "hbm", "kernel": name, "achieved": d["gbs"], "peak": peak,
                     "unit": "GB/s", "frac": d["gbs"] / peak if d["gbs"] else None,
                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
-                    "algorithmic_bytes_per_launch": d["bytes_per_call"], "traffic": None}
+                    "algorithmic_bytes_per_launch": d["bytes_per_call"],
+                    "traffic": ncu_traffic(name, sorted({T for T, _ in combos}))}
     units = sum(T * neurons for T, _ in combos)
     rec = {"workload": cfg["desc"], "value": world * K * units / (ms / 1e3), "unit": UNIT,
            "ms_per_step": ms / K, "steps": K, "warmup": W, "n_gpus": world,
