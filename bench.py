@@ -740,6 +740,16 @@ def run_native(args):
                                                 "example-reference")
             net["reference_kernels"] = refnet
         line["network"] = net
+        # the second network configuration: Spikformer256 (T = 8), same measurements
+        spk = measure_network(args, "spikformer256", dev, world, local, False, Kn, 3,
+                              args.network_source)
+        spk["amp"] = measure_network(args, "spikformer256", dev, world, local, True, Kn, 3,
+                                     args.network_source)
+        if args.network_source == "example" and not args.no_gpu_reference:
+            refspk = measure_network(args, "spikformer256", dev, world, local, False, Kn, 3,
+                                     "example-reference")
+            spk["reference_kernels"] = refspk
+        line["network_spikformer256"] = spk
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -1053,12 +1063,12 @@ def make_cnn128(dev):
 NETWORKS = {
     # name: (builder, T, B, classes, frame kind, description)
     "cnn128": ("make_cnn128", CNN_T, CNN_B, CNN_CLASSES, "poisson",
-               "CNN128 (5x conv128-BN-LIF-pool, fc512-LIF, fc256-LIF, fc11) training step, SGD, "
+               "CNN128 (5x conv128-BN-LIF-pool, fc512-LIF, fc256-LIF, fc11) training step, AdamW, "
                "LIFNeuronFDE glmulti aligned full history, shared Softplus masses, T=16, B=16 per "
                "GPU, frames [16,16,2,128,128] Bernoulli(0.05)*Poisson(1), 11 classes"),
     "spikformer256": ("make_spikformer256", SPK_T, SPK_B, SPK_CLASSES, "bernoulli",
                       "Spikformer256 (SPS 2->256, 64 tokens, depth 2, 16 heads, MLP 1024) "
-                      "training step, SGD, LIFNeuronFDE glmulti aligned full history, shared "
+                      "training step, AdamW, LIFNeuronFDE glmulti aligned full history, shared "
                       "Softplus masses, T=8, B=16 per GPU, frames [8,16,2,128,128] "
                       "Bernoulli(0.05), 300 classes"),
 }
@@ -1083,7 +1093,8 @@ def example_network(name, dev, reference_kernels=False):
     from oracle import reference_gpu
     if not reference_gpu.staged() or (reference_kernels and reference_gpu.missing()):
         return None
-    from dfsnn_b200 import integrate
+    from dfsnn_b200 import fde_kernels, integrate
+    library = fde_kernels.LIFFDEGLMultiFunction      # before the example's install() patches it
     ref = reference_gpu.Reference(EXAMPLE_DIRS[name], standin=reference_kernels)
     if reference_kernels:
         ref.use_reference()
@@ -1098,8 +1109,6 @@ def example_network(name, dev, reference_kernels=False):
         import aligned_glmulti as alg
         model = alg.make_model("cupy", MULTI_BETA, True, MASSES, batch=SPK_B, T=SPK_T,
                                num_classes=SPK_CLASSES)
-    from dfsnn_b200 import fde_kernels
-    library = fde_kernels.LIFFDEGLMultiFunction
     if not reference_kernels:
         integrate.rebind_aligned(alg)
     model = model.to(dev)

@@ -306,3 +306,31 @@ def test_bench_clock_sampler_nvml(monkeypatch):
     assert rec["source"] == "nvml" and rec["sm_max_mhz"] == 1965.0
     assert rec["reasons"] == ["sw_power_cap"] and rec["samples"] >= 3
     assert 1700.0 <= rec["sm_mhz"] <= 1900.0
+
+
+def test_bench_example_networks_bind_the_native_function(monkeypatch):
+    """bench.py builds the reference examples' own CNN128 / Spikformer256 modules with this
+    library installed (install, the example's install('cupy'), rebind_aligned), imported with
+    no CuPy at all, and puts everything back afterwards (no GPU needed to build them)."""
+    import importlib
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    monkeypatch.syspath_prepend(repo)
+    from oracle import reference_gpu
+    if not reference_gpu.staged():
+        pytest.skip("reference not staged (oracle/stage_ref.py)")
+    bench = importlib.import_module("bench")
+    original = fde_kernels.LIFFDEGLMultiFunction
+    for name, n_lif in (("cnn128", 7), ("spikformer256", 19)):
+        model, reset, close = bench.example_network(name, torch.device("cpu"))
+        try:
+            assert "cupy" not in sys.modules
+            assert fde_kernels.LIFFDEGLMultiFunction is alg.AlignedGLMulti
+            example = sys.modules["aligned_glmulti"]
+            assert example.AlignedGLMulti is alg.AlignedGLMulti
+            lifs = [m for m in model.modules() if type(m).__name__ in ("LIFNeuronFDE", "Neuron")]
+            assert len(lifs) == n_lif
+            reset()
+        finally:
+            close()
+        assert fde_kernels.LIFFDEGLMultiFunction is original
+        assert not any(k.startswith("spikeDE_dis") for k in sys.modules)
