@@ -725,6 +725,10 @@ def run_native(args):
         for kind, Ks in (("long", max(1, min(K, args.sub_steps))), ("aligned", K)):
             line[kind] = measure_sub_workload(args, kind, Ks, W, dev, world, rank,
                                               gpu_reference=not args.no_gpu_reference)
+        # the history-table Functions (every N) and the SNN wrapper's GL integrator (one GPU)
+        line["history"] = measure_history(args, dev, world, rank, K, W)
+        if world == 1:
+            line["integrator"] = measure_integrator(args, dev, max(1, min(K, args.sub_steps)), W)
     if args.workload == "layers" and not args.no_network:
         # the network configuration at every N: CNN128 synthetic training, data-parallel
         Kn = max(1, args.network_steps)
@@ -1291,31 +1295,23 @@ def torch_rand(shape, dev, g):
     return torch.rand(shape, device=dev, generator=g)
 
 
-def run_history(args):
+def measure_history(args, dev, world, rank, K, W, shape=(16, 128, 64, 64), ts=(8, 16)):
     """One step: VO-GL1 (full history), FAGL1 (full history) and VO-PREDICTOR, each forward +
     backward with gradients for x, scale and weights, at T = 8 and 16 on [T, N] inputs with
-    per-sample tables (B = 16 samples of N/16 neurons)."""
+    per-sample tables (B = 16 samples of N/16 neurons).  Returns the record."""
     import torch
     import torch.distributed as dist
     from dfsnn_b200 import fde_kernels as fk
     from dfsnn_b200 import profiling
-    from dfsnn_b200.distributed import allreduce_flat, init_process_group
+    from dfsnn_b200.distributed import allreduce_flat
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        init_process_group("nccl", timeout_s=300, device=dev)
-    K, W = args.steps, max(args.warmup, 3)
-    B = SHAPE[0]
-    neurons = math.prod(SHAPE)
+    B = shape[0]
+    neurons = math.prod(shape)
     g = torch.Generator(device=dev).manual_seed(4321 + rank)
     x16 = torch.randn((16, neurons), device=dev, generator=g).mul_(0.5).add_(0.3)
     gS16 = torch.randn((16, neurons), device=dev, generator=g)
-    tabs = {T: history_tables(T, B, dev, g) for T in TS}
-    for T in TS:
+    tabs = {T: history_tables(T, B, dev, g) for T in ts}
+    for T in ts:
         for kind in HIST_KINDS:
             sc, Wt = tabs[T][kind]
             tabs[T][kind] = (None if sc is None else sc.detach().requires_grad_(True),
@@ -1325,7 +1321,7 @@ def run_history(args):
 
     def step():
         pgrads = []
-        for T in TS:
+        for T in ts:
             for kind in HIST_KINDS:
                 sc, Wt = tabs[T][kind]
                 x = x16[:T].detach().requires_grad_(True)
@@ -1349,7 +1345,7 @@ def run_history(args):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(dev.index)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     with profiling.NativeCallTimer() as timer:
@@ -1365,7 +1361,7 @@ def run_history(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    units = sum(TS) * neurons * len(HIST_KINDS)
+    units = sum(ts) * neurons * len(HIST_KINDS)
     summary = timer.summary()
     peak, peak_src = measured_hbm_peak()
     dom = max(summary.items(), key=lambda kv: kv[1]["ms_total"]) if summary else None
@@ -1376,28 +1372,47 @@ def run_history(args):
                     "unit": "GB/s", "frac": d["gbs"] / peak if d["gbs"] else None,
                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
                     "algorithmic_bytes_per_launch": d["bytes_per_call"], "traffic": None}
+    return {
+        "metric": "LIF-FDE history-table Functions neuron-timesteps/s fwd+bwd",
+        "value": world * K * units / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": ms / K,
+        "workload": "LIFFDEVOGL1Function (full history), LIFFDEFAGL1Function (full history), "
+                    "LIFFDEVOPREDICTORFunction fwd+bwd with grads of x, scale and weights; "
+                    "per-sample tables, B=16, x [T, 8,388,608] ~N(0.3,0.5^2), T=8 and 16",
+        "neurons_per_gpu": neurons,
+        "parallelism": f"dp{world}" + (" (one NCCL all-reduce of the table grads per step)"
+                                       if world > 1 else ""),
+        "gpu_launches": timer.total_launches(),
+        "roofline": roofline,
+        "kernels": {k: {"calls_per_step": v["calls"] / K,
+                        "ms_per_call": round(v["ms_per_call"], 4),
+                        "gbs": round(v["gbs"], 1) if v["gbs"] else None,
+                        "frac_of_hbm": round(v["gbs"] / peak, 4) if v["gbs"] else None}
+                    for k, v in summary.items()},
+        "clocks": clk,
+    }
+
+
+def run_history(args):
+    import torch
+    import torch.distributed as dist
+    from dfsnn_b200.distributed import init_process_group
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        init_process_group("nccl", timeout_s=300, device=dev)
+    rec = measure_history(args, dev, world, rank, args.steps, max(args.warmup, 3), SHAPE, TS)
     if rank == 0:
-        line = {
-            "metric": "LIF-FDE history-table Functions neuron-timesteps/s fwd+bwd",
-            "value": world * K * units / (ms / 1e3), "unit": UNIT, "n_gpus": world,
-            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "LIFFDEVOGL1Function (full history), LIFFDEFAGL1Function "
-                       "(full history), LIFFDEVOPREDICTORFunction fwd+bwd with grads of x, scale "
-                       "and weights; per-sample tables, B=16, x [T, 8,388,608] ~N(0.3,0.5^2), "
-                       "T=8 and 16", "neurons_per_gpu": neurons, "T": list(TS),
-                       "l2": "inputs larger than L2 (no flush)",
-                       "parallelism": f"dp{world}" + (" (one NCCL all-reduce of the table grads "
-                                                      "per step)" if world > 1 else "")},
-            "gpu_launches": timer.total_launches(),
-            "roofline": roofline,
-            "kernels": {k: {"calls_per_step": v["calls"] / K,
-                            "ms_per_call": round(v["ms_per_call"], 4),
-                            "gbs": round(v["gbs"], 1) if v["gbs"] else None,
-                            "frac_of_hbm": round(v["gbs"] / peak, 4) if v["gbs"] else None}
-                        for k, v in summary.items()},
-            "clocks": clk,
-        }
+        line = dict(rec)
+        line.update({"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                     "dtype": "f32", "data": "synthetic",
+                     "config": {"workload": rec["workload"], "neurons_per_gpu": rec["neurons_per_gpu"],
+                                "T": list(TS), "l2": "inputs larger than L2 (no flush)",
+                                "parallelism": rec["parallelism"]}})
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -1406,6 +1421,15 @@ def run_history(args):
 
 
 def run_integrator(args):
+    import torch
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    line = measure_integrator(args, dev, args.steps, max(args.warmup, 3))
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def measure_integrator(args, dev, K, W):
     """One step: the SNN wrapper's multi-term GL integration (forward_glmulti_cupy, as
     FDEAdjointMethod runs it, without autograd) over T = 64 steps of a [16, 64, 64, 64] =
     4,194,304-element state and its adjoint (backward_glmulti_cupy) over the same grid.  The
@@ -1415,9 +1439,6 @@ def run_integrator(args):
     import torch
     from dfsnn_b200 import fde_solver, profiling
 
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
-    K, W = args.steps, max(args.warmup, 3)
     T = 64
     shape = (16, 64, 64, 64)
     g = torch.Generator(device=dev).manual_seed(7)
@@ -1489,8 +1510,7 @@ def run_integrator(args):
                     for k, v in summary.items()},
         "clocks": clk,
     }
-    print(json.dumps(line), flush=True)
-    return 0
+    return line
 
 
 def main():
