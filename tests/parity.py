@@ -22,7 +22,7 @@ def assert_spikes(got, ref, p_ref, th, band=BAND):
 
 def assert_close(got, ref, rtol=RTOL, atol_scale=None, mask=None, what=""):
     """|got-ref| <= rtol*(|ref| + s), s = atol_scale or the rms of ref (so values that are
-    small only through cancellation are judged at the scale of their inputs)."""
+    small only through cancellation are measured at the scale of their inputs)."""
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     if mask is not None and got.ndim == 2:
