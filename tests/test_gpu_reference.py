@@ -487,3 +487,45 @@ def test_direct_euler_vs_reference_kernels(ref):
         assert_bitwise(p, q, f"direct Euler {what}")
     scale_q = float(want[4].abs().max()) + 1e-30
     assert float((got[4] - want[4]).abs().max()) <= 1e-4 * scale_q, "direct Euler scalar grads"
+
+
+# -------------------------------------------------------------------------------------
+# edge shapes: short and odd T, single neurons, N not a multiple of 4 / 32 / 256
+# -------------------------------------------------------------------------------------
+EDGE = [(T, N) for T in (1, 3, 17, 33) for N in (1, 255, 100003)]
+
+
+@pytest.mark.parametrize("T,N", EDGE)
+@pytest.mark.parametrize("scheme", ["gl", "trap", "predictor", "glmulti_full", "glmulti_trunc",
+                                    "aligned"])
+def test_edge_shapes_vs_reference_kernels(ref, scheme, T, N):
+    """Odd T and N take this library's fallback kernels (block-tiled, scalar, or the T > 32
+    paths); per-neuron outputs stay bit-identical to the reference's own kernels."""
+    x, gS, gV, v0 = gen(T, N, 77 * T + N, "spiking")
+    if scheme in ("gl", "trap", "predictor"):
+        name, args = single_args(scheme, T)
+        want = run_single(getattr(ref.kernels, name), x, v0, args, gS, gV)
+        got = run_single(getattr(fde_kernels, name), x, v0, args, gS, gV)
+        for what, a, b in zip(("spikes", "membrane", "grad_x", "grad_v0"), got, want):
+            assert_bitwise(a, b, f"{scheme} T={T} N={N} {what}")
+        return
+    scale, W = glmulti_schedule(T)
+    if scheme == "aligned":
+        import aligned_glmulti as alg
+        old = alg.BACKEND
+        alg.BACKEND = "cupy"
+        try:
+            v0 = torch.zeros_like(v0)
+            want = run_glmulti(alg.AlignedGLMulti, x, v0, scale, W, gS, True)
+            got = run_glmulti(native_aligned.AlignedGLMulti, x, v0, scale, W, gS, True)
+        finally:
+            alg.BACKEND = old
+    else:
+        full = scheme == "glmulti_full"
+        want = run_glmulti(ref.kernels.LIFFDEGLMultiFunction, x, v0, scale, W, gS, full)
+        got = run_glmulti(fde_kernels.LIFFDEGLMultiFunction, x, v0, scale, W, gS, full)
+    for what, a, b in zip(("spikes", "grad_x", "grad_v0"), got[:3], want[:3]):
+        assert_bitwise(a, b, f"{scheme} T={T} N={N} {what}")
+    for what, a, b in zip(("grad_scale", "grad_W"), got[3:], want[3:]):
+        s = float(b.abs().max()) + 1e-30
+        assert float((a - b).abs().max()) <= 1e-4 * s, f"{scheme} T={T} N={N} {what}"
