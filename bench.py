@@ -497,6 +497,13 @@ SUB_WORKLOADS = {
 }
 
 
+def by_steps_table(timer, K, peak):
+    """Per-kernel, per-T breakdown of the timed region (ms per call, fraction of HBM)."""
+    return {k: {"calls_per_step": v["calls"] / K, "ms_per_call": round(v["ms_per_call"], 4),
+                "frac_of_hbm": round(v["gbs"] / peak, 4) if v["gbs"] else None}
+            for k, v in timer.summary_by_steps().items()}
+
+
 def fp32_roofline(d, combos, neurons, K, mhz, sms):
     """Roofline of the single-order forward at T >= 64: its Kahan history chains (a fused
     multiply-add and three adds per term, in a fixed order) bound it on the FP32 lanes at
@@ -584,6 +591,7 @@ def measure_sub_workload(args, kind, K, W, dev, world, rank, gpu_reference=False
     rec = {"workload": cfg["desc"], "value": world * K * units / (ms / 1e3), "unit": UNIT,
            "ms_per_step": ms / K, "steps": K, "warmup": W, "n_gpus": world,
            "gpu_launches": timer.total_launches(), "roofline": roofline, "kernels": kernels,
+           "kernels_by_T": by_steps_table(timer, K, peak),
            "clocks": clk}
     if world == 1 and gpu_reference:
         # the reference's own GPU path on the same layers and inputs (bounded steps)
@@ -694,6 +702,7 @@ def run_native(args):
         "gpu_launches": launches,
         "roofline": roofline,
         "kernels": kernels,
+        "kernels_by_T": by_steps_table(timer, K, peak),
         "clocks": clk,
         "e2e": e2e,
     }

@@ -49,7 +49,7 @@ class AlignedGLMulti(torch.autograd.Function):
         T, N = x.shape
         s = torch.empty_like(x)
         with torch.cuda.device(x.device), _prof.native_call(
-                "aligned_forward", 1, _prof.glmulti_forward_bytes(T, N, elem), x.device):
+                "aligned_forward", 1, _prof.glmulti_forward_bytes(T, N, elem), x.device, steps=T):
             code = _capi.lib().dfsnn_aligned_forward_typed(
                 _capi.ptr(x), _capi.ptr(v), _capi.ptr(a), _capi.ptr(w), _capi.ptr(s), io, T, N,
                 float(tau), float(th), _capi.stream_of(x))
@@ -75,7 +75,7 @@ class AlignedGLMulti(torch.autograd.Function):
             ws_bytes = _capi.workspace_bytes("aligned", g.device, T, N)
             ws = torch.empty(max(int(ws_bytes), 8), dtype=torch.uint8, device=g.device)
         with torch.cuda.device(g.device), _prof.native_call(
-                "aligned_backward", launches, _prof.glmulti_backward_bytes(T, N), g.device):
+                "aligned_backward", launches, _prof.glmulti_backward_bytes(T, N), g.device, steps=T):
             code = L.dfsnn_aligned_backward(
                 _capi.ptr(g), _capi.ptr(x), _capi.ptr(v), _capi.ptr(a), _capi.ptr(w),
                 _capi.ptr(gx), _capi.ptr(gv), _capi.ptr(gs), _capi.ptr(gw), T, N, tau, th, sg,

@@ -48,7 +48,7 @@ def _single_forward(ctx, scheme, name, x_seq, v_init, weights, tau, beta, v_thre
     beta_f = float(beta.item() if isinstance(beta, torch.Tensor) else beta)
     tau_f = float(tau.item() if isinstance(tau, torch.Tensor) else tau)
     with torch.cuda.device(x.device), _prof.native_call(
-            "single_forward", 1, _prof.single_forward_bytes(T, N), x.device):
+            "single_forward", 1, _prof.single_forward_bytes(T, N), x.device, steps=T):
         code = _capi.lib().dfsnn_single_forward(
             scheme, _capi.ptr(x), _capi.ptr(v0), _capi.ptr(w), _capi.ptr(spike),
             _capi.ptr(v_seq), _capi.ptr(bits), T, N, tau_f, beta_f, float(v_threshold),
@@ -75,7 +75,7 @@ def _single_recompute_backward(ctx, grad_spike_seq, grad_v_seq):
     grad_v0 = torch.empty(N, dtype=torch.float32, device=x.device)
     tau, beta, th, sg, h_beta, gamma1 = ctx.consts
     with torch.cuda.device(x.device), _prof.native_call(
-            "single_backward", 1, _prof.single1_backward_bytes(T, N), x.device):
+            "single_backward", 1, _prof.single1_backward_bytes(T, N), x.device, steps=T):
         code = _capi.lib().dfsnn_single_recompute_backward(
             ctx.scheme, _capi.ptr(gS), _capi.ptr(gV), _capi.ptr(x), _capi.ptr(v0), _capi.ptr(w),
             _capi.ptr(grad_x), _capi.ptr(grad_v0), T, N, tau, th, sg, h_beta, _capi.stream_of(x))
@@ -95,7 +95,7 @@ def _single_backward(ctx, grad_spike_seq, grad_v_seq):
     grad_v0 = torch.empty(N, dtype=torch.float32, device=v_seq.device)
     tau, beta, th, sg, h_beta, gamma1 = ctx.consts
     with torch.cuda.device(v_seq.device), _prof.native_call(
-            "single_backward", 1, _prof.single_backward_bytes(T, N), v_seq.device):
+            "single_backward", 1, _prof.single_backward_bytes(T, N), v_seq.device, steps=T):
         code = _capi.lib().dfsnn_single_backward(
             ctx.scheme, _capi.ptr(gS), _capi.ptr(gV), _capi.ptr(v_seq), _capi.ptr(bits),
             _capi.ptr(w), _capi.ptr(grad_x), _capi.ptr(grad_v0), T, N, tau, beta, th, sg, h_beta,
@@ -192,7 +192,7 @@ class LIFFDEGLMultiFunction(torch.autograd.Function):
             raise ValueError("glmulti scale/weights must have shapes [T] and [T,T]")
         spike = torch.empty_like(x_f32)
         with torch.cuda.device(x_f32.device), _prof.native_call(
-                "glmulti_forward", 1, _prof.glmulti_forward_bytes(T, N), x_f32.device):
+                "glmulti_forward", 1, _prof.glmulti_forward_bytes(T, N), x_f32.device, steps=T):
             code = _capi.lib().dfsnn_glmulti_forward(
                 _capi.ptr(x_f32), _capi.ptr(v_f32), _capi.ptr(scale_f32), _capi.ptr(weights_f32),
                 _capi.ptr(spike), T, N, float(tau), float(threshold), _capi.stream_of(x_f32))
@@ -221,7 +221,7 @@ class LIFFDEGLMultiFunction(torch.autograd.Function):
             ws_bytes = _capi.workspace_bytes("glmulti", x.device, T, N, full)
             ws = torch.empty(max(int(ws_bytes), 8), dtype=torch.uint8, device=x.device)
         with torch.cuda.device(x.device), _prof.native_call(
-                "glmulti_backward", launches, _prof.glmulti_backward_bytes(T, N), x.device):
+                "glmulti_backward", launches, _prof.glmulti_backward_bytes(T, N), x.device, steps=T):
             code = L.dfsnn_glmulti_backward(
                 _capi.ptr(g), _capi.ptr(x), _capi.ptr(v0), _capi.ptr(scale), _capi.ptr(weights),
                 _capi.ptr(grad_x), _capi.ptr(grad_v), _capi.ptr(grad_scale),

@@ -25,6 +25,7 @@ class NativeCallTimer:
         self.launches = defaultdict(int)     # name -> kernels launched
         self.bytes = defaultdict(int)        # name -> algorithmic bytes moved
         self.calls = defaultdict(int)
+        self._by_steps = defaultdict(list)   # (name, T) -> [(start, end, nbytes)]
 
     def __enter__(self):
         global _ACTIVE
@@ -37,11 +38,25 @@ class NativeCallTimer:
         _ACTIVE = self._prev
         return False
 
-    def add(self, name, start, end, launches, nbytes):
+    def add(self, name, start, end, launches, nbytes, steps=None):
         self._events[name].append((start, end))
         self.launches[name] += launches
         self.bytes[name] += nbytes
         self.calls[name] += 1
+        if steps is not None:
+            self._by_steps[(name, steps)].append((start, end, nbytes))
+
+    def summary_by_steps(self):
+        """{f"{name}_T{T}": {calls, ms_per_call, bytes_per_call, gbs}} for the calls that gave
+        their step count (call after synchronising the device)."""
+        out = {}
+        for (name, T), evs in sorted(self._by_steps.items()):
+            ms = sum(s.elapsed_time(e) for s, e, _ in evs)
+            nb = sum(b for _, _, b in evs)
+            out[f"{name}_T{T}"] = {"calls": len(evs), "ms_per_call": ms / len(evs),
+                                   "bytes_per_call": nb / len(evs),
+                                   "gbs": (nb / 1e9) / (ms / 1e3) if ms > 0 else None}
+        return out
 
     def summary(self):
         """{name: {calls, launches, ms_total, ms_per_call, bytes_per_call, gbs}} (call after
@@ -65,8 +80,9 @@ class NativeCallTimer:
 
 
 @contextlib.contextmanager
-def native_call(name, launches, nbytes, device):
-    """Bracket one native call with CUDA events when a timer is active."""
+def native_call(name, launches, nbytes, device, steps=None):
+    """Bracket one native call with CUDA events when a timer is active (`steps`: the call's T,
+    for the per-T breakdown)."""
     timer = _ACTIVE
     if timer is None:
         yield
@@ -77,7 +93,7 @@ def native_call(name, launches, nbytes, device):
     start.record(stream)
     yield
     end.record(stream)
-    timer.add(name, start, end, launches, int(nbytes))
+    timer.add(name, start, end, launches, int(nbytes), steps)
 
 
 # Algorithmic bytes per call (fp32 I/O): compulsory HBM reads + writes of one call.
