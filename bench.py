@@ -16,6 +16,7 @@ N > 1 runs one process per GPU under torchrun: every rank processes its own 8.4M
 all-reduce per step.  Rank 0 prints one JSON line.
 """
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -377,6 +378,64 @@ class ClockSampler:
                 "samples": len(samples), "source": self.source}
 
 
+class StepCosts:
+    """What a step spends besides its kernels, reported beside the device time per step:
+
+    * host_ms_per_step: the host's own time to launch one step, the median over a few
+      isolated steps, each started on an idle device and synchronized after it, so that the
+      launch queue never fills and blocks the host (in the timed loop it does, and then the
+      host's time equals the device's whatever the limit is).  A step whose host time comes
+      close to its device time runs at the host's pace;
+    * exchange_ms_per_step: the device time of the gradient all-reduce inside the timed steps
+      (CUDA events around it on the launching stream), which includes any wait for a rank
+      whose launches arrive later.
+
+    Both are the maximum over ranks.  Every rank makes the same calls in the same order."""
+
+    def __init__(self):
+        self.spans = []
+        self.on = False
+
+    @contextlib.contextmanager
+    def exchange(self):
+        if not self.on:
+            yield
+            return
+        import torch
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        yield
+        e.record()
+        self.spans.append((s, e))
+
+    @staticmethod
+    def host_step_ms(step, reps=5):
+        import torch
+        times = []
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            step()
+            times.append((time.perf_counter() - t0) * 1e3)
+            torch.cuda.synchronize()
+        return statistics.median(times)
+
+    def summary(self, K, host_ms, dev, world, exchange=True):
+        """Call after the timed region has been synchronized (exchange=False: the step's
+        collective is not bracketed, e.g. DDP's, which runs inside backward)."""
+        import torch
+        import torch.distributed as dist
+        exch = sum(s.elapsed_time(e) for s, e in self.spans) / K if self.spans else 0.0
+        t = torch.tensor([host_ms, exch], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out = {"host_ms_per_step": round(float(t[0]), 4)}
+        if world > 1 and exchange:
+            out["exchange_ms_per_step"] = round(float(t[1]), 4)
+        return out
+
+
 def make_layers(device, combos=None, batch=None):
     from dfsnn_b200.neuron import LIFNeuronFDE
     combos = COMBOS if combos is None else combos
@@ -524,8 +583,7 @@ def measure_sub_workload(args, kind, K, W, dev, world, rank, gpu_reference=False
     and max-over-ranks rule as the headline): the long-history configuration or the
     examples' aligned glmulti layer."""
     import torch
-    import torch.distributed as dist
-    from dfsnn_b200 import fde_kernels, profiling
+    from dfsnn_b200 import fde_kernels
     from dfsnn_b200.distributed import allreduce_flat
     cfg = SUB_WORKLOADS[kind]
     combos, shape = cfg["combos"], cfg["shape"]
@@ -539,34 +597,35 @@ def measure_sub_workload(args, kind, K, W, dev, world, rank, gpu_reference=False
     try:
         layers = make_layers(dev, combos, shape[0])
 
-        def step():
+        def compute():
             grads = []
             for T, sch in combos:
                 _, _, pg = layer_step(layers[(T, sch)], x[:T], gS[:T], gV[:T],
                                       sch not in ("glmulti", "aligned"))
                 grads += pg
-            if world > 1 and grads:
-                allreduce_flat(grads)
+            return grads
 
-        for _ in range(W):
-            step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        clocks = ClockSampler(dev.index)
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        with profiling.NativeCallTimer() as timer:
-            start.record()
-            for _ in range(K):
-                step()
-            end.record()
-            torch.cuda.synchronize()
-        clk = clocks.stop()
-        t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        def exchanger(costs):
+            def exchange(grads):
+                if world > 1 and grads:
+                    with costs.exchange():
+                        allreduce_flat(grads)
+            return exchange
+
+        ecosts = StepCosts()
+        eexchange = exchanger(ecosts)
+
+        def estep():
+            grads = compute()
+            eexchange(grads)
+
+        ms_eager, timer, clk_eager = timed_region(estep, K, W, dev, world, ecosts)
+        eager_costs = ecosts.summary(K, ecosts.host_step_ms(estep), dev, world)
+        gcosts = StepCosts()
+        graph, gstep, per_replay = graph_step(compute, exchanger(gcosts), dev)
+        ms, _, clk = timed_region(gstep, K, W, dev, world, gcosts, timer=False)
+        step_costs = gcosts.summary(K, gcosts.host_step_ms(gstep), dev, world)
+        del graph, gstep
     finally:
         fde_kernels.LIFFDEGLMultiFunction = library
     summary = timer.summary()
@@ -578,7 +637,7 @@ def measure_sub_workload(args, kind, K, W, dev, world, rank, gpu_reference=False
     if kind == "long" and "single_forward" in summary:
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
         roofline = fp32_roofline(summary["single_forward"], combos, neurons, K,
-                                 (clk or {}).get("sm_mhz") or 1965.0, sms)
+                                 (clk_eager or {}).get("sm_mhz") or 1965.0, sms)
         roofline["hbm_frac_of_measured"] = kernels["single_forward"]["frac_of_hbm"]
     else:
         name, d = max(summary.items(), key=lambda kv: kv[1]["ms_total"])
@@ -590,9 +649,12 @@ def measure_sub_workload(args, kind, K, W, dev, world, rank, gpu_reference=False
     units = sum(T * neurons for T, _ in combos)
     rec = {"workload": cfg["desc"], "value": world * K * units / (ms / 1e3), "unit": UNIT,
            "ms_per_step": ms / K, "steps": K, "warmup": W, "n_gpus": world,
-           "gpu_launches": timer.total_launches(), "roofline": roofline, "kernels": kernels,
-           "kernels_by_T": by_steps_table(timer, K, peak),
-           "clocks": clk}
+           "launch": LAUNCH_DESC, "gpu_launches": per_replay * K, "roofline": roofline,
+           "kernels": kernels, "kernels_by_T": by_steps_table(timer, K, peak),
+           "step_costs": step_costs, "clocks": clk,
+           "eager": {"value": world * K * units / (ms_eager / 1e3), "ms_per_step": ms_eager / K,
+                     "gpu_launches": timer.total_launches(), "step_costs": eager_costs,
+                     "clocks": clk_eager}}
     if world == 1 and gpu_reference:
         # the reference's own GPU path on the same layers and inputs (bounded steps)
         long_t = kind == "long"      # about a second per reference step: bounded sample
@@ -604,11 +666,112 @@ def measure_sub_workload(args, kind, K, W, dev, world, rank, gpu_reference=False
     return rec
 
 
-def run_native(args):
+LAUNCH_DESC = ("each step's compute (the layers' forward and backward) replayed from a CUDA graph "
+               "captured once; the gradient all-reduce (world > 1) issued after each replay; "
+               "per-kernel durations and the roofline from an eager region of the same steps")
+
+
+def timed_region(step, K, W, dev, world, costs, timer=True):
+    """W untimed steps, then K steps between two CUDA events on the launching stream, with a
+    synchronize and (world > 1) a barrier on both sides and the SM clocks sampled meanwhile.
+    Returns (ms for the K steps, max over ranks; the NativeCallTimer of the region or None;
+    the clock record).  `costs` brackets the region's exchanges (StepCosts)."""
     import torch
     import torch.distributed as dist
     from dfsnn_b200 import profiling
-    from dfsnn_b200.distributed import allreduce_flat, init_process_group
+    for _ in range(W):
+        step()
+    clocks = ClockSampler(dev.index)     # NVML set-up (milliseconds) before the start line
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    tm = profiling.NativeCallTimer() if timer else contextlib.nullcontext()
+    torch.cuda.synchronize()
+    start_line(dev, world)
+    with tm:
+        costs.on = True
+        start.record()
+        for _ in range(K):
+            step()
+        end.record()
+        costs.on = False
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()), (tm if timer else None), clk
+
+
+def graph_step(compute, exchange, dev):
+    """A step whose compute -- the layers' forward and backward, every native kernel and the
+    PyTorch glue between them -- is captured once into a CUDA graph (after three eager runs
+    on a side stream, as capture requires) and replayed; the exchange (the NCCL all-reduce
+    of the parameter gradients when world > 1) stays outside the graph and runs after each
+    replay on the captured outputs, which every replay rewrites.  The host then launches one
+    graph per step instead of about twenty native kernels and their glue, so its launch cost
+    (0.25-0.36 ms per layer forward + backward) no longer paces the device when several
+    ranks share the host's cores.  Returns (graph, step, native kernels per replay)."""
+    import torch
+    from dfsnn_b200 import profiling
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            compute()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with profiling.NativeCallTimer() as timer:
+        with torch.cuda.graph(graph):
+            out = compute()
+
+    def step():
+        graph.replay()
+        exchange(out)
+        return out
+    return graph, step, timer.captured_launches()
+
+
+def start_line(dev, world):
+    """Line the ranks up for a timed region: a host barrier, then a one-element all-reduce on
+    the launching stream right before the region's start event, so that on every rank the
+    event fires when the last rank has arrived (host skew after the barrier -- a rank's
+    thread descheduled for a few milliseconds -- stays out of the max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(torch.zeros(1, device=dev))
+
+
+def start_ranks(dev, world):
+    """The NCCL process group for world > 1, with NCCL's INIT log on (one "Init COMPLETE" line
+    per rank, with its transport choices) unless the environment sets NCCL_DEBUG itself."""
+    from dfsnn_b200.distributed import init_process_group
+    if world > 1:
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        init_process_group("nccl", timeout_s=300, device=dev)
+
+
+def finish_ranks(line, rank, world):
+    """Tear the process group down, then rank 0 prints the one JSON line.  NCCL writes its
+    teardown lines to stdout as well, so the line comes after rank 0's own and, a second
+    later, after the other ranks' (which have passed the same barrier)."""
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+        if rank == 0:
+            time.sleep(1.0)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_native(args):
+    import torch
+    from dfsnn_b200.distributed import allreduce_flat
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -617,8 +780,7 @@ def run_native(args):
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        init_process_group("nccl", timeout_s=300, device=dev)
+    start_ranks(dev, world)
     K, W = args.steps, max(args.warmup, 3)
     neurons = math.prod(SHAPE)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
@@ -628,41 +790,46 @@ def run_native(args):
     gV16 = torch.randn((TMAX,) + SHAPE, device=dev, generator=g)
     layers = make_layers(dev)
 
-    def step():
+    def compute():
         mass_grads = []
         for T, sch in COMBOS:
             _, _, pg = layer_step(layers[(T, sch)], x16[:T], gS16[:T], gV16[:T],
                                   sch not in ("glmulti", "aligned"))
             mass_grads += pg
-        if world > 1:
-            allreduce_flat(mass_grads)       # the one gradient exchange per step
         return mass_grads
 
-    for _ in range(W):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = ClockSampler(local)
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    with profiling.NativeCallTimer() as timer:
-        start.record()
-        for _ in range(K):
-            step()
-        end.record()
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clk = clocks.stop()
-    ms = start.elapsed_time(end)
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    def exchanger(costs):
+        def exchange(grads):
+            if world > 1:
+                with costs.exchange():
+                    allreduce_flat(grads)    # the one gradient exchange per step
+        return exchange
+
+    # eager region: every native call bracketed by CUDA events (per-kernel durations)
+    ecosts = StepCosts()
+    eexchange = exchanger(ecosts)
+
+    def estep():
+        grads = compute()
+        eexchange(grads)
+        return grads
+
+    ms_eager, timer, clk_eager = timed_region(estep, K, W, dev, world, ecosts)
+    eager_costs = ecosts.summary(K, ecosts.host_step_ms(estep), dev, world)
+    # the headline region: the same steps with their compute replayed from a CUDA graph
+    gcosts = StepCosts()
+    graph, gstep, per_replay = graph_step(compute, exchanger(gcosts), dev)
+    ms_max, _, clk = timed_region(gstep, K, W, dev, world, gcosts, timer=False)
+    step_costs = gcosts.summary(K, gcosts.host_step_ms(gstep), dev, world)
+    del graph, gstep
     value = world * K * units_per_step(neurons) / (ms_max / 1e3)
     summary = timer.summary()
-    launches = timer.total_launches()
+    launches = per_replay * K
+    eager = {"value": world * K * units_per_step(neurons) / (ms_eager / 1e3),
+             "ms_per_step": ms_eager / K, "gpu_launches": timer.total_launches(),
+             "step_costs": eager_costs, "clocks": clk_eager,
+             "launch": "eager: every layer's native calls and PyTorch glue launched from the "
+                       "host each step; the per-kernel durations below are this region's"}
 
     # dominant kernel (largest device time in the timed region) and its roofline
     dom = max(summary.items(), key=lambda kv: kv[1]["ms_total"]) if summary else None
@@ -680,7 +847,8 @@ def run_native(args):
         # T >= 64: the forward's Kahan history chains are FP32-bound (no tensor cores apply)
         d = summary["single_forward"]
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        roofline = fp32_roofline(d, COMBOS, neurons, K, (clk or {}).get("sm_mhz") or 1965.0, sms)
+        roofline = fp32_roofline(d, COMBOS, neurons, K,
+                                 (clk_eager or {}).get("sm_mhz") or 1965.0, sms)
         roofline["hbm_frac_of_measured"] = d["gbs"] / peak if d["gbs"] else None
     kernels = {k: {"calls_per_step": v["calls"] / K, "ms_per_call": round(v["ms_per_call"], 4),
                    "gbs": round(v["gbs"], 1) if v["gbs"] else None,
@@ -698,11 +866,14 @@ def run_native(args):
         "config": {"workload": WORKLOAD, "neurons_per_gpu": neurons, "T": list(TS),
                    "schemes": list(SCHEMES), "l2": "inputs larger than L2 (no flush)",
                    "parallelism": f"dp{world}" + (" (one NCCL all-reduce of the mass grads per step)"
-                                                  if world > 1 else "")},
+                                                  if world > 1 else ""),
+                   "launch": LAUNCH_DESC},
         "gpu_launches": launches,
         "roofline": roofline,
         "kernels": kernels,
         "kernels_by_T": by_steps_table(timer, K, peak),
+        "step_costs": step_costs,
+        "eager": eager,
         "clocks": clk,
         "e2e": e2e,
     }
@@ -763,11 +934,7 @@ def run_native(args):
                                      "example-reference")
             spk["reference_kernels"] = refspk
         line["network_spikformer256"] = spk
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    finish_ranks(line, rank, world)
     return 0
 
 
@@ -835,11 +1002,10 @@ def run_e2e(args, layers, x16, gS16, gV16, dev, world):
 
     ev = issue_h2d(0)
     one(0, ev)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start_line(dev, world)             # on `comp`, the current stream
     start.record(comp)
     h2d_s.wait_stream(comp)
     ev = issue_h2d(1)
@@ -1162,12 +1328,6 @@ def measure_network(args, name, dev, world, local, amp, K, W, source="example"):
     else:
         model, reset, close = built
     try:
-        net = model
-        if world > 1:
-            net = torch.nn.parallel.DistributedDataParallel(
-                model, device_ids=[local], broadcast_buffers=False,
-                gradient_as_bucket_view=True, static_graph=True)
-        opt = torch.optim.AdamW(model.parameters(), lr=1e-4)
         scaler = torch.amp.GradScaler("cuda", enabled=amp)
         g = torch.Generator(device=dev).manual_seed(99 + int(os.environ.get("RANK", "0")))
         shape = (NT, NB, 2, 128, 128)
@@ -1176,23 +1336,55 @@ def measure_network(args, name, dev, world, local, amp, K, W, source="example"):
             frames = frames * torch.poisson(torch.ones(shape, device=dev), generator=g)
         labels = torch.randint(0, NCLS, (NB,), device=dev, generator=g)
 
-        def step():
-            reset()
-            with torch.autocast("cuda", dtype=torch.float16, enabled=amp):
-                loss = F.cross_entropy(net(frames), labels)
-            opt.zero_grad(set_to_none=True)
-            scaler.scale(loss).backward()
-            scaler.step(opt)
-            scaler.update()
-            return loss
+        def make_step(net, opt):
+            def step():
+                reset()
+                with torch.autocast("cuda", dtype=torch.float16, enabled=amp):
+                    loss = F.cross_entropy(net(frames), labels)
+                opt.zero_grad(set_to_none=True)
+                scaler.scale(loss).backward()
+                scaler.step(opt)
+                scaler.update()
+                return loss
+            return step
+
+        replica = None
+        if world > 1 and not amp:
+            # the bare module trained on every rank at once with no collective (before the
+            # DDP wrap, whose construction then broadcasts rank 0's parameters): the step
+            # time each GPU reaches while the ranks share the node but wait for no one
+            rstep = make_step(model, torch.optim.AdamW(model.parameters(), lr=1e-4))
+            for _ in range(W):
+                rstep()
+            torch.cuda.synchronize()
+            dist.barrier()
+            r0 = torch.cuda.Event(enable_timing=True)
+            r1 = torch.cuda.Event(enable_timing=True)
+            r0.record()
+            for _ in range(K):
+                rstep()
+            r1.record()
+            torch.cuda.synchronize()
+            tr = torch.tensor([r0.elapsed_time(r1) / K], device=dev, dtype=torch.float64)
+            gathered = [torch.zeros_like(tr) for _ in range(world)]
+            dist.all_gather(gathered, tr)
+            replica = [round(float(x.item()), 3) for x in gathered]
+            del rstep
+            model.zero_grad(set_to_none=True)
+        net = model
+        if world > 1:
+            net = torch.nn.parallel.DistributedDataParallel(
+                model, device_ids=[local], broadcast_buffers=False,
+                gradient_as_bucket_view=True, static_graph=True)
+        opt = torch.optim.AdamW(model.parameters(), lr=1e-4)
+        step = make_step(net, opt)
 
         for _ in range(W):
             step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start_line(dev, world)
         with profiling.NativeCallTimer() as timer:
             start.record()
             for _ in range(K):
@@ -1225,6 +1417,10 @@ def measure_network(args, name, dev, world, local, amp, K, W, source="example"):
             allreduce = e0.elapsed_time(e1) / 10
         ms = float(t.item())
         summary = timer.summary()
+        # the host's own time per step; with AMP the GradScaler reads its overflow flag on
+        # the host every step, so the host waits for the device and the figure says nothing
+        step_costs = (StepCosts().summary(K, StepCosts.host_step_ms(step), dev, world,
+                                          exchange=False) if not amp else None)
         rec = {
             "metric": f"{'CNN128' if name == 'cnn128' else 'Spikformer256'} synthetic training "
                       "samples/s", "value": world * NB * K / (ms / 1e3), "unit": "samples/s",
@@ -1243,6 +1439,8 @@ def measure_network(args, name, dev, world, local, amp, K, W, source="example"):
             "lif_launches_per_step": timer.total_launches() / K,
             "allreduce_ms": allreduce,
             "per_rank_ms_per_step": [round(x / K, 3) for x in per_rank],
+            "replica_ms_per_step": replica,
+            "step_costs": step_costs,
             "loss": float(loss.item()),
         }
         if world > 1:
@@ -1254,32 +1452,25 @@ def measure_network(args, name, dev, world, local, amp, K, W, source="example"):
 
 def run_network(args, name):
     import torch
-    import torch.distributed as dist
-    from dfsnn_b200.distributed import init_process_group
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        init_process_group("nccl", timeout_s=300, device=dev)
+    start_ranks(dev, world)
     K, W = args.steps, max(args.warmup, 3)
     clocks = ClockSampler(local)
     recs = [measure_network(args, name, dev, world, local, amp, K, W, args.network_source)
             for amp in (False, True)]
     clk = clocks.stop()
-    if rank == 0:
-        line = dict(recs[0])
-        line.update({"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                     "dtype": "f32", "data": "synthetic",
-                     "config": {"workload": recs[0]["workload"],
-                                "parallelism": recs[0]["parallelism"]},
-                     "amp": recs[1], "clocks": clk})
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    line = dict(recs[0])
+    line.update({"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                 "dtype": "f32", "data": "synthetic",
+                 "config": {"workload": recs[0]["workload"],
+                            "parallelism": recs[0]["parallelism"]},
+                 "amp": recs[1], "clocks": clk})
+    finish_ranks(line, rank, world)
     return 0
 
 
@@ -1309,9 +1500,7 @@ def measure_history(args, dev, world, rank, K, W, shape=(16, 128, 64, 64), ts=(8
     backward with gradients for x, scale and weights, at T = 8 and 16 on [T, N] inputs with
     per-sample tables (B = 16 samples of N/16 neurons).  Returns the record."""
     import torch
-    import torch.distributed as dist
     from dfsnn_b200 import fde_kernels as fk
-    from dfsnn_b200 import profiling
     from dfsnn_b200.distributed import allreduce_flat
 
     B = shape[0]
@@ -1328,7 +1517,7 @@ def measure_history(args, dev, world, rank, K, W, shape=(16, 128, 64, 64), ts=(8
     v0 = torch.zeros(neurons, device=dev)
     hb = H ** 0.5
 
-    def step():
+    def compute():
         pgrads = []
         for T in ts:
             for kind in HIST_KINDS:
@@ -1345,31 +1534,29 @@ def measure_history(args, dev, world, rank, K, W, shape=(16, 128, 64, 64), ts=(8
                     ins = [x, sc, Wt]
                 res = torch.autograd.grad([s], ins, [gS16[:T]])
                 pgrads += list(res[1:])
-        if world > 1:
-            allreduce_flat(pgrads)
         return pgrads
 
-    for _ in range(W):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = ClockSampler(dev.index)
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    with profiling.NativeCallTimer() as timer:
-        start.record()
-        for _ in range(K):
-            step()
-        end.record()
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clk = clocks.stop()
-    t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    def exchanger(costs):
+        def exchange(grads):
+            if world > 1:
+                with costs.exchange():
+                    allreduce_flat(grads)
+        return exchange
+
+    ecosts = StepCosts()
+    eexchange = exchanger(ecosts)
+
+    def estep():
+        grads = compute()
+        eexchange(grads)
+
+    ms_eager, timer, clk_eager = timed_region(estep, K, W, dev, world, ecosts)
+    eager_costs = ecosts.summary(K, ecosts.host_step_ms(estep), dev, world)
+    gcosts = StepCosts()
+    graph, gstep, per_replay = graph_step(compute, exchanger(gcosts), dev)
+    ms, _, clk = timed_region(gstep, K, W, dev, world, gcosts, timer=False)
+    step_costs = gcosts.summary(K, gcosts.host_step_ms(gstep), dev, world)
+    del graph, gstep
     units = sum(ts) * neurons * len(HIST_KINDS)
     summary = timer.summary()
     peak, peak_src = measured_hbm_peak()
@@ -1391,41 +1578,39 @@ def measure_history(args, dev, world, rank, K, W, shape=(16, 128, 64, 64), ts=(8
         "neurons_per_gpu": neurons,
         "parallelism": f"dp{world}" + (" (one NCCL all-reduce of the table grads per step)"
                                        if world > 1 else ""),
-        "gpu_launches": timer.total_launches(),
+        "launch": LAUNCH_DESC,
+        "gpu_launches": per_replay * K,
         "roofline": roofline,
         "kernels": {k: {"calls_per_step": v["calls"] / K,
                         "ms_per_call": round(v["ms_per_call"], 4),
                         "gbs": round(v["gbs"], 1) if v["gbs"] else None,
                         "frac_of_hbm": round(v["gbs"] / peak, 4) if v["gbs"] else None}
                     for k, v in summary.items()},
+        "step_costs": step_costs,
         "clocks": clk,
+        "eager": {"value": world * K * units / (ms_eager / 1e3), "ms_per_step": ms_eager / K,
+                  "gpu_launches": timer.total_launches(), "step_costs": eager_costs,
+                  "clocks": clk_eager},
     }
 
 
 def run_history(args):
     import torch
-    import torch.distributed as dist
-    from dfsnn_b200.distributed import init_process_group
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        init_process_group("nccl", timeout_s=300, device=dev)
+    start_ranks(dev, world)
     rec = measure_history(args, dev, world, rank, args.steps, max(args.warmup, 3), SHAPE, TS)
-    if rank == 0:
-        line = dict(rec)
-        line.update({"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                     "dtype": "f32", "data": "synthetic",
-                     "config": {"workload": rec["workload"], "neurons_per_gpu": rec["neurons_per_gpu"],
-                                "T": list(TS), "l2": "inputs larger than L2 (no flush)",
-                                "parallelism": rec["parallelism"]}})
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    line = dict(rec)
+    line.update({"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                 "dtype": "f32", "data": "synthetic",
+                 "config": {"workload": rec["workload"], "neurons_per_gpu": rec["neurons_per_gpu"],
+                            "T": list(TS), "l2": "inputs larger than L2 (no flush)",
+                            "parallelism": rec["parallelism"]}})
+    finish_ranks(line, rank, world)
     return 0
 
 

@@ -5,6 +5,7 @@ C-ABI call made by the autograd Functions is bracketed by a pair of CUDA events 
 on the stream the kernels are launched on, together with the number of kernels the call
 launches and its algorithmic HBM bytes (compulsory reads + writes), so a harness can
 report per-kernel durations and achieved bandwidth measured inside its own timed region.
+Calls made while the stream is being captured into a CUDA graph are counted only.
 
     with profiling.NativeCallTimer() as timer:
         ... run steps ...
@@ -26,6 +27,7 @@ class NativeCallTimer:
         self.bytes = defaultdict(int)        # name -> algorithmic bytes moved
         self.calls = defaultdict(int)
         self._by_steps = defaultdict(list)   # (name, T) -> [(start, end, nbytes)]
+        self.captured = defaultdict(int)     # name -> kernels recorded into a CUDA graph
 
     def __enter__(self):
         global _ACTIVE
@@ -78,6 +80,11 @@ class NativeCallTimer:
     def total_launches(self):
         return sum(self.launches.values())
 
+    def captured_launches(self):
+        """Kernels recorded into CUDA graphs while the timer was active (each replay of such a
+        graph launches them again)."""
+        return sum(self.captured.values())
+
 
 @contextlib.contextmanager
 def native_call(name, launches, nbytes, device, steps=None):
@@ -85,6 +92,11 @@ def native_call(name, launches, nbytes, device, steps=None):
     for the per-T breakdown)."""
     timer = _ACTIVE
     if timer is None:
+        yield
+        return
+    if torch.cuda.is_current_stream_capturing():
+        # a capturing stream takes no timing events: count the kernels the graph will launch
+        timer.captured[name] += launches
         yield
         return
     stream = torch.cuda.current_stream(device)

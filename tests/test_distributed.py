@@ -1,6 +1,7 @@
 """Data-parallel host logic on CPU (gloo, world size 2): sharded neuron ranges cover the axis,
 per-shard parameter gradients summed by one all-reduce equal the single-process result, and a
 rank that fails before the collective makes its peer fail within the process-group timeout."""
+import json
 import os
 import socket
 import sys
@@ -104,3 +105,31 @@ def test_failed_rank_is_detected_by_timeout(tmp_path):
     status, secs = open(out).read().split()
     assert status != "completed"
     assert float(secs) < 60
+
+
+def _worker_step_costs(rank, world, port, out_path):
+    sys.path[:0] = [REPO, os.path.join(REPO, "df-snn-official_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    import bench
+    init_process_group("gloo", timeout_s=30)
+    bench.start_line(torch.device("cpu"), world)    # both ranks meet at the start line
+    costs = bench.StepCosts()
+    out = costs.summary(4, 1.0 + rank, torch.device("cpu"), world)
+    no_exch = costs.summary(4, 5.0 - rank, torch.device("cpu"), world, exchange=False)
+    if rank == 0:
+        with open(out_path, "w") as f:
+            json.dump([out, no_exch], f)
+    dist.destroy_process_group()
+
+
+def test_bench_step_costs_max_over_ranks(tmp_path):
+    """The bench's start line and per-step host and exchange costs: every rank takes part in
+    the same collectives, and the costs are the maximum over ranks (gloo, world size 2)."""
+    out = str(tmp_path / "c.txt")
+    mp.start_processes(_worker_step_costs, args=(2, _free_port(), out), nprocs=2,
+                       start_method="spawn")
+    with open(out) as f:
+        a, b = json.load(f)
+    assert a == {"host_ms_per_step": 2.0, "exchange_ms_per_step": 0.0}
+    assert b == {"host_ms_per_step": 5.0}

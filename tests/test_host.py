@@ -334,3 +334,44 @@ def test_bench_example_networks_bind_the_native_function(monkeypatch):
             close()
         assert fde_kernels.LIFFDEGLMultiFunction is original
         assert not any(k.startswith("spikeDE_dis") for k in sys.modules)
+
+
+class _FakeEvent:
+    """A CUDA event stand-in whose 'device' time is the host clock."""
+
+    def __init__(self, enable_timing=False):
+        self.t = None
+
+    def record(self, stream=None):
+        import time
+        self.t = time.perf_counter()
+
+    def elapsed_time(self, other):
+        return (other.t - self.t) * 1e3
+
+
+def test_bench_step_costs(monkeypatch):
+    """StepCosts: the host time of isolated steps (median) and the exchange spans recorded
+    only while the timed loop is on; no exchange figure on one rank."""
+    import importlib
+    import time
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    monkeypatch.syspath_prepend(repo)
+    bench = importlib.import_module("bench")
+    syncs = []
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a: syncs.append(1))
+    monkeypatch.setattr(torch.cuda, "Event", _FakeEvent)
+    costs = bench.StepCosts()
+    with costs.exchange():
+        pass
+    assert costs.spans == []
+    costs.on = True
+    for _ in range(4):
+        with costs.exchange():
+            time.sleep(0.002)
+    costs.on = False
+    assert len(costs.spans) == 4
+    host = bench.StepCosts.host_step_ms(lambda: time.sleep(0.003), reps=5)
+    assert len(syncs) == 10 and 2.5 <= host < 50
+    one = costs.summary(4, host, torch.device("cpu"), 1)
+    assert set(one) == {"host_ms_per_step"} and one["host_ms_per_step"] == round(host, 4)
