@@ -388,7 +388,7 @@ class StepCosts:
       close to its device time runs at the host's pace;
     * exchange_ms_per_step: the device time of the gradient all-reduce inside the timed steps
       (CUDA events around it on the launching stream), which includes any wait for a rank
-      whose launches arrive later.
+      whose launches arrive later; exchange_ms_longest: the longest single one.
 
     Both are the maximum over ranks.  Every rank makes the same calls in the same order."""
 
@@ -426,13 +426,16 @@ class StepCosts:
         collective is not bracketed, e.g. DDP's, which runs inside backward)."""
         import torch
         import torch.distributed as dist
-        exch = sum(s.elapsed_time(e) for s, e in self.spans) / K if self.spans else 0.0
-        t = torch.tensor([host_ms, exch], device=dev, dtype=torch.float64)
+        spans = [s.elapsed_time(e) for s, e in self.spans]
+        exch = sum(spans) / K if spans else 0.0
+        t = torch.tensor([host_ms, exch, max(spans, default=0.0)], device=dev,
+                         dtype=torch.float64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         out = {"host_ms_per_step": round(float(t[0]), 4)}
         if world > 1 and exchange:
             out["exchange_ms_per_step"] = round(float(t[1]), 4)
+            out["exchange_ms_longest"] = round(float(t[2]), 4)
         return out
 
 
@@ -661,7 +664,10 @@ def measure_sub_workload(args, kind, K, W, dev, world, rank, gpu_reference=False
         gref = run_gpu_reference(args, x, gS, gV, dev, combos, shape[0],
                                  max_steps=3 if long_t else K, warmup=1 if long_t else None)
         if gref.get("value"):
-            gref["native_over_reference"] = rec["value"] / gref["value"]
+            # like for like: this library's eager steps against the reference's eager steps;
+            # the CUDA-graph replay of the same steps beside it
+            gref["native_over_reference"] = rec["eager"]["value"] / gref["value"]
+            gref["graph_over_reference"] = rec["value"] / gref["value"]
         rec["gpu_reference"] = gref
     return rec
 
@@ -746,19 +752,22 @@ def start_line(dev, world):
 
 
 def start_ranks(dev, world):
-    """The NCCL process group for world > 1, with NCCL's INIT log on (one "Init COMPLETE" line
-    per rank, with its transport choices) unless the environment sets NCCL_DEBUG itself."""
+    """The NCCL process group for world > 1, with NCCL's INFO log on for its INIT subsystem
+    (one "Init COMPLETE" line per rank, with its transport choices), also where the
+    environment sets another level or subsystem list."""
     from dfsnn_b200.distributed import init_process_group
     if world > 1:
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ["NCCL_DEBUG"] = "INFO"
+        os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
         init_process_group("nccl", timeout_s=300, device=dev)
 
 
 def finish_ranks(line, rank, world):
     """Tear the process group down, then rank 0 prints the one JSON line.  NCCL writes its
-    teardown lines to stdout as well, so the line comes after rank 0's own and, a second
-    later, after the other ranks' (which have passed the same barrier)."""
+    teardown lines to stdout as well, at the destroy and again at process exit, so with
+    world > 1 the line comes a second after the destroy (which every rank has reached
+    through the same barrier) and every rank then leaves with os._exit(0) once its streams
+    are flushed: no exit-time output can follow the line."""
     import torch.distributed as dist
     if world > 1:
         dist.barrier()
@@ -767,6 +776,10 @@ def finish_ranks(line, rank, world):
             time.sleep(1.0)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if world > 1:
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
 
 
 def run_native(args):
@@ -880,7 +893,8 @@ def run_native(args):
     if rank == 0 and world == 1 and args.workload == "layers" and not args.no_gpu_reference:
         gref = run_gpu_reference(args, x16, gS16, gV16, dev)
         if gref.get("value"):
-            gref["native_over_reference"] = value / gref["value"]
+            gref["native_over_reference"] = eager["value"] / gref["value"]    # eager vs eager
+            gref["graph_over_reference"] = value / gref["value"]
         line["gpu_reference"] = gref
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "layers":
         n = args.cpu_sample

@@ -131,5 +131,36 @@ def test_bench_step_costs_max_over_ranks(tmp_path):
                        start_method="spawn")
     with open(out) as f:
         a, b = json.load(f)
-    assert a == {"host_ms_per_step": 2.0, "exchange_ms_per_step": 0.0}
+    assert a == {"host_ms_per_step": 2.0, "exchange_ms_per_step": 0.0, "exchange_ms_longest": 0.0}
     assert b == {"host_ms_per_step": 5.0}
+
+
+_FINISH_SCRIPT = """
+import os, sys
+sys.path[:0] = [{repo!r}, os.path.join({repo!r}, "df-snn-official_b200")]
+import bench
+from dfsnn_b200.distributed import init_process_group
+init_process_group("gloo", timeout_s=30)
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+print(f"rank {{rank}} before", flush=True)
+bench.finish_ranks({{"metric": "m", "value": 1.0, "n_gpus": world}}, rank, world)
+print("never printed", flush=True)
+"""
+
+
+def test_bench_finish_ranks_prints_the_line_last(tmp_path):
+    """Under torchrun (gloo, world size 2) every rank exits 0 and rank 0's JSON line is the
+    last line of the run's stdout: nothing a rank prints at exit can follow it."""
+    import json
+    import subprocess
+    script = tmp_path / "finish.py"
+    script.write_text(_FINISH_SCRIPT.format(repo=REPO))
+    proc = subprocess.run(
+        [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+         "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(script)],
+        capture_output=True, text=True, timeout=120)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = [l for l in proc.stdout.splitlines() if l.strip()]
+    assert json.loads(lines[-1]) == {"metric": "m", "value": 1.0, "n_gpus": 2}
+    assert sum(l.startswith("{") for l in lines) == 1
+    assert "never printed" not in proc.stdout
