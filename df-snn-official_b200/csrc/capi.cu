@@ -295,8 +295,9 @@ int dfsnn_single_recompute_backward(int scheme, const float* grad_spike, const f
 // ---------------------------------------------------------------------------------------
 namespace {
 
-// Workspace: grad_pre [T, N] floats, then the partial rows (B*chunks rows of T + T*T
-// doubles), then the summed rows ((per_batch ? B : 1) of them), each on a 256-byte boundary.
+// Workspace: grad_pre [T, N] floats (not for T = 8 and 16, whose sweep kernel forms the
+// parameter rows itself), then the partial rows (B*chunks rows of T + T*T doubles), then the
+// summed rows ((per_batch ? B : 1) of them), each on a 256-byte boundary.
 struct HistWs {
     size_t gpre, part, msum, total;
     int chunks;
@@ -305,9 +306,10 @@ struct HistWs {
 HistWs hist_ws(int T, long long N, int B, int per_batch) {
     HistWs w;
     const size_t R = (size_t)T + (size_t)T * T;
+    const bool fused = dfsnn::hfam_backward_fused(T);
     w.chunks = dfsnn::param_rows_chunks(T, N, B);
     w.gpre = 0;
-    w.part = round256((size_t)T * (size_t)N * sizeof(float));
+    w.part = fused ? 0 : round256((size_t)T * (size_t)N * sizeof(float));
     w.msum = w.part + round256((size_t)B * w.chunks * R * sizeof(double));
     w.total = w.msum + round256((size_t)(per_batch ? B : 1) * R * sizeof(double));
     return w;
@@ -357,22 +359,25 @@ int hist_backward(int kind, int full, const float* grad_spike, const float* scal
     const HistWs w = hist_ws(T, N, batch, per_batch);
     if (!workspace || !aligned8(workspace) || workspace_bytes < w.total) return DFSNN_ERR_WORKSPACE;
     char* ws = static_cast<char*>(workspace);
-    float* gpre = reinterpret_cast<float*>(ws + w.gpre);
+    const bool fused = dfsnn::hfam_backward_fused(T);
+    float* gpre = fused ? nullptr : reinterpret_cast<float*>(ws + w.gpre);
     double* part = reinterpret_cast<double*>(ws + w.part);
     double* msum = reinterpret_cast<double*>(ws + w.msum);
     cudaStream_t st = (cudaStream_t)stream;
     const bool p2 = tau_is_pow2(tau);
+    const float* Ediag = (kind == dfsnn::kVOGL1 && grad_scale) ? E : nullptr;
     cudaError_t e = dfsnn::hfam_backward_launch(kind, full != 0, grad_spike, scale, h_beta,
                                                 weights, batch, per_batch != 0, v_pre, grad_x,
-                                                grad_v0, gpre, T, N, tau, threshold,
-                                                surrogate_scale, residual_mix, p2, st);
+                                                grad_v0, gpre, params ? V : nullptr, Ediag, part,
+                                                w.chunks, T, N, tau, threshold, surrogate_scale,
+                                                residual_mix, p2, st);
     if (e != cudaSuccess || !params) return cuda_status(e);
-    if (N > 0) {
+    if (N == 0) {
+        e = cudaMemsetAsync(part, 0, (size_t)batch * w.chunks * (T + (size_t)T * T) * sizeof(double), st);
+    } else if (!fused) {                  // T = 8 and 16: the sweep kernel wrote the rows
         const int diag = (kind == dfsnn::kVOGL1 && grad_scale) ? dfsnn::kDiagProduct
                                                                : dfsnn::kDiagNone;
         e = dfsnn::param_rows_launch(gpre, V, E, T, N, batch, diag, part, w.chunks, true, st);
-    } else {
-        e = cudaMemsetAsync(part, 0, (size_t)batch * w.chunks * (T + (size_t)T * T) * sizeof(double), st);
     }
     if (e != cudaSuccess) return cuda_status(e);
     return cuda_status(dfsnn::hfam_param_finalize(kind, part, w.chunks, batch, per_batch != 0, T,

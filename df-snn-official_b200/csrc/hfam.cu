@@ -18,11 +18,13 @@
 // column per thread (T <= 256).
 // Backward: the reverse sweeps of :1633-1668 (truncated: grad_v_next = -gp*(s/tau + sum_i
 // W[t,i])), :1670-1709 (full history, T <= 64: an adjoint per earlier step) and :1058-1096
-// (VO-PREDICTOR: grad_v_next = gp*(rm - s/tau)), writing grad_x, grad_v0 and grad_pre.  The
-// parameter gradients are reductions of grad_pre against the saved history (param_long.cu)
-// finished here by hfam_sum + hfam_epilogue.
+// (VO-PREDICTOR: grad_v_next = gp*(rm - s/tau)), writing grad_x and grad_v0.  The parameter
+// gradients are reductions of grad_pre against the saved history: for T = 8 and 16 inside
+// the sweep kernel (hfam_bwd_f, grad_pre never stored), otherwise by param_long.cu over the
+// grad_pre [T, N] the sweep writes; hfam_sum + hfam_epilogue finish both.
 #include "kernels.h"
 #include "lif_common.cuh"
+#include "mma_tf32.cuh"
 
 namespace dfsnn {
 
@@ -161,46 +163,6 @@ __device__ __forceinline__ float trunc_next(const HfBwd& a, const float* w, int 
     }
 }
 
-template <int HM, int TT, bool TAU_POW2, bool FAST_SG>
-__global__ void __launch_bounds__(256) hfam_bwd_r(HfBwd a) {
-    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (n >= a.N) return;
-    const long long N = a.N;
-    const int b = a.tab.sample(n);
-    float gr[TT], pr[TT];
-#pragma unroll
-    for (int t = 0; t < TT; ++t) {
-        gr[t] = ld_stream(a.gS + (long long)t * N + n);
-        pr[t] = ld_stream(a.vpre + (long long)t * N + n);
-    }
-    float A[HM == kFull ? TT : 1];
-#pragma unroll
-    for (int t = 0; t < (HM == kFull ? TT : 1); ++t) A[t] = 0.0f;
-    float gvn = 0.0f, ginit = 0.0f;
-#pragma unroll
-    for (int t = TT - 1; t >= 0; --t) {
-        const long long o = (long long)t * N + n;
-        const float sur = surr<FAST_SG>(__fsub_rn(pr[t], a.th), a.sg);
-        float gp;
-        if constexpr (HM == kFull) gp = __fmaf_rn(gr[t], sur, A[t]);
-        else gp = __fmaf_rn(gr[t], sur, gvn);
-        const float sv = a.tab.s(t, b);
-        const float* w = a.tab.wrow(t, b, TT);
-        st_stream(a.gpre + o, gp);
-        st_stream(a.gx + o, div_tau<TAU_POW2>(__fmul_rn(gp, sv), a.tau, a.inv_tau));
-        if constexpr (HM == kFull) {
-            const float prev = div_tau<TAU_POW2>(__fmul_rn(-gp, sv), a.tau, a.inv_tau);
-            if (t == 0) ginit = __fadd_rn(ginit, prev);
-            else A[t > 0 ? t - 1 : 0] = __fadd_rn(A[t > 0 ? t - 1 : 0], prev);
-#pragma unroll
-            for (int i = 0; i < t; ++i) A[i] = __fmaf_rn(-__ldg(w + i), gp, A[i]);
-        } else {
-            gvn = trunc_next<HM, TAU_POW2>(a, w, t, gp, sv);
-        }
-    }
-    a.gv0[n] = HM == kFull ? ginit : gvn;
-}
-
 // any T; the full-history adjoints live in a shared-memory column per thread (T <= 64)
 template <int HM, bool TAU_POW2, bool FAST_SG>
 __global__ void __launch_bounds__(128) hfam_bwd_s(HfBwd a) {
@@ -232,6 +194,183 @@ __global__ void __launch_bounds__(128) hfam_bwd_s(HfBwd a) {
         }
     }
     a.gv0[n] = HM == kFull ? ginit : gvn;
+}
+
+// ---- T = 8 and 16: the reverse sweep and the parameter products in one kernel ----------
+// One block per partial row s = b*chunks + c (segment c of sample b, the rows param_small
+// writes), eight warps taking 32-neuron tiles of the segment in turn, one neuron per lane.
+// A lane runs the reverse sweep of hfam_bwd_s on its neuron, with the inputs and (full
+// history) adjoints in registers, writes grad_x and grad_v0 and keeps grad_pre in registers; when parameter gradients are wanted it writes grad_pre and
+// the saved history values of its neuron as column `lane` of the warp's padded GP / V rows
+// and the warp adds the tile's P[t][i] = sum_n GP[t,n] V[i,n] on the tensor pipe (3xTF32,
+// as warp_tile.cuh); VO-GL1's diagonal sum_n grad_pre[t,n] drift[t,n] is a per-lane fp32
+// sum.  grad_pre never goes to global memory, which saves writing and reading back
+// 8 bytes per neuron-step.  Rows reduce in double in a fixed order (deterministic).
+template <int TT>
+struct HfFusedCfg {
+    static constexpr int kWarps = 8;
+    static constexpr int TN = 32;                     // neurons per warp tile
+    static constexpr int RS = 40;                     // row stride: 8 banks apart
+    static constexpr int NT = TT / 8;                 // mma n-tiles of 8 output columns
+    static constexpr int NACC = 4 * NT;               // product accumulators per lane
+    static constexpr int NRED = NACC + TT;            // doubles per thread in the reduction
+    static constexpr int PER_WARP = 2 * TT * RS;      // GP rows, V rows
+    static constexpr size_t kTiles = sizeof(float) * kWarps * PER_WARP;
+    static constexpr size_t kRed = sizeof(double) * 32 * kWarps * NRED;
+    static constexpr size_t kBytes = kTiles > kRed ? kTiles : kRed;
+    static_assert(TT == 8 || TT == 16, "fused history backward covers T = 8 and T = 16");
+    static_assert(RS % 32 == 8, "fragment loads are conflict-free for rows 8 banks apart");
+};
+
+// acc[4*nt + e] += sum over the tile's 32 columns of GP[t] * V[i], fragment entry e of
+// n-tile nt: t = g + 8*(e >= 2), i = 8*nt + 2c + (e & 1) (g = lane / 4, c = lane % 4)
+template <int TT>
+__device__ __forceinline__ void hf_tile_product(const float* GP, const float* Vs, int lane,
+                                                float (&acc)[HfFusedCfg<TT>::NACC]) {
+    using C = HfFusedCfg<TT>;
+    constexpr int RS = C::RS;
+    const int g = lane >> 2, c = lane & 3;
+    float d[C::NT][4];
+#pragma unroll
+    for (int nt = 0; nt < C::NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) d[nt][e] = 0.0f;
+#pragma unroll
+    for (int k0 = 0; k0 < C::TN; k0 += 8) {
+        const float2 ar0 = *reinterpret_cast<const float2*>(GP + g * RS + k0 + 2 * c);
+        uint32_t ah[4], al[4];
+        split_tf32(ar0.x, ah[0], al[0]);
+        split_tf32(ar0.y, ah[2], al[2]);
+        if constexpr (TT == 16) {
+            const float2 ar1 = *reinterpret_cast<const float2*>(GP + (g + 8) * RS + k0 + 2 * c);
+            split_tf32(ar1.x, ah[1], al[1]);
+            split_tf32(ar1.y, ah[3], al[3]);
+        } else {
+            ah[1] = al[1] = ah[3] = al[3] = 0u;
+        }
+#pragma unroll
+        for (int nt = 0; nt < C::NT; ++nt) {
+            const float2 br = *reinterpret_cast<const float2*>(Vs + (8 * nt + g) * RS + k0 + 2 * c);
+            uint32_t bh0, bl0, bh1, bl1;
+            split_tf32(br.x, bh0, bl0);
+            split_tf32(br.y, bh1, bl1);
+            mma_tf32(d[nt], al[0], al[1], al[2], al[3], bh0, bh1);
+            mma_tf32(d[nt], ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+            mma_tf32(d[nt], ah[0], ah[1], ah[2], ah[3], bh0, bh1);
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < C::NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[4 * nt + e] = __fadd_rn(acc[4 * nt + e], d[nt][e]);
+}
+
+struct HfFusedOut {
+    const float* V;       // saved history sequence paired with grad_pre (NULL: no products)
+    const float* E;       // drift for VO-GL1's grad_scale (NULL: no diagonal)
+    double* part;         // partial rows [B*chunks][T + T*T]
+    int chunks;
+    long long per;        // neurons per segment
+};
+
+template <int HM, int TT, bool TAU_POW2, bool FAST_SG>
+__global__ void __launch_bounds__(256, 3) hfam_bwd_f(HfBwd a, HfFusedOut o) {
+    using C = HfFusedCfg<TT>;
+    constexpr int RS = C::RS;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float* GP = reinterpret_cast<float*>(smem) + warp * C::PER_WARP;
+    float* Vs = GP + TT * RS;
+    const long long N = a.N, F = a.tab.F;
+    const int b = blockIdx.x / o.chunks, c = blockIdx.x % o.chunks;
+    const long long nb = (long long)b * F + (long long)c * o.per;
+    const long long send = (long long)b * F + F;
+    const long long ne = nb + o.per < send ? nb + o.per : send;
+    const bool prod = o.V != nullptr, diag = o.E != nullptr;
+    float acc[C::NACC], gsd[TT];
+#pragma unroll
+    for (int e = 0; e < C::NACC; ++e) acc[e] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < TT; ++t) gsd[t] = 0.0f;
+    for (long long n0 = nb + (long long)warp * C::TN; n0 < ne; n0 += (long long)C::kWarps * C::TN) {
+        const long long n = n0 + lane;
+        const bool on = n < ne;
+        float gp[TT];
+        if (on) {
+            float pr[TT];
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+                gp[t] = ld_stream(a.gS + (long long)t * N + n);      // grad_spike, then grad_pre
+                pr[t] = ld_stream(a.vpre + (long long)t * N + n);
+            }
+            float A[HM == kFull ? TT : 1];
+#pragma unroll
+            for (int t = 0; t < (HM == kFull ? TT : 1); ++t) A[t] = 0.0f;
+            float gvn = 0.0f, ginit = 0.0f;
+#pragma unroll
+            for (int t = TT - 1; t >= 0; --t) {
+                const float sur = surr<FAST_SG>(__fsub_rn(pr[t], a.th), a.sg);
+                const float g = HM == kFull ? __fmaf_rn(gp[t], sur, A[t])
+                                            : __fmaf_rn(gp[t], sur, gvn);
+                gp[t] = g;
+                const float sv = a.tab.s(t, b);
+                const float* w = a.tab.wrow(t, b, TT);
+                st_stream(a.gx + (long long)t * N + n,
+                          div_tau<TAU_POW2>(__fmul_rn(g, sv), a.tau, a.inv_tau));
+                if constexpr (HM == kFull) {
+                    const float prev = div_tau<TAU_POW2>(__fmul_rn(-g, sv), a.tau, a.inv_tau);
+                    if (t == 0) ginit = __fadd_rn(ginit, prev);
+                    else A[t > 0 ? t - 1 : 0] = __fadd_rn(A[t > 0 ? t - 1 : 0], prev);
+#pragma unroll
+                    for (int i = 0; i < t; ++i) A[i] = __fmaf_rn(-__ldg(w + i), g, A[i]);
+                } else {
+                    gvn = trunc_next<HM, TAU_POW2>(a, w, t, g, sv);
+                }
+            }
+            a.gv0[n] = HM == kFull ? ginit : gvn;
+        } else {
+#pragma unroll
+            for (int t = 0; t < TT; ++t) gp[t] = 0.0f;
+        }
+        if (prod) {
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+                GP[t * RS + lane] = gp[t];
+                Vs[t * RS + lane] = on ? ld_stream(o.V + (long long)t * N + n) : 0.0f;
+            }
+            if (diag && on) {
+#pragma unroll
+                for (int t = 0; t < TT; ++t)
+                    gsd[t] = __fmaf_rn(gp[t], ld_stream(o.E + (long long)t * N + n), gsd[t]);
+            }
+            __syncwarp();
+            hf_tile_product<TT>(GP, Vs, lane, acc);
+            __syncwarp();                             // the rows are rewritten by the next tile
+        }
+    }
+    if (!prod) return;                                // uniform: no block barrier follows
+    __syncthreads();                                  // every warp is done with its rows
+    double* red = reinterpret_cast<double*>(smem);
+    double* mine = red + (size_t)tid * C::NRED;
+#pragma unroll
+    for (int e = 0; e < C::NACC; ++e) mine[e] = (double)acc[e];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) mine[C::NACC + t] = (double)gsd[t];
+    __syncthreads();
+    double* row = o.part + (size_t)blockIdx.x * (TT + TT * TT);
+    for (int q = tid; q < TT + TT * TT; q += blockDim.x) {
+        double sum = 0.0;
+        if (q < TT) {
+            if (diag)
+                for (int r = 0; r < C::kWarps * 32; ++r) sum += red[(size_t)r * C::NRED + C::NACC + q];
+        } else {
+            const int t = (q - TT) / TT, i = (q - TT) % TT;
+            const int ln = 4 * (t & 7) + ((i & 7) >> 1);
+            const int slot = 4 * (i >> 3) + (t >= 8 ? 2 : 0) + (i & 1);
+            for (int w = 0; w < C::kWarps; ++w) sum += red[(size_t)(w * 32 + ln) * C::NRED + slot];
+        }
+        row[q] = sum;
+    }
 }
 
 // msum[u][e] = sum of the rows of output unit u (sample u, or every row when shared) --
@@ -354,23 +493,26 @@ bool fast_sg(float sg) {
 }
 
 template <int HM>
-cudaError_t bwd_dispatch(const HfBwd& a, bool tau_pow2, bool fsg, cudaStream_t st) {
+cudaError_t bwd_dispatch(const HfBwd& a, const HfFusedOut& o, int B, bool tau_pow2, bool fsg,
+                         cudaStream_t st) {
     const int T = a.T;
-    if (T == 8 || T == 16) {
-        const unsigned grid = (unsigned)((a.N + 255) / 256);
-#define DFSNN_HF_BWD(TV)                                                                      \
-        if (T == TV) {                                                                        \
-            if (tau_pow2) {                                                                   \
-                if (fsg) hfam_bwd_r<HM, TV, true, true><<<grid, 256, 0, st>>>(a);             \
-                else hfam_bwd_r<HM, TV, true, false><<<grid, 256, 0, st>>>(a);                \
-            } else {                                                                          \
-                if (fsg) hfam_bwd_r<HM, TV, false, true><<<grid, 256, 0, st>>>(a);            \
-                else hfam_bwd_r<HM, TV, false, false><<<grid, 256, 0, st>>>(a);               \
-            }                                                                                 \
+    if (hfam_backward_fused(T)) {
+        const unsigned grid = (unsigned)((long long)B * o.chunks);
+#define DFSNN_HF_BWD(TV, P2, FS)                                                              \
+        if (T == TV && tau_pow2 == P2 && fsg == FS) {                                         \
+            auto k = hfam_bwd_f<HM, TV, P2, FS>;                                              \
+            const int bytes = (int)HfFusedCfg<TV>::kBytes;                                    \
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); \
+            if (e != cudaSuccess) return e;                                                   \
+            k<<<grid, 256, bytes, st>>>(a, o);                                                \
+            return cudaGetLastError();                                                        \
         }
-        DFSNN_HF_BWD(8) DFSNN_HF_BWD(16)
+        DFSNN_HF_BWD(8, true, true) DFSNN_HF_BWD(8, true, false)
+        DFSNN_HF_BWD(8, false, true) DFSNN_HF_BWD(8, false, false)
+        DFSNN_HF_BWD(16, true, true) DFSNN_HF_BWD(16, true, false)
+        DFSNN_HF_BWD(16, false, true) DFSNN_HF_BWD(16, false, false)
 #undef DFSNN_HF_BWD
-        return cudaGetLastError();
+        return cudaErrorInvalidValue;
     }
     const unsigned grid = (unsigned)((a.N + 127) / 128);
     const size_t smem = HM == kFull ? (size_t)T * 128 * sizeof(float) : 0;
@@ -386,9 +528,12 @@ cudaError_t bwd_dispatch(const HfBwd& a, bool tau_pow2, bool fsg, cudaStream_t s
 
 }  // namespace
 
+bool hfam_backward_fused(int T) { return T == 8 || T == 16; }
+
 cudaError_t hfam_backward_launch(int kind, bool full, const float* gS, const float* scale,
                                  float h_beta, const float* W, int B, bool per_batch,
-                                 const float* vpre, float* gx, float* gv0, float* gpre, int T,
+                                 const float* vpre, float* gx, float* gv0, float* gpre,
+                                 const float* V, const float* E, double* part, int chunks, int T,
                                  long long N, float tau, float th, float sg, float rm,
                                  bool tau_pow2, cudaStream_t st) {
     if (N <= 0) return cudaSuccess;
@@ -406,10 +551,17 @@ cudaError_t hfam_backward_launch(int kind, bool full, const float* gS, const flo
     a.th = th;
     a.sg = sg;
     a.rm = rm;
+    HfFusedOut o;
+    o.V = V;
+    o.E = V ? E : nullptr;
+    o.part = part;
+    o.chunks = chunks < 1 ? 1 : chunks;
+    const long long F = N / B;
+    o.per = (F + o.chunks - 1) / o.chunks;
     const bool fsg = fast_sg(sg);
-    if (kind == kVOPRED) return bwd_dispatch<kPredMode>(a, tau_pow2, fsg, st);
-    if (full) return bwd_dispatch<kFull>(a, tau_pow2, fsg, st);
-    return bwd_dispatch<kTrunc>(a, tau_pow2, fsg, st);
+    if (kind == kVOPRED) return bwd_dispatch<kPredMode>(a, o, B, tau_pow2, fsg, st);
+    if (full) return bwd_dispatch<kFull>(a, o, B, tau_pow2, fsg, st);
+    return bwd_dispatch<kTrunc>(a, o, B, tau_pow2, fsg, st);
 }
 
 cudaError_t hfam_param_finalize(int kind, const double* part, int chunks, int B, bool per_batch,

@@ -56,9 +56,15 @@ cudaError_t hfam_forward_launch(int kind, const float* x, const float* v0, const
                                 float h_beta, const float* W, int B, bool per_batch, float* spike,
                                 float* vpre, float* hsrc, float* drift, int T, long long N,
                                 float tau, float th, float rm, bool tau_pow2, cudaStream_t st);
+// T = 8 and 16: one kernel runs the reverse sweep and writes the parameter rows (part, the
+// layout of param_rows_launch with B*chunks rows) from V (and E, VO-GL1's drift) itself, when
+// V is non-NULL; grad_pre is never stored.  Other T: the sweep writes grad_pre [T, N] and the
+// caller reduces it with param_rows_launch.
+bool hfam_backward_fused(int T);
 cudaError_t hfam_backward_launch(int kind, bool full, const float* gS, const float* scale,
                                  float h_beta, const float* W, int B, bool per_batch,
-                                 const float* vpre, float* gx, float* gv0, float* gpre, int T,
+                                 const float* vpre, float* gx, float* gv0, float* gpre,
+                                 const float* V, const float* E, double* part, int chunks, int T,
                                  long long N, float tau, float th, float sg, float rm,
                                  bool tau_pow2, cudaStream_t st);
 // gscale / gW from the summed rows (either may be NULL); msum holds (per_batch ? B : 1) rows

@@ -323,6 +323,14 @@ def _hist_save(ctx, x, tau, threshold, surrogate_grad_scale, original_dtype, B, 
     ctx.residual_mix = float(residual_mix)
 
 
+def _hist_launches(T, params):
+    """Kernels one history-table backward launches: the sweep, and with parameter gradients
+    the row reduction (fused into the sweep for T = 8 and 16), the row sums and the epilogue."""
+    if not params:
+        return 1
+    return 3 if T in (8, 16) else 4
+
+
 def _hist_workspace(ctx, device):
     T, N = ctx.input_shape
     nbytes = _capi.history_workspace_bytes(device, T, N, ctx.batch_size, ctx.per_batch)
@@ -374,7 +382,7 @@ class LIFFDEVOGL1Function(torch.autograd.Function):
         nparam = (2 if grad_weights is not None else 0) + (1 if grad_scale is not None else 0)
         with torch.cuda.device(dev):
             ws = _hist_workspace(ctx, dev)
-            with _prof.native_call("vo_gl1_backward", 4 if nparam else 1,
+            with _prof.native_call("vo_gl1_backward", _hist_launches(T, nparam),
                                    _prof.history_backward_bytes(T, N, min(nparam, 2)), dev):
                 code = _capi.lib().dfsnn_vo_gl1_backward(
                     _capi.ptr(g), _capi.ptr(s), _capi.ptr(w), _capi.ptr(v_pre), _capi.ptr(v_hist),
@@ -451,7 +459,7 @@ class LIFFDEFAGL1Function(torch.autograd.Function):
         grad_weights = torch.empty_like(w) if ctx.needs_input_grad[2] else None
         with torch.cuda.device(dev):
             ws = _hist_workspace(ctx, dev)
-            with _prof.native_call("fa_gl1_backward", 4 if grad_weights is not None else 1,
+            with _prof.native_call("fa_gl1_backward", _hist_launches(T, grad_weights is not None),
                                    _prof.history_backward_bytes(
                                        T, N, 1 if grad_weights is not None else 0), dev):
                 code = _capi.lib().dfsnn_fa_gl1_backward(
@@ -493,7 +501,7 @@ class LIFFDEFAGL1TorchFunction(torch.autograd.Function):
                        device=dev, dtype=torch.float32)
         with torch.cuda.device(dev):
             ws = _hist_workspace(ctx, dev)
-            with _prof.native_call("fa_gl1_backward", 4 if grad_weights is not None else 1,
+            with _prof.native_call("fa_gl1_backward", _hist_launches(T, grad_weights is not None),
                                    _prof.history_backward_bytes(
                                        T, N, 1 if grad_weights is not None else 0), dev):
                 code = _capi.lib().dfsnn_vo_gl1_backward(
@@ -552,7 +560,7 @@ class LIFFDEVOPREDICTORFunction(torch.autograd.Function):
         params = grad_scale is not None or grad_weights is not None
         with torch.cuda.device(dev):
             ws = _hist_workspace(ctx, dev)
-            with _prof.native_call("vo_predictor_backward", 4 if params else 1,
+            with _prof.native_call("vo_predictor_backward", _hist_launches(T, params),
                                    _prof.history_backward_bytes(T, N, 1 if params else 0), dev):
                 code = _capi.lib().dfsnn_vo_predictor_backward(
                     _capi.ptr(g), _capi.ptr(s), _capi.ptr(w), _capi.ptr(v_pre), _capi.ptr(drift),

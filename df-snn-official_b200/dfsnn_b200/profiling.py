@@ -144,9 +144,11 @@ def history_forward_bytes(T, N, seqs_out):
 
 
 def history_backward_bytes(T, N, param_seqs):
-    # grad_spike, v_pre in; grad_x, grad_pre out; grad_v0 out; the parameter reduction reads
-    # grad_pre and the saved sequences back (param_seqs of them, 0 when no parameter grads)
-    return N * (4 * T * (4 + (1 + param_seqs if param_seqs else 0)) + 4)
+    # compulsory: grad_spike, v_pre in; grad_x out; grad_v0 out; the saved sequences the
+    # parameter gradients pair with grad_pre (param_seqs of them, 0 without parameter grads).
+    # grad_pre itself is an intermediate (T = 8 and 16 never store it; other T write it and
+    # read it back, 8 more bytes per neuron-step than counted here)
+    return N * (4 * T * (3 + param_seqs) + 4)
 
 
 def euler_forward_bytes(T, N):
