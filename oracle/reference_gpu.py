@@ -112,6 +112,8 @@ class Reference:
         self.pkg = sys.modules["spikeDE_dis"]
 
     def use_reference(self):
+        from dfsnn_b200 import integrate
+        integrate.uninstall_schedule()
         sys.modules[FDE] = self.kernels
         sys.modules[EULER] = self.euler
         self.pkg.fde_cupy_kernels_all = self.kernels
@@ -122,6 +124,8 @@ class Reference:
         integrate.install()
 
     def close(self):
+        from dfsnn_b200 import integrate
+        integrate.uninstall_schedule()
         for name in list(sys.modules):
             if name not in self._before and name.split(".")[0] in _OWNED:
                 del sys.modules[name]

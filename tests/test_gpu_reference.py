@@ -336,6 +336,52 @@ def test_reference_neuron_drop_in(ref, method, T):
         assert float((pg - pw).abs().max()) <= RTOL * scale * 10, f"{tag} mass gradient"
 
 
+@pytest.mark.parametrize("T", [8, 16])
+@pytest.mark.parametrize("learn", [True, False])
+def test_reference_glmulti_schedule_native(ref, T, learn):
+    """integrate.install() also rebinds the reference neuron's own _build_glmulti_schedule
+    (neuron.py:1494-1514) to the native one: scale and W from one launch are bit-identical to
+    the reference's chain of small PyTorch kernels, and the gradient to the raw Softplus masses
+    (one more launch, accumulated in double) agrees within the suite's tolerance."""
+    from dfsnn_b200 import profiling
+    kw = dict(tau=TAU, threshold=TH, surrogate_grad_scale=SG, surrogate_function="arctan",
+              T=T, method="glmulti", step_size=H, batchsize=16, step_mode="m", backend="cupy",
+              beta=0.3, multi_beta=[0.3, 0.4, 0.5], multi_coefficient=[0.5, 0.5, 0.7],
+              learn_coefficient=learn, coefficient_constraint="softplus",
+              glmulti_history_grad="full")
+    g = torch.Generator(device=DEV).manual_seed(900 + T)
+    gs = torch.randn(T, device=DEV, generator=g)
+    gw = torch.randn(T, T, device=DEV, generator=g)
+
+    def run(layer):
+        terms = layer._build_glmulti_schedule(T, torch.device(DEV))
+        params = [p for p in layer.parameters() if p.requires_grad]
+        grads = (torch.autograd.grad([terms["scale"], terms["weights"]], params, [gs, gw])
+                 if params else [])
+        return terms["scale"].detach(), terms["weights"].detach(), list(grads)
+
+    try:
+        ref.use_reference()
+        own = ref.neuron.LIFNeuronFDE._build_glmulti_schedule
+        want = run(ref.neuron.LIFNeuronFDE(**kw).to(DEV))
+        ref.use_native()
+        assert ref.neuron.LIFNeuronFDE._build_glmulti_schedule is not own
+        with profiling.NativeCallTimer() as timer:
+            got = run(ref.neuron.LIFNeuronFDE(**kw).to(DEV))
+            torch.cuda.synchronize()
+        assert timer.calls["glmulti_schedule_forward"] == 1
+        assert timer.calls["glmulti_schedule_backward"] == (1 if learn else 0)
+    finally:
+        ref.use_reference()
+    assert ref.neuron.LIFNeuronFDE._build_glmulti_schedule is own
+    assert_bitwise_gpu(got[0], want[0], f"T={T} scale")
+    assert_bitwise_gpu(got[1], want[1], f"T={T} weights")
+    assert len(got[2]) == len(want[2]) == (1 if learn else 0)
+    for pg, pw in zip(got[2], want[2]):
+        scale = float(pw.abs().max()) + 1e-30
+        assert float((pg - pw).abs().max()) <= RTOL * scale, f"T={T} raw-mass gradient"
+
+
 # -------------------------------------------------------------------------------------
 # the CNN128 example itself (examples/cnn128/cnn128_aligned.py), unmodified
 # -------------------------------------------------------------------------------------

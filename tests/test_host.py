@@ -137,6 +137,7 @@ def test_integrate_registers_reference_module_names():
         assert fde_kernels.LIFFDEGLMultiFunction is alg.AlignedGLMulti
         fde_kernels.LIFFDEGLMultiFunction = original
     finally:
+        integrate.uninstall_schedule()
         for k, v in saved.items():
             if v is None:
                 sys.modules.pop(k, None)
@@ -375,3 +376,32 @@ def test_bench_step_costs(monkeypatch):
     assert len(syncs) == 10 and 2.5 <= host < 50
     one = costs.summary(4, host, torch.device("cpu"), 1)
     assert set(one) == {"host_ms_per_step"} and one["host_ms_per_step"] == round(host, 4)
+
+
+def test_integrate_rebinds_reference_glmulti_schedule():
+    """install() rebinds the reference neuron's _build_glmulti_schedule to this library's
+    (on CPU tensors it keeps the PyTorch chain, bitwise equal to the reference's own), and
+    the reference harness gives the class its own method back."""
+    from oracle import reference_gpu
+    if not reference_gpu.staged():
+        pytest.skip("reference not staged (oracle/stage_ref.py)")
+    ref = reference_gpu.Reference(standin=False)
+    try:
+        cls = ref.neuron.LIFNeuronFDE
+        own = cls._build_glmulti_schedule
+        layer = cls(tau=TAU, threshold=TH, surrogate_grad_scale=SG, surrogate_function="arctan",
+                    beta=MULTI_BETA[0], T=8, method="glmulti", step_size=H, batchsize=4,
+                    step_mode="m", backend="cupy", multi_beta=MULTI_BETA,
+                    multi_coefficient=MASSES, learn_coefficient=True,
+                    coefficient_constraint="softplus", glmulti_history_grad="full")
+        want = layer._build_glmulti_schedule(8, torch.device("cpu"))
+        ref.use_native()
+        assert cls._build_glmulti_schedule is neuron.LIFNeuronFDE._build_glmulti_schedule
+        got = layer._build_glmulti_schedule(8, torch.device("cpu"))
+        for k in ("scale", "weights"):
+            assert_bitwise(got[k].detach().numpy(), want[k].detach().numpy(), what=k)
+        ref.use_reference()
+        assert cls._build_glmulti_schedule is own
+    finally:
+        ref.close()
+    assert not integrate._SAVED_SCHEDULE
